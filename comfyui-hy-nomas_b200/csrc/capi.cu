@@ -1,0 +1,319 @@
+// capi.cu - the extern "C" entry points declared in include/hynomas_b200.h.
+//
+// Each entry validates its arguments on the host (shapes, null pointers, enum values, the 16-byte
+// alignment the vector/TMA paths rely on), checks once per device that it is a compute capability 10.0
+// part, launches on the caller's stream and returns an hn_status. Errors never abort the process; the
+// message is kept per calling thread for hn_last_error().
+#include <stdarg.h>
+#include <stdio.h>
+#include <string.h>
+
+#include <mutex>
+#include <string>
+
+#include "../../include/hynomas_b200.h"
+#include "hn_common.cuh"
+#include "hn_kernels.h"
+
+namespace hn {
+
+static thread_local std::string t_last_error;
+
+static int fail(int code, const char *fmt, ...) __attribute__((format(printf, 2, 3)));
+static int fail(int code, const char *fmt, ...) {
+    char buf[512];
+    va_list ap;
+    va_start(ap, fmt);
+    vsnprintf(buf, sizeof(buf), fmt, ap);
+    va_end(ap);
+    t_last_error = buf;
+    return code;
+}
+
+static int cuda_fail(cudaError_t e, const char *what) {
+    return fail(HN_ERR_CUDA, "%s: %s (%s)", what, cudaGetErrorString(e), cudaGetErrorName(e));
+}
+
+constexpr int MAX_DEV = 64;
+static int g_sms[MAX_DEV];
+static int g_arch_ok[MAX_DEV];  // 0 unknown, 1 ok, -1 not sm_100
+static std::mutex g_mu;
+
+static int current_device(int *dev) {
+    cudaError_t e = cudaGetDevice(dev);
+    if (e != cudaSuccess) return cuda_fail(e, "cudaGetDevice");
+    if (*dev < 0 || *dev >= MAX_DEV) return fail(HN_ERR_ARG, "device index %d out of range", *dev);
+    return HN_OK;
+}
+
+static int check_arch() {
+    int dev;
+    int rc = current_device(&dev);
+    if (rc) return rc;
+    if (g_arch_ok[dev] == 0) {
+        std::lock_guard<std::mutex> lk(g_mu);
+        int major = 0, minor = 0, sms = 0;
+        cudaDeviceGetAttribute(&major, cudaDevAttrComputeCapabilityMajor, dev);
+        cudaDeviceGetAttribute(&minor, cudaDevAttrComputeCapabilityMinor, dev);
+        cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
+        g_sms[dev] = sms;
+        g_arch_ok[dev] = (major == 10 && minor == 0) ? 1 : -1;
+        if (g_arch_ok[dev] < 0) t_last_error = "";
+    }
+    if (g_arch_ok[dev] < 0) {
+        int major = 0, minor = 0;
+        cudaDeviceGetAttribute(&major, cudaDevAttrComputeCapabilityMajor, dev);
+        cudaDeviceGetAttribute(&minor, cudaDevAttrComputeCapabilityMinor, dev);
+        return fail(HN_ERR_ARCH, "device %d is sm_%d%d; this library runs on sm_100a (B200) only", dev, major, minor);
+    }
+    return HN_OK;
+}
+
+int num_sms() {
+    int dev = 0;
+    if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= MAX_DEV) return 148;
+    if (g_sms[dev] == 0) {
+        int sms = 0;
+        cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
+        g_sms[dev] = sms > 0 ? sms : 148;
+    }
+    return g_sms[dev];
+}
+
+static inline bool al16(const void *p) { return (reinterpret_cast<uintptr_t>(p) & 15) == 0; }
+static inline bool al8(const void *p) { return (reinterpret_cast<uintptr_t>(p) & 7) == 0; }
+static inline int dsize(int dt) { return dt == HN_DTYPE_FP32 || dt == HN_DTYPE_INT32 ? 4 : 2; }
+
+static int launched(cudaError_t e, const char *what) {
+    if (e != cudaSuccess) return cuda_fail(e, what);
+    t_last_error.clear();
+    return HN_OK;
+}
+
+} // namespace hn
+
+using namespace hn;
+
+#define CHECK_ARCH()                  \
+    do {                              \
+        int _rc = check_arch();       \
+        if (_rc != HN_OK) return _rc; \
+    } while (0)
+#define REQUIRE(cond, code, ...)                      \
+    do {                                              \
+        if (!(cond)) return fail((code), __VA_ARGS__); \
+    } while (0)
+
+extern "C" {
+
+const char *hn_last_error(void) { return t_last_error.c_str(); }
+
+int hn_abi_version(void) { return HN_ABI_VERSION; }
+
+int hn_num_sms(void) {
+    int n = 0;
+    if (cudaGetDeviceCount(&n) != cudaSuccess || n == 0) {
+        cudaGetLastError();
+        return 0;
+    }
+    return num_sms();
+}
+
+int hn_device_error(void *stream, int *code_host) {
+    REQUIRE(code_host != nullptr, HN_ERR_ARG, "code_host is NULL");
+    cudaStream_t st = static_cast<cudaStream_t>(stream);
+    cudaError_t e = cudaStreamSynchronize(st);
+    if (e != cudaSuccess) return cuda_fail(e, "cudaStreamSynchronize");
+    int v = 0;
+    e = read_and_clear_device_error(&v);
+    if (e != cudaSuccess) return cuda_fail(e, "reading the device error word");
+    *code_host = v;
+    if (v & HN_DEVERR_TIMEOUT) return fail(HN_ERR_TIMEOUT, "a device-side wait ran past its limit");
+    t_last_error.clear();
+    return HN_OK;
+}
+
+int hn_selftest_wait_timeout(uint32_t timeout_us, void *stream) {
+    CHECK_ARCH();
+    REQUIRE(timeout_us > 0 && timeout_us <= 2000000u, HN_ERR_ARG, "timeout_us must be in (0, 2e6]");
+    return launched(launch_wait_selftest(timeout_us, static_cast<cudaStream_t>(stream)), "wait self-test launch");
+}
+
+int hn_quant_act(const void *x, int64_t ldx, int x_dtype, int64_t M, int64_t K, int kind, int per_row, void *q,
+                 int64_t ldq, float *s, int64_t lds, void *stream) {
+    REQUIRE(x && q && s, HN_ERR_ARG, "hn_quant_act: null pointer");
+    REQUIRE(x_dtype == HN_DTYPE_BF16 || x_dtype == HN_DTYPE_FP16 || x_dtype == HN_DTYPE_FP32, HN_ERR_ARG,
+            "hn_quant_act: x_dtype %d not bf16/fp16/fp32", x_dtype);
+    REQUIRE(kind == HN_KIND_INT8 || kind == HN_KIND_FP8E4M3, HN_ERR_ARG, "hn_quant_act: unknown kind %d", kind);
+    REQUIRE(M >= 0 && K > 0 && K % 128 == 0, HN_ERR_SHAPE, "hn_quant_act: need K %% 128 == 0 (M=%lld K=%lld)",
+            (long long)M, (long long)K);
+    REQUIRE(ldx >= K && ldq >= K && lds >= (per_row ? 1 : K / 128), HN_ERR_SHAPE, "hn_quant_act: leading dimension too small");
+    REQUIRE(M <= 0x7fffffffLL, HN_ERR_SHAPE, "hn_quant_act: M too large");
+    REQUIRE(al16(x) && (ldx * dsize(x_dtype)) % 16 == 0 && al16(q) && ldq % 16 == 0, HN_ERR_ALIGN,
+            "hn_quant_act: x/q must be 16-byte aligned with 16-byte row pitch");
+    if (M == 0) return HN_OK;
+    CHECK_ARCH();
+    return launched(launch_quant_act(x, ldx, x_dtype, M, K, kind, per_row, q, ldq, s, lds, (cudaStream_t)stream),
+                    "hn_quant_act launch");
+}
+
+int hn_block_gemm(const void *qa, int64_t lda, const float *sa, int64_t ldsa, int sa_mode, const void *qw,
+                  int64_t ldw, const float *sw, int64_t ldsw, int sw_mode, const void *bias, int bias_dtype, void *out,
+                  int64_t ldo, int out_dtype, float *qs, int64_t ldqs, int64_t M, int64_t N, int64_t K, int kind,
+                  int epilogue, void *stream) {
+    REQUIRE(qa && sa && qw && sw && out, HN_ERR_ARG, "hn_block_gemm: null pointer");
+    REQUIRE(kind == HN_KIND_INT8 || kind == HN_KIND_FP8E4M3, HN_ERR_ARG, "hn_block_gemm: unknown kind %d", kind);
+    REQUIRE(sa_mode == HN_SCALE_GROUP || sa_mode == HN_SCALE_ROW, HN_ERR_ARG, "hn_block_gemm: bad sa_mode %d", sa_mode);
+    REQUIRE(sw_mode >= HN_SCALE_GROUP && sw_mode <= HN_SCALE_BLOCK, HN_ERR_ARG, "hn_block_gemm: bad sw_mode %d", sw_mode);
+    REQUIRE(epilogue >= HN_EPI_NONE && epilogue <= HN_EPI_GELU_QUANT, HN_ERR_ARG, "hn_block_gemm: bad epilogue %d", epilogue);
+    REQUIRE(M >= 0 && N > 0 && K > 0 && K % 128 == 0, HN_ERR_SHAPE,
+            "hn_block_gemm: need K %% 128 == 0, N > 0 (M=%lld N=%lld K=%lld)", (long long)M, (long long)N, (long long)K);
+    REQUIRE(M < (1LL << 31) && N < (1LL << 31) && K < (1LL << 31), HN_ERR_SHAPE, "hn_block_gemm: dimension too large");
+    REQUIRE(lda >= K && ldw >= K && ldo >= N, HN_ERR_SHAPE, "hn_block_gemm: leading dimension too small");
+    REQUIRE(sa_mode != HN_SCALE_GROUP || ldsa >= K / 128, HN_ERR_SHAPE, "hn_block_gemm: ldsa < K/128");
+    REQUIRE(sw_mode != HN_SCALE_GROUP || ldsw >= K / 128, HN_ERR_SHAPE, "hn_block_gemm: ldsw < K/128");
+    REQUIRE(sw_mode != HN_SCALE_BLOCK || ldsw >= K / 128, HN_ERR_SHAPE, "hn_block_gemm: ldsw < K/128 (block)");
+    REQUIRE(al16(qa) && al16(qw) && lda % 16 == 0 && ldw % 16 == 0, HN_ERR_ALIGN,
+            "hn_block_gemm: qa/qw must be 16-byte aligned with row pitch a multiple of 16");
+    if (epilogue == HN_EPI_GELU_QUANT) {
+        REQUIRE(qs != nullptr, HN_ERR_ARG, "hn_block_gemm: gelu_quant needs qs");
+        REQUIRE(N % 128 == 0, HN_ERR_SHAPE, "hn_block_gemm: gelu_quant needs N %% 128 == 0");
+        REQUIRE(ldqs >= N / 128, HN_ERR_SHAPE, "hn_block_gemm: ldqs < N/128");
+        REQUIRE(al16(out) && ldo % 16 == 0, HN_ERR_ALIGN, "hn_block_gemm: int8 output must be 16-byte aligned");
+    } else if (epilogue == HN_EPI_GELU) {
+        REQUIRE(out_dtype == HN_DTYPE_BF16, HN_ERR_UNSUPPORTED, "hn_block_gemm: gelu output is bf16");
+    } else {
+        REQUIRE(out_dtype >= HN_DTYPE_BF16 && out_dtype <= HN_DTYPE_INT32, HN_ERR_ARG, "hn_block_gemm: bad out_dtype %d", out_dtype);
+    }
+    if (out_dtype == HN_DTYPE_INT32)
+        REQUIRE(kind == HN_KIND_INT8 && sa_mode == HN_SCALE_ROW && sw_mode == HN_SCALE_ROW && bias == nullptr &&
+                    epilogue == HN_EPI_NONE,
+                HN_ERR_UNSUPPORTED, "hn_block_gemm: int32 output is the raw int8 accumulator (row scales, no bias)");
+    if (bias) REQUIRE(bias_dtype == HN_DTYPE_BF16 || bias_dtype == HN_DTYPE_FP16 || bias_dtype == HN_DTYPE_FP32,
+                      HN_ERR_ARG, "hn_block_gemm: bad bias dtype %d", bias_dtype);
+    if (bias && N % 8 == 0) REQUIRE(al16(bias), HN_ERR_ALIGN, "hn_block_gemm: bias must be 16-byte aligned");
+    if (M == 0) return HN_OK;
+    CHECK_ARCH();
+    GemmArgs a;
+    a.qa = qa; a.lda = lda; a.sa = sa; a.ldsa = ldsa; a.sa_mode = sa_mode;
+    a.qw = qw; a.ldw = ldw; a.sw = sw; a.ldsw = ldsw; a.sw_mode = sw_mode;
+    a.bias = bias; a.bias_dtype = bias_dtype;
+    a.out = out; a.ldo = ldo; a.out_dtype = out_dtype; a.qs = qs; a.ldqs = ldqs;
+    a.M = M; a.N = N; a.K = K; a.kind = kind; a.epilogue = epilogue;
+    const char *msg = nullptr;
+    cudaError_t e = launch_block_gemm(a, (cudaStream_t)stream, &msg);
+    if (e != cudaSuccess && msg) return fail(HN_ERR_ALIGN, "hn_block_gemm: %s", msg);
+    return launched(e, "hn_block_gemm launch");
+}
+
+static int ln_common(const void *x, const void *shift, const void *scale, int64_t B, int64_t L, int64_t D, int quant,
+                     const char *name) {
+    REQUIRE(x && shift && scale, HN_ERR_ARG, "%s: null pointer", name);
+    REQUIRE(B > 0 && L >= 0 && D > 0 && D <= 16384, HN_ERR_SHAPE, "%s: bad shape B=%lld L=%lld D=%lld", name,
+            (long long)B, (long long)L, (long long)D);
+    REQUIRE(quant ? D % 128 == 0 : D % 16 == 0, HN_ERR_SHAPE, "%s: D %% %d != 0", name, quant ? 128 : 16);
+    REQUIRE(B * L < (1LL << 31), HN_ERR_SHAPE, "%s: too many rows", name);
+    REQUIRE(al16(x) && al16(shift) && al16(scale), HN_ERR_ALIGN, "%s: inputs must be 16-byte aligned", name);
+    return HN_OK;
+}
+
+int hn_adaln_quant(const void *x, const void *shift, const void *scale, int64_t B, int64_t L, int64_t D, float eps,
+                   int8_t *q, float *s, void *stream) {
+    int rc = ln_common(x, shift, scale, B, L, D, 1, "hn_adaln_quant");
+    if (rc) return rc;
+    REQUIRE(q && s && al16(q), HN_ERR_ARG, "hn_adaln_quant: null or misaligned output");
+    if (L == 0) return HN_OK;
+    CHECK_ARCH();
+    return launched(launch_ln_row(1, x, nullptr, nullptr, shift, scale, B, L, D, eps, nullptr, q, s, (cudaStream_t)stream),
+                    "hn_adaln_quant launch");
+}
+
+int hn_adaln(const void *x, const void *shift, const void *scale, int64_t B, int64_t L, int64_t D, float eps, void *y,
+             void *stream) {
+    int rc = ln_common(x, shift, scale, B, L, D, 0, "hn_adaln");
+    if (rc) return rc;
+    REQUIRE(y && al16(y), HN_ERR_ARG, "hn_adaln: null or misaligned output");
+    if (L == 0) return HN_OK;
+    CHECK_ARCH();
+    return launched(launch_ln_row(0, x, nullptr, nullptr, shift, scale, B, L, D, eps, y, nullptr, nullptr, (cudaStream_t)stream),
+                    "hn_adaln launch");
+}
+
+int hn_gated_residual_adaln_quant(const void *x, const void *y, const void *gate, const void *shift, const void *scale,
+                                  int64_t B, int64_t L, int64_t D, float eps, void *out, int8_t *q, float *s,
+                                  void *stream) {
+    int rc = ln_common(x, shift, scale, B, L, D, 1, "hn_gated_residual_adaln_quant");
+    if (rc) return rc;
+    REQUIRE(y && gate && out && q && s, HN_ERR_ARG, "hn_gated_residual_adaln_quant: null pointer");
+    REQUIRE(al16(y) && al16(gate) && al16(out) && al16(q), HN_ERR_ALIGN,
+            "hn_gated_residual_adaln_quant: buffers must be 16-byte aligned");
+    if (L == 0) return HN_OK;
+    CHECK_ARCH();
+    return launched(launch_ln_row(2, x, y, gate, shift, scale, B, L, D, eps, out, q, s, (cudaStream_t)stream),
+                    "hn_gated_residual_adaln_quant launch");
+}
+
+int hn_gated_residual(const void *x, const void *y, const void *gate, int64_t B, int64_t L, int64_t D, void *out,
+                      void *stream) {
+    REQUIRE(x && y && gate && out, HN_ERR_ARG, "hn_gated_residual: null pointer");
+    REQUIRE(B > 0 && L >= 0 && D > 0 && D % 8 == 0, HN_ERR_SHAPE, "hn_gated_residual: need D %% 8 == 0");
+    REQUIRE(al16(x) && al16(y) && al16(gate) && al16(out), HN_ERR_ALIGN, "hn_gated_residual: buffers must be 16-byte aligned");
+    if (L == 0) return HN_OK;
+    CHECK_ARCH();
+    return launched(launch_gated_residual(x, y, gate, B, L, D, out, (cudaStream_t)stream), "hn_gated_residual launch");
+}
+
+static int qk_common(const void *x, int64_t row_stride, const void *w, const float *cos, const float *sin, int64_t B,
+                     int64_t L, int64_t H, int64_t D, const void *y) {
+    REQUIRE(x && w && y, HN_ERR_ARG, "hn_qk_norm_rope: null pointer");
+    REQUIRE((cos == nullptr) == (sin == nullptr), HN_ERR_ARG, "hn_qk_norm_rope: cos and sin must both be given or both NULL");
+    REQUIRE(D == 128, HN_ERR_UNSUPPORTED, "hn_qk_norm_rope: head dim %lld (kernels are built for 128)", (long long)D);
+    REQUIRE(B > 0 && L >= 0 && H > 0 && row_stride >= H * D, HN_ERR_SHAPE, "hn_qk_norm_rope: bad shape/stride");
+    REQUIRE(al8(x) && row_stride % 4 == 0 && al8(w) && al8(y), HN_ERR_ALIGN, "hn_qk_norm_rope: x/w/y must be 8-byte aligned");
+    REQUIRE(cos == nullptr || (al16(cos) && al16(sin)), HN_ERR_ALIGN, "hn_qk_norm_rope: cos/sin must be 16-byte aligned");
+    return HN_OK;
+}
+
+int hn_qk_norm_rope(const void *x, int64_t row_stride, const void *weight, const float *cos, const float *sin,
+                    int64_t B, int64_t L, int64_t H, int64_t D, float eps, void *y, void *stream) {
+    int rc = qk_common(x, row_stride, weight, cos, sin, B, L, H, D, y);
+    if (rc) return rc;
+    if (L == 0) return HN_OK;
+    CHECK_ARCH();
+    return launched(launch_qk_norm_rope(1, x, nullptr, row_stride, weight, nullptr, cos, sin, B, L, H, eps, y, nullptr,
+                                        (cudaStream_t)stream),
+                    "hn_qk_norm_rope launch");
+}
+
+int hn_qk_norm_rope2(const void *xq, const void *xk, int64_t row_stride, const void *wq, const void *wk,
+                     const float *cos, const float *sin, int64_t B, int64_t L, int64_t H, int64_t D, float eps,
+                     void *yq, void *yk, void *stream) {
+    int rc = qk_common(xq, row_stride, wq, cos, sin, B, L, H, D, yq);
+    if (rc) return rc;
+    rc = qk_common(xk, row_stride, wk, cos, sin, B, L, H, D, yk);
+    if (rc) return rc;
+    if (L == 0) return HN_OK;
+    CHECK_ARCH();
+    return launched(launch_qk_norm_rope(2, xq, xk, row_stride, wq, wk, cos, sin, B, L, H, eps, yq, yk, (cudaStream_t)stream),
+                    "hn_qk_norm_rope2 launch");
+}
+
+int hn_pixelumm_qk(const void *x, int64_t row_stride, const void *weight_t, const void *weight_hw, const float *cos,
+                   const float *sin, int64_t N, int64_t H, int64_t D, float eps, void *y, void *stream) {
+    REQUIRE(x && weight_t && weight_hw && cos && sin && y, HN_ERR_ARG, "hn_pixelumm_qk: null pointer");
+    REQUIRE(D == 128, HN_ERR_UNSUPPORTED, "hn_pixelumm_qk: head dim %lld (kernels are built for 128)", (long long)D);
+    REQUIRE(N >= 0 && H > 0 && row_stride >= H * D, HN_ERR_SHAPE, "hn_pixelumm_qk: bad shape/stride");
+    REQUIRE(al8(x) && row_stride % 4 == 0 && al8(weight_t) && al8(weight_hw) && al16(cos) && al16(sin) && al8(y),
+            HN_ERR_ALIGN, "hn_pixelumm_qk: misaligned buffer");
+    if (N == 0) return HN_OK;
+    CHECK_ARCH();
+    return launched(launch_pixelumm_qk(x, row_stride, weight_t, weight_hw, cos, sin, N, H, eps, y, (cudaStream_t)stream),
+                    "hn_pixelumm_qk launch");
+}
+
+int hn_quantize_kv(const void *x, int64_t rows, int64_t D, int8_t *q, float *s, void *stream) {
+    REQUIRE(D > 0 && D % 128 == 0, HN_ERR_SHAPE, "hn_quantize_kv: need D %% 128 == 0");
+    return hn_quant_act(x, D, HN_DTYPE_BF16, rows, D, HN_KIND_INT8, D == 128 ? 0 : 1, q, D, s, 1, stream);
+}
+
+} // extern "C"

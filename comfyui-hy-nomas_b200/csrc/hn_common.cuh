@@ -1,0 +1,182 @@
+// hn_common.cuh - shared device helpers of the B200 quantized DiT linear path (sm_100a only).
+//
+// Rounding helpers follow the reference's arithmetic (hy_nomas/kernels.py, hy_nomas/fused.py): every
+// fp32 operation that the reference rounds separately is written with an explicit _rn intrinsic so the
+// compiler cannot contract it into an FMA; where an FMA is intended it is written as __fmaf_rn.
+#pragma once
+
+#include <cuda_bf16.h>
+#include <cuda_fp16.h>
+#include <cuda_fp8.h>
+#include <cuda_runtime.h>
+#include <stdint.h>
+
+#if defined(__CUDA_ARCH__) && (__CUDA_ARCH__ != 1000)
+#error "this library is built for sm_100a (B200) only"
+#endif
+
+namespace hn {
+
+// Bits of the device error word (defined in gemm.cu): bounded waits OR them in and return instead of
+// hanging.
+constexpr int HN_DEVERR_TIMEOUT = 1;
+
+// ---------------------------------------------------------------------------------------------------
+// bf16 / code helpers
+
+// hy_nomas/kernels.py:67-71 (_rbf16): fp32 -> nearest-even bf16 value, kept in fp32.
+__device__ __forceinline__ float rbf16(float x) {
+    uint32_t b = __float_as_uint(x);
+    b = (b + (((b >> 16) & 1u) + 0x7FFFu)) & 0xFFFF0000u;
+    return __uint_as_float(b);
+}
+__device__ __forceinline__ float bf16_lo(uint32_t w) { return __uint_as_float(w << 16); }
+__device__ __forceinline__ float bf16_hi(uint32_t w) { return __uint_as_float(w & 0xFFFF0000u); }
+// two bf16-valued floats -> packed bf16x2 (exact: the low halves are zero)
+__device__ __forceinline__ uint32_t pack_bf16_exact(float lo, float hi) {
+    return (__float_as_uint(lo) >> 16) | (__float_as_uint(hi) & 0xFFFF0000u);
+}
+// round two floats to bf16 (nearest even) and pack
+__device__ __forceinline__ uint32_t pack_bf16_rn(float lo, float hi) {
+    __nv_bfloat162 v = __floats2bfloat162_rn(lo, hi);
+    return *reinterpret_cast<uint32_t *>(&v);
+}
+__device__ __forceinline__ uint32_t pack_f16_rn(float lo, float hi) {
+    __half2 v = __floats2half2_rn(lo, hi);
+    return *reinterpret_cast<uint32_t *>(&v);
+}
+
+// round half away from zero, clamp +-127 (hy_nomas/kernels.py:35-36, ops.py:50-51)
+__device__ __forceinline__ int code_i8(float y) {
+    float r = (y >= 0.0f) ? floorf(__fadd_rn(y, 0.5f)) : ceilf(__fsub_rn(y, 0.5f));
+    r = fminf(fmaxf(r, -127.0f), 127.0f);
+    return (int)r;
+}
+__device__ __forceinline__ uint32_t pack4_i8(int a, int b, int c, int d) {
+    return (uint32_t)(a & 0xFF) | ((uint32_t)(b & 0xFF) << 8) | ((uint32_t)(c & 0xFF) << 16) |
+           ((uint32_t)(d & 0xFF) << 24);
+}
+// two floats -> two e4m3 bytes, nearest even, saturating to +-448 (cvt.rn.satfinite.e4m3x2.f32)
+__device__ __forceinline__ uint32_t pack2_e4m3(float lo, float hi) {
+    return (uint32_t)__nv_cvt_float2_to_fp8x2(make_float2(lo, hi), __NV_SATFINITE, __NV_E4M3);
+}
+
+// int8 quantization scale of a 128-group (kernels.py:33): peak > 0 ? peak / 127 : 1
+__device__ __forceinline__ float i8_scale(float peak) { return peak > 0.0f ? __fdiv_rn(peak, 127.0f) : 1.0f; }
+// e4m3 scale (kernels.py:39): max(peak, 1e-12) / 448
+__device__ __forceinline__ float e4m3_scale(float peak) { return __fdiv_rn(fmaxf(peak, 1e-12f), 448.0f); }
+
+// 1/sqrt(v) with both steps correctly rounded (the tl.rsqrt of the reference, evaluated as the Triton
+// interpreter evaluates it).
+__device__ __forceinline__ float rsqrt_cr(float v) { return __fdiv_rn(1.0f, __fsqrt_rn(v)); }
+
+// ---------------------------------------------------------------------------------------------------
+// exp / GELU (hy_nomas/kernels.py:74-77). exp_cw: Cody & Waite (1980) reduction x = k*ln2 + r with the
+// two-part ln2 of fdlibm's expf, Taylor series of e^r to degree 7 (Horner, fused multiply-adds), scaling
+// by 2^k in two exact steps. The CPU oracle evaluates the same operations, so GELU outputs compare
+// bit-for-bit.
+__device__ __forceinline__ float exp_cw(float x) {
+    if (x != x) return x;
+    if (x > 88.7228394f) return __int_as_float(0x7F800000);
+    if (x < -103.972084f) return 0.0f;
+    const float log2e = 0x1.715476p+0f, ln2_hi = 0x1.62e4p-1f, ln2_lo = 0x1.7f7d1cp-20f;
+    float kf = rintf(__fmul_rn(x, log2e));
+    float r = __fmaf_rn(-kf, ln2_hi, x);
+    r = __fmaf_rn(-kf, ln2_lo, r);
+    float p = 0x1.a01a02p-13f;
+    p = __fmaf_rn(p, r, 0x1.6c16c2p-10f);
+    p = __fmaf_rn(p, r, 0x1.111112p-7f);
+    p = __fmaf_rn(p, r, 0x1.555556p-5f);
+    p = __fmaf_rn(p, r, 0x1.555556p-3f);
+    p = __fmaf_rn(p, r, 0.5f);
+    p = __fmaf_rn(p, r, 1.0f);
+    p = __fmaf_rn(p, r, 1.0f);
+    int k = (int)kf;
+    int k1 = k / 2, k2 = k - k1;
+    p = __fmul_rn(p, __uint_as_float((uint32_t)(k1 + 127) << 23));
+    p = __fmul_rn(p, __uint_as_float((uint32_t)(k2 + 127) << 23));
+    return p;
+}
+
+// 0.5 x (1 + (2 sigmoid(2u) - 1)), u = 0.79788456 (x + 0.044715 x^3), left to right, one rounding per op
+__device__ __forceinline__ float gelu_tanh(float x) {
+    float x3 = __fmul_rn(__fmul_rn(__fmul_rn(0.044715f, x), x), x);
+    float inner = __fmul_rn(0.7978845608028654f, __fadd_rn(x, x3));
+    float z = __fmul_rn(2.0f, inner);
+    float sig = __fdiv_rn(1.0f, __fadd_rn(1.0f, exp_cw(-z)));
+    return __fmul_rn(__fmul_rn(0.5f, x), __fadd_rn(1.0f, __fsub_rn(__fmul_rn(2.0f, sig), 1.0f)));
+}
+
+// ---------------------------------------------------------------------------------------------------
+// vector loads: 8 bf16 / fp16 or 4 fp32 elements -> fp32
+
+template <typename T> struct Elem;
+template <> struct Elem<__nv_bfloat16> {
+    static __device__ __forceinline__ void load8(const __nv_bfloat16 *p, float *v) {
+        uint4 w = *reinterpret_cast<const uint4 *>(p);
+        v[0] = bf16_lo(w.x); v[1] = bf16_hi(w.x); v[2] = bf16_lo(w.y); v[3] = bf16_hi(w.y);
+        v[4] = bf16_lo(w.z); v[5] = bf16_hi(w.z); v[6] = bf16_lo(w.w); v[7] = bf16_hi(w.w);
+    }
+    static __device__ __forceinline__ float load1(const __nv_bfloat16 *p) { return __bfloat162float(*p); }
+};
+template <> struct Elem<__half> {
+    static __device__ __forceinline__ void load8(const __half *p, float *v) {
+        uint4 w = *reinterpret_cast<const uint4 *>(p);
+        const __half2 *h = reinterpret_cast<const __half2 *>(&w);
+        for (int i = 0; i < 4; ++i) { float2 f = __half22float2(h[i]); v[2 * i] = f.x; v[2 * i + 1] = f.y; }
+    }
+    static __device__ __forceinline__ float load1(const __half *p) { return __half2float(*p); }
+};
+template <> struct Elem<float> {
+    static __device__ __forceinline__ void load8(const float *p, float *v) {
+        float4 a = *reinterpret_cast<const float4 *>(p), b = *reinterpret_cast<const float4 *>(p + 4);
+        v[0] = a.x; v[1] = a.y; v[2] = a.z; v[3] = a.w; v[4] = b.x; v[5] = b.y; v[6] = b.z; v[7] = b.w;
+    }
+    static __device__ __forceinline__ float load1(const float *p) { return *p; }
+};
+
+// streaming 16-byte load that does not allocate in L1
+__device__ __forceinline__ uint4 ldg_stream(const void *p) {
+    uint4 r;
+    asm volatile("ld.global.nc.L1::no_allocate.v4.u32 {%0,%1,%2,%3}, [%4];"
+                 : "=r"(r.x), "=r"(r.y), "=r"(r.z), "=r"(r.w) : "l"(p));
+    return r;
+}
+
+// ---------------------------------------------------------------------------------------------------
+// warp reductions
+
+__device__ __forceinline__ float warp_max_xor(float v, int width) {
+    for (int o = 1; o < width; o <<= 1) v = fmaxf(v, __shfl_xor_sync(0xffffffffu, v, o));
+    return v;
+}
+// butterfly sum over the 32 lanes: every lane ends with the same balanced pairwise tree in lane order
+__device__ __forceinline__ float warp_sum_tree(float v) {
+    for (int o = 1; o < 32; o <<= 1) v = __fadd_rn(v, __shfl_xor_sync(0xffffffffu, v, o));
+    return v;
+}
+
+// pairwise tree of 16 values in index order
+__device__ __forceinline__ float tree16(const float *v) {
+    float a[8];
+#pragma unroll
+    for (int i = 0; i < 8; ++i) a[i] = __fadd_rn(v[2 * i], v[2 * i + 1]);
+#pragma unroll
+    for (int i = 0; i < 4; ++i) a[i] = __fadd_rn(a[2 * i], a[2 * i + 1]);
+    a[0] = __fadd_rn(a[0], a[1]);
+    a[1] = __fadd_rn(a[2], a[3]);
+    return __fadd_rn(a[0], a[1]);
+}
+
+// ---------------------------------------------------------------------------------------------------
+// time
+
+__device__ __forceinline__ uint64_t globaltimer_ns() {
+    uint64_t t;
+    asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
+    return t;
+}
+
+__host__ __device__ constexpr int64_t cdiv(int64_t a, int64_t b) { return (a + b - 1) / b; }
+
+} // namespace hn

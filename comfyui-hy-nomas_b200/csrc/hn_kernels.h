@@ -1,0 +1,49 @@
+// hn_kernels.h - internal launcher declarations (host side). The C ABI in capi.cu validates arguments
+// and calls these; each returns the launch's cudaError_t.
+#pragma once
+
+#include <cuda_runtime.h>
+#include <stdint.h>
+
+namespace hn {
+
+int num_sms();  // SM count of the current device (cached per device)
+
+cudaError_t launch_quant_act(const void *x, int64_t ldx, int x_dtype, int64_t M, int64_t K, int kind, int per_row,
+                             void *q, int64_t ldq, float *s, int64_t lds, cudaStream_t st);
+
+// mode 0: adaln (bf16 y), 1: adaln_quant, 2: gated residual + adaln_quant
+cudaError_t launch_ln_row(int mode, const void *x, const void *y, const void *gate, const void *shift,
+                          const void *scale, int64_t B, int64_t L, int64_t D, float eps, void *out_bf16, int8_t *q,
+                          float *s, cudaStream_t st);
+
+cudaError_t launch_gated_residual(const void *x, const void *y, const void *gate, int64_t B, int64_t L, int64_t D,
+                                  void *out, cudaStream_t st);
+
+cudaError_t launch_qk_norm_rope(int ntensors, const void *x0, const void *x1, int64_t row_stride, const void *w0,
+                                const void *w1, const float *cos, const float *sin, int64_t B, int64_t L, int64_t H,
+                                float eps, void *y0, void *y1, cudaStream_t st);
+
+cudaError_t launch_pixelumm_qk(const void *x, int64_t row_stride, const void *wt, const void *whw, const float *cos,
+                               const float *sin, int64_t N, int64_t H, float eps, void *y, cudaStream_t st);
+
+struct GemmArgs {
+    const void *qa; int64_t lda;
+    const float *sa; int64_t ldsa; int sa_mode;
+    const void *qw; int64_t ldw;
+    const float *sw; int64_t ldsw; int sw_mode;
+    const void *bias; int bias_dtype;
+    void *out; int64_t ldo; int out_dtype;
+    float *qs; int64_t ldqs;
+    int64_t M, N, K;
+    int kind, epilogue;
+};
+// Returns cudaSuccess, or cudaErrorInvalidValue with *msg set when a TMA descriptor cannot be encoded.
+cudaError_t launch_block_gemm(const GemmArgs &a, cudaStream_t st, const char **msg);
+
+cudaError_t launch_wait_selftest(uint32_t timeout_us, cudaStream_t st);
+
+// read the device error word into *value and clear it (synchronous)
+cudaError_t read_and_clear_device_error(int *value);
+
+} // namespace hn

@@ -1,0 +1,141 @@
+// quant.cu - K1 activation quantizer (hy_nomas/kernels.py:22-54) and the int8 KV quantizer
+// (hy_nomas/world.py:83-90).
+//
+// Layout: one 128-element group (row m, group g) per 8 consecutive lanes, 16 contiguous elements per lane
+// (two 16-byte loads of bf16), 4 groups per warp. The group absmax is a 3-step xor-shuffle max; each lane
+// writes its 16 codes as one 16-byte store; the first lane of the group writes the fp32 scale.
+// HBM-bound: per element 2 bytes read (bf16) + 1 byte written, plus 4 bytes of scale per 128 elements.
+#include "hn_common.cuh"
+#include "hn_kernels.h"
+
+namespace hn {
+
+template <typename TIn, int KIND>
+__global__ void __launch_bounds__(256) k_quant_group(const TIn *__restrict__ x, int64_t ldx, int64_t M, int64_t G,
+                                                     uint8_t *__restrict__ q, int64_t ldq, float *__restrict__ s,
+                                                     int64_t lds) {
+    const int lane = threadIdx.x & 31, sub = lane & 7;
+    const int64_t ngroups = M * G;
+    const int64_t warp0 = (int64_t)blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5);
+    const int64_t wstride = (int64_t)gridDim.x * (blockDim.x >> 5);
+    for (int64_t base = warp0 * 4; base < ngroups; base += wstride * 4) {
+        const int64_t gi = base + (lane >> 3);
+        const bool active = gi < ngroups;
+        int64_t m = 0, g = 0;
+        float v[16];
+        if (active) {
+            m = gi / G;
+            g = gi - m * G;
+            const TIn *p = x + m * ldx + g * 128 + sub * 16;
+            Elem<TIn>::load8(p, v);
+            Elem<TIn>::load8(p + 8, v + 8);
+        } else {
+#pragma unroll
+            for (int i = 0; i < 16; ++i) v[i] = 0.0f;
+        }
+        float peak = 0.0f;
+#pragma unroll
+        for (int i = 0; i < 16; ++i) peak = fmaxf(peak, fabsf(v[i]));
+        peak = warp_max_xor(peak, 8);
+        float sc;
+        uint4 out;
+        if (KIND == 0) {
+            sc = i8_scale(peak);
+            int c[16];
+#pragma unroll
+            for (int i = 0; i < 16; ++i) c[i] = code_i8(__fdiv_rn(v[i], sc));
+            out.x = pack4_i8(c[0], c[1], c[2], c[3]);
+            out.y = pack4_i8(c[4], c[5], c[6], c[7]);
+            out.z = pack4_i8(c[8], c[9], c[10], c[11]);
+            out.w = pack4_i8(c[12], c[13], c[14], c[15]);
+        } else {
+            sc = e4m3_scale(peak);
+            uint32_t h[8];
+#pragma unroll
+            for (int i = 0; i < 8; ++i) h[i] = pack2_e4m3(__fdiv_rn(v[2 * i], sc), __fdiv_rn(v[2 * i + 1], sc));
+            out.x = h[0] | (h[1] << 16);
+            out.y = h[2] | (h[3] << 16);
+            out.z = h[4] | (h[5] << 16);
+            out.w = h[6] | (h[7] << 16);
+        }
+        if (active) {
+            *reinterpret_cast<uint4 *>(q + m * ldq + g * 128 + sub * 16) = out;
+            if (sub == 0) s[m * lds + g] = sc;
+        }
+    }
+}
+
+// Per-row (per-token) variant: one CTA per row, two passes over the row (the second hits L1/L2).
+template <typename TIn, int KIND>
+__global__ void __launch_bounds__(256) k_quant_row(const TIn *__restrict__ x, int64_t ldx, int64_t K,
+                                                   uint8_t *__restrict__ q, int64_t ldq, float *__restrict__ s,
+                                                   int64_t lds) {
+    __shared__ float red[8];
+    const int64_t m = blockIdx.x;
+    const TIn *row = x + m * ldx;
+    float peak = 0.0f;
+    for (int64_t c = (int64_t)threadIdx.x * 8; c < K; c += (int64_t)blockDim.x * 8) {
+        float v[8];
+        Elem<TIn>::load8(row + c, v);
+#pragma unroll
+        for (int i = 0; i < 8; ++i) peak = fmaxf(peak, fabsf(v[i]));
+    }
+    peak = warp_max_xor(peak, 32);
+    if ((threadIdx.x & 31) == 0) red[threadIdx.x >> 5] = peak;
+    __syncthreads();
+    peak = 0.0f;
+    for (int w = 0; w < (int)(blockDim.x >> 5); ++w) peak = fmaxf(peak, red[w]);
+    const float sc = KIND == 0 ? i8_scale(peak) : e4m3_scale(peak);
+    for (int64_t c = (int64_t)threadIdx.x * 8; c < K; c += (int64_t)blockDim.x * 8) {
+        float v[8];
+        Elem<TIn>::load8(row + c, v);
+        uint2 out;
+        if (KIND == 0) {
+            int cc[8];
+#pragma unroll
+            for (int i = 0; i < 8; ++i) cc[i] = code_i8(__fdiv_rn(v[i], sc));
+            out.x = pack4_i8(cc[0], cc[1], cc[2], cc[3]);
+            out.y = pack4_i8(cc[4], cc[5], cc[6], cc[7]);
+        } else {
+            uint32_t h[4];
+#pragma unroll
+            for (int i = 0; i < 4; ++i) h[i] = pack2_e4m3(__fdiv_rn(v[2 * i], sc), __fdiv_rn(v[2 * i + 1], sc));
+            out.x = h[0] | (h[1] << 16);
+            out.y = h[2] | (h[3] << 16);
+        }
+        *reinterpret_cast<uint2 *>(q + m * ldq + c) = out;
+    }
+    if (threadIdx.x == 0) s[m * lds] = sc;
+}
+
+template <typename TIn>
+static cudaError_t launch_quant_t(const void *x, int64_t ldx, int64_t M, int64_t K, int kind, int per_row, void *q,
+                                  int64_t ldq, float *s, int64_t lds, cudaStream_t st) {
+    const TIn *xp = static_cast<const TIn *>(x);
+    uint8_t *qp = static_cast<uint8_t *>(q);
+    if (per_row) {
+        dim3 grid((unsigned)M), block(256);
+        if (kind == 0) k_quant_row<TIn, 0><<<grid, block, 0, st>>>(xp, ldx, K, qp, ldq, s, lds);
+        else k_quant_row<TIn, 1><<<grid, block, 0, st>>>(xp, ldx, K, qp, ldq, s, lds);
+    } else {
+        const int64_t G = K / 128;
+        const int64_t warps = cdiv(M * G, 4);
+        int64_t blocks = cdiv(warps, 8);
+        const int64_t cap = (int64_t)num_sms() * 16;
+        if (blocks > cap) blocks = cap;
+        if (kind == 0) k_quant_group<TIn, 0><<<(unsigned)blocks, 256, 0, st>>>(xp, ldx, M, G, qp, ldq, s, lds);
+        else k_quant_group<TIn, 1><<<(unsigned)blocks, 256, 0, st>>>(xp, ldx, M, G, qp, ldq, s, lds);
+    }
+    return cudaGetLastError();
+}
+
+cudaError_t launch_quant_act(const void *x, int64_t ldx, int x_dtype, int64_t M, int64_t K, int kind, int per_row,
+                             void *q, int64_t ldq, float *s, int64_t lds, cudaStream_t st) {
+    switch (x_dtype) {
+    case 0: return launch_quant_t<__nv_bfloat16>(x, ldx, M, K, kind, per_row, q, ldq, s, lds, st);
+    case 1: return launch_quant_t<__half>(x, ldx, M, K, kind, per_row, q, ldq, s, lds, st);
+    default: return launch_quant_t<float>(x, ldx, M, K, kind, per_row, q, ldq, s, lds, st);
+    }
+}
+
+} // namespace hn

@@ -1,0 +1,92 @@
+"""ctypes binding of libhynomas_b200.so (the C ABI declared in include/hynomas_b200.h).
+
+The library is the only compute path: there is no Triton, no torch or CPU fallback. If the shared object
+is missing, importing this module raises; if a call fails, the C status becomes a RuntimeError carrying
+hn_last_error(). Tensors are passed as raw device pointers; every launch goes on torch's current stream
+of the tensor's device.
+"""
+import ctypes
+import os
+
+import torch
+
+_HERE = os.path.dirname(os.path.abspath(__file__))
+LIB_PATH = os.path.join(_HERE, "libhynomas_b200.so")
+
+HN_OK = 0
+STATUS = {0: "HN_OK", 1: "HN_ERR_SHAPE", 2: "HN_ERR_ALIGN", 3: "HN_ERR_ARCH", 4: "HN_ERR_CUDA", 5: "HN_ERR_ARG",
+          6: "HN_ERR_TIMEOUT", 7: "HN_ERR_UNSUPPORTED"}
+
+DTYPE = {torch.bfloat16: 0, torch.float16: 1, torch.float32: 2, torch.int32: 3}
+KIND = {"int8": 0, "fp8": 1}
+SCALE_MODE = {"group": 0, "row": 1, "block": 2}
+
+# name -> argtypes (all entry points return int)
+_V, _I64, _I32, _F32, _U32 = ctypes.c_void_p, ctypes.c_int64, ctypes.c_int, ctypes.c_float, ctypes.c_uint32
+SIGNATURES = {
+    "hn_abi_version": [],
+    "hn_num_sms": [],
+    "hn_device_error": [_V, ctypes.POINTER(ctypes.c_int)],
+    "hn_selftest_wait_timeout": [_U32, _V],
+    "hn_quant_act": [_V, _I64, _I32, _I64, _I64, _I32, _I32, _V, _I64, _V, _I64, _V],
+    "hn_block_gemm": [_V, _I64, _V, _I64, _I32, _V, _I64, _V, _I64, _I32, _V, _I32, _V, _I64, _I32, _V, _I64,
+                      _I64, _I64, _I64, _I32, _I32, _V],
+    "hn_adaln_quant": [_V, _V, _V, _I64, _I64, _I64, _F32, _V, _V, _V],
+    "hn_adaln": [_V, _V, _V, _I64, _I64, _I64, _F32, _V, _V],
+    "hn_qk_norm_rope": [_V, _I64, _V, _V, _V, _I64, _I64, _I64, _I64, _F32, _V, _V],
+    "hn_qk_norm_rope2": [_V, _V, _I64, _V, _V, _V, _V, _I64, _I64, _I64, _I64, _F32, _V, _V, _V],
+    "hn_gated_residual": [_V, _V, _V, _I64, _I64, _I64, _V, _V],
+    "hn_gated_residual_adaln_quant": [_V, _V, _V, _V, _V, _I64, _I64, _I64, _F32, _V, _V, _V, _V],
+    "hn_pixelumm_qk": [_V, _I64, _V, _V, _V, _V, _I64, _I64, _I64, _F32, _V, _V],
+    "hn_quantize_kv": [_V, _I64, _I64, _V, _V, _V],
+}
+
+
+def _load():
+    if not os.path.exists(LIB_PATH):
+        raise ImportError(f"{LIB_PATH} is missing: build it with `python -m hy_nomas_b200.build` "
+                          "(this package has no fallback path)")
+    lib = ctypes.CDLL(LIB_PATH)
+    lib.hn_last_error.restype = ctypes.c_char_p
+    lib.hn_last_error.argtypes = []
+    for name, args in SIGNATURES.items():
+        fn = getattr(lib, name)
+        fn.argtypes = args
+        fn.restype = ctypes.c_int
+    return lib
+
+
+lib = _load()
+
+
+def last_error():
+    return lib.hn_last_error().decode(errors="replace")
+
+
+def check(rc, what):
+    if rc != HN_OK:
+        raise RuntimeError(f"{what} failed with {STATUS.get(rc, rc)}: {last_error()}")
+
+
+def ptr(t):
+    return None if t is None else ctypes.c_void_p(t.data_ptr())
+
+
+def stream_of(t):
+    """torch's current stream on the tensor's device, as a cudaStream_t value."""
+    return ctypes.c_void_p(torch.cuda.current_stream(t.device).cuda_stream)
+
+
+def require_cuda(*tensors):
+    for t in tensors:
+        if t is not None and not t.is_cuda:
+            raise RuntimeError("hy_nomas_b200 kernels run on CUDA tensors only (there is no CPU path); "
+                               f"got a tensor on {t.device}")
+
+
+def device_error(stream=None):
+    """Synchronize `stream` and return (and clear) the device error word of the bounded waits."""
+    code = ctypes.c_int(0)
+    s = ctypes.c_void_p(stream.cuda_stream if stream is not None else torch.cuda.current_stream().cuda_stream)
+    rc = lib.hn_device_error(s, ctypes.byref(code))
+    return rc, code.value

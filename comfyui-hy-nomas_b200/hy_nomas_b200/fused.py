@@ -1,0 +1,148 @@
+"""Fused elementwise kernels of the DiT block - the drop-in for hy_nomas/fused.py.
+
+Same functions and arguments as the reference (hy_nomas/fused.py:22-186); each is one HBM pass in
+libhynomas_b200.so and rounds where the reference rounds:
+
+* `adaln`: LayerNorm in fp32, `* rbf16(1 + scale)`, `+ shift`, one bf16 rounding;
+* `qk_norm_rope`: RMSNorm in fp32 rounded to bf16, times the bf16 weight (rounded), interleaved RoPE in fp32,
+  rounded;
+* `gated_residual`: `x + y * gate`, the product and the sum each rounded to bf16;
+* `pixelumm_qk`: PixelUMM's split T/HW RMSNorm + rotate-half MRoPE.
+
+Two fused variants go further than the reference: `gated_residual_adaln_quant` (the residual and the next
+LayerNorm/modulate/int8 quantization in one pass, hy_nomas/model.py:280-282) and `qk_norm_rope2` (q and k
+in one launch, reading the RoPE tables once). `HY_NOMAS_FUSED=0` disables `available()`, as in the
+reference.
+"""
+import os
+
+import torch
+
+from . import _lib
+
+ENABLED = os.environ.get("HY_NOMAS_FUSED", "1") != "0"
+
+
+def available(x):
+    return ENABLED and x.is_cuda and x.dtype == torch.bfloat16
+
+
+def _bf16(*ts):
+    for t in ts:
+        if t.dtype != torch.bfloat16:
+            raise TypeError(f"expected a bf16 tensor, got {t.dtype}")
+
+
+def adaln(x, shift, scale, eps=1e-6):
+    """x [B, L, D] bf16, shift/scale [B, D] bf16 -> modulate(layer_norm(x), shift, scale) in bf16."""
+    _lib.require_cuda(x, shift, scale)
+    _bf16(x, shift, scale)
+    b, l, d = x.shape
+    x, shift, scale = x.contiguous(), shift.contiguous(), scale.contiguous()
+    y = torch.empty(x.shape, device=x.device, dtype=x.dtype)
+    rc = _lib.lib.hn_adaln(_lib.ptr(x), _lib.ptr(shift), _lib.ptr(scale), b, l, d, eps, _lib.ptr(y),
+                           _lib.stream_of(x))
+    _lib.check(rc, "adaln")
+    return y
+
+
+def _qk_input(x):
+    b, l, h, d = x.shape
+    if x.stride(3) != 1 or x.stride(2) != d or x.stride(0) != l * x.stride(1) or x.stride(1) % 4 or \
+            x.data_ptr() % 8:
+        x = x.contiguous()
+    return x
+
+
+def _rope_tables(rope, device):
+    if rope is None:
+        return None, None
+    cos, sin = rope
+    cos = cos.to(device=device, dtype=torch.float32).contiguous()
+    sin = sin.to(device=device, dtype=torch.float32).contiguous()
+    return cos, sin
+
+
+def qk_norm_rope(x, weight, rope=None, eps=1e-6):
+    """x [B, L, H, D] bf16 (rows may be strided, heads contiguous), weight [D] -> RMSNorm(x) * weight, then RoPE
+    with (cos, sin) [L, D] fp32 when given. Returns a contiguous [B, L, H, D] bf16 tensor."""
+    _lib.require_cuda(x, weight)
+    _bf16(x)
+    b, l, h, d = x.shape
+    x = _qk_input(x)
+    y = torch.empty((b, l, h, d), device=x.device, dtype=torch.bfloat16)
+    w = weight.to(torch.bfloat16).contiguous()
+    cos, sin = _rope_tables(rope, x.device)
+    rc = _lib.lib.hn_qk_norm_rope(_lib.ptr(x), x.stride(1), _lib.ptr(w), _lib.ptr(cos), _lib.ptr(sin), b, l, h, d,
+                                  eps, _lib.ptr(y), _lib.stream_of(x))
+    _lib.check(rc, "qk_norm_rope")
+    return y
+
+
+def qk_norm_rope2(q, k, weight_q, weight_k, rope=None, eps=1e-6):
+    """`qk_norm_rope` of q and k (same shape and token stride) in one launch -> (q_out, k_out)."""
+    _lib.require_cuda(q, k, weight_q, weight_k)
+    _bf16(q, k)
+    b, l, h, d = q.shape
+    q, k = _qk_input(q), _qk_input(k)
+    if q.stride(1) != k.stride(1):
+        q, k = q.contiguous(), k.contiguous()
+    yq = torch.empty((b, l, h, d), device=q.device, dtype=torch.bfloat16)
+    yk = torch.empty_like(yq)
+    wq = weight_q.to(torch.bfloat16).contiguous()
+    wk = weight_k.to(torch.bfloat16).contiguous()
+    cos, sin = _rope_tables(rope, q.device)
+    rc = _lib.lib.hn_qk_norm_rope2(_lib.ptr(q), _lib.ptr(k), q.stride(1), _lib.ptr(wq), _lib.ptr(wk), _lib.ptr(cos),
+                                   _lib.ptr(sin), b, l, h, d, eps, _lib.ptr(yq), _lib.ptr(yk), _lib.stream_of(q))
+    _lib.check(rc, "qk_norm_rope2")
+    return yq, yk
+
+
+def gated_residual(x, y, gate):
+    """x + y * gate[:, None] with bf16 rounding of the product and the sum; x, y [B, L, D], gate [B, D]."""
+    _lib.require_cuda(x, y, gate)
+    _bf16(x, y, gate)
+    b, l, d = x.shape
+    x, y, gate = x.contiguous(), y.contiguous(), gate.contiguous()
+    out = torch.empty(x.shape, device=x.device, dtype=x.dtype)
+    rc = _lib.lib.hn_gated_residual(_lib.ptr(x), _lib.ptr(y), _lib.ptr(gate), b, l, d, _lib.ptr(out),
+                                    _lib.stream_of(x))
+    _lib.check(rc, "gated_residual")
+    return out
+
+
+def gated_residual_adaln_quant(x, y, gate, shift, scale, eps=1e-6):
+    """x' = gated_residual(x, y, gate) and kernels.adaln_quant(x', shift, scale) in one pass -> (x', q, s)."""
+    _lib.require_cuda(x, y, gate, shift, scale)
+    _bf16(x, y, gate, shift, scale)
+    b, l, d = x.shape
+    x, y, gate = x.contiguous(), y.contiguous(), gate.contiguous()
+    shift, scale = shift.contiguous(), scale.contiguous()
+    out = torch.empty(x.shape, device=x.device, dtype=x.dtype)
+    q = torch.empty((b * l, d), device=x.device, dtype=torch.int8)
+    s = torch.empty((b * l, d // 128), device=x.device, dtype=torch.float32)
+    rc = _lib.lib.hn_gated_residual_adaln_quant(_lib.ptr(x), _lib.ptr(y), _lib.ptr(gate), _lib.ptr(shift),
+                                                _lib.ptr(scale), b, l, d, eps, _lib.ptr(out), _lib.ptr(q),
+                                                _lib.ptr(s), _lib.stream_of(x))
+    _lib.check(rc, "gated_residual_adaln_quant")
+    return out, q, s
+
+
+def pixelumm_qk(x, weight_t, weight_hw, cos, sin, eps=1e-6):
+    """x [1, N, H, D] (a projection's output, heads contiguous), cos/sin [N, D] fp32 -> bf16 [1, N, H, D]."""
+    _lib.require_cuda(x, weight_t, weight_hw, cos, sin)
+    _bf16(x)
+    b, n, h, d = x.shape
+    if b != 1:
+        raise ValueError("pixelumm_qk: batch must be 1 (the decoder's layout)")
+    if x.stride(3) != 1 or x.stride(2) != d or x.stride(1) % 4 or x.data_ptr() % 8:
+        x = x.contiguous()
+    y = torch.empty((b, n, h, d), device=x.device, dtype=torch.bfloat16)
+    wt = weight_t.to(torch.bfloat16).contiguous()
+    whw = weight_hw.to(torch.bfloat16).contiguous()
+    cos = cos.to(torch.float32).contiguous()
+    sin = sin.to(torch.float32).contiguous()
+    rc = _lib.lib.hn_pixelumm_qk(_lib.ptr(x), x.stride(1), _lib.ptr(wt), _lib.ptr(whw), _lib.ptr(cos), _lib.ptr(sin),
+                                 n, h, d, eps, _lib.ptr(y), _lib.stream_of(x))
+    _lib.check(rc, "pixelumm_qk")
+    return y

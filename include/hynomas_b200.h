@@ -1,0 +1,199 @@
+/*
+ * hynomas_b200.h - C ABI of the B200 (sm_100a) quantized DiT linear path.
+ *
+ * Every entry point replaces one Triton kernel (or one torch expression) of ComfyUI-Hy-Nomas. The
+ * reference interface each one stands in for is cited beside it as `file:line` inside that project
+ * (hy_nomas/kernels.py, hy_nomas/fused.py, hy_nomas/ops.py, hy_nomas/model.py, hy_nomas/pixelumm.py,
+ * hy_nomas/world.py).
+ *
+ * Conventions
+ *  - All pointers are DEVICE pointers unless the name ends in `_host`. Nothing here allocates device
+ *    memory; outputs are caller-owned buffers of the documented shape. Inputs are never written.
+ *  - Matrices are row-major with an explicit leading dimension in ELEMENTS (ld >= number of columns).
+ *  - `stream` is a cudaStream_t (NULL = legacy default stream) of the device that owns the pointers.
+ *  - Return value: HN_OK (0) or an hn_status code. On error nothing was launched and the message is
+ *    available from hn_last_error() (per calling thread). Kernels never trap; device-side waits are
+ *    bounded and report HN_ERR_TIMEOUT through hn_device_error().
+ *  - bf16/fp16/fp32 inputs are named by the HN_DTYPE_* codes. Quantized codes are int8 or
+ *    float8_e4m3fn bytes (HN_KIND_*).
+ */
+#ifndef HYNOMAS_B200_H
+#define HYNOMAS_B200_H
+
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+/* the library is built with hidden visibility; everything declared here is exported */
+#if defined(__GNUC__)
+#pragma GCC visibility push(default)
+#endif
+
+#define HN_ABI_VERSION 1
+
+typedef enum {
+    HN_OK = 0,
+    HN_ERR_SHAPE = 1,       /* a dimension is zero/negative where not allowed, or not a multiple of 128 */
+    HN_ERR_ALIGN = 2,       /* a pointer or leading dimension breaks the 16-byte rule of a vector/TMA path */
+    HN_ERR_ARCH = 3,        /* the current device is not compute capability 10.0 (B200 / sm_100a) */
+    HN_ERR_CUDA = 4,        /* a CUDA runtime/driver call failed (message holds the CUDA error string) */
+    HN_ERR_ARG = 5,         /* null pointer or unknown enum value */
+    HN_ERR_TIMEOUT = 6,     /* a device-side wait ran past its limit (read via hn_device_error) */
+    HN_ERR_UNSUPPORTED = 7  /* a combination of modes that the kernels do not implement */
+} hn_status;
+
+/* input element types */
+#define HN_DTYPE_BF16 0
+#define HN_DTYPE_FP16 1
+#define HN_DTYPE_FP32 2
+#define HN_DTYPE_INT32 3 /* output only: the raw integer accumulator */
+
+/* quantized code types */
+#define HN_KIND_INT8 0
+#define HN_KIND_FP8E4M3 1
+
+/* scale layouts of the block-scaled GEMM (hn_block_gemm) */
+#define HN_SCALE_GROUP 0  /* one fp32 per row and 128-wide K group: [rows, K/128] (the reference layout) */
+#define HN_SCALE_ROW 1    /* one fp32 per row: per-token activations / per-output-channel weights */
+#define HN_SCALE_BLOCK 2  /* weights only: one fp32 per 128x128 block, [N/128, K/128] (FP8 decoder layout) */
+
+/* GEMM epilogues, same numbering as kernels.EPILOGUES (hy_nomas/kernels.py:149) */
+#define HN_EPI_NONE 0
+#define HN_EPI_GELU 1
+#define HN_EPI_GELU_QUANT 2
+
+/* Message of the last failed call on this thread ("" if none). */
+const char *hn_last_error(void);
+
+/* ABI version (HN_ABI_VERSION) and the number of SMs the kernels size their grids for (0 if no GPU). */
+int hn_abi_version(void);
+int hn_num_sms(void);
+
+/*
+ * Device error word written by bounded waits inside the kernels (0 = none). Synchronizes `stream`,
+ * copies the word to *code_host and clears it. Returns HN_ERR_TIMEOUT if a wait timed out.
+ */
+int hn_device_error(void *stream, int *code_host);
+
+/*
+ * Test hook for the bounded-wait machinery: launches one CTA that waits on an mbarrier that nothing
+ * completes, with a limit of `timeout_us` microseconds, then returns. The timeout is recorded in the
+ * device error word exactly as a stuck GEMM pipeline would record it. No counterpart in the reference
+ * (the reference's Triton kernels have no device-side waits).
+ */
+int hn_selftest_wait_timeout(uint32_t timeout_us, void *stream);
+
+/*
+ * K1 - per (row, 128-group) absmax activation quantizer.
+ * Replaces hy_nomas/kernels.py:22-54 (_quantize_kernel / quantize_activations).
+ * x [M, K] (dtype x_dtype, leading dim ldx), K % 128 == 0 ->
+ *   codes q [M, K] (int8, or e4m3 bytes for HN_KIND_FP8E4M3; leading dim ldq),
+ *   scales s [M, K/128] fp32 (leading dim lds).
+ * int8: s = peak > 0 ? peak/127 : 1, q = round-half-away(x/s) clamped to +-127.
+ * e4m3: s = max(peak, 1e-12)/448, q = e4m3(x/s) round-to-nearest-even, saturating.
+ * `per_row` != 0 uses one group spanning all K (per-token scale; s is then [M] with stride lds) -
+ * the per-token quantization that BASELINE config 1 names; no counterpart in the reference.
+ */
+int hn_quant_act(const void *x, int64_t ldx, int x_dtype, int64_t M, int64_t K, int kind, int per_row,
+                 void *q, int64_t ldq, float *s, int64_t lds, void *stream);
+
+/*
+ * K2 - block-scaled W8A8 / FP8 GEMM on the 5th-generation tensor cores (tcgen05, TMEM accumulators).
+ * Replaces hy_nomas/kernels.py:80-170 (_gemm_body / block_gemm).
+ *   y[m, n] = sum_g sa[m, g] * sw[n, g] * dot_g(qa[m, :], qw[n, :])  (+ bias[n])
+ * qa [M, K] codes (lda), qw [N, K] codes (ldw; K-major, the layout the checkpoints store), both of
+ * `kind`. K % 128 == 0, lda and ldw multiples of 16, qa/qw 16-byte aligned.
+ * sa: sa_mode HN_SCALE_GROUP -> [M, K/128] (ldsa) | HN_SCALE_ROW -> [M].
+ * sw: sw_mode HN_SCALE_GROUP -> [N, K/128] (ldsw) | HN_SCALE_ROW -> [N] | HN_SCALE_BLOCK -> [N/128, K/128].
+ * bias: NULL or [N] of bias_dtype (bf16/fp16/fp32).
+ * epilogue HN_EPI_NONE: out [M, N] of out_dtype (bf16/fp16/fp32), ldo.
+ *          HN_EPI_GELU: out bf16 = rbf16(gelu_tanh(rbf16(y))).
+ *          HN_EPI_GELU_QUANT: out int8 [M, N] codes of the GELU output quantized per row and 128
+ *                             columns, qs [M, N/128] fp32 (ldqs). Needs N % 128 == 0.
+ * out_dtype HN_DTYPE_INT32 (int8 kind, both scale modes HN_SCALE_ROW, no bias, HN_EPI_NONE): out is the
+ * exact int32 accumulator sum_k qa*qw - the raw integer result, no scaling.
+ */
+int hn_block_gemm(const void *qa, int64_t lda, const float *sa, int64_t ldsa, int sa_mode,
+                  const void *qw, int64_t ldw, const float *sw, int64_t ldsw, int sw_mode,
+                  const void *bias, int bias_dtype,
+                  void *out, int64_t ldo, int out_dtype, float *qs, int64_t ldqs,
+                  int64_t M, int64_t N, int64_t K, int kind, int epilogue, void *stream);
+
+/*
+ * K3 - LayerNorm (no affine) + adaLN modulate + int8 quantize per 128 channels.
+ * Replaces hy_nomas/kernels.py:173-207 (_adaln_quant_kernel / adaln_quant).
+ * x [B*L, D] bf16 contiguous, shift/scale [B, D] bf16 -> q [B*L, D] int8, s [B*L, D/128] fp32.
+ * D % 128 == 0, D <= 16384.
+ */
+int hn_adaln_quant(const void *x, const void *shift, const void *scale, int64_t B, int64_t L, int64_t D,
+                   float eps, int8_t *q, float *s, void *stream);
+
+/*
+ * K4 - LayerNorm + modulate -> bf16. Replaces hy_nomas/fused.py:37-62 (_adaln_kernel / adaln).
+ * x [B*L, D] bf16, shift/scale [B, D] bf16 -> y [B*L, D] bf16. D % 16 == 0, D <= 16384.
+ */
+int hn_adaln(const void *x, const void *shift, const void *scale, int64_t B, int64_t L, int64_t D, float eps,
+             void *y, void *stream);
+
+/*
+ * K5 - per-head RMSNorm (fp32, rounded to bf16) x weight (bf16), then interleaved-pair RoPE.
+ * Replaces hy_nomas/fused.py:65-105 (_qk_norm_rope_kernel / qk_norm_rope).
+ * x: B*L token rows of H heads x D (D == 128), heads contiguous, token row stride `row_stride`
+ * elements (>= H*D; e.g. 3*H*D inside a fused qkv buffer); rows of batch b start at b*L*row_stride.
+ * weight [D] bf16. cos/sin [L, D] fp32 or both NULL (no RoPE). y [B, L, H, D] bf16 contiguous.
+ */
+int hn_qk_norm_rope(const void *x, int64_t row_stride, const void *weight, const float *cos, const float *sin,
+                    int64_t B, int64_t L, int64_t H, int64_t D, float eps, void *y, void *stream);
+
+/*
+ * K5 x2 - the same for the q and k tensors of one attention in a single launch (the RoPE tables are
+ * read once per token for both). Same arguments as hn_qk_norm_rope, per tensor.
+ * Replaces the pair of calls at hy_nomas/model.py:266-267.
+ */
+int hn_qk_norm_rope2(const void *xq, const void *xk, int64_t row_stride, const void *wq, const void *wk,
+                     const float *cos, const float *sin, int64_t B, int64_t L, int64_t H, int64_t D, float eps,
+                     void *yq, void *yk, void *stream);
+
+/*
+ * K6 - gated residual x + rbf16(y * gate[b]) -> bf16.
+ * Replaces hy_nomas/fused.py:108-128 (_gated_residual_kernel / gated_residual).
+ * x, y [B*L, D] bf16, gate [B, D] bf16 -> out [B*L, D] bf16. D % 8 == 0.
+ */
+int hn_gated_residual(const void *x, const void *y, const void *gate, int64_t B, int64_t L, int64_t D, void *out,
+                      void *stream);
+
+/*
+ * K6+K3 - gated residual, then the next LayerNorm/modulate/int8 quantize of its result, in one pass.
+ * Replaces the pair fused.gated_residual + kernels.adaln_quant at hy_nomas/model.py:280-282.
+ * out = x + rbf16(y * gate) (bf16, written) and (q, s) = adaln_quant(out, shift, scale, eps).
+ */
+int hn_gated_residual_adaln_quant(const void *x, const void *y, const void *gate, const void *shift,
+                                  const void *scale, int64_t B, int64_t L, int64_t D, float eps, void *out,
+                                  int8_t *q, float *s, void *stream);
+
+/*
+ * K7 - PixelUMM decoder q/k prep: split T / HW RMSNorm (own weights) + rotate-half MRoPE.
+ * Replaces hy_nomas/fused.py:131-186 (_pixelumm_qk_kernel / pixelumm_qk).
+ * x: N tokens x H heads x D (D == 128), token stride row_stride; weight_t/weight_hw [D/2] bf16;
+ * cos/sin [N, D] fp32 -> y [N, H, D] bf16.
+ */
+int hn_pixelumm_qk(const void *x, int64_t row_stride, const void *weight_t, const void *weight_hw, const float *cos,
+                   const float *sin, int64_t N, int64_t H, int64_t D, float eps, void *y, void *stream);
+
+/*
+ * int8 KV quantizer per (token, head): absmax/127, round half away from zero.
+ * Replaces hy_nomas/world.py:83-90 (quantize_kv). x [L*H, D] bf16 -> q [L*H, D] int8, s [L*H] fp32.
+ */
+int hn_quantize_kv(const void *x, int64_t rows, int64_t D, int8_t *q, float *s, void *stream);
+
+#if defined(__GNUC__)
+#pragma GCC visibility pop
+#endif
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* HYNOMAS_B200_H */

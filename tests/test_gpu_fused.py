@@ -1,0 +1,150 @@
+"""The fused elementwise kernels (hy_nomas/fused.py, kernels.adaln_quant) on the GPU: bit-exact against the
+oracle (same reduction tree, correctly rounded rsqrt), and within the reference's own tolerances
+(its tests/test_fused.py) against the torch arithmetic of hy_nomas/model.py."""
+import numpy as np
+import pytest
+import torch
+
+from hn_testutil import bf16_from_bits, bits16, f32
+
+pytestmark = pytest.mark.gpu
+
+
+@pytest.mark.parametrize("b,l,d", [(2, 20, 2048), (1, 12, 4096), (1, 37, 3072), (3, 5, 128)])
+def test_adaln_quant_and_adaln_bit_exact(hn, oracle, cuda, b, l, d):
+    gen = torch.Generator().manual_seed(b * l + d)
+    x = (torch.randn(b, l, d, generator=gen) * 3).bfloat16()
+    shift, scale = torch.randn(b, d, generator=gen).bfloat16(), torch.randn(b, d, generator=gen).bfloat16()
+    q, s = hn.kernels.adaln_quant(x.to(cuda), shift.to(cuda), scale.to(cuda))
+    y = hn.fused.adaln(x.to(cuda), shift.to(cuda), scale.to(cuda))
+    qo, so = oracle.adaln_quant(f32(x), f32(shift), f32(scale))
+    assert np.array_equal(q.cpu().numpy(), qo) and np.array_equal(f32(s), so)
+    yo = oracle.bf16_bits(oracle.round_bf16(oracle.adaln(f32(x), f32(shift), f32(scale))))
+    assert np.array_equal(bits16(y), yo)
+
+
+def test_adaln_golden(hn, golden, cuda):
+    d = golden("adaln")
+    for tag, b in (("d2048", 2), ("d4096", 1)):
+        D = int(tag[1:])
+        x = bf16_from_bits(d[f"{tag}_x"], cuda).view(b, -1, D)
+        sh, sc = bf16_from_bits(d[f"{tag}_shift"], cuda).view(b, D), bf16_from_bits(d[f"{tag}_scale"], cuda).view(b, D)
+        q, s = hn.kernels.adaln_quant(x, sh, sc)
+        assert (q.cpu().numpy() != d[f"{tag}_q"]).mean() < 1e-3
+        assert np.allclose(f32(s), d[f"{tag}_s"], rtol=1e-3)
+        y = hn.fused.adaln(x, sh, sc)
+        assert (bits16(y).reshape(-1) != d[f"{tag}_torch_y"].reshape(-1)).mean() < 1e-3
+
+
+def test_reference_adaln_strided(hn, cuda):
+    """tests/test_fused.py:12-21 of the reference: strided input, mismatch < 1e-3, max abs < 0.05."""
+    from oracle import torch_ref
+    x = (torch.randn(2, 2048, 777) * 3).bfloat16().transpose(1, 2)
+    shift, scale = torch.randn(2, 2048).bfloat16(), torch.randn(2, 2048).bfloat16()
+    ref = torch_ref.modulate(torch_ref.layer_norm(x), shift, scale).to(torch.bfloat16)
+    got = hn.fused.adaln(x.to(cuda), shift.to(cuda), scale.to(cuda)).cpu()
+    assert (got != ref).float().mean().item() < 1e-3
+    assert (got.float() - ref.float()).abs().max().item() < 0.05
+
+
+def test_reference_adaln_quant_matches_unfused(hn, cuda):
+    """tests/test_fused.py:52-60: K3 against K1(K4); here the codes are identical by construction."""
+    x = (torch.randn(1, 2048, 300) * 3).bfloat16().transpose(1, 2).to(cuda)
+    shift, scale = torch.randn(1, 2048).bfloat16().to(cuda), torch.randn(1, 2048).bfloat16().to(cuda)
+    q, s = hn.kernels.adaln_quant(x, shift, scale)
+    q_ref, s_ref = hn.kernels.quantize_activations(hn.fused.adaln(x, shift, scale).view(-1, 2048))
+    assert torch.equal(q, q_ref) and torch.equal(s, s_ref)
+
+
+def test_gated_residual_exact(hn, golden, cuda):
+    d = golden("gated_residual")
+    x = bf16_from_bits(d["x"], cuda).view(2, 33, 256)
+    y = bf16_from_bits(d["y"], cuda).view(2, 33, 256)
+    g = bf16_from_bits(d["g"], cuda).view(2, 256)
+    out = hn.fused.gated_residual(x, y, g)
+    assert np.array_equal(bits16(out).reshape(-1), d["out"].reshape(-1))
+
+
+def test_reference_gated_residual_strided(hn, cuda):
+    """tests/test_fused.py:43-49: exact equality with x + y * g."""
+    x = torch.randn(1, 2048, 500).bfloat16().transpose(1, 2).to(cuda)
+    y = torch.randn(1, 500, 2048).bfloat16().to(cuda)
+    g = torch.randn(1, 2048).bfloat16().to(cuda)
+    assert torch.equal(hn.fused.gated_residual(x, y, g), x + y * g.unsqueeze(1))
+
+
+@pytest.mark.parametrize("b,l,d", [(1, 40, 4096), (2, 9, 2048)])
+def test_gated_residual_adaln_quant_bit_exact(hn, oracle, cuda, b, l, d):
+    gen = torch.Generator().manual_seed(l)
+    x, y = torch.randn(b, l, d, generator=gen).bfloat16(), torch.randn(b, l, d, generator=gen).bfloat16()
+    g = (torch.randn(b, d, generator=gen) * 0.1).bfloat16()
+    sh, sc = torch.randn(b, d, generator=gen).bfloat16(), torch.randn(b, d, generator=gen).bfloat16()
+    xo, q, s = hn.fused.gated_residual_adaln_quant(*(t.to(cuda) for t in (x, y, g, sh, sc)))
+    xr, qr, sr = oracle.gated_residual_adaln_quant(f32(x), f32(y), f32(g), f32(sh), f32(sc))
+    assert np.array_equal(bits16(xo), oracle.bf16_bits(xr))
+    assert np.array_equal(q.cpu().numpy(), qr) and np.array_equal(f32(s), sr)
+    # the same as the two unfused calls
+    x2 = hn.fused.gated_residual(x.to(cuda), y.to(cuda), g.to(cuda))
+    q2, s2 = hn.kernels.adaln_quant(x2, sh.to(cuda), sc.to(cuda))
+    assert torch.equal(x2, xo) and torch.equal(q2, q) and torch.equal(s2, s)
+
+
+def test_qk_norm_rope_golden_and_oracle(hn, oracle, golden, cuda):
+    d = golden("qk_norm_rope")
+    x = bf16_from_bits(d["x"], cuda)
+    w = bf16_from_bits(d["w"], cuda)
+    cos, sin = torch.from_numpy(d["cos"]).to(cuda), torch.from_numpy(d["sin"]).to(cuda)
+    yr = hn.fused.qk_norm_rope(x, w, (cos, sin))
+    yp = hn.fused.qk_norm_rope(x, w, None)
+    ro = oracle.bf16_bits(oracle.qk_norm_rope(f32(x), f32(w), (d["cos"], d["sin"])))
+    po = oracle.bf16_bits(oracle.qk_norm_rope(f32(x), f32(w), None))
+    assert np.array_equal(bits16(yr), ro) and np.array_equal(bits16(yp), po)
+    assert (bits16(yr) != d["torch_rope"]).mean() < 1e-2
+    assert (bits16(yp) != d["torch_plain"]).mean() < 1e-3
+
+
+def test_reference_qk_norm_rope(hn, cuda):
+    """tests/test_fused.py:24-40 of the reference (b2, l96, h16, d128, rope [16, 56, 56] theta 256)."""
+    from oracle import torch_ref
+    b, l, h, d = 2, 96, 16, 128
+    lin = (torch.randn(b, l, h * d) * 5).bfloat16()
+    x = lin.view(b, l, h, d)
+    weight = (torch.rand(d) + 0.5).bfloat16()
+    cos, sin = torch_ref.rope_freqs([16, 56, 56], 256, 4, 4, 6)
+    ref_plain = torch_ref.rms_norm(x, weight)
+    ref = torch_ref.apply_rope(ref_plain, cos, sin)
+    got = hn.fused.qk_norm_rope(x.to(cuda), weight.to(cuda), (cos.to(cuda), sin.to(cuda))).cpu()
+    got_plain = hn.fused.qk_norm_rope(x.to(cuda), weight.to(cuda), None).cpu()
+    assert (got_plain != ref_plain).float().mean().item() < 1e-3
+    assert (got != ref).float().mean().item() < 1e-2
+    assert ((got.float() - ref.float()).norm() / ref.float().norm()).item() < 1e-3
+
+
+def test_qk_norm_rope_strided_qkv_and_pair(hn, oracle, cuda):
+    """q/k as column slices of a fused [L, 3 * H * D] qkv buffer (token stride 3HD), one and two per launch,
+    with BASELINE's 3-D RoPE (t,h,w axes 16/56/56, theta 10000)."""
+    from oracle import torch_ref
+    b, l, h, d = 1, 2 * 3 * 4, 32, 128
+    qkv = (torch.randn(b, l, 3 * h * d, generator=torch.Generator().manual_seed(4)) * 2).bfloat16().to(cuda)
+    q = qkv[..., : h * d].view(b, l, h, d)
+    k = qkv[..., h * d: 2 * h * d].view(b, l, h, d)
+    wq, wk = (torch.rand(d) + 0.5).bfloat16().to(cuda), (torch.rand(d) + 0.5).bfloat16().to(cuda)
+    cos, sin = torch_ref.rope_freqs([16, 56, 56], 10000, 2, 3, 4)
+    rope = (cos.to(cuda), sin.to(cuda))
+    yq = hn.fused.qk_norm_rope(q, wq, rope)
+    yq2, yk2 = hn.fused.qk_norm_rope2(q, k, wq, wk, rope)
+    assert torch.equal(yq, yq2)
+    for got, src, w in ((yq2, q, wq), (yk2, k, wk)):
+        ref = oracle.qk_norm_rope(f32(src.contiguous()), f32(w), (cos.numpy(), sin.numpy()))
+        assert np.array_equal(bits16(got), oracle.bf16_bits(ref))
+
+
+def test_pixelumm_qk(hn, oracle, golden, cuda):
+    d = golden("pixelumm_qk")
+    x = bf16_from_bits(d["x"], cuda)
+    wt, whw = bf16_from_bits(d["wt"], cuda), bf16_from_bits(d["whw"], cuda)
+    cos, sin = torch.from_numpy(d["cos"]).to(cuda), torch.from_numpy(d["sin"]).to(cuda)
+    y = hn.fused.pixelumm_qk(x, wt, whw, cos, sin)
+    ref = oracle.pixelumm_qk(f32(x), f32(wt), f32(whw), d["cos"], d["sin"])
+    assert np.array_equal(bits16(y), oracle.bf16_bits(ref))
+    assert (bits16(y) != d["y"]).mean() < 1e-3

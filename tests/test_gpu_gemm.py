@@ -1,0 +1,176 @@
+"""K2 block-scaled GEMM (hy_nomas/kernels.py:80-170) on the sm_100a tensor cores against the oracle.
+
+Bit-exact: the int32 accumulator, and the fp32 result of the scale promotion (the kernel and the oracle
+evaluate the same per-group fma sequence), hence the bf16 / GELU / requantized outputs. FP8 partials come
+from the tensor core's fp32 accumulation, so FP8 is held to rel-L2 <= 1e-2 (the stated tolerance)."""
+import numpy as np
+import pytest
+import torch
+
+from hn_testutil import bf16_from_bits, f32, rel_l2, u8
+
+pytestmark = pytest.mark.gpu
+
+
+def no_device_error(hn):
+    rc, code = hn.lib.device_error()
+    assert rc == 0 and code == 0, (rc, code, hn.lib.last_error())
+
+
+def rand_codes(gen, *shape, lo=-127, hi=128):
+    return torch.randint(lo, hi, shape, generator=gen, dtype=torch.int8)
+
+
+@pytest.mark.parametrize("m,n,k", [(300, 520, 4096), (128, 256, 128), (1, 16, 256), (257, 1000, 1024)])
+def test_int32_accumulator_exact(hn, oracle, cuda, m, n, k):
+    gen = torch.Generator().manual_seed(m + n + k)
+    qa, qw = rand_codes(gen, m, k, lo=-128), rand_codes(gen, n, k, lo=-128)
+    ones_m, ones_n = torch.ones(m, device=cuda), torch.ones(n, device=cuda)
+    out = hn.kernels.block_gemm(qa.to(cuda), ones_m, qw.to(cuda), ones_n, out_dtype=torch.int32)
+    no_device_error(hn)
+    ref = oracle.int32_gemm(qa.numpy(), qw.numpy())
+    assert np.array_equal(out.cpu().numpy().astype(np.int64), ref)
+
+
+def test_group_scaled_golden(hn, oracle, golden, cuda):
+    d = golden("block_gemm")
+    qa, sa = torch.from_numpy(d["qa"]).to(cuda), torch.from_numpy(d["sa"]).to(cuda)
+    qw, sw = torch.from_numpy(d["qw"]).to(cuda), torch.from_numpy(d["sw"]).to(cuda)
+    bias = bf16_from_bits(d["bias"], cuda)
+    bias_f = bias.float().cpu().numpy()
+    acc = hn.kernels.block_gemm(qa, sa, qw, sw, bias, out_dtype=torch.float32)
+    y0 = hn.kernels.block_gemm(qa, sa, qw, sw, bias)
+    y1 = hn.kernels.block_gemm(qa, sa, qw, sw, bias, epilogue="gelu")
+    q2, s2 = hn.kernels.block_gemm(qa, sa, qw, sw, bias, epilogue="gelu_quant")
+    no_device_error(hn)
+    ref = oracle.block_gemm(d["qa"], d["sa"], d["qw"], d["sw"], bias_f)
+    assert np.array_equal(f32(acc).view(np.uint32), ref.view(np.uint32))
+    assert np.array_equal(y0.cpu().view(torch.int16).numpy().view(np.uint16), oracle.bf16_bits(oracle.round_bf16(ref)))
+    h = oracle.block_gemm(d["qa"], d["sa"], d["qw"], d["sw"], bias_f, epilogue="gelu")
+    assert np.array_equal(y1.cpu().view(torch.int16).numpy().view(np.uint16), oracle.bf16_bits(h))
+    _, qh, qs = oracle.block_gemm(d["qa"], d["sa"], d["qw"], d["sw"], bias_f, epilogue="gelu_quant")
+    assert np.array_equal(q2.cpu().numpy(), qh) and np.array_equal(f32(s2), qs)
+    # and against the reference's own kernel (interpreter, no FMA contraction): within rounding
+    assert (y0.cpu().view(torch.int16).numpy().view(np.uint16) != d["ep0_bf16"]).mean() < 1e-2
+    assert (q2.cpu().numpy() != d["ep2_q"]).mean() < 1e-3
+    assert rel_l2(f32(acc), d["acc_f32"]) < 1e-6
+
+
+MODES = [("group", "group"), ("group", "row"), ("row", "group"), ("row", "row"), ("group", "block"),
+         ("row", "block")]
+
+
+@pytest.mark.parametrize("sa_mode,sw_mode", MODES)
+@pytest.mark.parametrize("m,n,k", [(200, 384, 1024), (1, 128, 128), (333, 256, 512)])
+def test_scale_modes_int8_bit_exact(hn, oracle, cuda, sa_mode, sw_mode, m, n, k):
+    gen = torch.Generator().manual_seed(m * 31 + n + k)
+    qa, qw = rand_codes(gen, m, k), rand_codes(gen, n, k)
+    g = k // 128
+    sa = torch.rand(m, g, generator=gen) * 0.02 + 1e-3 if sa_mode == "group" else torch.rand(m, generator=gen) * 0.02
+    if sw_mode == "group":
+        sw = torch.rand(n, g, generator=gen) * 4e-3 + 1e-3
+    elif sw_mode == "row":
+        sw = torch.rand(n, generator=gen) * 4e-3 + 1e-3
+    else:
+        sw = torch.rand((n + 127) // 128, g, generator=gen) * 4e-3 + 1e-3
+    bias = (torch.randn(n, generator=gen) * 0.1).bfloat16()
+    out = hn.kernels.block_gemm(qa.to(cuda), sa.to(cuda), qw.to(cuda), sw.to(cuda), bias.to(cuda),
+                                out_dtype=torch.float32)
+    no_device_error(hn)
+    ref = oracle.block_gemm(qa.numpy(), sa.numpy(), qw.numpy(), sw.numpy(), bias.float().numpy(), sa_mode=sa_mode,
+                            sw_mode=sw_mode)
+    assert np.array_equal(f32(out).view(np.uint32), ref.view(np.uint32))
+
+
+@pytest.mark.parametrize("out_dtype", [torch.bfloat16, torch.float16])
+def test_output_dtypes_and_ragged_n(hn, oracle, cuda, out_dtype):
+    gen = torch.Generator().manual_seed(11)
+    m, n, k = 77, 200, 384   # N not a multiple of the 256-wide tile; row pitch 200 -> scalar-store path
+    qa, qw = rand_codes(gen, m, k), rand_codes(gen, n, k)
+    sa, sw = torch.rand(m, 3, generator=gen) * 0.01, torch.rand(n, 3, generator=gen) * 0.01
+    out = hn.kernels.block_gemm(qa.to(cuda), sa.to(cuda), qw.to(cuda), sw.to(cuda), out_dtype=out_dtype)
+    no_device_error(hn)
+    ref = oracle.block_gemm(qa.numpy(), sa.numpy(), qw.numpy(), sw.numpy())
+    expect = torch.from_numpy(ref).to(out_dtype)
+    assert torch.equal(out.cpu(), expect)
+
+
+@pytest.mark.parametrize("sw_layout", ["block", "group"])
+def test_fp8_golden(hn, oracle, golden, cuda, sw_layout):
+    d = golden("block_gemm")
+    qa = torch.from_numpy(d["fp8_qa"]).view(torch.float8_e4m3fn).to(cuda)
+    qw = torch.from_numpy(d["fp8_qw"]).view(torch.float8_e4m3fn).to(cuda)
+    sa = torch.from_numpy(d["fp8_sa"]).to(cuda)
+    swb = torch.from_numpy(d["fp8_sw_block"])
+    sw = swb if sw_layout == "block" else swb.repeat_interleave(128, dim=0)
+    bias = bf16_from_bits(d["bias"], cuda)
+    acc = hn.kernels.block_gemm(qa, sa, qw, sw.to(cuda), bias, out_dtype=torch.float32, kind="fp8")
+    no_device_error(hn)
+    assert rel_l2(f32(acc), d["fp8_acc_f32"]) < 1e-2       # stated FP8 tolerance
+    assert rel_l2(f32(acc), d["fp8_acc_f32"]) < 1e-5       # what the tensor core actually delivers here
+
+
+def test_reference_gelu_quant_epilogue(hn, cuda):
+    """The reference's own test (tests/test_fused.py:63-78) run on this path."""
+    from oracle import torch_ref
+    torch.manual_seed(0)
+    x = torch.randn(1000, 2048).bfloat16().to(cuda)
+    w = torch.randn(8192, 2048) * 0.02
+    bias = (torch.randn(8192) * 0.1).bfloat16().to(cuda)
+    qw, sw = torch_ref.quantize_g128(w)
+    qw, sw = qw.to(cuda), sw.to(cuda)
+    K = hn.kernels
+    qa, sa = K.quantize_activations(x)
+    plain = K.block_gemm(qa, sa, qw, sw, bias)
+    gelu = K.block_gemm(qa, sa, qw, sw, bias, epilogue="gelu")
+    ref = torch.nn.functional.gelu(plain, approximate="tanh")
+    assert (gelu.float() - ref.float()).abs().max().item() <= 2 ** -6 * ref.float().abs().max().item()
+    qh, sh = K.block_gemm(qa, sa, qw, sw, bias, epilogue="gelu_quant")
+    qh_ref, sh_ref = K.quantize_activations(gelu)
+    assert (qh != qh_ref).float().mean().item() < 1e-3
+    assert torch.allclose(sh, sh_ref, rtol=1e-3)
+    no_device_error(hn)
+
+
+def test_block_linear_matches_dequant_path(hn, oracle, cuda):
+    """int8_g128_linear against the reference's exact (dequantize + bf16 F.linear) path and the oracle."""
+    from oracle import torch_ref
+    gen = torch.Generator().manual_seed(2)
+    x = (torch.randn(3, 100, 1024, generator=gen) * 2).bfloat16()
+    w = torch.randn(768, 1024, generator=gen) * 0.02
+    bias = (torch.randn(768, generator=gen) * 0.02).bfloat16()
+    qw, sw = torch_ref.quantize_g128(w)
+    y = hn.kernels.int8_g128_linear(x.to(cuda), qw.to(cuda), sw.to(cuda), bias.to(cuda))
+    assert y.shape == (3, 100, 768) and y.dtype == torch.bfloat16
+    qa, sa = oracle.quantize_activations(f32(x).reshape(-1, 1024))
+    ref = oracle.block_gemm(qa, sa, qw.numpy(), sw.numpy(), bias.float().numpy())
+    assert np.array_equal(y.reshape(-1, 768).cpu().view(torch.int16).numpy().view(np.uint16),
+                          oracle.bf16_bits(oracle.round_bf16(ref)))
+    exact = torch_ref.int8_linear_cpu(x.float(), qw, sw, bias.float())
+    assert rel_l2(y.float().cpu().numpy(), exact.numpy()) < 2e-2   # activation quantization error only
+
+
+def test_block_linear_ragged_k_takes_dequant_path(hn, cuda):
+    from oracle import torch_ref
+    x = torch.randn(5, 200).bfloat16().to(cuda)
+    qw, sw = torch_ref.quantize_g128(torch.randn(64, 200) * 0.02)
+    y = hn.kernels.int8_g128_linear(x, qw.to(cuda), sw.to(cuda))
+    ref = torch.nn.functional.linear(x, torch_ref.dequantize_g128(qw, sw).to(cuda))
+    assert torch.equal(y, ref)
+
+
+@pytest.mark.slow
+def test_full_size_sampled_rows(hn, oracle, cuda):
+    """BASELINE shapes: M = 20240 tokens, K = N = 4096, per-group scales; 96 sampled rows vs the oracle."""
+    gen = torch.Generator().manual_seed(7)
+    m, n, k = 20240, 4096, 4096
+    x = (torch.randn(m, k, generator=gen)).bfloat16().to(cuda)
+    qw = rand_codes(gen, n, k).to(cuda)
+    sw = (torch.rand(n, k // 128, generator=gen) * 4e-3 + 1e-3).to(cuda)
+    qa, sa = hn.kernels.quantize_activations(x)
+    y = hn.kernels.block_gemm(qa, sa, qw, sw, out_dtype=torch.float32)
+    no_device_error(hn)
+    rows = torch.randperm(m, generator=gen)[:96].sort().values
+    rows = torch.cat([rows, torch.tensor([0, m - 1])])
+    ref = oracle.block_gemm(u8(qa[rows.to(cuda)]), f32(sa[rows.to(cuda)]), u8(qw), f32(sw))
+    assert np.array_equal(f32(y[rows.to(cuda)]).view(np.uint32), ref.view(np.uint32))

@@ -1,0 +1,80 @@
+"""K1 activation quantizer (hy_nomas/kernels.py:22-54), ops.quantize_g128 (ops.py:41-52) and the int8 KV
+quantizer (world.py:83-90) on the GPU against the oracle and the reference's golden vectors: codes and
+scales bit-exact."""
+import numpy as np
+import pytest
+import torch
+
+from hn_testutil import bf16_from_bits, f32, u8
+
+pytestmark = pytest.mark.gpu
+
+
+def test_golden_vectors(hn, golden, cuda):
+    d = golden("quant_act")
+    x = bf16_from_bits(d["x"], cuda)
+    for kind in ("int8", "fp8"):
+        q, s = hn.kernels.quantize_activations(x, kind)
+        torch.cuda.synchronize()
+        assert np.array_equal(u8(q), d[f"{kind}_q"]), kind
+        assert np.array_equal(f32(s).view(np.uint32), d[f"{kind}_s"].view(np.uint32)), kind
+
+
+@pytest.mark.parametrize("dtype", [torch.bfloat16, torch.float16, torch.float32])
+@pytest.mark.parametrize("m,k", [(1, 128), (17, 384), (1000, 2048), (300, 4096)])
+@pytest.mark.parametrize("kind", ["int8", "fp8"])
+def test_random_shapes_bit_exact(hn, oracle, cuda, dtype, m, k, kind):
+    gen = torch.Generator().manual_seed(m * 7 + k)
+    x = (torch.randn(m, k, generator=gen) * 3).to(dtype)
+    x[:, torch.randperm(k, generator=gen)[: max(1, k // 100)]] *= 20
+    if m > 3:
+        x[2] = 0
+    q, s = hn.kernels.quantize_activations(x.to(cuda), kind)
+    qo, so = oracle.quantize_activations(f32(x), kind)
+    assert np.array_equal(u8(q), qo)
+    assert np.array_equal(f32(s), so)
+
+
+def test_strided_rows(hn, oracle, cuda):
+    base = (torch.randn(64, 1024) * 2).bfloat16()
+    x = base[:, :512]                       # row pitch 1024, 512 columns
+    q, s = hn.kernels.quantize_activations(base.to(cuda)[:, :512], "int8")
+    qo, so = oracle.quantize_activations(f32(x), "int8")
+    assert np.array_equal(u8(q), qo) and np.array_equal(f32(s), so)
+
+
+@pytest.mark.parametrize("kind", ["int8", "fp8"])
+def test_per_token(hn, oracle, cuda, kind):
+    x = (torch.randn(100, 4096, generator=torch.Generator().manual_seed(3)) * 2).bfloat16()
+    q, s = hn.kernels.quantize_activations(x.to(cuda), kind, per_token=True)
+    qo, so = oracle.quantize_activations(f32(x), kind, per_row=True)
+    assert np.array_equal(u8(q), qo) and np.array_equal(f32(s), so)
+
+
+def test_ops_quantize_g128(hn, golden, cuda):
+    d = golden("quantize_g128")
+    q, s = hn.ops.quantize_g128(torch.from_numpy(d["w"]).to(cuda))
+    assert np.array_equal(q.cpu().numpy(), d["q"]) and np.array_equal(f32(s), d["s"])
+    deq = hn.ops.dequantize_g128(q, s)
+    assert np.array_equal(deq.cpu().view(torch.int16).numpy().view(np.uint16), d["deq"])
+
+
+def test_ops_quantize_g128_ragged_k(hn, cuda):
+    from oracle import torch_ref
+    w = torch.randn(33, 200, generator=torch.Generator().manual_seed(5)) * 0.05
+    q, s = hn.ops.quantize_g128(w.to(cuda))
+    qr, sr = torch_ref.quantize_g128(w)
+    assert torch.equal(q.cpu(), qr) and torch.equal(s.cpu(), sr)
+
+
+def test_quantize_kv(hn, golden, cuda):
+    d = golden("quantize_kv")
+    x = bf16_from_bits(d["x"], cuda)
+    l, h, dd = x.shape
+    q = torch.empty((l * h, dd), dtype=torch.int8, device=cuda)
+    s = torch.empty((l * h,), dtype=torch.float32, device=cuda)
+    rc = hn.lib.lib.hn_quantize_kv(hn.lib.ptr(x), l * h, dd, hn.lib.ptr(q), hn.lib.ptr(s), hn.lib.stream_of(x))
+    hn.lib.check(rc, "hn_quantize_kv")
+    torch.cuda.synchronize()
+    assert np.array_equal(q.cpu().numpy().reshape(d["q"].shape), d["q"])
+    assert np.array_equal(f32(s).reshape(d["s"].shape), d["s"])
