@@ -84,6 +84,17 @@ static inline bool al16(const void *p) { return (reinterpret_cast<uintptr_t>(p) 
 static inline bool al8(const void *p) { return (reinterpret_cast<uintptr_t>(p) & 7) == 0; }
 static inline int dsize(int dt) { return dt == HN_DTYPE_FP32 || dt == HN_DTYPE_INT32 ? 4 : 2; }
 
+// A [rows, groups] scale tensor addressed as s[r * rs + g * gs] must not alias two entries: one stride
+// must cover the whole extent of the other dimension (row-major: rs >= groups * gs; group-major:
+// gs >= rows * rs).
+static bool scale_strides_ok(int64_t rows, int64_t groups, int64_t rs, int64_t gs) {
+    if (rows <= 1 && groups <= 1) return true;
+    if (rows <= 1) return gs >= 1;
+    if (groups <= 1) return rs >= 1;
+    if (rs < 1 || gs < 1) return false;
+    return rs >= groups * gs || gs >= rows * rs;
+}
+
 static int launched(cudaError_t e, const char *what) {
     if (e != cudaSuccess) return cuda_fail(e, what);
     t_last_error.clear();
@@ -140,27 +151,29 @@ int hn_selftest_wait_timeout(uint32_t timeout_us, void *stream) {
 }
 
 int hn_quant_act(const void *x, int64_t ldx, int x_dtype, int64_t M, int64_t K, int kind, int per_row, void *q,
-                 int64_t ldq, float *s, int64_t lds, void *stream) {
+                 int64_t ldq, float *s, int64_t s_rs, int64_t s_gs, void *stream) {
     REQUIRE(x && q && s, HN_ERR_ARG, "hn_quant_act: null pointer");
     REQUIRE(x_dtype == HN_DTYPE_BF16 || x_dtype == HN_DTYPE_FP16 || x_dtype == HN_DTYPE_FP32, HN_ERR_ARG,
             "hn_quant_act: x_dtype %d not bf16/fp16/fp32", x_dtype);
     REQUIRE(kind == HN_KIND_INT8 || kind == HN_KIND_FP8E4M3, HN_ERR_ARG, "hn_quant_act: unknown kind %d", kind);
     REQUIRE(M >= 0 && K > 0 && K % 128 == 0, HN_ERR_SHAPE, "hn_quant_act: need K %% 128 == 0 (M=%lld K=%lld)",
             (long long)M, (long long)K);
-    REQUIRE(ldx >= K && ldq >= K && lds >= (per_row ? 1 : K / 128), HN_ERR_SHAPE, "hn_quant_act: leading dimension too small");
+    REQUIRE(ldx >= K && ldq >= K, HN_ERR_SHAPE, "hn_quant_act: leading dimension too small");
+    REQUIRE(scale_strides_ok(M, per_row ? 1 : K / 128, s_rs, s_gs), HN_ERR_SHAPE,
+            "hn_quant_act: scale strides (%lld, %lld) overlap", (long long)s_rs, (long long)s_gs);
     REQUIRE(M <= 0x7fffffffLL, HN_ERR_SHAPE, "hn_quant_act: M too large");
     REQUIRE(al16(x) && (ldx * dsize(x_dtype)) % 16 == 0 && al16(q) && ldq % 16 == 0, HN_ERR_ALIGN,
             "hn_quant_act: x/q must be 16-byte aligned with 16-byte row pitch");
     if (M == 0) return HN_OK;
     CHECK_ARCH();
-    return launched(launch_quant_act(x, ldx, x_dtype, M, K, kind, per_row, q, ldq, s, lds, (cudaStream_t)stream),
+    return launched(launch_quant_act(x, ldx, x_dtype, M, K, kind, per_row, q, ldq, s, s_rs, s_gs, (cudaStream_t)stream),
                     "hn_quant_act launch");
 }
 
-int hn_block_gemm(const void *qa, int64_t lda, const float *sa, int64_t ldsa, int sa_mode, const void *qw,
-                  int64_t ldw, const float *sw, int64_t ldsw, int sw_mode, const void *bias, int bias_dtype, void *out,
-                  int64_t ldo, int out_dtype, float *qs, int64_t ldqs, int64_t M, int64_t N, int64_t K, int kind,
-                  int epilogue, void *stream) {
+int hn_block_gemm(const void *qa, int64_t lda, const float *sa, int64_t sa_rs, int64_t sa_gs, int sa_mode,
+                  const void *qw, int64_t ldw, const float *sw, int64_t sw_rs, int64_t sw_gs, int sw_mode,
+                  const void *bias, int bias_dtype, void *out, int64_t ldo, int out_dtype, float *qs, int64_t qs_rs,
+                  int64_t qs_gs, int64_t M, int64_t N, int64_t K, int kind, int epilogue, void *stream) {
     REQUIRE(qa && sa && qw && sw && out, HN_ERR_ARG, "hn_block_gemm: null pointer");
     REQUIRE(kind == HN_KIND_INT8 || kind == HN_KIND_FP8E4M3, HN_ERR_ARG, "hn_block_gemm: unknown kind %d", kind);
     REQUIRE(sa_mode == HN_SCALE_GROUP || sa_mode == HN_SCALE_ROW, HN_ERR_ARG, "hn_block_gemm: bad sa_mode %d", sa_mode);
@@ -170,15 +183,20 @@ int hn_block_gemm(const void *qa, int64_t lda, const float *sa, int64_t ldsa, in
             "hn_block_gemm: need K %% 128 == 0, N > 0 (M=%lld N=%lld K=%lld)", (long long)M, (long long)N, (long long)K);
     REQUIRE(M < (1LL << 31) && N < (1LL << 31) && K < (1LL << 31), HN_ERR_SHAPE, "hn_block_gemm: dimension too large");
     REQUIRE(lda >= K && ldw >= K && ldo >= N, HN_ERR_SHAPE, "hn_block_gemm: leading dimension too small");
-    REQUIRE(sa_mode != HN_SCALE_GROUP || ldsa >= K / 128, HN_ERR_SHAPE, "hn_block_gemm: ldsa < K/128");
-    REQUIRE(sw_mode != HN_SCALE_GROUP || ldsw >= K / 128, HN_ERR_SHAPE, "hn_block_gemm: ldsw < K/128");
-    REQUIRE(sw_mode != HN_SCALE_BLOCK || ldsw >= K / 128, HN_ERR_SHAPE, "hn_block_gemm: ldsw < K/128 (block)");
+    REQUIRE(sa_mode != HN_SCALE_GROUP || scale_strides_ok(M, K / 128, sa_rs, sa_gs), HN_ERR_SHAPE,
+            "hn_block_gemm: activation scale strides overlap");
+    REQUIRE(sw_mode != HN_SCALE_GROUP || scale_strides_ok(N, K / 128, sw_rs, sw_gs), HN_ERR_SHAPE,
+            "hn_block_gemm: weight scale strides overlap");
+    REQUIRE(sw_mode != HN_SCALE_BLOCK || scale_strides_ok(cdiv(N, 128), K / 128, sw_rs, sw_gs), HN_ERR_SHAPE,
+            "hn_block_gemm: weight block scale strides overlap");
+    REQUIRE(sa_mode != HN_SCALE_ROW || sa_rs >= 1, HN_ERR_SHAPE, "hn_block_gemm: sa_rs < 1");
+    REQUIRE(sw_mode != HN_SCALE_ROW || sw_rs >= 1, HN_ERR_SHAPE, "hn_block_gemm: sw_rs < 1");
     REQUIRE(al16(qa) && al16(qw) && lda % 16 == 0 && ldw % 16 == 0, HN_ERR_ALIGN,
             "hn_block_gemm: qa/qw must be 16-byte aligned with row pitch a multiple of 16");
     if (epilogue == HN_EPI_GELU_QUANT) {
         REQUIRE(qs != nullptr, HN_ERR_ARG, "hn_block_gemm: gelu_quant needs qs");
         REQUIRE(N % 128 == 0, HN_ERR_SHAPE, "hn_block_gemm: gelu_quant needs N %% 128 == 0");
-        REQUIRE(ldqs >= N / 128, HN_ERR_SHAPE, "hn_block_gemm: ldqs < N/128");
+        REQUIRE(scale_strides_ok(M, N / 128, qs_rs, qs_gs), HN_ERR_SHAPE, "hn_block_gemm: qs strides overlap");
         REQUIRE(al16(out) && ldo % 16 == 0, HN_ERR_ALIGN, "hn_block_gemm: int8 output must be 16-byte aligned");
     } else if (epilogue == HN_EPI_GELU) {
         REQUIRE(out_dtype == HN_DTYPE_BF16, HN_ERR_UNSUPPORTED, "hn_block_gemm: gelu output is bf16");
@@ -195,10 +213,10 @@ int hn_block_gemm(const void *qa, int64_t lda, const float *sa, int64_t ldsa, in
     if (M == 0) return HN_OK;
     CHECK_ARCH();
     GemmArgs a;
-    a.qa = qa; a.lda = lda; a.sa = sa; a.ldsa = ldsa; a.sa_mode = sa_mode;
-    a.qw = qw; a.ldw = ldw; a.sw = sw; a.ldsw = ldsw; a.sw_mode = sw_mode;
+    a.qa = qa; a.lda = lda; a.sa = sa; a.sa_rs = sa_rs; a.sa_gs = sa_gs; a.sa_mode = sa_mode;
+    a.qw = qw; a.ldw = ldw; a.sw = sw; a.sw_rs = sw_rs; a.sw_gs = sw_gs; a.sw_mode = sw_mode;
     a.bias = bias; a.bias_dtype = bias_dtype;
-    a.out = out; a.ldo = ldo; a.out_dtype = out_dtype; a.qs = qs; a.ldqs = ldqs;
+    a.out = out; a.ldo = ldo; a.out_dtype = out_dtype; a.qs = qs; a.qs_rs = qs_rs; a.qs_gs = qs_gs;
     a.M = M; a.N = N; a.K = K; a.kind = kind; a.epilogue = epilogue;
     const char *msg = nullptr;
     cudaError_t e = launch_block_gemm(a, (cudaStream_t)stream, &msg);
@@ -218,13 +236,15 @@ static int ln_common(const void *x, const void *shift, const void *scale, int64_
 }
 
 int hn_adaln_quant(const void *x, const void *shift, const void *scale, int64_t B, int64_t L, int64_t D, float eps,
-                   int8_t *q, float *s, void *stream) {
+                   int8_t *q, float *s, int64_t s_rs, int64_t s_gs, void *stream) {
     int rc = ln_common(x, shift, scale, B, L, D, 1, "hn_adaln_quant");
     if (rc) return rc;
     REQUIRE(q && s && al16(q), HN_ERR_ARG, "hn_adaln_quant: null or misaligned output");
+    REQUIRE(scale_strides_ok(B * L, D / 128, s_rs, s_gs), HN_ERR_SHAPE, "hn_adaln_quant: scale strides overlap");
     if (L == 0) return HN_OK;
     CHECK_ARCH();
-    return launched(launch_ln_row(1, x, nullptr, nullptr, shift, scale, B, L, D, eps, nullptr, q, s, (cudaStream_t)stream),
+    return launched(launch_ln_row(1, x, nullptr, nullptr, shift, scale, B, L, D, eps, nullptr, q, s, s_rs, s_gs,
+                                  (cudaStream_t)stream),
                     "hn_adaln_quant launch");
 }
 
@@ -235,21 +255,24 @@ int hn_adaln(const void *x, const void *shift, const void *scale, int64_t B, int
     REQUIRE(y && al16(y), HN_ERR_ARG, "hn_adaln: null or misaligned output");
     if (L == 0) return HN_OK;
     CHECK_ARCH();
-    return launched(launch_ln_row(0, x, nullptr, nullptr, shift, scale, B, L, D, eps, y, nullptr, nullptr, (cudaStream_t)stream),
+    return launched(launch_ln_row(0, x, nullptr, nullptr, shift, scale, B, L, D, eps, y, nullptr, nullptr, 0, 0,
+                                  (cudaStream_t)stream),
                     "hn_adaln launch");
 }
 
 int hn_gated_residual_adaln_quant(const void *x, const void *y, const void *gate, const void *shift, const void *scale,
                                   int64_t B, int64_t L, int64_t D, float eps, void *out, int8_t *q, float *s,
-                                  void *stream) {
+                                  int64_t s_rs, int64_t s_gs, void *stream) {
     int rc = ln_common(x, shift, scale, B, L, D, 1, "hn_gated_residual_adaln_quant");
     if (rc) return rc;
     REQUIRE(y && gate && out && q && s, HN_ERR_ARG, "hn_gated_residual_adaln_quant: null pointer");
     REQUIRE(al16(y) && al16(gate) && al16(out) && al16(q), HN_ERR_ALIGN,
             "hn_gated_residual_adaln_quant: buffers must be 16-byte aligned");
+    REQUIRE(scale_strides_ok(B * L, D / 128, s_rs, s_gs), HN_ERR_SHAPE,
+            "hn_gated_residual_adaln_quant: scale strides overlap");
     if (L == 0) return HN_OK;
     CHECK_ARCH();
-    return launched(launch_ln_row(2, x, y, gate, shift, scale, B, L, D, eps, out, q, s, (cudaStream_t)stream),
+    return launched(launch_ln_row(2, x, y, gate, shift, scale, B, L, D, eps, out, q, s, s_rs, s_gs, (cudaStream_t)stream),
                     "hn_gated_residual_adaln_quant launch");
 }
 
@@ -313,7 +336,7 @@ int hn_pixelumm_qk(const void *x, int64_t row_stride, const void *weight_t, cons
 
 int hn_quantize_kv(const void *x, int64_t rows, int64_t D, int8_t *q, float *s, void *stream) {
     REQUIRE(D > 0 && D % 128 == 0, HN_ERR_SHAPE, "hn_quantize_kv: need D %% 128 == 0");
-    return hn_quant_act(x, D, HN_DTYPE_BF16, rows, D, HN_KIND_INT8, D == 128 ? 0 : 1, q, D, s, 1, stream);
+    return hn_quant_act(x, D, HN_DTYPE_BF16, rows, D, HN_KIND_INT8, D == 128 ? 0 : 1, q, D, s, 1, 1, stream);
 }
 
 } // extern "C"

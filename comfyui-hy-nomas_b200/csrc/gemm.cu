@@ -2,22 +2,30 @@
 //
 //   y[m, n] = sum_g sa[m, g] * sw[n, g] * dot_g(qa[m, :], qw[n, :])  (+ bias[n]),  g over 128-wide K groups
 //
-// Design (one persistent CTA per SM, 384 threads, tile 128 x 256, one K group = 128 bytes per stage):
-//   warp 0      producer: cp.async.bulk.tensor 2-D loads of the A tile [128 x 128 B] and the B tile
-//               [256 x 128 B] (both 128B-swizzled) into a 4-stage shared-memory ring (48 KB a stage), and
-//               (when the weight scale varies per group) the 256 weight scales of each group into a
-//               4-slot scale ring.
-//   warp 1      MMA issuer: allocates 512 TMEM columns (two 256-column accumulators), and for each K group
-//               issues 4 x tcgen05.mma.kind::{i8,f8f6f4} (M=128, N=256, K=32) into one accumulator, then
-//               tcgen05.commit to free the smem stage and to signal the epilogue.
-//   warps 4-11  epilogue / promotion: warp w reads TMEM lanes 32*(w%4).. (its 32 rows) and the column
-//               half (w-4)/4, i.e. each thread owns one output row x 128 columns, held in 64 packed
-//               f32x2 registers. Per group: tcgen05.ld of the int32 (or fp32) partial, exact int->float
-//               conversion (add 0x4B400000, subtract 1.5*2^23: exact for |p| < 2^22), scale by sa/sw with
-//               packed f32x2 multiply / FMA, and release of the accumulator. While the epilogue promotes
-//               group g, the tensor core computes group g+1 into the other accumulator.
-//   After the last group: scale by the per-row weight scale when it was factored out, + bias, then
-//   the epilogue of kernels.py:123-137 (cast / GELU / GELU + int8 requantization per 128 columns).
+// Design: one persistent CTA per SM, 640 threads (5 warpgroups), one K group (128 bytes of K) per pipeline
+// stage, tiles of 128 rows x BN columns.
+//   warps 0, 2  producers: cp.async.bulk.tensor 2-D loads (128B swizzle, no multicast) of the A tile
+//               [128 x 128 B] (warp 0) and the B tile [BN x 128 B] (warp 2) into a ring of shared-memory
+//               stages; one thread's bulk-tensor requests are serviced in order, so two issuing warps
+//               double the operand rate an SM can draw from L2.
+//   warp 3      when the weight scale varies per group: the BN weight scales of each group into a ring.
+//   warp 1      MMA issuer: owns 512 TMEM columns = NBUF accumulators of BN columns; per K group it issues
+//               4 x tcgen05.mma.kind::{i8,f8f6f4} (M=128, N=BN, K=32) and tcgen05.commit's the stage back
+//               to the producer and the accumulator to the epilogue.
+//   warps 4-19  epilogue: warp w owns TMEM lanes 32*(w%4).. (32 output rows) and column quarter (w-4)/4,
+//               i.e. each thread one row x BN/4 columns; four epilogue warps per SM sub-partition hide
+//               the TMEM-load and FMA latencies of one another.
+// Two tile shapes, by how the scales vary along K:
+//   * per-group scales (PMODE 0, 1): BN = 128, NBUF = 4. For every group the epilogue reads the int32 (or
+//     fp32) partial from TMEM, converts it exactly (int32 + 0x4B400000 reinterpreted, minus 1.5 * 2^23:
+//     exact for |p| < 2^22) and folds it into 32 fp32 accumulators per thread with packed f32x2
+//     multiply / FMA, while the tensor core fills the next three accumulators.
+//   * per-row scales on both sides (PMODE 2): BN = 256, NBUF = 2; the tensor core accumulates all of K in
+//     one accumulator and the epilogue streams it out of TMEM in 32-column chunks, overlapped with the
+//     next tile's MMAs.
+// After the last group: the per-row weight scale when it was factored out, + bias, then the epilogue of
+// kernels.py:123-137 (cast / GELU / GELU + int8 requantization per 128 columns; the column quarters of
+// a quantization group exchange their absmax through shared memory).
 //
 // Promotion arithmetic (the CPU oracle evaluates the same):
 //   PMODE 0 (sw per row x group):  t = RN(p * sa[m,g]);  acc = fma(t, sw[n,g], acc)
@@ -27,7 +35,7 @@
 //
 // Every wait on an mbarrier is bounded (globaltimer); on expiry the kernel records HN_DEVERR_TIMEOUT,
 // makes the other roles leave their loops, waits briefly for its own copies/MMAs in flight, frees TMEM
-// and returns. No TMA multicast is used anywhere (every CTA loads its own tiles).
+// and returns.
 #include <cuda.h>
 #include <cudaTypedefs.h>
 
@@ -48,36 +56,58 @@ cudaError_t read_and_clear_device_error(int *value) {
 
 namespace gemm {
 
-constexpr int BM = 128, BN = 256, BK = 128;
-constexpr int STAGES = 4;
-constexpr int A_STAGE = BM * BK;  // bytes
-constexpr int B_STAGE = BN * BK;
-constexpr int THREADS = 384;   // 3 warpgroups
-constexpr int EPI_WARP0 = 4;   // warpgroups 1-2 are the epilogue
-// 384 threads at one CTA per SM give every thread 168 registers (registers are allocated per SM
-// sub-partition: 3 warps x 32 x 168 <= 16384). The epilogue's 64 packed accumulators fit in that budget,
-// so no warpgroup register split (setmaxnreg) is used.
-constexpr int SW_SLOTS = 4;
+constexpr int BM = 128, BK = 128;
+constexpr int EPI_WARP0 = 4;  // warpgroup 0: producers, MMA issuer, scale ring; epilogue warpgroups follow
+constexpr int SW_SLOTS = 8;   // scale-ring depth (groups the scale producer runs ahead)
+// K groups per pipeline stage (and per TMA request) for the 128-wide and the 256-wide tile
+constexpr int GPS_NARROW = 2, GPS_WIDE = 1;
+// epilogue warpgroups (column parts of a tile row): the per-group promotion modes hand every 128-column
+// group over from TMEM, so more epilogue warps shorten that handoff; the whole-K mode reads TMEM once per
+// tile and keeps two
+constexpr int NPART_NARROW = 4, NPART_WIDE = 2;
 constexpr int TMEM_COLS = 512;
 constexpr uint64_t WAIT_NS = 2000000000ull;  // 2 s
 
-// shared-memory map (offsets from a 1024-aligned base)
-constexpr int OFF_A = 0;
-constexpr int OFF_B = OFF_A + STAGES * A_STAGE;
-constexpr int OFF_SW = OFF_B + STAGES * B_STAGE;                  // float[SW_SLOTS][256]
-constexpr int OFF_BAR = OFF_SW + SW_SLOTS * 256 * 4;              // full[S] empty[S] tfull[2] tempty[2] sfull[W] sempty[W]
-constexpr int OFF_MISC = OFF_BAR + (2 * STAGES + 4 + 2 * SW_SLOTS) * 8;  // tmem base, abort flag
-constexpr int SMEM_BYTES = OFF_MISC + 16 + 1024;         // + alignment slack
+template <int BN_, int GPS_, int NPART_> struct Cfg {
+    static constexpr int BN = BN_;
+    static constexpr int NPART = NPART_;                              // epilogue warpgroups
+    static constexpr int EPI_WARPS = 4 * NPART;
+    static constexpr int THREADS = 128 + 32 * EPI_WARPS;
+    static constexpr int GPS = GPS_;                                  // K groups per pipeline stage
+    static constexpr int A_GROUP = BM * BK;                           // bytes of one group's A tile
+    static constexpr int B_GROUP = BN * BK;
+    static constexpr int A_STAGE = GPS * A_GROUP;
+    static constexpr int B_STAGE = GPS * B_GROUP;
+    static constexpr int STAGES = (192 * 1024) / (A_STAGE + B_STAGE);  // 3 (BN 128, 2 groups) / 4 (BN 256, 1)
+    static constexpr int NBUF = TMEM_COLS / BN;                       // 4 or 2 accumulators
+    static constexpr int CPT = BN / NPART;                            // columns per epilogue thread
+    static constexpr int PARTS_PER_GROUP = 128 / CPT;                 // parts sharing one quant group
+    static constexpr int OFF_A = 0;
+    static constexpr int OFF_B = OFF_A + STAGES * A_STAGE;
+    // scale ring slot: activation scales of the tile's 128 rows, weight scales of its BN columns, and the
+    // weight block scales of its BN / 128 column blocks (padded to 16 bytes)
+    static constexpr int RING_SA = 0, RING_SW = 128, RING_SB = 128 + BN, RING_FLOATS = 128 + BN + 4;
+    static constexpr int OFF_SW = OFF_B + STAGES * B_STAGE;           // float[SW_SLOTS][RING_FLOATS]
+    static constexpr int OFF_PX = OFF_SW + SW_SLOTS * RING_FLOATS * 4; // float[2][NPART][128] absmax exchange
+    static constexpr int OFF_BAR = OFF_PX + 2 * NPART * 128 * 4;
+    static constexpr int NBARS = 2 * STAGES + 2 * NBUF + 2 * SW_SLOTS + 2;
+    static constexpr int OFF_MISC = OFF_BAR + NBARS * 8;              // tmem base, abort flag
+    static constexpr int SMEM = OFF_MISC + 16 + 1024;                 // + alignment slack
+    static_assert(SMEM <= 232448, "shared memory budget");
+};
 
 struct Params {
-    const float *sa; int64_t ldsa; int sa_mode;
-    const float *sw; int64_t ldsw; int sw_mode;
+    const float *sa; int64_t sa_rs, sa_gs; int sa_mode;
+    const float *sw; int64_t sw_rs, sw_gs; int sw_mode;
     const void *bias; int bias_dtype;
     void *out; int64_t ldo; int out_dtype;
-    float *qs; int64_t ldqs;
+    float *qs; int64_t qs_rs, qs_gs;
     int M, N, K, G;
     int n_blocks, num_tiles;
     int vec_store;
+    int sw_vec;     // per-row weight scales contiguous and 16-byte aligned (vector loads)
+    int sa_bulk;    // group activation scales group-major, 16-byte aligned: one bulk copy per group
+    int sw_bulk;    // group weight scales group-major, 16-byte aligned
 };
 
 // ---------------------------------------------------------------------------------------------------
@@ -121,9 +151,27 @@ __device__ __forceinline__ bool mbar_wait(uint32_t bar, uint32_t parity, volatil
     }
 }
 
-__device__ __forceinline__ void tma_load_2d(const CUtensorMap *map, uint32_t dst, uint32_t bar, int x, int y) {
-    asm volatile("cp.async.bulk.tensor.2d.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1, {%3, %4}], [%2];"
-                 ::"r"(dst), "l"((uint64_t)map), "r"(bar), "r"(x), "r"(y)
+// 3-D tile load: {128 bytes of one K group, rows, GPS groups} -> GPS stacked [rows][128 B] swizzled tiles
+// One lane polls the barrier and the result is broadcast to the warp: a try_wait costs ~100 cycles even
+// on a completed phase, and 32 lanes polling one barrier serialize. The shuffle also orders the other
+// lanes after the waiting lane's acquire.
+__device__ __forceinline__ bool warp_wait(int lane, uint32_t bar, uint32_t parity, volatile int *abort_flag,
+                                          uint64_t limit_ns) {
+    bool ok = true;
+    if (lane == 0) ok = mbar_wait(bar, parity, abort_flag, limit_ns);
+    return __shfl_sync(0xffffffffu, ok ? 1 : 0, 0) != 0;
+}
+
+// 1-D bulk copy global -> shared (16-byte aligned, size a multiple of 16), completing on an mbarrier
+__device__ __forceinline__ void bulk_load(uint32_t dst, const void *src, uint32_t bytes, uint32_t bar) {
+    asm volatile("cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];"
+                 ::"r"(dst), "l"(src), "r"(bytes), "r"(bar)
+                 : "memory");
+}
+
+__device__ __forceinline__ void tma_load_3d(const CUtensorMap *map, uint32_t dst, uint32_t bar, int row, int group) {
+    asm volatile("cp.async.bulk.tensor.3d.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1, {%3, %4, %5}], [%2];"
+                 ::"r"(dst), "l"((uint64_t)map), "r"(bar), "r"(0), "r"(row), "r"(group)
                  : "memory");
 }
 
@@ -138,7 +186,7 @@ __device__ __forceinline__ uint64_t sdesc(uint32_t saddr) {
 }
 
 template <int KIND>
-__device__ __forceinline__ void mma_128x256x32(uint32_t d_tmem, uint64_t ad, uint64_t bd, uint32_t idesc, uint32_t acc) {
+__device__ __forceinline__ void mma_128xNx32(uint32_t d_tmem, uint64_t ad, uint64_t bd, uint32_t idesc, uint32_t acc) {
     if (KIND == 0)
         asm volatile("{\n\t.reg .pred p;\n\tsetp.ne.b32 p, %4, 0;\n\t"
                      "tcgen05.mma.cta_group::1.kind::i8 [%0], %1, %2, %3, p;\n\t}"
@@ -241,46 +289,85 @@ __device__ __forceinline__ float load_bias1(const void *bias, int dtype, int64_t
 
 // ---------------------------------------------------------------------------------------------------
 
-template <int KIND, int PMODE, int EPI>
-__global__ void __launch_bounds__(THREADS, 1)
+// ---------------------------------------------------------------------------------------------------
+// epilogue output helpers
+
+// store `n` consecutive results of one row (n a multiple of 8, 16-byte aligned destination)
+template <int NV>
+__device__ __forceinline__ void store_row_vec(void *out, int od, int64_t off, const float *v) {
+    if (od == 0 || od == 1) {
+        uint16_t *o16 = reinterpret_cast<uint16_t *>(out) + off;
+#pragma unroll
+        for (int j = 0; j < NV; j += 8) {
+            uint4 o;
+            uint32_t *ow = &o.x;
+#pragma unroll
+            for (int w = 0; w < 4; ++w)
+                ow[w] = od == 0 ? pack_bf16_rn(v[j + 2 * w], v[j + 2 * w + 1]) : pack_f16_rn(v[j + 2 * w], v[j + 2 * w + 1]);
+            *reinterpret_cast<uint4 *>(o16 + j) = o;
+        }
+    } else {
+        uint32_t *o32 = reinterpret_cast<uint32_t *>(out) + off;
+#pragma unroll
+        for (int j = 0; j < NV; j += 4) {
+            uint4 o = make_uint4(__float_as_uint(v[j]), __float_as_uint(v[j + 1]), __float_as_uint(v[j + 2]),
+                                 __float_as_uint(v[j + 3]));
+            *reinterpret_cast<uint4 *>(o32 + j) = o;
+        }
+    }
+}
+__device__ __forceinline__ void store_one(void *out, int od, int64_t off, float v) {
+    if (od == 0) reinterpret_cast<__nv_bfloat16 *>(out)[off] = __float2bfloat16_rn(v);
+    else if (od == 1) reinterpret_cast<__half *>(out)[off] = __float2half_rn(v);
+    else reinterpret_cast<uint32_t *>(out)[off] = __float_as_uint(v);
+}
+
+// ---------------------------------------------------------------------------------------------------
+
+template <int KIND, int PMODE, int EPI, int BN, int GPS, int NP>
+__global__ void __launch_bounds__(128 + 128 * NP, 1)
     k_block_gemm(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB, const Params p) {
+    using C = Cfg<BN, GPS, NP>;
+    constexpr int STAGES = C::STAGES, NBUF = C::NBUF, CPT = C::CPT, NPART = C::NPART, EPI_WARPS = C::EPI_WARPS;
     extern __shared__ uint8_t smem_raw[];
     uint8_t *smem = reinterpret_cast<uint8_t *>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~(uintptr_t)1023);
     const uint32_t sbase = smem_u32(smem);
-    const uint32_t bar_full = sbase + OFF_BAR;
+    const uint32_t bar_full = sbase + C::OFF_BAR;
     const uint32_t bar_empty = bar_full + STAGES * 8;
     const uint32_t bar_tfull = bar_empty + STAGES * 8;
-    const uint32_t bar_tempty = bar_tfull + 2 * 8;
-    const uint32_t bar_sfull = bar_tempty + 2 * 8;
+    const uint32_t bar_tempty = bar_tfull + NBUF * 8;
+    const uint32_t bar_sfull = bar_tempty + NBUF * 8;
     const uint32_t bar_sempty = bar_sfull + SW_SLOTS * 8;
-    uint32_t *tmem_slot = reinterpret_cast<uint32_t *>(smem + OFF_MISC);
-    volatile int *abort_flag = reinterpret_cast<volatile int *>(smem + OFF_MISC + 4);
-    float *sw_s = reinterpret_cast<float *>(smem + OFF_SW);
+    const uint32_t bar_px = bar_sempty + SW_SLOTS * 8;
+    uint32_t *tmem_slot = reinterpret_cast<uint32_t *>(smem + C::OFF_MISC);
+    volatile int *abort_flag = reinterpret_cast<volatile int *>(smem + C::OFF_MISC + 4);
+    float *sw_s = reinterpret_cast<float *>(smem + C::OFF_SW);
+    float *px_s = reinterpret_cast<float *>(smem + C::OFF_PX);
 
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     const int G = p.G;
 
     if (threadIdx.x == 0) {
         for (int s = 0; s < STAGES; ++s) {
-            mbar_init(bar_full + 8 * s, 1);
+            mbar_init(bar_full + 8 * s, 2);   // the A and the B producer each arm it
             mbar_init(bar_empty + 8 * s, 1);
         }
-        for (int b = 0; b < 2; ++b) {
+        for (int b = 0; b < NBUF; ++b) {
             mbar_init(bar_tfull + 8 * b, 1);
-            mbar_init(bar_tempty + 8 * b, 8);
+            mbar_init(bar_tempty + 8 * b, EPI_WARPS);
         }
         for (int s = 0; s < SW_SLOTS; ++s) {
-            mbar_init(bar_sfull + 8 * s, 32);
-            mbar_init(bar_sempty + 8 * s, 8);
+            mbar_init(bar_sfull + 8 * s, 1);
+            mbar_init(bar_sempty + 8 * s, EPI_WARPS);
         }
+        mbar_init(bar_px, EPI_WARPS);
+        mbar_init(bar_px + 8, EPI_WARPS);
         *abort_flag = 0;
         asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
         asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
     }
-    if (warp == 0 && lane == 0) {
-        asm volatile("prefetch.tensormap [%0];" ::"l"((uint64_t)&tmA) : "memory");
-        asm volatile("prefetch.tensormap [%0];" ::"l"((uint64_t)&tmB) : "memory");
-    }
+    if (warp == 0 && lane == 0) asm volatile("prefetch.tensormap [%0];" ::"l"((uint64_t)&tmA) : "memory");
+    if (warp == 2 && lane == 0) asm volatile("prefetch.tensormap [%0];" ::"l"((uint64_t)&tmB) : "memory");
     if (warp == 1) {
         asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_u32(tmem_slot)),
                      "r"(TMEM_COLS)
@@ -292,42 +379,36 @@ __global__ void __launch_bounds__(THREADS, 1)
     tc_fence_after();
     const uint32_t tmem_base = *tmem_slot;
 
-    if (warp == 0) {
-        // ------------------------------------------------------------------ producer (TMA + scale ring)
-        int stage = 0, slot = 0;
-        uint32_t phase = 0, sphase = 0;
+    if (warp == 0 || warp == 2) {
+        // ------------------------------------------------------------------ producers: A tiles (warp 0), B tiles
+        // (warp 2). TMA requests issued by one thread are processed one after another, so the two operands
+        // come from two issuing warps; each arms the stage's full barrier with its own byte count.
+        const bool is_a = warp == 0;
+        int stage = 0;
+        uint32_t phase = 0;
         int issued = 0;
         bool ok = true;
         for (int tile = blockIdx.x; tile < p.num_tiles && ok; tile += gridDim.x) {
             const int m0 = (tile / p.n_blocks) * BM, n0 = (tile % p.n_blocks) * BN;
-            for (int g = 0; g < G; ++g) {
-                ok = __all_sync(0xffffffffu, mbar_wait(bar_empty + 8 * stage, phase ^ 1, abort_flag, WAIT_NS));
+            for (int g0 = 0; g0 < G; g0 += GPS) {
+                ok = warp_wait(lane, bar_empty + 8 * stage, phase ^ 1, abort_flag, WAIT_NS);
                 if (!ok) break;
                 if (lane == 0) {
+                    // a box that runs past the last group is zero-filled and still counts its full bytes
                     const uint32_t fb = bar_full + 8 * stage;
-                    mbar_arrive_tx(fb, A_STAGE + B_STAGE);
-                    tma_load_2d(&tmA, sbase + OFF_A + stage * A_STAGE, fb, g * BK, m0);
-                    tma_load_2d(&tmB, sbase + OFF_B + stage * B_STAGE, fb, g * BK, n0);
+                    if (is_a) {
+                        mbar_arrive_tx(fb, C::A_STAGE);
+                        tma_load_3d(&tmA, sbase + C::OFF_A + stage * C::A_STAGE, fb, m0, g0);
+                    } else {
+                        mbar_arrive_tx(fb, C::B_STAGE);
+                        tma_load_3d(&tmB, sbase + C::OFF_B + stage * C::B_STAGE, fb, n0, g0);
+                    }
                 }
                 ++issued;
                 if (++stage == STAGES) { stage = 0; phase ^= 1; }
-                if (PMODE == 0) {
-                    // weight scales of this group for the tile's 256 columns
-                    ok = __all_sync(0xffffffffu, mbar_wait(bar_sempty + 8 * slot, sphase ^ 1, abort_flag, WAIT_NS));
-                    if (!ok) break;
-                    float *dst = sw_s + slot * 256;
-#pragma unroll
-                    for (int i = 0; i < 8; ++i) {
-                        const int c = lane + 32 * i;
-                        const int n = n0 + c;
-                        dst[c] = (n < p.N) ? p.sw[(int64_t)n * p.ldsw + g] : 0.0f;
-                    }
-                    mbar_arrive(bar_sfull + 8 * slot);
-                    if (++slot == SW_SLOTS) { slot = 0; sphase ^= 1; }
-                }
             }
         }
-        // drain: wait (briefly) until the last copies issued have landed before the CTA can exit
+        // drain: the last copies issued land before the CTA can exit
         int st = stage;
         uint32_t ph = phase;
         for (int i = 0; i < STAGES && i < issued; ++i) {
@@ -335,55 +416,121 @@ __global__ void __launch_bounds__(THREADS, 1)
             volatile int never = 0;
             mbar_wait(bar_full + 8 * st, ph, &never, 100000000ull);
         }
+    } else if (warp == 3) {
+        // ------------------------------------------------------------------ scale ring (PMODE 0, 1)
+        // Per K group: the activation scales of the tile's rows, the weight scales of its columns (group
+        // mode) or of its 128-column blocks (block mode). Group-major scales arrive by bulk copies that
+        // complete on the slot's barrier; other layouts are gathered with plain loads.
+        if (PMODE != 2) {
+            int slot = 0, issued = 0;
+            uint32_t sphase = 0;
+            bool ok = true;
+            for (int tile = blockIdx.x; tile < p.num_tiles && ok; tile += gridDim.x) {
+                const int m0 = (tile / p.n_blocks) * BM, n0 = (tile % p.n_blocks) * BN;
+                const int rows = min(BM, p.M - m0), cols = min(BN, p.N - n0);
+                for (int g = 0; g < G; ++g) {
+                    ok = warp_wait(lane, bar_sempty + 8 * slot, sphase ^ 1, abort_flag, WAIT_NS);
+                    if (!ok) break;
+                    float *ring = sw_s + slot * C::RING_FLOATS;
+                    const uint32_t rbase = smem_u32(ring);
+                    uint32_t bytes = 0;
+                    const bool sa_grp = p.sa_mode == 0, sw_grp = PMODE == 0, sw_blk = PMODE == 1 && p.sw_mode == 2;
+                    if (sa_grp && !p.sa_bulk) {
+#pragma unroll
+                        for (int i = 0; i < BM / 32; ++i) {
+                            const int r = lane + 32 * i;
+                            ring[C::RING_SA + r] = r < rows ? p.sa[(int64_t)(m0 + r) * p.sa_rs + (int64_t)g * p.sa_gs] : 0.0f;
+                        }
+                    }
+                    if (sw_grp && !p.sw_bulk) {
+#pragma unroll
+                        for (int i = 0; i < BN / 32; ++i) {
+                            const int c = lane + 32 * i;
+                            ring[C::RING_SW + c] = c < cols ? p.sw[(int64_t)(n0 + c) * p.sw_rs + (int64_t)g * p.sw_gs] : 0.0f;
+                        }
+                    }
+                    if (sw_blk && lane < BN / 128) {
+                        const int nb = n0 / 128 + lane;
+                        ring[C::RING_SB + lane] = (nb * 128 < p.N) ? p.sw[(int64_t)nb * p.sw_rs + (int64_t)g * p.sw_gs] : 0.0f;
+                    }
+                    __syncwarp();
+                    if (lane == 0) {
+                        const uint32_t sa_bytes = (sa_grp && p.sa_bulk) ? (uint32_t)(((rows + 3) & ~3) * 4) : 0u;
+                        const uint32_t sw_bytes = (sw_grp && p.sw_bulk) ? (uint32_t)(((cols + 3) & ~3) * 4) : 0u;
+                        bytes = sa_bytes + sw_bytes;
+                        const uint32_t fb = bar_sfull + 8 * slot;
+                        if (bytes) mbar_arrive_tx(fb, bytes);
+                        else mbar_arrive(fb);
+                        if (sa_bytes) bulk_load(rbase + 4 * C::RING_SA, p.sa + (int64_t)g * p.sa_gs + m0, sa_bytes, fb);
+                        if (sw_bytes) bulk_load(rbase + 4 * C::RING_SW, p.sw + (int64_t)g * p.sw_gs + n0, sw_bytes, fb);
+                    }
+                    ++issued;
+                    if (++slot == SW_SLOTS) { slot = 0; sphase ^= 1; }
+                }
+            }
+            // drain: the last bulk copies land before the CTA can exit
+            int st = slot;
+            uint32_t ph = sphase;
+            for (int i = 0; i < SW_SLOTS && i < issued; ++i) {
+                if (--st < 0) { st = SW_SLOTS - 1; ph ^= 1; }
+                volatile int never = 0;
+                if (lane == 0) mbar_wait(bar_sfull + 8 * st, ph, &never, 100000000ull);
+            }
+            __syncwarp();
+        }
     } else if (warp == 1) {
         // ------------------------------------------------------------------ MMA issuer
         const uint32_t idesc = KIND == 0
                                    ? ((2u << 4) | (1u << 7) | (1u << 10) | ((uint32_t)(BN >> 3) << 17) | ((uint32_t)(BM >> 4) << 24))
                                    : ((1u << 4) | ((uint32_t)(BN >> 3) << 17) | ((uint32_t)(BM >> 4) << 24));
-        int stage = 0;
-        uint32_t phase = 0;
-        int tb = 0;
-        uint32_t tphase = 0;
+        int stage = 0, tb = 0;
+        uint32_t phase = 0, tphase = 0;
         bool ok = true;
         int last_stage = -1;
         uint32_t last_phase = 0;
         for (int tile = blockIdx.x; tile < p.num_tiles && ok; tile += gridDim.x) {
             if (PMODE == 2) {
-                ok = __all_sync(0xffffffffu, mbar_wait(bar_tempty + 8 * tb, tphase ^ 1, abort_flag, WAIT_NS));
+                ok = warp_wait(lane, bar_tempty + 8 * tb, tphase ^ 1, abort_flag, WAIT_NS);
                 if (!ok) break;
                 tc_fence_after();
             }
-            for (int g = 0; g < G; ++g) {
-                if (PMODE != 2) {
-                    ok = __all_sync(0xffffffffu, mbar_wait(bar_tempty + 8 * tb, tphase ^ 1, abort_flag, WAIT_NS));
-                    if (!ok) break;
-                    tc_fence_after();
-                }
-                ok = __all_sync(0xffffffffu, mbar_wait(bar_full + 8 * stage, phase, abort_flag, WAIT_NS));
+            for (int g0 = 0; g0 < G && ok; g0 += GPS) {
+                ok = warp_wait(lane, bar_full + 8 * stage, phase, abort_flag, WAIT_NS);
                 if (!ok) break;
                 tc_fence_after();
-                if (lane == 0) {
-                    const uint32_t d = tmem_base + (uint32_t)(tb * BN);
-                    const uint64_t ad = sdesc(sbase + OFF_A + stage * A_STAGE);
-                    const uint64_t bd = sdesc(sbase + OFF_B + stage * B_STAGE);
 #pragma unroll
-                    for (int k = 0; k < BK / 32; ++k)
-                        mma_128x256x32<KIND>(d, ad + 2 * k, bd + 2 * k, idesc,
-                                             (PMODE == 2) ? (uint32_t)(g > 0 || k > 0) : (uint32_t)(k > 0));
-                    mma_commit(bar_empty + 8 * stage);
-                    if (PMODE != 2) mma_commit(bar_tfull + 8 * tb);
+                for (int gi = 0; gi < GPS; ++gi) {
+                    const int g = g0 + gi;
+                    if (g >= G) break;
+                    if (PMODE != 2) {
+                        ok = warp_wait(lane, bar_tempty + 8 * tb, tphase ^ 1, abort_flag, WAIT_NS);
+                        if (!ok) break;
+                        tc_fence_after();
+                    }
+                    if (lane == 0) {
+                        const uint32_t d = tmem_base + (uint32_t)(tb * BN);
+                        const uint64_t ad = sdesc(sbase + C::OFF_A + stage * C::A_STAGE + gi * C::A_GROUP);
+                        const uint64_t bd = sdesc(sbase + C::OFF_B + stage * C::B_STAGE + gi * C::B_GROUP);
+#pragma unroll
+                        for (int k = 0; k < BK / 32; ++k)
+                            mma_128xNx32<KIND>(d, ad + 2 * k, bd + 2 * k, idesc,
+                                               (PMODE == 2) ? (uint32_t)(g > 0 || k > 0) : (uint32_t)(k > 0));
+                        if (PMODE != 2) mma_commit(bar_tfull + 8 * tb);
+                    }
+                    __syncwarp();
+                    if (PMODE != 2) { if (++tb == NBUF) { tb = 0; tphase ^= 1; } }
                 }
+                if (!ok) break;
+                if (lane == 0) mma_commit(bar_empty + 8 * stage);
                 __syncwarp();
                 last_stage = stage;
                 last_phase = phase;
                 if (++stage == STAGES) { stage = 0; phase ^= 1; }
-                if (PMODE != 2) { tb ^= 1; if (tb == 0) tphase ^= 1; }
             }
             if (PMODE == 2 && ok) {
                 if (lane == 0) mma_commit(bar_tfull + 8 * tb);
                 __syncwarp();
-                tb ^= 1;
-                if (tb == 0) tphase ^= 1;
+                if (++tb == NBUF) { tb = 0; tphase ^= 1; }
             }
         }
         // drain: the MMAs behind the last commit finish before TMEM is released
@@ -392,197 +539,231 @@ __global__ void __launch_bounds__(THREADS, 1)
             mbar_wait(bar_empty + 8 * last_stage, last_phase, &never, 100000000ull);
         }
     } else if (warp >= EPI_WARP0) {
-        // ------------------------------------------------------------------ epilogue / promotion (warps 4-11)
+        // ------------------------------------------------------------------ epilogue
         const int ew = warp - EPI_WARP0;
         const int q = warp & 3;
-        const int hf = ew >> 2;
+        const int hf = ew >> 2;  // column part 0..NPART-1
         const int row = q * 32 + lane;
         const uint32_t lane_addr = tmem_base + ((uint32_t)(q * 32) << 16);
-        int tb = 0, slot = 0;
+        int tb = 0, slot = 0, it = 0;
         uint32_t tphase = 0, sphase = 0;
         bool ok = true;
-        for (int tile = blockIdx.x; tile < p.num_tiles && ok; tile += gridDim.x) {
+        for (int tile = blockIdx.x; tile < p.num_tiles && ok; tile += gridDim.x, ++it) {
             const int m0 = (tile / p.n_blocks) * BM, n0 = (tile % p.n_blocks) * BN;
             const int m = m0 + row;
             const int mm = m < p.M ? m : p.M - 1;
-            const int ncol0 = n0 + hf * 128;
-            uint64_t acc[64];
-#pragma unroll
-            for (int i = 0; i < 64; ++i) acc[i] = 0ull;
+            const int ncol0 = n0 + hf * CPT;
+            const bool row_ok = m < p.M;
+            const bool full_cols = ncol0 + CPT <= p.N;
+            const int od = (EPI == 1) ? 0 : p.out_dtype;
             if (PMODE != 2) {
-                float sa_next = (p.sa_mode == 0) ? p.sa[(int64_t)mm * p.ldsa] : p.sa[mm];
+                // ------------------------------------------------ per-group promotion into registers
+                static_assert(PMODE == 2 || CPT == 32 || CPT == 64, "per-group promotion: 32 or 64 columns a thread");
+                uint64_t acc[CPT / 2];
+#pragma unroll
+                for (int i = 0; i < CPT / 2; ++i) acc[i] = 0ull;
+                const float sa_row = (p.sa_mode == 1) ? p.sa[(int64_t)mm * p.sa_rs] : 0.0f;
                 for (int g = 0; g < G; ++g) {
-                    const float sa_g = sa_next;
-                    if (g + 1 < G && p.sa_mode == 0) sa_next = p.sa[(int64_t)mm * p.ldsa + g + 1];
+                    ok = warp_wait(lane, bar_sfull + 8 * slot, sphase, abort_flag, WAIT_NS);
+                    if (!ok) break;
+                    const float *ring = sw_s + slot * C::RING_FLOATS;
+                    const float sa_g = (p.sa_mode == 0) ? ring[C::RING_SA + row] : sa_row;
                     float s = sa_g;
-                    if (PMODE == 1 && p.sw_mode == 2) s = __fmul_rn(sa_g, p.sw[(int64_t)(ncol0 >> 7) * p.ldsw + g]);
+                    if (PMODE == 1 && p.sw_mode == 2)
+                        s = (ncol0 < p.N) ? __fmul_rn(sa_g, ring[C::RING_SB + (hf * CPT) / 128]) : 0.0f;
                     const uint64_t s2 = pk(s, s);
-                    if (PMODE == 0) {
-                        ok = __all_sync(0xffffffffu, mbar_wait(bar_sfull + 8 * slot, sphase, abort_flag, WAIT_NS));
-                        if (!ok) break;
-                    }
-                    ok = __all_sync(0xffffffffu, mbar_wait(bar_tfull + 8 * tb, tphase, abort_flag, WAIT_NS));
+                    ok = warp_wait(lane, bar_tfull + 8 * tb, tphase, abort_flag, WAIT_NS);
                     if (!ok) break;
                     tc_fence_after();
-                    const uint32_t tcol = lane_addr + (uint32_t)(tb * BN + hf * 128);
-                    const float *sws = sw_s + slot * 256 + hf * 128;
+                    // move this group's partials out of TMEM and hand the accumulator straight back to the
+                    // tensor core, then fold them in from registers
+                    uint32_t r[CPT];
 #pragma unroll
-                    for (int c = 0; c < 4; ++c) {
-                        uint32_t r[32];
-                        tmem_ld32(tcol + c * 32, r);
-#pragma unroll
-                        for (int j = 0; j < 32; j += 4) {
-                            if (PMODE == 0) {
-                                const float4 w4 = *reinterpret_cast<const float4 *>(sws + c * 32 + j);
-                                promote_gen<KIND>(acc[c * 16 + j / 2], r[j], r[j + 1], s2, pk(w4.x, w4.y));
-                                promote_gen<KIND>(acc[c * 16 + j / 2 + 1], r[j + 2], r[j + 3], s2, pk(w4.z, w4.w));
-                            } else {
-                                promote_row<KIND>(acc[c * 16 + j / 2], r[j], r[j + 1], s2);
-                                promote_row<KIND>(acc[c * 16 + j / 2 + 1], r[j + 2], r[j + 3], s2);
-                            }
-                        }
-                    }
+                    for (int c = 0; c < CPT / 32; ++c)
+                        tmem_ld32(lane_addr + (uint32_t)(tb * BN + hf * CPT + 32 * c), *reinterpret_cast<uint32_t(*)[32]>(r + 32 * c));
                     tc_fence_before();
                     __syncwarp();
-                    if (lane == 0) {
-                        mbar_arrive(bar_tempty + 8 * tb);
-                        if (PMODE == 0) mbar_arrive(bar_sempty + 8 * slot);
+                    if (lane == 0) mbar_arrive(bar_tempty + 8 * tb);
+                    const float *sws = ring + C::RING_SW + hf * CPT;
+#pragma unroll
+                    for (int j = 0; j < CPT; j += 4) {
+                        if (PMODE == 0) {
+                            const float4 w4 = *reinterpret_cast<const float4 *>(sws + j);
+                            promote_gen<KIND>(acc[j / 2], r[j], r[j + 1], s2, pk(w4.x, w4.y));
+                            promote_gen<KIND>(acc[j / 2 + 1], r[j + 2], r[j + 3], s2, pk(w4.z, w4.w));
+                        } else {
+                            promote_row<KIND>(acc[j / 2], r[j], r[j + 1], s2);
+                            promote_row<KIND>(acc[j / 2 + 1], r[j + 2], r[j + 3], s2);
+                        }
                     }
-                    tb ^= 1;
-                    if (tb == 0) tphase ^= 1;
-                    if (PMODE == 0) { if (++slot == SW_SLOTS) { slot = 0; sphase ^= 1; } }
+                    __syncwarp();
+                    if (lane == 0) mbar_arrive(bar_sempty + 8 * slot);
+                    if (++tb == NBUF) { tb = 0; tphase ^= 1; }
+                    if (++slot == SW_SLOTS) { slot = 0; sphase ^= 1; }
                 }
                 if (!ok) break;
-                if (PMODE == 1 && p.sw_mode == 1) {
+                float v[CPT];
 #pragma unroll
-                    for (int j = 0; j < 128; j += 2) {
-                        const int n = ncol0 + j;
-                        const float w0 = (n < p.N) ? p.sw[n] : 0.0f, w1 = (n + 1 < p.N) ? p.sw[n + 1] : 0.0f;
-                        acc[j / 2] = pk(__fmul_rn(acc_lo(acc[j / 2]), w0), __fmul_rn(acc_hi(acc[j / 2]), w1));
+                for (int i = 0; i < CPT / 2; ++i) { v[2 * i] = acc_lo(acc[i]); v[2 * i + 1] = acc_hi(acc[i]); }
+                if (PMODE == 1 && p.sw_mode == 1) {
+                    if (full_cols && p.sw_vec) {
+#pragma unroll
+                        for (int j = 0; j < CPT; j += 4) {
+                            const float4 w4 = *reinterpret_cast<const float4 *>(p.sw + ncol0 + j);
+                            v[j] = __fmul_rn(v[j], w4.x);
+                            v[j + 1] = __fmul_rn(v[j + 1], w4.y);
+                            v[j + 2] = __fmul_rn(v[j + 2], w4.z);
+                            v[j + 3] = __fmul_rn(v[j + 3], w4.w);
+                        }
+                    } else {
+#pragma unroll
+                        for (int j = 0; j < CPT; ++j) v[j] = __fmul_rn(v[j], (ncol0 + j < p.N) ? p.sw[(int64_t)(ncol0 + j) * p.sw_rs] : 0.0f);
+                    }
+                }
+                if (p.bias != nullptr) {
+#pragma unroll
+                    for (int j = 0; j < CPT; j += 8) {
+                        float b[8];
+                        if (full_cols) load_bias8(p.bias, p.bias_dtype, ncol0 + j, b);
+                        else {
+#pragma unroll
+                            for (int i = 0; i < 8; ++i)
+                                b[i] = (ncol0 + j + i < p.N) ? load_bias1(p.bias, p.bias_dtype, ncol0 + j + i) : 0.0f;
+                        }
+#pragma unroll
+                        for (int i = 0; i < 8; ++i) v[j + i] = __fadd_rn(v[j + i], b[i]);
+                    }
+                }
+                if (EPI != 0) {
+#pragma unroll
+                    for (int j = 0; j < CPT; ++j) v[j] = rbf16(gelu_tanh(rbf16(v[j])));
+                }
+                if (EPI == 2) {
+                    // absmax over the 128-column group: this thread's 64 columns + the other half's
+                    float peak = 0.0f;
+#pragma unroll
+                    for (int j = 0; j < CPT; ++j) peak = fmaxf(peak, fabsf(v[j]));
+                    const int pb = it & 1;
+                    px_s[(pb * NPART + hf) * 128 + row] = peak;
+                    __syncwarp();
+                    if (lane == 0) mbar_arrive(bar_px + 8 * pb);
+                    ok = warp_wait(lane, bar_px + 8 * pb, (it >> 1) & 1, abort_flag, WAIT_NS);
+                    if (!ok) break;
+                    const int first = hf - hf % C::PARTS_PER_GROUP;
+#pragma unroll
+                    for (int o = 0; o < C::PARTS_PER_GROUP; ++o) peak = fmaxf(peak, px_s[(pb * NPART + first + o) * 128 + row]);
+                    const float sc = i8_scale(peak);
+                    if (row_ok && full_cols) {
+                        int8_t *qrow = static_cast<int8_t *>(p.out) + (int64_t)m * p.ldo + ncol0;
+#pragma unroll
+                        for (int j = 0; j < CPT; j += 16) {
+                            uint4 o;
+                            uint32_t *ow = &o.x;
+#pragma unroll
+                            for (int w = 0; w < 4; ++w)
+                                ow[w] = pack4_i8(code_i8(__fdiv_rn(v[j + 4 * w], sc)), code_i8(__fdiv_rn(v[j + 4 * w + 1], sc)),
+                                                 code_i8(__fdiv_rn(v[j + 4 * w + 2], sc)), code_i8(__fdiv_rn(v[j + 4 * w + 3], sc)));
+                            *reinterpret_cast<uint4 *>(qrow + j) = o;
+                        }
+                        if (hf % C::PARTS_PER_GROUP == 0) p.qs[(int64_t)m * p.qs_rs + (int64_t)(ncol0 >> 7) * p.qs_gs] = sc;
+                    }
+                } else if (row_ok) {
+                    if (full_cols && p.vec_store) store_row_vec<CPT>(p.out, od, (int64_t)m * p.ldo + ncol0, v);
+                    else {
+#pragma unroll
+                        for (int j = 0; j < CPT; ++j)
+                            if (ncol0 + j < p.N) store_one(p.out, od, (int64_t)m * p.ldo + ncol0 + j, v[j]);
                     }
                 }
             } else {
-                // PMODE 2: one accumulator over all of K
-                ok = __all_sync(0xffffffffu, mbar_wait(bar_tfull + 8 * tb, tphase, abort_flag, WAIT_NS));
+                // ------------------------------------------------ whole-K accumulator, streamed from TMEM
+                ok = warp_wait(lane, bar_tfull + 8 * tb, tphase, abort_flag, WAIT_NS);
                 if (!ok) break;
                 tc_fence_after();
-                const uint32_t tcol = lane_addr + (uint32_t)(tb * BN + hf * 128);
-                const float sam = p.sa[mm];
+                const uint32_t tcol = lane_addr + (uint32_t)(tb * BN + hf * CPT);
+                const float sam = p.sa[(int64_t)mm * p.sa_rs];
                 const bool raw = (p.out_dtype == 3);
+                uint32_t hpk[EPI == 2 ? CPT / 2 : 1];
+                float peak = 0.0f;
 #pragma unroll
-                for (int c = 0; c < 4; ++c) {
+                for (int c = 0; c < CPT / 32; ++c) {
                     uint32_t r[32];
                     tmem_ld32(tcol + c * 32, r);
+                    float v[32];
+                    const int nc = ncol0 + c * 32;
+                    const bool chunk_full = nc + 32 <= p.N;
 #pragma unroll
-                    for (int j = 0; j < 32; j += 2) {
-                        float a0, a1;
-                        if (raw) {
-                            a0 = __uint_as_float(r[j]);
-                            a1 = __uint_as_float(r[j + 1]);
-                        } else {
-                            const int n = ncol0 + c * 32 + j;
-                            const float w0 = (n < p.N) ? p.sw[n] : 0.0f, w1 = (n + 1 < p.N) ? p.sw[n + 1] : 0.0f;
-                            const float d0 = KIND == 0 ? __int2float_rn((int)r[j]) : __uint_as_float(r[j]);
-                            const float d1 = KIND == 0 ? __int2float_rn((int)r[j + 1]) : __uint_as_float(r[j + 1]);
-                            a0 = __fmul_rn(__fmul_rn(d0, sam), w0);
-                            a1 = __fmul_rn(__fmul_rn(d1, sam), w1);
+                    for (int j = 0; j < 32; ++j) {
+                        if (raw) { v[j] = __uint_as_float(r[j]); continue; }
+                        const float w = (nc + j < p.N) ? p.sw[(int64_t)(nc + j) * p.sw_rs] : 0.0f;
+                        const float d = KIND == 0 ? __int2float_rn((int)r[j]) : __uint_as_float(r[j]);
+                        v[j] = __fmul_rn(__fmul_rn(d, sam), w);
+                    }
+                    if (p.bias != nullptr && !raw) {
+#pragma unroll
+                        for (int j = 0; j < 32; j += 8) {
+                            float b[8];
+                            if (chunk_full) load_bias8(p.bias, p.bias_dtype, nc + j, b);
+                            else {
+#pragma unroll
+                                for (int i = 0; i < 8; ++i)
+                                    b[i] = (nc + j + i < p.N) ? load_bias1(p.bias, p.bias_dtype, nc + j + i) : 0.0f;
+                            }
+#pragma unroll
+                            for (int i = 0; i < 8; ++i) v[j + i] = __fadd_rn(v[j + i], b[i]);
                         }
-                        acc[c * 16 + j / 2] = pk(a0, a1);
+                    }
+                    if (EPI != 0) {
+#pragma unroll
+                        for (int j = 0; j < 32; ++j) v[j] = rbf16(gelu_tanh(rbf16(v[j])));
+                    }
+                    if (EPI == 2) {
+#pragma unroll
+                        for (int j = 0; j < 32; j += 2) {
+                            peak = fmaxf(peak, fmaxf(fabsf(v[j]), fabsf(v[j + 1])));
+                            hpk[c * 16 + j / 2] = pack_bf16_exact(v[j], v[j + 1]);
+                        }
+                    } else if (row_ok) {
+                        if (chunk_full && p.vec_store) store_row_vec<32>(p.out, od, (int64_t)m * p.ldo + nc, v);
+                        else {
+#pragma unroll
+                            for (int j = 0; j < 32; ++j)
+                                if (nc + j < p.N) store_one(p.out, od, (int64_t)m * p.ldo + nc + j, v[j]);
+                        }
                     }
                 }
                 tc_fence_before();
                 __syncwarp();
                 if (lane == 0) mbar_arrive(bar_tempty + 8 * tb);
-                tb ^= 1;
-                if (tb == 0) tphase ^= 1;
-            }
-
-            // ---------------------------------------------------------- bias + output epilogue
-            const bool row_ok = m < p.M;
-            const bool full_cols = ncol0 + 128 <= p.N;
-            if (p.bias != nullptr && !(PMODE == 2 && p.out_dtype == 3)) {
-#pragma unroll
-                for (int j = 0; j < 128; j += 8) {
-                    float b[8];
-                    if (full_cols) load_bias8(p.bias, p.bias_dtype, ncol0 + j, b);
-                    else {
-#pragma unroll
-                        for (int i = 0; i < 8; ++i)
-                            b[i] = (ncol0 + j + i < p.N) ? load_bias1(p.bias, p.bias_dtype, ncol0 + j + i) : 0.0f;
-                    }
-#pragma unroll
-                    for (int i = 0; i < 8; i += 2)
-                        acc[(j + i) / 2] = pk(__fadd_rn(acc_lo(acc[(j + i) / 2]), b[i]), __fadd_rn(acc_hi(acc[(j + i) / 2]), b[i + 1]));
-                }
-            }
-            if (EPI != 0) {
-#pragma unroll
-                for (int i = 0; i < 64; ++i)
-                    acc[i] = pk(rbf16(gelu_tanh(rbf16(acc_lo(acc[i])))), rbf16(gelu_tanh(rbf16(acc_hi(acc[i])))));
-            }
-            if (row_ok) {
+                if (++tb == NBUF) { tb = 0; tphase ^= 1; }
                 if (EPI == 2) {
-                    if (full_cols) {  // N % 128 == 0: a 128-column group is entirely inside or outside
-                        float peak = 0.0f;
+                    // absmax over the 128-column group shared by PARTS_PER_GROUP column parts
+                    const int pb = it & 1;
+                    px_s[(pb * NPART + hf) * 128 + row] = peak;
+                    __syncwarp();
+                    if (lane == 0) mbar_arrive(bar_px + 8 * pb);
+                    ok = warp_wait(lane, bar_px + 8 * pb, (it >> 1) & 1, abort_flag, WAIT_NS);
+                    if (!ok) break;
+                    const int first = hf - hf % C::PARTS_PER_GROUP;
 #pragma unroll
-                        for (int i = 0; i < 64; ++i) peak = fmaxf(peak, fmaxf(fabsf(acc_lo(acc[i])), fabsf(acc_hi(acc[i]))));
-                        const float sc = i8_scale(peak);
-                        int8_t *qrow = static_cast<int8_t *>(p.out) + (int64_t)m * p.ldo + ncol0;
+                    for (int o = 0; o < C::PARTS_PER_GROUP; ++o) peak = fmaxf(peak, px_s[(pb * NPART + first + o) * 128 + row]);
+                }
+                if (EPI == 2 && row_ok && full_cols) {
+                    const float sc = i8_scale(peak);
+                    int8_t *qrow = static_cast<int8_t *>(p.out) + (int64_t)m * p.ldo + ncol0;
 #pragma unroll
-                        for (int j = 0; j < 128; j += 16) {
-                            uint4 o;
-                            uint32_t *ow = &o.x;
+                    for (int j = 0; j < CPT; j += 16) {
+                        uint4 o;
+                        uint32_t *ow = &o.x;
 #pragma unroll
-                            for (int w = 0; w < 4; ++w) {
-                                const uint64_t a = acc[(j + 4 * w) / 2], b2 = acc[(j + 4 * w) / 2 + 1];
-                                ow[w] = pack4_i8(code_i8(__fdiv_rn(acc_lo(a), sc)), code_i8(__fdiv_rn(acc_hi(a), sc)),
-                                                 code_i8(__fdiv_rn(acc_lo(b2), sc)), code_i8(__fdiv_rn(acc_hi(b2), sc)));
-                            }
-                            *reinterpret_cast<uint4 *>(qrow + j) = o;
+                        for (int w = 0; w < 4; ++w) {
+                            const uint32_t a = hpk[(j + 4 * w) / 2], b2 = hpk[(j + 4 * w) / 2 + 1];
+                            ow[w] = pack4_i8(code_i8(__fdiv_rn(bf16_lo(a), sc)), code_i8(__fdiv_rn(bf16_hi(a), sc)),
+                                             code_i8(__fdiv_rn(bf16_lo(b2), sc)), code_i8(__fdiv_rn(bf16_hi(b2), sc)));
                         }
-                        p.qs[(int64_t)m * p.ldqs + (ncol0 >> 7)] = sc;
+                        *reinterpret_cast<uint4 *>(qrow + j) = o;
                     }
-                } else {
-                    const int od = (EPI == 1) ? 0 : p.out_dtype;
-                    uint8_t *orow = static_cast<uint8_t *>(p.out);
-                    if (full_cols && p.vec_store) {
-                        if (od == 0 || od == 1) {
-                            uint16_t *o16 = reinterpret_cast<uint16_t *>(orow) + (int64_t)m * p.ldo + ncol0;
-#pragma unroll
-                            for (int j = 0; j < 128; j += 8) {
-                                uint4 o;
-                                uint32_t *ow = &o.x;
-#pragma unroll
-                                for (int w = 0; w < 4; ++w) {
-                                    const uint64_t a = acc[(j + 2 * w) / 2];
-                                    ow[w] = od == 0 ? pack_bf16_rn(acc_lo(a), acc_hi(a)) : pack_f16_rn(acc_lo(a), acc_hi(a));
-                                }
-                                *reinterpret_cast<uint4 *>(o16 + j) = o;
-                            }
-                        } else {
-                            uint32_t *o32 = reinterpret_cast<uint32_t *>(orow) + (int64_t)m * p.ldo + ncol0;
-#pragma unroll
-                            for (int j = 0; j < 128; j += 4) {
-                                uint4 o;
-                                o.x = __float_as_uint(acc_lo(acc[j / 2]));
-                                o.y = __float_as_uint(acc_hi(acc[j / 2]));
-                                o.z = __float_as_uint(acc_lo(acc[j / 2 + 1]));
-                                o.w = __float_as_uint(acc_hi(acc[j / 2 + 1]));
-                                *reinterpret_cast<uint4 *>(o32 + j) = o;
-                            }
-                        }
-                    } else {
-#pragma unroll
-                        for (int j = 0; j < 128; ++j) {
-                            const int n = ncol0 + j;
-                            if (n < p.N) {
-                                const float v = (j & 1) ? acc_hi(acc[j / 2]) : acc_lo(acc[j / 2]);
-                                if (od == 0) reinterpret_cast<__nv_bfloat16 *>(orow)[(int64_t)m * p.ldo + n] = __float2bfloat16_rn(v);
-                                else if (od == 1) reinterpret_cast<__half *>(orow)[(int64_t)m * p.ldo + n] = __float2half_rn(v);
-                                else reinterpret_cast<uint32_t *>(orow)[(int64_t)m * p.ldo + n] = __float_as_uint(v);
-                            }
-                        }
-                    }
+                    if (hf % C::PARTS_PER_GROUP == 0) p.qs[(int64_t)m * p.qs_rs + (int64_t)(ncol0 >> 7) * p.qs_gs] = sc;
                 }
             }
         }
@@ -614,39 +795,44 @@ static PFN_cuTensorMapEncodeTiled_v12000 encode_fn() {
 
 // 2-D map over a row-major byte matrix [rows, cols] with row pitch ld bytes; box = 128 bytes x box_rows,
 // 128B swizzle (matches the UMMA SWIZZLE_128B K-major layout), zero fill outside the matrix.
-static bool make_map(CUtensorMap *map, const void *base, uint64_t rows, uint64_t cols, uint64_t ld, uint32_t box_rows) {
+// A row-major byte matrix [rows, cols] (row pitch ld bytes, cols % 128 == 0) seen as 3-D
+// {128 bytes within a K group, row, K group}; box = {128, box_rows, box_groups}, 128B swizzle (the UMMA
+// SWIZZLE_128B K-major layout, one [box_rows][128 B] tile per group), zero fill outside the matrix.
+static bool make_map(CUtensorMap *map, const void *base, uint64_t rows, uint64_t cols, uint64_t ld, uint32_t box_rows,
+                     uint32_t box_groups) {
     PFN_cuTensorMapEncodeTiled_v12000 fn = encode_fn();
     if (fn == nullptr) return false;
-    cuuint64_t dims[2] = {cols, rows};
-    cuuint64_t strides[1] = {ld};
-    cuuint32_t box[2] = {128, box_rows};
-    cuuint32_t estr[2] = {1, 1};
-    CUresult r = fn(map, CU_TENSOR_MAP_DATA_TYPE_UINT8, 2, const_cast<void *>(base), dims, strides, box, estr,
+    cuuint64_t dims[3] = {128, rows, cols / 128};
+    cuuint64_t strides[2] = {ld, 128};
+    cuuint32_t box[3] = {128, box_rows, box_groups};
+    cuuint32_t estr[3] = {1, 1, 1};
+    CUresult r = fn(map, CU_TENSOR_MAP_DATA_TYPE_UINT8, 3, const_cast<void *>(base), dims, strides, box, estr,
                     CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
                     CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
     return r == CUDA_SUCCESS;
 }
 
-template <int KIND, int PMODE, int EPI>
+template <int KIND, int PMODE, int EPI, int BN, int GPS, int NP>
 static cudaError_t launch_t(const CUtensorMap &ma, const CUtensorMap &mb, const Params &p, int grid, cudaStream_t st) {
-    auto kern = k_block_gemm<KIND, PMODE, EPI>;
-    static bool configured = false;  // per instantiation; attribute setting is idempotent
+    using C = Cfg<BN, GPS, NP>;
+    auto kern = k_block_gemm<KIND, PMODE, EPI, BN, GPS, NP>;
+    static bool configured = false;  // per instantiation; setting the attribute again is harmless
     if (!configured) {
-        cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, SMEM_BYTES);
+        cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, C::SMEM);
         if (e != cudaSuccess) return e;
         configured = true;
     }
-    kern<<<grid, THREADS, SMEM_BYTES, st>>>(ma, mb, p);
+    kern<<<grid, C::THREADS, C::SMEM, st>>>(ma, mb, p);
     return cudaGetLastError();
 }
 
-template <int KIND, int PMODE>
+template <int KIND, int PMODE, int BN, int GPS, int NP>
 static cudaError_t launch_epi(int epi, const CUtensorMap &ma, const CUtensorMap &mb, const Params &p, int grid,
                               cudaStream_t st) {
     switch (epi) {
-    case 0: return launch_t<KIND, PMODE, 0>(ma, mb, p, grid, st);
-    case 1: return launch_t<KIND, PMODE, 1>(ma, mb, p, grid, st);
-    default: return launch_t<KIND, PMODE, 2>(ma, mb, p, grid, st);
+    case 0: return launch_t<KIND, PMODE, 0, BN, GPS, NP>(ma, mb, p, grid, st);
+    case 1: return launch_t<KIND, PMODE, 1, BN, GPS, NP>(ma, mb, p, grid, st);
+    default: return launch_t<KIND, PMODE, 2, BN, GPS, NP>(ma, mb, p, grid, st);
     }
 }
 
@@ -654,37 +840,46 @@ static cudaError_t launch_epi(int epi, const CUtensorMap &ma, const CUtensorMap 
 
 cudaError_t launch_block_gemm(const GemmArgs &a, cudaStream_t st, const char **msg) {
     using namespace gemm;
-    CUtensorMap ma, mb;
-    if (!make_map(&ma, a.qa, (uint64_t)a.M, (uint64_t)a.K, (uint64_t)a.lda, BM) ||
-        !make_map(&mb, a.qw, (uint64_t)a.N, (uint64_t)a.K, (uint64_t)a.ldw, BN)) {
-        *msg = "cuTensorMapEncodeTiled failed (pointer/stride alignment or driver entry point)";
-        return cudaErrorInvalidValue;
-    }
-    Params p;
-    p.sa = a.sa; p.ldsa = a.ldsa; p.sa_mode = a.sa_mode;
-    p.sw = a.sw; p.ldsw = a.ldsw; p.sw_mode = a.sw_mode;
-    p.bias = a.bias; p.bias_dtype = a.bias_dtype;
-    p.out = a.out; p.ldo = a.ldo; p.out_dtype = a.out_dtype;
-    p.qs = a.qs; p.ldqs = a.ldqs;
-    p.M = (int)a.M; p.N = (int)a.N; p.K = (int)a.K; p.G = (int)(a.K / 128);
-    p.n_blocks = (int)cdiv(a.N, BN);
-    p.num_tiles = (int)(cdiv(a.M, BM) * p.n_blocks);
-    const int esz = (a.epilogue == 2) ? 1 : (a.out_dtype == 0 || a.out_dtype == 1) ? 2 : 4;
-    p.vec_store = ((reinterpret_cast<uintptr_t>(a.out) % 16) == 0 && (a.ldo * esz) % 16 == 0) ? 1 : 0;
-    int grid = num_sms();
-    if (grid > p.num_tiles) grid = p.num_tiles;
     int pmode;
     if (a.sa_mode == 1 && a.sw_mode == 1) pmode = 2;
     else if (a.sw_mode == 0) pmode = 0;
     else pmode = 1;
-    if (a.kind == 0) {
-        if (pmode == 0) return launch_epi<0, 0>(a.epilogue, ma, mb, p, grid, st);
-        if (pmode == 1) return launch_epi<0, 1>(a.epilogue, ma, mb, p, grid, st);
-        return launch_epi<0, 2>(a.epilogue, ma, mb, p, grid, st);
+    const int bn = pmode == 2 ? 256 : 128;
+    const int gps = pmode == 2 ? GPS_WIDE : GPS_NARROW;
+    CUtensorMap ma, mb;
+    if (!make_map(&ma, a.qa, (uint64_t)a.M, (uint64_t)a.K, (uint64_t)a.lda, BM, (uint32_t)gps) ||
+        !make_map(&mb, a.qw, (uint64_t)a.N, (uint64_t)a.K, (uint64_t)a.ldw, (uint32_t)bn, (uint32_t)gps)) {
+        *msg = "cuTensorMapEncodeTiled failed (pointer/stride alignment or driver entry point)";
+        return cudaErrorInvalidValue;
     }
-    if (pmode == 0) return launch_epi<1, 0>(a.epilogue, ma, mb, p, grid, st);
-    if (pmode == 1) return launch_epi<1, 1>(a.epilogue, ma, mb, p, grid, st);
-    return launch_epi<1, 2>(a.epilogue, ma, mb, p, grid, st);
+    Params p;
+    p.sa = a.sa; p.sa_rs = a.sa_rs; p.sa_gs = a.sa_gs; p.sa_mode = a.sa_mode;
+    p.sw = a.sw; p.sw_rs = a.sw_rs; p.sw_gs = a.sw_gs; p.sw_mode = a.sw_mode;
+    p.bias = a.bias; p.bias_dtype = a.bias_dtype;
+    p.out = a.out; p.ldo = a.ldo; p.out_dtype = a.out_dtype;
+    p.qs = a.qs; p.qs_rs = a.qs_rs; p.qs_gs = a.qs_gs;
+    p.M = (int)a.M; p.N = (int)a.N; p.K = (int)a.K; p.G = (int)(a.K / 128);
+    p.n_blocks = (int)cdiv(a.N, bn);
+    p.num_tiles = (int)(cdiv(a.M, BM) * p.n_blocks);
+    const int esz = (a.epilogue == 2) ? 1 : (a.out_dtype == 0 || a.out_dtype == 1) ? 2 : 4;
+    p.vec_store = ((reinterpret_cast<uintptr_t>(a.out) % 16) == 0 && (a.ldo * esz) % 16 == 0) ? 1 : 0;
+    p.sw_vec = (reinterpret_cast<uintptr_t>(a.sw) % 16) == 0 && a.sw_rs == 1 ? 1 : 0;
+    // bulk copies of one group's scales: group-major, 16-byte aligned rows, and a row count that is a
+    // multiple of 4 so no copy reads past the last row
+    p.sa_bulk = (a.sa_mode == 0 && a.sa_rs == 1 && a.sa_gs % 4 == 0 && a.M % 4 == 0 &&
+                 reinterpret_cast<uintptr_t>(a.sa) % 16 == 0) ? 1 : 0;
+    p.sw_bulk = (a.sw_mode == 0 && a.sw_rs == 1 && a.sw_gs % 4 == 0 && a.N % 4 == 0 &&
+                 reinterpret_cast<uintptr_t>(a.sw) % 16 == 0) ? 1 : 0;
+    int grid = num_sms();
+    if (grid > p.num_tiles) grid = p.num_tiles;
+    if (a.kind == 0) {
+        if (pmode == 0) return launch_epi<0, 0, 128, GPS_NARROW, NPART_NARROW>(a.epilogue, ma, mb, p, grid, st);
+        if (pmode == 1) return launch_epi<0, 1, 128, GPS_NARROW, NPART_NARROW>(a.epilogue, ma, mb, p, grid, st);
+        return launch_epi<0, 2, 256, GPS_WIDE, NPART_WIDE>(a.epilogue, ma, mb, p, grid, st);
+    }
+    if (pmode == 0) return launch_epi<1, 0, 128, GPS_NARROW, NPART_NARROW>(a.epilogue, ma, mb, p, grid, st);
+    if (pmode == 1) return launch_epi<1, 1, 128, GPS_NARROW, NPART_NARROW>(a.epilogue, ma, mb, p, grid, st);
+    return launch_epi<1, 2, 256, GPS_WIDE, NPART_WIDE>(a.epilogue, ma, mb, p, grid, st);
 }
 
 // ---------------------------------------------------------------------------------------------------

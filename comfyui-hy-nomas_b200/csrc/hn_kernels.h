@@ -10,12 +10,12 @@ namespace hn {
 int num_sms();  // SM count of the current device (cached per device)
 
 cudaError_t launch_quant_act(const void *x, int64_t ldx, int x_dtype, int64_t M, int64_t K, int kind, int per_row,
-                             void *q, int64_t ldq, float *s, int64_t lds, cudaStream_t st);
+                             void *q, int64_t ldq, float *s, int64_t s_rs, int64_t s_gs, cudaStream_t st);
 
 // mode 0: adaln (bf16 y), 1: adaln_quant, 2: gated residual + adaln_quant
 cudaError_t launch_ln_row(int mode, const void *x, const void *y, const void *gate, const void *shift,
                           const void *scale, int64_t B, int64_t L, int64_t D, float eps, void *out_bf16, int8_t *q,
-                          float *s, cudaStream_t st);
+                          float *s, int64_t s_rs, int64_t s_gs, cudaStream_t st);
 
 cudaError_t launch_gated_residual(const void *x, const void *y, const void *gate, int64_t B, int64_t L, int64_t D,
                                   void *out, cudaStream_t st);
@@ -29,12 +29,12 @@ cudaError_t launch_pixelumm_qk(const void *x, int64_t row_stride, const void *wt
 
 struct GemmArgs {
     const void *qa; int64_t lda;
-    const float *sa; int64_t ldsa; int sa_mode;
+    const float *sa; int64_t sa_rs, sa_gs; int sa_mode;
     const void *qw; int64_t ldw;
-    const float *sw; int64_t ldsw; int sw_mode;
+    const float *sw; int64_t sw_rs, sw_gs; int sw_mode;
     const void *bias; int bias_dtype;
     void *out; int64_t ldo; int out_dtype;
-    float *qs; int64_t ldqs;
+    float *qs; int64_t qs_rs, qs_gs;
     int64_t M, N, K;
     int kind, epilogue;
 };

@@ -51,7 +51,7 @@ __global__ void __launch_bounds__(WP * 32) k_ln_row(const bf16 *__restrict__ x, 
                                                    const bf16 *__restrict__ gate, const bf16 *__restrict__ shift,
                                                    const bf16 *__restrict__ scale, int64_t L, int D, float eps,
                                                    bf16 *__restrict__ out, int8_t *__restrict__ q,
-                                                   float *__restrict__ s) {
+                                                   float *__restrict__ s, int64_t s_rs, int64_t s_gs) {
     __shared__ float red1[WP], red2[WP];
     const int t = threadIdx.x, lane = t & 31, warp = t >> 5;
     const int64_t row = blockIdx.x;
@@ -125,36 +125,36 @@ __global__ void __launch_bounds__(WP * 32) k_ln_row(const bf16 *__restrict__ x, 
         o.z = pack4_i8(c[8], c[9], c[10], c[11]);
         o.w = pack4_i8(c[12], c[13], c[14], c[15]);
         *reinterpret_cast<uint4 *>(q + off) = o;
-        if ((t & 7) == 0) s[row * (D >> 7) + (t >> 3)] = qsc;
+        if ((t & 7) == 0) s[row * s_rs + (int64_t)(t >> 3) * s_gs] = qsc;
     }
 }
 
 template <int WP>
 static void launch_ln_wp(int mode, const void *x, const void *y, const void *gate, const void *shift,
                          const void *scale, int64_t B, int64_t L, int64_t D, float eps, void *out, int8_t *q,
-                         float *s, cudaStream_t st) {
+                         float *s, int64_t s_rs, int64_t s_gs, cudaStream_t st) {
     const int warps = (int)cdiv(D / 16, 32);
     dim3 grid((unsigned)(B * L)), block(warps * 32);
     const bf16 *xp = (const bf16 *)x, *yp = (const bf16 *)y, *gp = (const bf16 *)gate;
     const bf16 *shp = (const bf16 *)shift, *scp = (const bf16 *)scale;
-    if (mode == 0) k_ln_row<WP, 0><<<grid, block, 0, st>>>(xp, yp, gp, shp, scp, L, (int)D, eps, (bf16 *)out, q, s);
-    else if (mode == 1) k_ln_row<WP, 1><<<grid, block, 0, st>>>(xp, yp, gp, shp, scp, L, (int)D, eps, (bf16 *)out, q, s);
-    else k_ln_row<WP, 2><<<grid, block, 0, st>>>(xp, yp, gp, shp, scp, L, (int)D, eps, (bf16 *)out, q, s);
+    if (mode == 0) k_ln_row<WP, 0><<<grid, block, 0, st>>>(xp, yp, gp, shp, scp, L, (int)D, eps, (bf16 *)out, q, s, s_rs, s_gs);
+    else if (mode == 1) k_ln_row<WP, 1><<<grid, block, 0, st>>>(xp, yp, gp, shp, scp, L, (int)D, eps, (bf16 *)out, q, s, s_rs, s_gs);
+    else k_ln_row<WP, 2><<<grid, block, 0, st>>>(xp, yp, gp, shp, scp, L, (int)D, eps, (bf16 *)out, q, s, s_rs, s_gs);
 }
 
 cudaError_t launch_ln_row(int mode, const void *x, const void *y, const void *gate, const void *shift,
                           const void *scale, int64_t B, int64_t L, int64_t D, float eps, void *out, int8_t *q,
-                          float *s, cudaStream_t st) {
+                          float *s, int64_t s_rs, int64_t s_gs, cudaStream_t st) {
     const int warps = (int)cdiv(D / 16, 32);
     int wp = 1;
     while (wp < warps) wp <<= 1;
     switch (wp) {
-    case 1: launch_ln_wp<1>(mode, x, y, gate, shift, scale, B, L, D, eps, out, q, s, st); break;
-    case 2: launch_ln_wp<2>(mode, x, y, gate, shift, scale, B, L, D, eps, out, q, s, st); break;
-    case 4: launch_ln_wp<4>(mode, x, y, gate, shift, scale, B, L, D, eps, out, q, s, st); break;
-    case 8: launch_ln_wp<8>(mode, x, y, gate, shift, scale, B, L, D, eps, out, q, s, st); break;
-    case 16: launch_ln_wp<16>(mode, x, y, gate, shift, scale, B, L, D, eps, out, q, s, st); break;
-    case 32: launch_ln_wp<32>(mode, x, y, gate, shift, scale, B, L, D, eps, out, q, s, st); break;
+    case 1: launch_ln_wp<1>(mode, x, y, gate, shift, scale, B, L, D, eps, out, q, s, s_rs, s_gs, st); break;
+    case 2: launch_ln_wp<2>(mode, x, y, gate, shift, scale, B, L, D, eps, out, q, s, s_rs, s_gs, st); break;
+    case 4: launch_ln_wp<4>(mode, x, y, gate, shift, scale, B, L, D, eps, out, q, s, s_rs, s_gs, st); break;
+    case 8: launch_ln_wp<8>(mode, x, y, gate, shift, scale, B, L, D, eps, out, q, s, s_rs, s_gs, st); break;
+    case 16: launch_ln_wp<16>(mode, x, y, gate, shift, scale, B, L, D, eps, out, q, s, s_rs, s_gs, st); break;
+    case 32: launch_ln_wp<32>(mode, x, y, gate, shift, scale, B, L, D, eps, out, q, s, s_rs, s_gs, st); break;
     default: return cudaErrorInvalidValue;
     }
     return cudaGetLastError();

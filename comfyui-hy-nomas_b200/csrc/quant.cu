@@ -13,7 +13,7 @@ namespace hn {
 template <typename TIn, int KIND>
 __global__ void __launch_bounds__(256) k_quant_group(const TIn *__restrict__ x, int64_t ldx, int64_t M, int64_t G,
                                                      uint8_t *__restrict__ q, int64_t ldq, float *__restrict__ s,
-                                                     int64_t lds) {
+                                                     int64_t s_rs, int64_t s_gs) {
     const int lane = threadIdx.x & 31, sub = lane & 7;
     const int64_t ngroups = M * G;
     const int64_t warp0 = (int64_t)blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5);
@@ -60,7 +60,7 @@ __global__ void __launch_bounds__(256) k_quant_group(const TIn *__restrict__ x, 
         }
         if (active) {
             *reinterpret_cast<uint4 *>(q + m * ldq + g * 128 + sub * 16) = out;
-            if (sub == 0) s[m * lds + g] = sc;
+            if (sub == 0) s[m * s_rs + g * s_gs] = sc;
         }
     }
 }
@@ -69,7 +69,7 @@ __global__ void __launch_bounds__(256) k_quant_group(const TIn *__restrict__ x, 
 template <typename TIn, int KIND>
 __global__ void __launch_bounds__(256) k_quant_row(const TIn *__restrict__ x, int64_t ldx, int64_t K,
                                                    uint8_t *__restrict__ q, int64_t ldq, float *__restrict__ s,
-                                                   int64_t lds) {
+                                                   int64_t s_rs) {
     __shared__ float red[8];
     const int64_t m = blockIdx.x;
     const TIn *row = x + m * ldx;
@@ -105,36 +105,36 @@ __global__ void __launch_bounds__(256) k_quant_row(const TIn *__restrict__ x, in
         }
         *reinterpret_cast<uint2 *>(q + m * ldq + c) = out;
     }
-    if (threadIdx.x == 0) s[m * lds] = sc;
+    if (threadIdx.x == 0) s[m * s_rs] = sc;
 }
 
 template <typename TIn>
 static cudaError_t launch_quant_t(const void *x, int64_t ldx, int64_t M, int64_t K, int kind, int per_row, void *q,
-                                  int64_t ldq, float *s, int64_t lds, cudaStream_t st) {
+                                  int64_t ldq, float *s, int64_t s_rs, int64_t s_gs, cudaStream_t st) {
     const TIn *xp = static_cast<const TIn *>(x);
     uint8_t *qp = static_cast<uint8_t *>(q);
     if (per_row) {
         dim3 grid((unsigned)M), block(256);
-        if (kind == 0) k_quant_row<TIn, 0><<<grid, block, 0, st>>>(xp, ldx, K, qp, ldq, s, lds);
-        else k_quant_row<TIn, 1><<<grid, block, 0, st>>>(xp, ldx, K, qp, ldq, s, lds);
+        if (kind == 0) k_quant_row<TIn, 0><<<grid, block, 0, st>>>(xp, ldx, K, qp, ldq, s, s_rs);
+        else k_quant_row<TIn, 1><<<grid, block, 0, st>>>(xp, ldx, K, qp, ldq, s, s_rs);
     } else {
         const int64_t G = K / 128;
         const int64_t warps = cdiv(M * G, 4);
         int64_t blocks = cdiv(warps, 8);
         const int64_t cap = (int64_t)num_sms() * 16;
         if (blocks > cap) blocks = cap;
-        if (kind == 0) k_quant_group<TIn, 0><<<(unsigned)blocks, 256, 0, st>>>(xp, ldx, M, G, qp, ldq, s, lds);
-        else k_quant_group<TIn, 1><<<(unsigned)blocks, 256, 0, st>>>(xp, ldx, M, G, qp, ldq, s, lds);
+        if (kind == 0) k_quant_group<TIn, 0><<<(unsigned)blocks, 256, 0, st>>>(xp, ldx, M, G, qp, ldq, s, s_rs, s_gs);
+        else k_quant_group<TIn, 1><<<(unsigned)blocks, 256, 0, st>>>(xp, ldx, M, G, qp, ldq, s, s_rs, s_gs);
     }
     return cudaGetLastError();
 }
 
 cudaError_t launch_quant_act(const void *x, int64_t ldx, int x_dtype, int64_t M, int64_t K, int kind, int per_row,
-                             void *q, int64_t ldq, float *s, int64_t lds, cudaStream_t st) {
+                             void *q, int64_t ldq, float *s, int64_t s_rs, int64_t s_gs, cudaStream_t st) {
     switch (x_dtype) {
-    case 0: return launch_quant_t<__nv_bfloat16>(x, ldx, M, K, kind, per_row, q, ldq, s, lds, st);
-    case 1: return launch_quant_t<__half>(x, ldx, M, K, kind, per_row, q, ldq, s, lds, st);
-    default: return launch_quant_t<float>(x, ldx, M, K, kind, per_row, q, ldq, s, lds, st);
+    case 0: return launch_quant_t<__nv_bfloat16>(x, ldx, M, K, kind, per_row, q, ldq, s, s_rs, s_gs, st);
+    case 1: return launch_quant_t<__half>(x, ldx, M, K, kind, per_row, q, ldq, s, s_rs, s_gs, st);
+    default: return launch_quant_t<float>(x, ldx, M, K, kind, per_row, q, ldq, s, s_rs, s_gs, st);
     }
 }
 

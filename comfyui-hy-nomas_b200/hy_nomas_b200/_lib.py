@@ -28,15 +28,15 @@ SIGNATURES = {
     "hn_num_sms": [],
     "hn_device_error": [_V, ctypes.POINTER(ctypes.c_int)],
     "hn_selftest_wait_timeout": [_U32, _V],
-    "hn_quant_act": [_V, _I64, _I32, _I64, _I64, _I32, _I32, _V, _I64, _V, _I64, _V],
-    "hn_block_gemm": [_V, _I64, _V, _I64, _I32, _V, _I64, _V, _I64, _I32, _V, _I32, _V, _I64, _I32, _V, _I64,
-                      _I64, _I64, _I64, _I32, _I32, _V],
-    "hn_adaln_quant": [_V, _V, _V, _I64, _I64, _I64, _F32, _V, _V, _V],
+    "hn_quant_act": [_V, _I64, _I32, _I64, _I64, _I32, _I32, _V, _I64, _V, _I64, _I64, _V],
+    "hn_block_gemm": [_V, _I64, _V, _I64, _I64, _I32, _V, _I64, _V, _I64, _I64, _I32, _V, _I32, _V, _I64, _I32,
+                      _V, _I64, _I64, _I64, _I64, _I64, _I32, _I32, _V],
+    "hn_adaln_quant": [_V, _V, _V, _I64, _I64, _I64, _F32, _V, _V, _I64, _I64, _V],
     "hn_adaln": [_V, _V, _V, _I64, _I64, _I64, _F32, _V, _V],
     "hn_qk_norm_rope": [_V, _I64, _V, _V, _V, _I64, _I64, _I64, _I64, _F32, _V, _V],
     "hn_qk_norm_rope2": [_V, _V, _I64, _V, _V, _V, _V, _I64, _I64, _I64, _I64, _F32, _V, _V, _V],
     "hn_gated_residual": [_V, _V, _V, _I64, _I64, _I64, _V, _V],
-    "hn_gated_residual_adaln_quant": [_V, _V, _V, _V, _V, _I64, _I64, _I64, _F32, _V, _V, _V, _V],
+    "hn_gated_residual_adaln_quant": [_V, _V, _V, _V, _V, _I64, _I64, _I64, _F32, _V, _V, _V, _I64, _I64, _V],
     "hn_pixelumm_qk": [_V, _I64, _V, _V, _V, _V, _I64, _I64, _I64, _F32, _V, _V],
     "hn_quantize_kv": [_V, _I64, _I64, _V, _V, _V],
 }
@@ -82,6 +82,22 @@ def require_cuda(*tensors):
         if t is not None and not t.is_cuda:
             raise RuntimeError("hy_nomas_b200 kernels run on CUDA tensors only (there is no CPU path); "
                                f"got a tensor on {t.device}")
+
+
+def group_scales(rows, groups, device):
+    """Scale storage for [rows, groups] in group-major layout (each group's rows contiguous, rows padded to a
+    multiple of 4): returns (the [rows, groups] view handed to callers, row stride, group stride)."""
+    padded = (rows + 3) // 4 * 4
+    store = torch.empty((groups, padded), device=device, dtype=torch.float32)
+    view = store[:, :rows].t()
+    return view, 1, padded
+
+
+def scale_strides(s):
+    """(row stride, group stride) of a [rows, groups] or [rows] scale tensor, in elements."""
+    if s.dim() == 1:
+        return s.stride(0), 0
+    return s.stride(0), s.stride(1)
 
 
 def device_error(stream=None):

@@ -120,10 +120,10 @@ def gated_residual_adaln_quant(x, y, gate, shift, scale, eps=1e-6):
     shift, scale = shift.contiguous(), scale.contiguous()
     out = torch.empty(x.shape, device=x.device, dtype=x.dtype)
     q = torch.empty((b * l, d), device=x.device, dtype=torch.int8)
-    s = torch.empty((b * l, d // 128), device=x.device, dtype=torch.float32)
+    s, srs, sgs = _lib.group_scales(b * l, d // 128, x.device)
     rc = _lib.lib.hn_gated_residual_adaln_quant(_lib.ptr(x), _lib.ptr(y), _lib.ptr(gate), _lib.ptr(shift),
                                                 _lib.ptr(scale), b, l, d, eps, _lib.ptr(out), _lib.ptr(q),
-                                                _lib.ptr(s), _lib.stream_of(x))
+                                                _lib.ptr(s), srs, sgs, _lib.stream_of(x))
     _lib.check(rc, "gated_residual_adaln_quant")
     return out, q, s
 

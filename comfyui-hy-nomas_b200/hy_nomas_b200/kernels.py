@@ -36,9 +36,13 @@ def quantize_activations(x, kind="int8", per_token=False):
         x = x.contiguous()
     dtype = torch.int8 if kind == "int8" else torch.float8_e4m3fn
     q = torch.empty((m, k), device=x.device, dtype=dtype)
-    s = torch.empty((m, 1 if per_token else k // GROUP), device=x.device, dtype=torch.float32)
+    if per_token:
+        s = torch.empty((m, 1), device=x.device, dtype=torch.float32)
+        srs, sgs = 1, 1
+    else:
+        s, srs, sgs = _lib.group_scales(m, k // GROUP, x.device)
     rc = _lib.lib.hn_quant_act(_lib.ptr(x), x.stride(0), _lib.DTYPE[x.dtype], m, k, _lib.KIND[kind],
-                               1 if per_token else 0, _lib.ptr(q), q.stride(0), _lib.ptr(s), s.stride(0),
+                               1 if per_token else 0, _lib.ptr(q), q.stride(0), _lib.ptr(s), srs, sgs,
                                _lib.stream_of(x))
     _lib.check(rc, "quantize_activations")
     return q, s
@@ -73,8 +77,6 @@ def block_gemm(qa, sa, qw, sw, bias=None, out_dtype=torch.bfloat16, kind="int8",
         sa = sa.float()
     if sw.dtype != torch.float32:
         sw = sw.float()
-    sa = sa.contiguous() if sa.stride(-1) != 1 else sa
-    sw = sw.contiguous() if sw.stride(-1) != 1 else sw
     if not _aligned(qa):
         qa = qa.contiguous()
     if not _aligned(qw):
@@ -83,18 +85,18 @@ def block_gemm(qa, sa, qw, sw, bias=None, out_dtype=torch.bfloat16, kind="int8",
         bias = bias.contiguous()
     if mode == 2:
         out = torch.empty((m, n), device=qa.device, dtype=torch.int8)
-        qs = torch.empty((m, n // GROUP), device=qa.device, dtype=torch.float32)
+        qs, qrs, qgs = _lib.group_scales(m, n // GROUP, qa.device)
     else:
         out = torch.empty((m, n), device=qa.device, dtype=out_dtype if mode == 0 else torch.bfloat16)
-        qs = None
-    ld_sa = sa.stride(0) if sa.dim() == 2 else 1
-    ld_sw = sw.stride(0) if sw.dim() == 2 else 1
+        qs, qrs, qgs = None, 0, 0
+    sa_rs, sa_gs = _lib.scale_strides(sa)
+    sw_rs, sw_gs = _lib.scale_strides(sw)
     rc = _lib.lib.hn_block_gemm(
-        _lib.ptr(qa), qa.stride(0), _lib.ptr(sa), ld_sa, _lib.SCALE_MODE[sa_mode],
-        _lib.ptr(qw), qw.stride(0), _lib.ptr(sw), ld_sw, _lib.SCALE_MODE[sw_mode],
+        _lib.ptr(qa), qa.stride(0), _lib.ptr(sa), sa_rs, sa_gs, _lib.SCALE_MODE[sa_mode],
+        _lib.ptr(qw), qw.stride(0), _lib.ptr(sw), sw_rs, sw_gs, _lib.SCALE_MODE[sw_mode],
         _lib.ptr(bias), _lib.DTYPE[bias.dtype] if bias is not None else 0,
         _lib.ptr(out), out.stride(0), _lib.DTYPE[out.dtype] if mode != 2 else 0,
-        _lib.ptr(qs), qs.stride(0) if qs is not None else 0,
+        _lib.ptr(qs), qrs, qgs,
         m, n, k, _lib.KIND[kind], mode, _lib.stream_of(qa))
     _lib.check(rc, "block_gemm")
     return (out, qs) if mode == 2 else out
@@ -109,9 +111,9 @@ def adaln_quant(x, shift, scale, eps=1e-6):
         raise TypeError("adaln_quant: x, shift and scale must be bf16")
     x, shift, scale = x.contiguous(), shift.contiguous(), scale.contiguous()
     q = torch.empty((b * l, d), device=x.device, dtype=torch.int8)
-    s = torch.empty((b * l, d // GROUP), device=x.device, dtype=torch.float32)
+    s, srs, sgs = _lib.group_scales(b * l, d // GROUP, x.device)
     rc = _lib.lib.hn_adaln_quant(_lib.ptr(x), _lib.ptr(shift), _lib.ptr(scale), b, l, d, eps, _lib.ptr(q),
-                                 _lib.ptr(s), _lib.stream_of(x))
+                                 _lib.ptr(s), srs, sgs, _lib.stream_of(x))
     _lib.check(rc, "adaln_quant")
     return q, s
 

@@ -24,9 +24,9 @@ def quantize_g128(weight):
         w = F.pad(w, (0, groups * GROUP - k))
     w = w.contiguous()
     q = torch.empty((n, groups * GROUP), device=w.device, dtype=torch.int8)
-    s = torch.empty((n, groups), device=w.device, dtype=torch.float32)
+    s, srs, sgs = _lib.group_scales(n, groups, w.device)
     rc = _lib.lib.hn_quant_act(_lib.ptr(w), w.stride(0), _lib.DTYPE[torch.float32], n, groups * GROUP,
-                               _lib.KIND["int8"], 0, _lib.ptr(q), q.stride(0), _lib.ptr(s), s.stride(0),
+                               _lib.KIND["int8"], 0, _lib.ptr(q), q.stride(0), _lib.ptr(s), srs, sgs,
                                _lib.stream_of(w))
     _lib.check(rc, "quantize_g128")
     return q[:, :k].contiguous(), s

@@ -16,6 +16,11 @@
  *    bounded and report HN_ERR_TIMEOUT through hn_device_error().
  *  - bf16/fp16/fp32 inputs are named by the HN_DTYPE_* codes. Quantized codes are int8 or
  *    float8_e4m3fn bytes (HN_KIND_*).
+ *  - Quantization scales are fp32 with one value per (row, 128-wide group). A scale tensor is given as a
+ *    pointer plus two strides in elements: s[row * s_rs + group * s_gs]. The reference's layout is
+ *    row-major [rows, groups] (s_rs = groups, s_gs = 1). The group-major layout (s_rs = 1, s_gs >= rows,
+ *    i.e. [groups, rows]) lets the GEMM stream one group's scales for a whole tile with one bulk copy;
+ *    the quantizers here produce it and the Python layer hands it back as a [rows, groups] view.
  */
 #ifndef HYNOMAS_B200_H
 #define HYNOMAS_B200_H
@@ -90,14 +95,14 @@ int hn_selftest_wait_timeout(uint32_t timeout_us, void *stream);
  * Replaces hy_nomas/kernels.py:22-54 (_quantize_kernel / quantize_activations).
  * x [M, K] (dtype x_dtype, leading dim ldx), K % 128 == 0 ->
  *   codes q [M, K] (int8, or e4m3 bytes for HN_KIND_FP8E4M3; leading dim ldq),
- *   scales s [M, K/128] fp32 (leading dim lds).
+ *   scales s: one per (row, group) at s[m * s_rs + g * s_gs].
  * int8: s = peak > 0 ? peak/127 : 1, q = round-half-away(x/s) clamped to +-127.
  * e4m3: s = max(peak, 1e-12)/448, q = e4m3(x/s) round-to-nearest-even, saturating.
- * `per_row` != 0 uses one group spanning all K (per-token scale; s is then [M] with stride lds) -
- * the per-token quantization that BASELINE config 1 names; no counterpart in the reference.
+ * `per_row` != 0 uses one group spanning all K (per-token scale s[m * s_rs]) - the per-token
+ * quantization that BASELINE config 1 names; no counterpart in the reference.
  */
 int hn_quant_act(const void *x, int64_t ldx, int x_dtype, int64_t M, int64_t K, int kind, int per_row,
-                 void *q, int64_t ldq, float *s, int64_t lds, void *stream);
+                 void *q, int64_t ldq, float *s, int64_t s_rs, int64_t s_gs, void *stream);
 
 /*
  * K2 - block-scaled W8A8 / FP8 GEMM on the 5th-generation tensor cores (tcgen05, TMEM accumulators).
@@ -105,30 +110,32 @@ int hn_quant_act(const void *x, int64_t ldx, int x_dtype, int64_t M, int64_t K, 
  *   y[m, n] = sum_g sa[m, g] * sw[n, g] * dot_g(qa[m, :], qw[n, :])  (+ bias[n])
  * qa [M, K] codes (lda), qw [N, K] codes (ldw; K-major, the layout the checkpoints store), both of
  * `kind`. K % 128 == 0, lda and ldw multiples of 16, qa/qw 16-byte aligned.
- * sa: sa_mode HN_SCALE_GROUP -> [M, K/128] (ldsa) | HN_SCALE_ROW -> [M].
- * sw: sw_mode HN_SCALE_GROUP -> [N, K/128] (ldsw) | HN_SCALE_ROW -> [N] | HN_SCALE_BLOCK -> [N/128, K/128].
+ * sa: sa_mode HN_SCALE_GROUP -> sa[m * sa_rs + g * sa_gs] | HN_SCALE_ROW -> sa[m * sa_rs].
+ * sw: sw_mode HN_SCALE_GROUP -> sw[n * sw_rs + g * sw_gs] | HN_SCALE_ROW -> sw[n * sw_rs] |
+ *     HN_SCALE_BLOCK -> sw[(n / 128) * sw_rs + g * sw_gs] (one per 128 x 128 weight block).
+ * Group scales with unit row stride (group-major) are streamed by bulk copies; others by plain loads.
  * bias: NULL or [N] of bias_dtype (bf16/fp16/fp32).
  * epilogue HN_EPI_NONE: out [M, N] of out_dtype (bf16/fp16/fp32), ldo.
  *          HN_EPI_GELU: out bf16 = rbf16(gelu_tanh(rbf16(y))).
  *          HN_EPI_GELU_QUANT: out int8 [M, N] codes of the GELU output quantized per row and 128
- *                             columns, qs [M, N/128] fp32 (ldqs). Needs N % 128 == 0.
+ *                             columns, scales qs[m * qs_rs + c * qs_gs]. Needs N % 128 == 0.
  * out_dtype HN_DTYPE_INT32 (int8 kind, both scale modes HN_SCALE_ROW, no bias, HN_EPI_NONE): out is the
  * exact int32 accumulator sum_k qa*qw - the raw integer result, no scaling.
  */
-int hn_block_gemm(const void *qa, int64_t lda, const float *sa, int64_t ldsa, int sa_mode,
-                  const void *qw, int64_t ldw, const float *sw, int64_t ldsw, int sw_mode,
+int hn_block_gemm(const void *qa, int64_t lda, const float *sa, int64_t sa_rs, int64_t sa_gs, int sa_mode,
+                  const void *qw, int64_t ldw, const float *sw, int64_t sw_rs, int64_t sw_gs, int sw_mode,
                   const void *bias, int bias_dtype,
-                  void *out, int64_t ldo, int out_dtype, float *qs, int64_t ldqs,
+                  void *out, int64_t ldo, int out_dtype, float *qs, int64_t qs_rs, int64_t qs_gs,
                   int64_t M, int64_t N, int64_t K, int kind, int epilogue, void *stream);
 
 /*
  * K3 - LayerNorm (no affine) + adaLN modulate + int8 quantize per 128 channels.
  * Replaces hy_nomas/kernels.py:173-207 (_adaln_quant_kernel / adaln_quant).
- * x [B*L, D] bf16 contiguous, shift/scale [B, D] bf16 -> q [B*L, D] int8, s [B*L, D/128] fp32.
- * D % 128 == 0, D <= 16384.
+ * x [B*L, D] bf16 contiguous, shift/scale [B, D] bf16 -> q [B*L, D] int8, scales s[r * s_rs + g * s_gs]
+ * for token row r and channel group g. D % 128 == 0, D <= 16384.
  */
 int hn_adaln_quant(const void *x, const void *shift, const void *scale, int64_t B, int64_t L, int64_t D,
-                   float eps, int8_t *q, float *s, void *stream);
+                   float eps, int8_t *q, float *s, int64_t s_rs, int64_t s_gs, void *stream);
 
 /*
  * K4 - LayerNorm + modulate -> bf16. Replaces hy_nomas/fused.py:37-62 (_adaln_kernel / adaln).
@@ -171,7 +178,7 @@ int hn_gated_residual(const void *x, const void *y, const void *gate, int64_t B,
  */
 int hn_gated_residual_adaln_quant(const void *x, const void *y, const void *gate, const void *shift,
                                   const void *scale, int64_t B, int64_t L, int64_t D, float eps, void *out,
-                                  int8_t *q, float *s, void *stream);
+                                  int8_t *q, float *s, int64_t s_rs, int64_t s_gs, void *stream);
 
 /*
  * K7 - PixelUMM decoder q/k prep: split T / HW RMSNorm (own weights) + rotate-half MRoPE.

@@ -42,13 +42,14 @@ FAKE = ctypes.c_void_p(0x10000)   # never dereferenced: every call below fails v
 
 def test_validation_errors_before_launch(hn):
     L = hn.lib.lib
-    assert L.hn_quant_act(None, 128, 0, 4, 128, 0, 0, FAKE, 128, FAKE, 1, None) == 5      # null x
+    assert L.hn_quant_act(None, 128, 0, 4, 128, 0, 0, FAKE, 128, FAKE, 1, 1, None) == 5      # null x
     assert b"null" in L.hn_last_error()
-    assert L.hn_quant_act(FAKE, 100, 0, 4, 100, 0, 0, FAKE, 100, FAKE, 1, None) == 1      # K % 128
-    assert L.hn_quant_act(FAKE, 128, 9, 4, 128, 0, 0, FAKE, 128, FAKE, 1, None) == 5      # dtype
-    assert L.hn_quant_act(ctypes.c_void_p(0x10008), 128, 0, 4, 128, 0, 0, FAKE, 128, FAKE, 1, None) == 2
-    args = dict(qa=FAKE, lda=256, sa=FAKE, ldsa=2, sam=0, qw=FAKE, ldw=256, sw=FAKE, ldsw=2, swm=0, bias=None, bd=0,
-                out=FAKE, ldo=256, od=0, qs=None, ldqs=0, M=64, N=256, K=256, kind=0, epi=0)
+    assert L.hn_quant_act(FAKE, 100, 0, 4, 100, 0, 0, FAKE, 100, FAKE, 1, 1, None) == 1      # K % 128
+    assert L.hn_quant_act(FAKE, 128, 9, 4, 128, 0, 0, FAKE, 128, FAKE, 1, 1, None) == 5      # dtype
+    assert L.hn_quant_act(ctypes.c_void_p(0x10008), 128, 0, 4, 128, 0, 0, FAKE, 128, FAKE, 1, 1, None) == 2
+    assert L.hn_quant_act(FAKE, 256, 0, 4, 256, 0, 0, FAKE, 256, FAKE, 1, 2, None) == 1      # scale strides alias
+    args = dict(qa=FAKE, lda=256, sa=FAKE, sars=2, sags=1, sam=0, qw=FAKE, ldw=256, sw=FAKE, swrs=2, swgs=1, swm=0,
+                bias=None, bd=0, out=FAKE, ldo=256, od=0, qs=None, qsrs=0, qsgs=0, M=64, N=256, K=256, kind=0, epi=0)
 
     def gemm(**kw):
         a = dict(args, **kw)
@@ -57,11 +58,12 @@ def test_validation_errors_before_launch(hn):
     assert gemm(kind=7) == 5
     assert gemm(sam=2) == 5                                        # activations cannot be block-scaled
     assert gemm(epi=2) == 5                                        # gelu_quant needs qs
-    assert gemm(epi=2, qs=FAKE, ldqs=2, N=200, ldo=256) == 1       # gelu_quant needs N % 128
+    assert gemm(epi=2, qs=FAKE, qsrs=2, qsgs=1, N=200, ldo=256) == 1   # gelu_quant needs N % 128
+    assert gemm(sars=1, sags=32) == 1                               # group-major sa needs sags >= M
     assert gemm(od=3) == 7                                         # int32 out needs row scales
     assert gemm(lda=100) == 1                                      # lda < K
     assert gemm(qa=ctypes.c_void_p(0x10004)) == 2                  # TMA base alignment
-    assert L.hn_adaln_quant(FAKE, FAKE, FAKE, 1, 4, 200, 1e-6, FAKE, FAKE, None) == 1   # D % 128
+    assert L.hn_adaln_quant(FAKE, FAKE, FAKE, 1, 4, 200, 1e-6, FAKE, FAKE, 1, 1, None) == 1   # D % 128
     assert L.hn_qk_norm_rope(FAKE, 4096, FAKE, FAKE, None, 1, 4, 32, 128, 1e-6, FAKE, None) == 5  # cos w/o sin
     assert L.hn_qk_norm_rope(FAKE, 4096, FAKE, None, None, 1, 4, 32, 64, 1e-6, FAKE, None) == 7   # D != 128
     assert L.hn_gated_residual(FAKE, FAKE, FAKE, 1, 4, 12, FAKE, None) == 1                     # D % 8
