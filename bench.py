@@ -3,21 +3,25 @@
     python bench.py [--gpus N] [--steps K] [--warmup W] [--workload dit|gemm|fp8|elementwise] [--impl ours|reference]
 
 Workloads (synthetic, seeded; the reference publishes no dataset for this path):
-  dit          BASELINE config 5: one denoise step of a 40-block Hy-Nomas-style DiT (hidden 4096, 32 x 128
-               heads, MLP 16384, adaLN modulation, W8A8 int8 linears with per-channel weight scales), L =
-               20240 tokens, batch 1, sequence-parallel over the ranks (per-block K/V all-gather over NCCL).
-               metric: tokens/s of the whole job; roofline: the W8A8 GEMM kernel inside the step.
-  gemm         BASELINE config 1 shape: W8A8 int8 linear 4096 x 4096 x 4096 (quantize + GEMM), per-128-group
-               activation scales and per-channel weight scales; ranks each run their own rows (replicas).
-  fp8          BASELINE config 2: FP8 e4m3 block-scaled GEMM, MLP-up 16384 x 4096 at M = 20240.
-  elementwise  BASELINE config 3: LayerNorm + modulate + int8 quantize at M = 20240, D = 4096.
+  dit          (default) BASELINE config 5: one denoise step of a 40-block Hy-Nomas-style DiT (hidden 4096,
+               32 x 128 heads, MLP 16384, adaLN modulation, W8A8 int8 linears with per-channel weight scales),
+               L = 20240 tokens, batch 1, sequence-parallel over the ranks (per-block K/V all-gather over
+               NCCL). metric: tokens/s of the whole job (strong scaling); roofline: the W8A8 GEMM kernel
+               inside the step.
+  gemm         BASELINE config 1: W8A8 int8 linear 4096 x 4096 x 4096 (quantize + GEMM), per-128-group
+               activation scales and per-channel weight scales; every rank runs its own copy (replicas).
+  fp8          BASELINE config 2: FP8 e4m3 block-scaled linear, MLP-up 16384 x 4096 at M = 20240 (quantize +
+               GEMM); the config's 12-shape sweep is reported per kernel in `config`.
+  elementwise  BASELINE config 3: the fused elementwise chain at M = 20240, D = 4096 (LN + modulate + int8
+               quantize; QK-RMSNorm + 3-D RoPE of q and k; gated residual; residual + LN + quantize).
 
 Timing: W warm-up steps, then exactly K steps between a barrier + cuda.synchronize on both sides, CUDA
-events on the launching stream, max over ranks. Inputs rotate over buffer sets larger than L2 (126 MB)
-so no step reads the previous step's data from L2. `e2e` repeats the step through the public API with
-the step's inputs copied from pinned host memory and its result read back inside the timed region.
-`--impl reference` times the reference's own CPU path for the same workload (the torch arithmetic it runs
-when the input is not on CUDA, restated in oracle/torch_ref.py) on this host's cores.
+events on the launching stream, max over ranks. Every step reads more than L2 (126 MB) before it reuses an
+input (inputs rotate over sets larger than L2, or - the DiT step - 12 GB of weights stream through between
+reuses). `e2e` repeats the step through the public API with the step's inputs copied from pinned host
+memory and its result read back inside the timed region. `--impl reference` times the reference's own CPU
+path for the same workload (the torch arithmetic it runs when the input is not on CUDA, restated in
+oracle/torch_ref.py) on this host's cores, rank 0 only.
 """
 import argparse
 import json
@@ -36,6 +40,7 @@ import torch  # noqa: E402
 import torch.distributed as dist  # noqa: E402
 
 L2_BYTES = 126 * 2 ** 20
+MB = 1e6
 
 
 # --------------------------------------------------------------------------------------------------------
@@ -58,13 +63,17 @@ class ClockSampler:
               "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
               "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
 
-    def __init__(self, bus_ids):
+    def __init__(self, bus_ids, enabled=True):
         self.bus_ids = {b.lower()[-12:] for b in bus_ids}
         self.rows = []
         self.proc = None
         self.thread = None
+        self.enabled = enabled
+        self.result = None
 
     def start(self):
+        if not self.enabled:
+            return
         try:
             self.proc = subprocess.Popen(["nvidia-smi", f"--query-gpu={self.FIELDS}", "--format=csv,noheader,nounits",
                                           "-lms", "200"], stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
@@ -88,6 +97,7 @@ class ClockSampler:
             self.proc.wait(timeout=5)
         except subprocess.TimeoutExpired:
             self.proc.kill()
+        self.proc = None
         rows = [r for r in self.rows if not self.bus_ids or r[1].lower()[-12:] in self.bus_ids] or self.rows
         if not rows:
             return None
@@ -96,11 +106,12 @@ class ClockSampler:
         names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
         reasons = sorted({names[i] for r in rows for i in range(4) if r[6 + i].lower().startswith("active")})
         loaded = [s for s in sm if mx and s > 0.3 * max(mx)] or sm
-        return {"sm_mhz": statistics.median(loaded) if loaded else None, "sm_max_mhz": max(mx) if mx else None,
-                "reasons": reasons, "samples": len(rows)}
+        self.result = {"sm_mhz": statistics.median(loaded) if loaded else None, "sm_max_mhz": max(mx) if mx else None,
+                       "reasons": reasons, "samples": len(rows)}
+        return self.result
 
 
-def init_dist(args):
+def init_dist():
     world = int(os.environ.get("WORLD_SIZE", "1"))
     rank = int(os.environ.get("RANK", "0"))
     local = int(os.environ.get("LOCAL_RANK", "0"))
@@ -135,8 +146,11 @@ def sum_over_ranks(value, world):
     return float(t.item())
 
 
-def timed_steps(step, steps, warmup, world, stream):
-    """Warm up, then time exactly `steps` calls of step(i) with CUDA events on `stream` (ms, max over ranks)."""
+def timed_steps(step, steps, warmup, world, stream, sampler=None):
+    """Warm up, then time exactly `steps` calls of step(i) with CUDA events on `stream` (ms, max over ranks).
+    `sampler` (rank 0's clock sampler) runs from the warm-up to the end of the timed region."""
+    if sampler is not None:
+        sampler.start()
     for i in range(warmup):
         step(i)
     torch.cuda.synchronize()
@@ -148,42 +162,65 @@ def timed_steps(step, steps, warmup, world, stream):
         step(warmup + i)
     end.record(stream)
     torch.cuda.synchronize()
+    if sampler is not None:
+        sampler.stop()
     barrier(world)
     torch.cuda.synchronize()
     return max_over_ranks(start.elapsed_time(end), world)
 
 
 class KernelTimer:
-    """CUDA events around individual launches of one kernel inside the timed region."""
+    """CUDA events around individual launches inside the timed region, with a per-launch work count."""
 
     def __init__(self, stream):
         self.stream = stream
         self.pairs = []
         self.active = False
 
-    def wrap(self, fn):
+    def wrap(self, fn, work=0.0):
         if not self.active:
             return fn()
         a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
         a.record(self.stream)
         out = fn()
         b.record(self.stream)
-        self.pairs.append((a, b))
+        self.pairs.append((a, b, work))
         return out
 
-    def mean_ms(self):
-        if not self.pairs:
-            return None
+    def total_ms(self):
         torch.cuda.synchronize()
-        return sum(a.elapsed_time(b) for a, b in self.pairs) / len(self.pairs)
+        return sum(a.elapsed_time(b) for a, b, _ in self.pairs)
+
+    def mean_ms(self):
+        return self.total_ms() / len(self.pairs) if self.pairs else None
+
+    def work(self):
+        return sum(w for _, _, w in self.pairs)
 
 
 def cpu_threads():
     return len(os.sched_getaffinity(0)), torch.get_num_threads()
 
 
+def traffic_for(workload):
+    """DRAM bytes per launch of the workload's dominant kernel, from the committed ncu summary."""
+    path = os.path.join(ROOT, "profiles", "traffic.json")
+    if os.path.exists(path):
+        with open(path) as f:
+            return json.load(f).get(workload)
+    return None
+
+
+def launch_count(fn):
+    """Library calls (kernel launches) made by one call of fn."""
+    from hy_nomas_b200 import _lib
+    c0 = _lib.calls
+    fn()
+    return _lib.calls - c0
+
+
 # --------------------------------------------------------------------------------------------------------
-# workloads
+# synthetic inputs
 
 
 def make_int8_weight(n, k, gen, device, per_channel=True):
@@ -203,7 +240,169 @@ def outlier_activations(m, k, gen):
     return x.bfloat16()
 
 
-def workload_gemm(args, world, rank, stream, pk):
+# --------------------------------------------------------------------------------------------------------
+# dit (config 5)
+
+
+DIT_LC = (128, 512)   # token counts of the CPU samples (the fit's two points)
+
+
+def workload_dit(args, world, rank, stream, pk, sampler):
+    from hy_nomas_b200 import kernels
+    from hy_nomas_b200.dit import CudaOps, DiTConfig, SyntheticDiT
+    from hy_nomas_b200.sequence_parallel import SequenceParallel
+    cfg = DiTConfig()
+    sp = SequenceParallel()
+    model = SyntheticDiT(cfg, device="cuda", seed=0, sp=sp)
+    lo, hi = model.token_range
+    L, d = cfg.tokens, cfg.hidden
+    gen = torch.Generator(device="cuda").manual_seed(1000)
+    x = torch.randn(1, L, d, generator=gen, device="cuda")[:, lo:hi].to(torch.bfloat16).contiguous()
+    vec = torch.randn(1, d, generator=gen, device="cuda").to(torch.bfloat16)
+
+    def step(i):
+        return model(x, vec)
+
+    ms = timed_steps(step, args.steps, args.warmup, world, stream, sampler)
+
+    # one instrumented step: CUDA events around every GEMM and attention call, and the launch count
+    gemm_t, attn_t = KernelTimer(stream), KernelTimer(stream)
+    gemm_t.active = attn_t.active = True
+    orig_gemm, orig_attn = kernels.block_gemm, CudaOps.attention
+
+    def gemm_wrap(qa, sa, qw, sw, *a, **kw):
+        return gemm_t.wrap(lambda: orig_gemm(qa, sa, qw, sw, *a, **kw), 2.0 * qa.shape[0] * qw.shape[0] * qa.shape[1])
+
+    def attn_wrap(q, k, v):
+        return attn_t.wrap(lambda: orig_attn(q, k, v), 4.0 * q.shape[0] * q.shape[1] * k.shape[1] * q.shape[2] * q.shape[3])
+
+    kernels.block_gemm, CudaOps.attention = gemm_wrap, staticmethod(attn_wrap)
+    try:
+        barrier(world)
+        launches = launch_count(lambda: step(0))
+        torch.cuda.synchronize()
+    finally:
+        kernels.block_gemm, CudaOps.attention = orig_gemm, staticmethod(orig_attn)
+    gemm_ms, attn_ms = gemm_t.total_ms(), attn_t.total_ms()
+    gemm_ops, attn_flops = gemm_t.work(), attn_t.work()
+
+    # e2e through the public API: this rank's tokens and vec from pinned host memory, the output read back
+    xh, vh = x.cpu().pin_memory(), vec.cpu().pin_memory()
+    yh = torch.empty_like(xh).pin_memory()
+
+    def e2e_step(i):
+        y = model(xh.to("cuda", non_blocking=True), vh.to("cuda", non_blocking=True))
+        yh.copy_(y, non_blocking=True)
+
+    e2e_ms = timed_steps(e2e_step, args.steps, 1, world, stream)
+    tokens = L * args.steps
+    value = tokens / (ms * 1e-3)
+    int8_peak = 2.0 * pk["bf16_tflops_sustained"]
+    achieved = gemm_ops / (gemm_ms * 1e-3) / 1e12
+    step_ms = ms / args.steps
+    roof = {"kernel": "hn::gemm::k_block_gemm<int8, group activation scales, per-channel weights> (all GEMMs of a "
+                      "step)", "bound": "tensor", "achieved": round(achieved, 1), "peak": round(int8_peak, 1),
+            "unit": "TOPS", "frac": round(achieved / int8_peak, 4),
+            "peak_note": f"int8 dense = 2 x {pk['source']} bf16 sustained ({pk['bf16_tflops_sustained']} TFLOP/s); "
+                         "the GEMMs run inside a long step",
+            "traffic": traffic_for("dit"), "gemm_ops_per_step_rank": gemm_ops}
+    config = {"workload": "dit_step_40x_hidden4096_L20240 (config 5): 40 DiT blocks, SDPA attention, W8A8 linears",
+              "model": "synthetic Hy-Nomas-style DiT (random init, seeded)", "global_batch": 1, "seq_len": L,
+              "tokens_per_rank": hi - lo, "blocks": cfg.blocks, "hidden": d, "heads": cfg.heads, "mlp": d * cfg.mlp_ratio,
+              "activation_scales": "per token x 128 channels", "weight_scales": "per output channel",
+              "parallelism": f"sp{world} (sequence-parallel, K/V all-gather over NCCL; weights replicated)",
+              "l2": "12 GB of weights stream through L2 between reuses of a step's input",
+              "step_breakdown_ms_rank0": {"gemm": round(gemm_ms, 2), "attention": round(attn_ms, 2),
+                                          "other": round(max(step_ms - gemm_ms - attn_ms, 0.0), 2)},
+              "attention_tflops": round(attn_flops / (attn_ms * 1e-3) / 1e12, 1) if attn_ms else None,
+              "floor_ms_rank0": {"gemm_at_int8_peak": round(gemm_ops / (int8_peak * 1e12) * 1e3, 2),
+                                 "attention_at_bf16_peak": round(attn_flops / (pk["bf16_tflops_sustained"] * 1e12) * 1e3, 2)}}
+    return dict(metric="DiT denoise step tokens/s (40 blocks, 20240 tokens)", value=round(value, 1), unit="tokens/s",
+                ms_per_step=round(step_ms, 3), higher_is_better=True, scaling="strong", dtype="int8 (GEMMs), bf16",
+                config=config,
+                e2e={"value": round(tokens / (e2e_ms * 1e-3), 1), "unit": "tokens/s",
+                     "h2d_bytes_per_step": int(sum_over_ranks(xh.numel() * 2 + vh.numel() * 2, world)),
+                     "d2h_bytes_per_step": int(sum_over_ranks(yh.numel() * 2, world))},
+                roofline=roof, gpu_launches=launches * args.steps,
+                cpu_baseline_fn=lambda: cpu_baseline_dit(cfg))
+
+
+def _cpu_dit_weights(cfg, gen):
+    from hy_nomas_b200.dit import make_block_weights
+    return make_block_weights(cfg, gen, "cpu")
+
+
+def cpu_dit_sample(cfg, w, lc, gen):
+    """One block of the reference's CPU path on `lc` tokens -> (seconds, attention seconds)."""
+    from hy_nomas_b200.dit import rope_freqs
+    from oracle import torch_ref
+    x = torch.randn(1, lc, cfg.hidden, generator=gen).to(torch.bfloat16)
+    vec = torch.randn(1, cfg.hidden, generator=gen).to(torch.bfloat16)
+    cos, sin = rope_freqs(cfg.rope_dims, cfg.theta, *cfg.grid)
+    rope = (cos[:lc], sin[:lc])
+    tm = {}
+    t0 = time.perf_counter()
+    torch_ref.dit_block_cpu(x, vec, w, rope, cfg.heads, timings=tm)
+    return time.perf_counter() - t0, tm.get("attention", 0.0)
+
+
+def dit_extrapolate(cfg, samples):
+    """Fit t(l) = a + b*l (everything but attention: the per-call weight dequantization is the fixed part)
+    and c*l^2 (attention) to the CPU samples, evaluate at the full sequence -> tokens/s of a 40-block step."""
+    (l1, t1, at1), (l2, t2, at2) = samples
+    n1, n2 = t1 - at1, t2 - at2
+    b = max((n2 - n1) / (l2 - l1), 0.0)
+    a = max(n1 - b * l1, 0.0)
+    c = at2 / (l2 * l2)
+    L = cfg.tokens
+    step_s = cfg.blocks * (a + b * L + c * L * L)
+    return L / step_s, step_s
+
+
+def cpu_baseline_dit(cfg, repeats=2):
+    gen = torch.Generator().manual_seed(7)
+    w = _cpu_dit_weights(cfg, gen)
+    samples = []
+    for lc in DIT_LC:
+        cpu_dit_sample(cfg, w, lc, gen)
+        runs = [cpu_dit_sample(cfg, w, lc, gen) for _ in range(repeats)]
+        samples.append((lc, statistics.median(r[0] for r in runs), statistics.median(r[1] for r in runs)))
+    value, step_s = dit_extrapolate(cfg, samples)
+    cores, threads = cpu_threads()
+    return {"value": round(value, 2), "unit": "tokens/s", "cores": threads, "kind": "port",
+            "sample": f"one block of the reference's CPU path (dequantize + bf16 F.linear per linear, torch norms, "
+                      f"RoPE and SDPA) at {DIT_LC[0]} and {DIT_LC[1]} tokens, median of {repeats}; extrapolated to "
+                      f"40 blocks x {cfg.tokens} tokens ({step_s:.0f} s per step) by a + b*L (linears, norms) + "
+                      f"c*L^2 (attention); {threads} threads on {cores} cores"}
+
+
+def reference_dit(args):
+    from hy_nomas_b200.dit import DiTConfig
+    cfg = DiTConfig()
+    gen = torch.Generator().manual_seed(7)
+    w = _cpu_dit_weights(cfg, gen)
+    first = cpu_dit_sample(cfg, w, DIT_LC[0], gen)
+    for _ in range(args.warmup - 1):
+        cpu_dit_sample(cfg, w, DIT_LC[1], gen)
+    runs = [cpu_dit_sample(cfg, w, DIT_LC[1], gen) for _ in range(args.steps)]
+    small = (DIT_LC[0], first[0], first[1])
+    big = (DIT_LC[1], statistics.median(r[0] for r in runs), statistics.median(r[1] for r in runs))
+    value, step_s = dit_extrapolate(cfg, [small, big])
+    cores, threads = cpu_threads()
+    sample = (f"each step: one block of the reference's CPU path at {DIT_LC[1]} tokens (a {DIT_LC[0]}-token block "
+              f"fixes the fit), extrapolated to 40 blocks x {cfg.tokens} tokens by a + b*L + c*L^2 "
+              f"({step_s:.0f} s per step); {threads} threads")
+    return dict(metric="DiT denoise step tokens/s (40 blocks, 20240 tokens)", value=round(value, 2), unit="tokens/s",
+                ms_per_step=round(step_s * 1e3, 1), higher_is_better=True, scaling="strong", dtype="bf16 (CPU)",
+                config={"workload": "dit_step_40x_hidden4096_L20240 (config 5)", "seq_len": cfg.tokens},
+                kind="port", sample=sample, cores=threads)
+
+
+# --------------------------------------------------------------------------------------------------------
+# gemm (config 1)
+
+
+def workload_gemm(args, world, rank, stream, pk, sampler):
     from hy_nomas_b200 import kernels
     m, n, k = 4096, 4096, 4096
     gen = torch.Generator().manual_seed(1234 + rank)
@@ -221,14 +420,14 @@ def workload_gemm(args, world, rank, stream, pk):
         qa, sa = kernels.quantize_activations(x)
         return timer.wrap(lambda: kernels.block_gemm(qa, sa, qw, sw, bias))
 
-    ms = timed_steps(step, args.steps, args.warmup, world, stream)
+    ms = timed_steps(step, args.steps, args.warmup, world, stream, sampler)
     timer.active = True
     timed_steps(step, args.steps, 0, world, stream)
     gemm_ms = timer.mean_ms()
+    launches = launch_count(lambda: step(0))
     ops = 2.0 * m * n * k
     total_ops = sum_over_ranks(ops * args.steps, world)
     value = total_ops / (ms * 1e-3) / 1e12
-    # e2e through the public API: x from pinned host memory, y read back, every step
     xh = [x.cpu().pin_memory() for x in xs[:2]]
     yh = torch.empty((m, n), dtype=torch.bfloat16).pin_memory()
 
@@ -240,23 +439,34 @@ def workload_gemm(args, world, rank, stream, pk):
 
     e2e_ms = timed_steps(e2e_step, args.steps, 2, world, stream)
     e2e = {"value": round(total_ops / (e2e_ms * 1e-3) / 1e12, 2), "unit": "TOPS",
-           "h2d_bytes_per_step": m * k * 2, "d2h_bytes_per_step": m * n * 2}
+           "h2d_bytes_per_step": m * k * 2 * world, "d2h_bytes_per_step": m * n * 2 * world}
     peak = 2.0 * pk["bf16_tflops"]
     achieved = ops / (gemm_ms * 1e-3) / 1e12
-    roof = {"kernel": "hn::gemm::k_block_gemm<int8, per-channel weights>", "bound": "tensor",
+    roof = {"kernel": "hn::gemm::k_block_gemm<int8, group activation scales, per-channel weights>", "bound": "tensor",
             "achieved": round(achieved, 1), "peak": round(peak, 1), "unit": "TOPS", "frac": round(achieved / peak, 4),
             "peak_note": f"int8 dense = 2 x {pk['source']} bf16 burst ({pk['bf16_tflops']} TFLOP/s)",
-            "traffic": traffic_for("gemm"), "algorithmic_bytes": m * k + n * k + m * n * 2 + m * 4 * (k // 128)}
-    out = dict(metric="W8A8 GEMM TOPS", value=round(value, 2), unit="TOPS", ms_per_step=round(ms / args.steps, 4),
-               higher_is_better=True, scaling="weak", dtype="int8",
-               config={"workload": "w8a8_linear_4096x4096x4096 (config 1 shape): quantize + block-scaled GEMM",
-                       "M": m, "N": n, "K": k, "activation_scales": "per token x 128 channels",
-                       "weight_scales": "per output channel", "l2": f"inputs rotate over {nsets} sets > L2",
-                       "parallelism": f"replicas x{world}"},
-               e2e=e2e, roofline=roof, gpu_launches=2 * args.steps)
-    out["config"]["kernel_variants_tops"] = gemm_variants(m, n, k, stream)
-    out["cpu_baseline_fn"] = lambda: cpu_baseline_gemm(m, n, k)
-    return out
+            "traffic": traffic_for("gemm"), "algorithmic_bytes": m * k + n * k + m * n * 2 + m * 4 * (k // 128) + n * 4}
+    config = {"workload": "w8a8_linear_4096x4096x4096 (config 1): quantize + block-scaled GEMM",
+              "M": m, "N": n, "K": k, "activation_scales": "per token x 128 channels",
+              "weight_scales": "per output channel", "l2": f"inputs rotate over {nsets} sets > L2",
+              "parallelism": f"replicas x{world}", "kernel_variants_tops": gemm_variants(m, n, k, stream)}
+    return dict(metric="W8A8 GEMM TOPS", value=round(value, 2), unit="TOPS", ms_per_step=round(ms / args.steps, 4),
+                higher_is_better=True, scaling="weak", dtype="int8", config=config, e2e=e2e, roofline=roof,
+                gpu_launches=launches * args.steps, cpu_baseline_fn=lambda: cpu_baseline_gemm(m, n, k))
+
+
+def _time_kernel(fn, stream, flush, iters):
+    fn()
+    times = []
+    for _ in range(iters):
+        flush.zero_()
+        a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        a.record(stream)
+        fn()
+        b.record(stream)
+        b.synchronize()
+        times.append(a.elapsed_time(b))
+    return statistics.median(times)
 
 
 def gemm_variants(m, n, k, stream, iters=20):
@@ -267,60 +477,43 @@ def gemm_variants(m, n, k, stream, iters=20):
     dev = torch.device("cuda")
     qa = torch.randint(-127, 128, (m, k), generator=gen, dtype=torch.int8).to(dev)
     qw = torch.randint(-127, 128, (n, k), generator=gen, dtype=torch.int8).to(dev)
-    sa_g = (torch.rand(m, k // 128, generator=gen) * 0.02).to(dev)
+    sa_g = kernels.quantize_activations(torch.randn(m, k, generator=gen).bfloat16().to(dev))[1]
     sa_r = (torch.rand(m, generator=gen) * 0.02).to(dev)
     sw_g = (torch.rand(n, k // 128, generator=gen) * 4e-3).to(dev)
     sw_r = (torch.rand(n, generator=gen) * 4e-3).to(dev)
     flush = torch.empty(2 * L2_BYTES, dtype=torch.uint8, device=dev)
-    cases = {"a_group_w_group": lambda: kernels.block_gemm(qa, sa_g, qw, sw_g),
+    cases = {"a_group_w_group_rowmajor": lambda: kernels.block_gemm(qa, sa_g, qw, sw_g),
              "a_group_w_channel": lambda: kernels.block_gemm(qa, sa_g, qw, sw_r),
              "a_token_w_channel": lambda: kernels.block_gemm(qa, sa_r, qw, sw_r),
              "cublaslt_int8_int32": lambda: torch._int_mm(qa, qw.t())}
     res = {}
     for name, fn in cases.items():
         try:
-            fn()
-            times = []
-            for _ in range(iters):
-                flush.zero_()
-                a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-                a.record(stream)
-                fn()
-                b.record(stream)
-                b.synchronize()
-                times.append(a.elapsed_time(b))
-            res[name] = round(2.0 * m * n * k / (statistics.median(times) * 1e-3) / 1e12, 1)
+            res[name] = round(2.0 * m * n * k / (_time_kernel(fn, stream, flush, iters) * 1e-3) / 1e12, 1)
         except RuntimeError as e:
             res[name] = f"unavailable: {str(e).splitlines()[0][:80]}"
     return res
 
 
-def traffic_for(workload):
-    path = os.path.join(ROOT, "profiles", "traffic.json")
-    if os.path.exists(path):
-        with open(path) as f:
-            t = json.load(f)
-        return t.get(workload)
-    return None
+def cpu_gemm_sample(rows, n, k, gen):
+    x = outlier_activations(rows, k, gen)
+    q, s = make_int8_weight(n, k, gen, "cpu", per_channel=False)
+    bias = (torch.randn(n, generator=gen) * 0.02).bfloat16()
+    return x, q, s, bias
 
 
 def cpu_baseline_gemm(m, n, k, budget_s=10.0):
     """The reference's CPU path (dequantize_g128 + bf16 F.linear, hy_nomas/ops.py:175-176) on a bounded
     sample of rows, on all host threads."""
     from oracle import torch_ref
-    gen = torch.Generator().manual_seed(5)
     rows = 512
-    x = outlier_activations(rows, k, gen)
-    q, s = make_int8_weight(n, k, gen, "cpu", per_channel=False)
-    bias = (torch.randn(n, generator=gen) * 0.02).bfloat16()
+    x, q, s, bias = cpu_gemm_sample(rows, n, k, torch.Generator().manual_seed(5))
     torch_ref.int8_linear_cpu(x, q, s, bias)
     t0 = time.perf_counter()
     it = 0
-    while True:
+    while time.perf_counter() - t0 < budget_s:
         torch_ref.int8_linear_cpu(x, q, s, bias)
         it += 1
-        if time.perf_counter() - t0 > budget_s:
-            break
     dt = (time.perf_counter() - t0) / it
     cores, threads = cpu_threads()
     return {"value": round(2.0 * rows * n * k / dt / 1e12, 4), "unit": "TOPS", "cores": threads, "kind": "port",
@@ -329,22 +522,11 @@ def cpu_baseline_gemm(m, n, k, budget_s=10.0):
                       f"{cores} cores)"}
 
 
-WORKLOADS = {"gemm": workload_gemm}
-
-
-def run_reference(args, world, rank):
-    """The reference's CPU path for the same workload and metric, rank 0 only."""
-    if rank != 0:
-        return None
-    if args.workload != "gemm":
-        raise SystemExit(f"--impl reference: workload {args.workload} not wired yet")
-    m, n, k = 4096, 4096, 4096
+def reference_gemm(args):
     from oracle import torch_ref
-    gen = torch.Generator().manual_seed(5)
+    m, n, k = 4096, 4096, 4096
     rows = 1024
-    x = outlier_activations(rows, k, gen)
-    q, s = make_int8_weight(n, k, gen, "cpu", per_channel=False)
-    bias = (torch.randn(n, generator=gen) * 0.02).bfloat16()
+    x, q, s, bias = cpu_gemm_sample(rows, n, k, torch.Generator().manual_seed(5))
     for _ in range(args.warmup):
         torch_ref.int8_linear_cpu(x, q, s, bias)
     t0 = time.perf_counter()
@@ -353,56 +535,354 @@ def run_reference(args, world, rank):
     dt = time.perf_counter() - t0
     value = 2.0 * rows * n * k * args.steps / dt / 1e12
     cores, threads = cpu_threads()
-    sample = f"{rows} of {m} rows per step (dequantize_g128 + bf16 F.linear on CPU, {threads} threads)"
-    return dict(metric="W8A8 GEMM TOPS", value=round(value, 4), unit="TOPS", n_gpus=world, steps=args.steps,
-                warmup=args.warmup, ms_per_step=round(dt / args.steps * 1e3, 3), higher_is_better=True,
-                scaling="weak", vs_baseline=None, dtype="int8", data="synthetic",
-                config={"workload": "w8a8_linear_4096x4096x4096 (config 1 shape)", "M": m, "N": n, "K": k},
-                impl="reference",
-                cpu_baseline={"value": round(value, 4), "unit": "TOPS", "cores": threads, "kind": "port",
-                              "sample": sample},
-                e2e={"value": round(value, 4), "unit": "TOPS", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0})
+    return dict(metric="W8A8 GEMM TOPS", value=round(value, 4), unit="TOPS", ms_per_step=round(dt / args.steps * 1e3, 3),
+                higher_is_better=True, scaling="weak", dtype="int8", kind="port", cores=threads,
+                config={"workload": "w8a8_linear_4096x4096x4096 (config 1)", "M": m, "N": n, "K": k},
+                sample=f"{rows} of {m} rows per step (dequantize_g128 + bf16 F.linear on CPU, {threads} threads)")
+
+
+# --------------------------------------------------------------------------------------------------------
+# fp8 (config 2)
+
+
+FP8_SHAPES = {"qkv": (12288, 4096), "mlp_up": (16384, 4096), "mlp_down": (4096, 16384)}
+FP8_M = (1024, 4096, 16384, 20240)
+
+
+def fp8_weight(n, k, gen, dev):
+    """fp32 N(0, 0.02) quantized per 128 x 128 block (pixelumm.py:77-82) by the product's quantizer."""
+    from hy_nomas_b200 import ops
+    w = torch.randn(n, k, generator=gen, device=dev) * 0.02
+    return ops.quantize_fp8_block(w)
+
+
+def workload_fp8(args, world, rank, stream, pk, sampler):
+    from hy_nomas_b200 import kernels
+    m, (n, k) = 20240, FP8_SHAPES["mlp_up"]
+    dev = torch.device("cuda")
+    gen = torch.Generator(device=dev).manual_seed(77 + rank)
+    nsets = 2
+    xs = [torch.randn(m, k, generator=gen, device=dev).to(torch.bfloat16) for _ in range(nsets)]
+    ws = [fp8_weight(n, k, gen, dev) for _ in range(nsets)]
+    bias = (torch.randn(n, generator=gen, device=dev) * 0.02).to(torch.bfloat16)
+    timer = KernelTimer(stream)
+    ops_ = 2.0 * m * n * k
+
+    def step(i):
+        qw, sw = ws[i % nsets]
+        qa, sa = kernels.quantize_activations(xs[i % nsets], "fp8")
+        return timer.wrap(lambda: kernels.block_gemm(qa, sa, qw, sw, bias, kind="fp8"), ops_)
+
+    ms = timed_steps(step, args.steps, args.warmup, world, stream, sampler)
+    timer.active = True
+    timed_steps(step, args.steps, 0, world, stream)
+    gemm_ms = timer.mean_ms()
+    launches = launch_count(lambda: step(0))
+    total = sum_over_ranks(ops_ * args.steps, world)
+    xh = [x.cpu().pin_memory() for x in xs]
+    yh = torch.empty((m, n), dtype=torch.bfloat16).pin_memory()
+
+    def e2e_step(i):
+        qw, sw = ws[i % nsets]
+        y = kernels.block_linear(xh[i % nsets].to(dev, non_blocking=True), qw, sw, bias, kind="fp8")
+        yh.copy_(y, non_blocking=True)
+
+    e2e_ms = timed_steps(e2e_step, args.steps, 1, world, stream)
+    peak = 2.0 * pk["bf16_tflops"]
+    achieved = ops_ / (gemm_ms * 1e-3) / 1e12
+    roof = {"kernel": "hn::gemm::k_block_gemm<e4m3, 1x128 activation blocks, 128x128 weight blocks>",
+            "bound": "tensor", "achieved": round(achieved, 1), "peak": round(peak, 1), "unit": "TFLOP/s",
+            "frac": round(achieved / peak, 4),
+            "peak_note": f"fp8 dense = 2 x {pk['source']} bf16 burst ({pk['bf16_tflops']} TFLOP/s)",
+            "traffic": traffic_for("fp8"), "algorithmic_bytes": m * k + n * k + m * n * 2 + m * 4 * (k // 128)}
+    config = {"workload": "fp8_block_linear_M20240_N16384_K4096 (config 2, MLP-up): quantize + GEMM",
+              "M": m, "N": n, "K": k, "activation_scales": "1 x 128 blocks (e4m3)", "weight_scales": "128 x 128 blocks",
+              "l2": "inputs rotate over 2 sets of 166 MB activations + 67 MB weights (> L2)",
+              "parallelism": f"replicas x{world}", "sweep_kernel_tflops": fp8_sweep(stream)}
+    return dict(metric="FP8 block GEMM TFLOP/s", value=round(total / (ms * 1e-3) / 1e12, 2), unit="TFLOP/s",
+                ms_per_step=round(ms / args.steps, 4), higher_is_better=True, scaling="weak", dtype="fp8 e4m3",
+                config=config,
+                e2e={"value": round(total / (e2e_ms * 1e-3) / 1e12, 2), "unit": "TFLOP/s",
+                     "h2d_bytes_per_step": m * k * 2 * world, "d2h_bytes_per_step": m * n * 2 * world},
+                roofline=roof, gpu_launches=launches * args.steps,
+                cpu_baseline_fn=lambda: cpu_baseline_fp8(m, n, k))
+
+
+def fp8_sweep(stream, iters=5):
+    """The config's 3 weight shapes x 4 token counts, GEMM kernel alone (L2 flushed before each launch)."""
+    from hy_nomas_b200 import kernels
+    dev = torch.device("cuda")
+    gen = torch.Generator(device=dev).manual_seed(5)
+    flush = torch.empty(2 * L2_BYTES, dtype=torch.uint8, device=dev)
+    res = {}
+    for name, (n, k) in FP8_SHAPES.items():
+        qw, sw = fp8_weight(n, k, gen, dev)
+        for m in FP8_M:
+            qa, sa = kernels.quantize_activations(torch.randn(m, k, generator=gen, device=dev).to(torch.bfloat16), "fp8")
+            t = _time_kernel(lambda: kernels.block_gemm(qa, sa, qw, sw, kind="fp8"), stream, flush, iters)
+            res[f"{name}_{n}x{k}_M{m}"] = round(2.0 * m * n * k / (t * 1e-3) / 1e12, 1)
+        del qw, sw
+    return res
+
+
+def cpu_fp8_sample(rows, n, k, gen):
+    from oracle import torch_ref
+    x = torch.randn(rows, k, generator=gen).to(torch.bfloat16)
+    q, s = torch_ref.fp8_block_quantize(torch.randn(n, k, generator=gen) * 0.02)
+    bias = (torch.randn(n, generator=gen) * 0.02).to(torch.bfloat16)
+    return x, q, s, bias
+
+
+def cpu_baseline_fp8(m, n, k, budget_s=10.0):
+    """The reference's CPU path for the FP8 linear (dequantize_fp8_block + bf16 F.linear, pixelumm.py:154-155)."""
+    from oracle import torch_ref
+    rows = 256
+    x, q, s, bias = cpu_fp8_sample(rows, n, k, torch.Generator().manual_seed(5))
+    torch_ref.fp8_linear_cpu(x, q, s, bias)
+    t0 = time.perf_counter()
+    it = 0
+    while time.perf_counter() - t0 < budget_s:
+        torch_ref.fp8_linear_cpu(x, q, s, bias)
+        it += 1
+    dt = (time.perf_counter() - t0) / it
+    cores, threads = cpu_threads()
+    return {"value": round(2.0 * rows * n * k / dt / 1e12, 4), "unit": "TFLOP/s", "cores": threads, "kind": "port",
+            "sample": f"{rows} of {m} rows, {it} iterations in {budget_s:.0f}+ s (dequantize_fp8_block + bf16 "
+                      f"F.linear, {threads} threads on {cores} cores)"}
+
+
+def reference_fp8(args):
+    from oracle import torch_ref
+    m, (n, k) = 20240, FP8_SHAPES["mlp_up"]
+    rows = 512
+    x, q, s, bias = cpu_fp8_sample(rows, n, k, torch.Generator().manual_seed(5))
+    for _ in range(args.warmup):
+        torch_ref.fp8_linear_cpu(x, q, s, bias)
+    t0 = time.perf_counter()
+    for _ in range(args.steps):
+        torch_ref.fp8_linear_cpu(x, q, s, bias)
+    dt = time.perf_counter() - t0
+    cores, threads = cpu_threads()
+    return dict(metric="FP8 block GEMM TFLOP/s", value=round(2.0 * rows * n * k * args.steps / dt / 1e12, 4),
+                unit="TFLOP/s", ms_per_step=round(dt / args.steps * 1e3, 3), higher_is_better=True, scaling="weak",
+                dtype="fp8 e4m3", kind="port", cores=threads,
+                config={"workload": "fp8_block_linear_M20240_N16384_K4096 (config 2)", "M": m, "N": n, "K": k},
+                sample=f"{rows} of {m} rows per step (dequantize_fp8_block + bf16 F.linear, {threads} threads)")
+
+
+# --------------------------------------------------------------------------------------------------------
+# elementwise (config 3)
+
+
+def elementwise_bytes(m, d, h, hd):
+    """Algorithmic HBM bytes per kernel (each tensor read or written once)."""
+    act = m * d * 2
+    codes, scales = m * d, m * (d // 128) * 4
+    tables = 2 * m * hd * 4
+    return {"adaln_quant": act + codes + scales + 2 * d * 2,
+            "qk_norm_rope2": 4 * m * h * hd * 2 + tables + 2 * hd * 2,
+            "gated_residual": 3 * act + d * 2,
+            "gated_residual_adaln_quant": 3 * act + codes + scales + 3 * d * 2}
+
+
+def workload_elementwise(args, world, rank, stream, pk, sampler):
+    from hy_nomas_b200 import fused, kernels
+    from hy_nomas_b200.dit import rope_freqs
+    m, d, h, hd = 20240, 4096, 32, 128
+    dev = torch.device("cuda")
+    gen = torch.Generator(device=dev).manual_seed(31 + rank)
+    bf = lambda *s, std=1.0: (torch.randn(*s, generator=gen, device=dev) * std).to(torch.bfloat16)  # noqa: E731
+    nsets = 2
+    sets = [dict(x=bf(1, m, d), y=bf(1, m, d), q=bf(1, m, h, hd), k=bf(1, m, h, hd)) for _ in range(nsets)]
+    shift, scale, gate = bf(1, d, std=0.1), bf(1, d, std=0.1), bf(1, d, std=0.1)
+    wq, wk = bf(hd, std=0.1) + 1, bf(hd, std=0.1) + 1
+    rope = rope_freqs((16, 56, 56), 10000.0, 23, 22, 40, device=dev)
+    nbytes = elementwise_bytes(m, d, h, hd)
+    timers = {name: KernelTimer(stream) for name in nbytes}
+
+    def step(i):
+        s = sets[i % nsets]
+        timers["adaln_quant"].wrap(lambda: kernels.adaln_quant(s["x"], shift, scale))
+        timers["qk_norm_rope2"].wrap(lambda: fused.qk_norm_rope2(s["q"], s["k"], wq, wk, rope))
+        timers["gated_residual"].wrap(lambda: fused.gated_residual(s["x"], s["y"], gate))
+        timers["gated_residual_adaln_quant"].wrap(
+            lambda: fused.gated_residual_adaln_quant(s["x"], s["y"], gate, shift, scale))
+
+    ms = timed_steps(step, args.steps, args.warmup, world, stream, sampler)
+    for t in timers.values():
+        t.active = True
+    timed_steps(step, args.steps, 0, world, stream)
+    per_kernel = {name: t.mean_ms() for name, t in timers.items()}
+    launches = launch_count(lambda: step(0))
+    step_bytes = sum(nbytes.values())
+    total = sum_over_ranks(step_bytes * args.steps, world)
+    gbs = {name: round(nbytes[name] / (per_kernel[name] * 1e-3) / 1e9, 1) for name in nbytes}
+    top = max(per_kernel, key=per_kernel.get)
+    peak = pk["hbm_gbs"]
+    roof = {"kernel": f"{top} (largest time share of the chain)", "bound": "hbm", "achieved": gbs[top],
+            "peak": peak, "unit": "GB/s", "frac": round(gbs[top] / peak, 4),
+            "peak_note": f"{pk['source']} HBM copy bandwidth", "traffic": (traffic_for("elementwise") or {}).get(top),
+            "algorithmic_bytes": nbytes[top],
+            "per_kernel_gbs": gbs, "per_kernel_frac": {k: round(v / peak, 4) for k, v in gbs.items()}}
+    # e2e through the public API: the chain's inputs from pinned host memory, every output a caller consumes
+    # (the codes and scales of both quantizing kernels, the normalized q and k, the new residual) read back
+    hsets = [{k_: v.cpu().pin_memory() for k_, v in s.items()} for s in sets]
+    outs_h = dict(q1=torch.empty((m, d), dtype=torch.int8).pin_memory(),
+                  s1=torch.empty((m, d // 128), dtype=torch.float32).pin_memory(),
+                  yq=torch.empty((1, m, h, hd), dtype=torch.bfloat16).pin_memory(),
+                  yk=torch.empty((1, m, h, hd), dtype=torch.bfloat16).pin_memory(),
+                  x2=torch.empty((1, m, d), dtype=torch.bfloat16).pin_memory(),
+                  q2=torch.empty((m, d), dtype=torch.int8).pin_memory(),
+                  s2=torch.empty((m, d // 128), dtype=torch.float32).pin_memory())
+
+    def e2e_step(i):
+        s = {k_: v.to(dev, non_blocking=True) for k_, v in hsets[i % nsets].items()}
+        q1, s1 = kernels.adaln_quant(s["x"], shift, scale)
+        yq, yk = fused.qk_norm_rope2(s["q"], s["k"], wq, wk, rope)
+        fused.gated_residual(s["x"], s["y"], gate)
+        x2, q2, s2 = fused.gated_residual_adaln_quant(s["x"], s["y"], gate, shift, scale)
+        for name, t in dict(q1=q1, s1=s1, yq=yq, yk=yk, x2=x2, q2=q2, s2=s2).items():
+            outs_h[name].copy_(t, non_blocking=True)
+
+    e2e_ms = timed_steps(e2e_step, args.steps, 1, world, stream)
+    e2e_total = sum_over_ranks(step_bytes * args.steps, world)
+    h2d = sum(v.numel() * v.element_size() for v in hsets[0].values())
+    d2h = sum(v.numel() * v.element_size() for v in outs_h.values())
+    config = {"workload": "dit_elementwise_chain_M20240_D4096 (config 3): adaln_quant, qk_norm_rope2 (q and k, "
+                          "3-D RoPE 16/56/56), gated_residual, gated_residual_adaln_quant",
+              "M": m, "D": d, "heads": h, "head_dim": hd, "bytes_per_step": step_bytes,
+              "l2": "inputs rotate over 2 sets (each tensor 166 MB > L2)", "parallelism": f"replicas x{world}"}
+    return dict(metric="fused DiT elementwise chain GB/s", value=round(total / (ms * 1e-3) / 1e9, 1), unit="GB/s",
+                ms_per_step=round(ms / args.steps, 4), higher_is_better=True, scaling="weak", dtype="bf16 -> int8",
+                config=config,
+                e2e={"value": round(e2e_total / (e2e_ms * 1e-3) / 1e9, 1), "unit": "GB/s",
+                     "h2d_bytes_per_step": h2d * world, "d2h_bytes_per_step": d2h * world},
+                roofline=roof, gpu_launches=launches * args.steps,
+                cpu_baseline_fn=lambda: cpu_baseline_elementwise(m, d, h, hd))
+
+
+def cpu_elementwise_chain(rows, d, h, hd, gen):
+    """The reference's CPU arithmetic for the chain on `rows` tokens (model.py:103-138, 280-284, ops.py:41-52)."""
+    from hy_nomas_b200.dit import rope_freqs
+    from oracle import torch_ref
+    bf = lambda *s, std=1.0: (torch.randn(*s, generator=gen) * std).to(torch.bfloat16)  # noqa: E731
+    x, y, q, k = bf(1, rows, d), bf(1, rows, d), bf(1, rows, h, hd), bf(1, rows, h, hd)
+    shift, scale, gate = bf(1, d, std=0.1), bf(1, d, std=0.1), bf(1, d, std=0.1)
+    w = bf(hd, std=0.1) + 1
+    cos, sin = rope_freqs((16, 56, 56), 10000.0, 23, 22, 40)
+    cos, sin = cos[:rows], sin[:rows]
+
+    def run():
+        xm = torch_ref.modulate(torch_ref.layer_norm(x), shift, scale).to(torch.bfloat16)
+        torch_ref.quantize_g128(xm[0])
+        torch_ref.apply_rope(torch_ref.rms_norm(q, w), cos, sin)
+        torch_ref.apply_rope(torch_ref.rms_norm(k, w), cos, sin)
+        x1 = x + y * gate.unsqueeze(1)
+        x2 = x + y * gate.unsqueeze(1)
+        torch_ref.quantize_g128(torch_ref.modulate(torch_ref.layer_norm(x2), shift, scale).to(torch.bfloat16)[0])
+        return x1
+    return run
+
+
+def cpu_baseline_elementwise(m, d, h, hd, budget_s=10.0):
+    rows = 1024
+    run = cpu_elementwise_chain(rows, d, h, hd, torch.Generator().manual_seed(3))
+    run()
+    t0 = time.perf_counter()
+    it = 0
+    while time.perf_counter() - t0 < budget_s:
+        run()
+        it += 1
+    dt = (time.perf_counter() - t0) / it
+    cores, threads = cpu_threads()
+    b = sum(elementwise_bytes(rows, d, h, hd).values())
+    return {"value": round(b / dt / 1e9, 2), "unit": "GB/s", "cores": threads, "kind": "port",
+            "sample": f"the chain on {rows} of {m} tokens, {it} iterations in {budget_s:.0f}+ s (torch layer_norm, "
+                      f"modulate, quantize_g128, RMSNorm, apply_rope, x + y*gate on CPU; {threads} threads on "
+                      f"{cores} cores); GB/s = the same algorithmic bytes per token"}
+
+
+def reference_elementwise(args):
+    m, d, h, hd = 20240, 4096, 32, 128
+    rows = 2048
+    run = cpu_elementwise_chain(rows, d, h, hd, torch.Generator().manual_seed(3))
+    for _ in range(args.warmup):
+        run()
+    t0 = time.perf_counter()
+    for _ in range(args.steps):
+        run()
+    dt = time.perf_counter() - t0
+    cores, threads = cpu_threads()
+    b = sum(elementwise_bytes(rows, d, h, hd).values())
+    return dict(metric="fused DiT elementwise chain GB/s", value=round(b * args.steps / dt / 1e9, 3), unit="GB/s",
+                ms_per_step=round(dt / args.steps * 1e3, 3), higher_is_better=True, scaling="weak",
+                dtype="bf16 -> int8", kind="port", cores=threads,
+                config={"workload": "dit_elementwise_chain_M20240_D4096 (config 3)", "M": m, "D": d},
+                sample=f"the chain on {rows} of {m} tokens per step (torch CPU arithmetic, {threads} threads)")
+
+
+# --------------------------------------------------------------------------------------------------------
+
+
+WORKLOADS = {"dit": (workload_dit, reference_dit), "gemm": (workload_gemm, reference_gemm),
+             "fp8": (workload_fp8, reference_fp8), "elementwise": (workload_elementwise, reference_elementwise)}
+
+
+def run_reference(args, world, rank):
+    """The reference's CPU path for the same workload and metric, rank 0 only (other ranks do no work)."""
+    if rank != 0:
+        return None
+    r = WORKLOADS[args.workload][1](args)
+    sample, kind, cores = r.pop("sample"), r.pop("kind"), r.pop("cores")
+    line = {"metric": r["metric"], "value": r["value"], "unit": r["unit"], "n_gpus": world, "steps": args.steps,
+            "warmup": args.warmup, "ms_per_step": r["ms_per_step"], "higher_is_better": r["higher_is_better"],
+            "scaling": r["scaling"], "vs_baseline": None, "dtype": r["dtype"], "data": "synthetic (seeded)",
+            "config": r["config"], "impl": "reference",
+            "cpu_baseline": {"value": r["value"], "unit": r["unit"], "cores": cores, "kind": kind, "sample": sample},
+            "e2e": {"value": r["value"], "unit": r["unit"], "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
+    return line
 
 
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
-    ap.add_argument("--steps", type=int, default=10)
+    ap.add_argument("--steps", type=int, default=None, help="timed steps (default: 10 for dit, 50 otherwise; "
+                                                            "3 for --impl reference)")
     ap.add_argument("--warmup", type=int, default=3)
-    ap.add_argument("--workload", default="gemm", choices=sorted(WORKLOADS))
+    ap.add_argument("--workload", default="dit", choices=sorted(WORKLOADS))
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
     ap.add_argument("--no-cpu-baseline", action="store_true")
     args = ap.parse_args()
     args.warmup = max(args.warmup, 3)
-    world, rank, local = init_dist(args)
-    if args.impl == "reference":
-        line = run_reference(args, world, rank)
-        if line is not None:
+    if args.steps is None:
+        args.steps = 3 if args.impl == "reference" else (10 if args.workload == "dit" else 50)
+    world, rank, local = init_dist()
+    try:
+        if args.impl == "reference":
+            line = run_reference(args, world, rank)
+            if line is not None:
+                print(json.dumps(line), flush=True)
+            return
+        pk = peaks()
+        stream = torch.cuda.current_stream()
+        props = torch.cuda.get_device_properties(torch.cuda.current_device())
+        bus = getattr(props, "pci_bus_id", None)
+        sampler = ClockSampler([f"{getattr(props, 'pci_domain_id', 0):08x}:{bus:02x}:00.0"] if bus is not None else [],
+                               enabled=(rank == 0))
+        res = WORKLOADS[args.workload][0](args, world, rank, stream, pk, sampler)
+        cpu_fn = res.pop("cpu_baseline_fn", None)
+        if rank == 0:
+            line = {"metric": res["metric"], "value": res["value"], "unit": res["unit"], "n_gpus": world,
+                    "steps": args.steps, "warmup": args.warmup, "ms_per_step": res["ms_per_step"],
+                    "higher_is_better": res["higher_is_better"], "scaling": res["scaling"], "vs_baseline": None,
+                    "dtype": res["dtype"], "data": "synthetic (seeded)", "config": res["config"], "e2e": res["e2e"],
+                    "roofline": res["roofline"], "gpu_launches": res["gpu_launches"], "clocks": sampler.result}
+            if world == 1 and cpu_fn is not None and not args.no_cpu_baseline:
+                line["cpu_baseline"] = cpu_fn()
             print(json.dumps(line), flush=True)
+    finally:
         if world > 1:
             dist.destroy_process_group()
-        return
-    pk = peaks()
-    stream = torch.cuda.current_stream()
-    props = torch.cuda.get_device_properties(torch.cuda.current_device())
-    bus = getattr(props, "pci_bus_id", None)
-    sampler = ClockSampler([f"{getattr(props, 'pci_domain_id', 0):08x}:{bus:02x}:00.0"] if bus is not None else [])
-    if rank == 0:
-        sampler.start()
-    res = WORKLOADS[args.workload](args, world, rank, stream, pk)
-    clocks = sampler.stop() if rank == 0 else None
-    cpu_fn = res.pop("cpu_baseline_fn", None)
-    if rank == 0:
-        line = {"metric": res["metric"], "value": res["value"], "unit": res["unit"], "n_gpus": world,
-                "steps": args.steps, "warmup": args.warmup, "ms_per_step": res["ms_per_step"],
-                "higher_is_better": res["higher_is_better"], "scaling": res["scaling"], "vs_baseline": None,
-                "dtype": res["dtype"], "data": "synthetic (seeded)", "config": res["config"], "e2e": res["e2e"],
-                "roofline": res["roofline"], "gpu_launches": res["gpu_launches"], "clocks": clocks}
-        if world == 1 and cpu_fn is not None and not args.no_cpu_baseline:
-            line["cpu_baseline"] = cpu_fn()
-        print(json.dumps(line), flush=True)
-    if world > 1:
-        dist.destroy_process_group()
 
 
 if __name__ == "__main__":

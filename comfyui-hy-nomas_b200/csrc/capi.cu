@@ -339,4 +339,17 @@ int hn_quantize_kv(const void *x, int64_t rows, int64_t D, int8_t *q, float *s, 
     return hn_quant_act(x, D, HN_DTYPE_BF16, rows, D, HN_KIND_INT8, D == 128 ? 0 : 1, q, D, s, 1, 1, stream);
 }
 
+int hn_quantize_fp8_block(const void *w, int w_dtype, int64_t N, int64_t K, void *q, float *s, void *stream) {
+    REQUIRE(w && q && s, HN_ERR_ARG, "hn_quantize_fp8_block: null pointer");
+    REQUIRE(w_dtype == HN_DTYPE_FP32 || w_dtype == HN_DTYPE_BF16, HN_ERR_ARG,
+            "hn_quantize_fp8_block: w_dtype %d not fp32/bf16", w_dtype);
+    REQUIRE(N >= 0 && K >= 0 && N % 128 == 0 && K % 128 == 0, HN_ERR_SHAPE,
+            "hn_quantize_fp8_block: need N %% 128 == 0 and K %% 128 == 0 (N=%lld K=%lld)", (long long)N, (long long)K);
+    REQUIRE(N / 128 <= 65535 && K / 128 <= 0x7fffffffLL, HN_ERR_SHAPE, "hn_quantize_fp8_block: too large");
+    REQUIRE(al16(w) && al16(q) && (reinterpret_cast<uintptr_t>(s) & 3) == 0, HN_ERR_ALIGN, "hn_quantize_fp8_block: misaligned buffer");
+    if (N == 0 || K == 0) return HN_OK;
+    CHECK_ARCH();
+    return launched(launch_quant_fp8_block(w, w_dtype, N, K, q, s, (cudaStream_t)stream), "hn_quantize_fp8_block launch");
+}
+
 } // extern "C"

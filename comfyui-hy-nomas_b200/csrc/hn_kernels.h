@@ -12,6 +12,9 @@ int num_sms();  // SM count of the current device (cached per device)
 cudaError_t launch_quant_act(const void *x, int64_t ldx, int x_dtype, int64_t M, int64_t K, int kind, int per_row,
                              void *q, int64_t ldq, float *s, int64_t s_rs, int64_t s_gs, cudaStream_t st);
 
+cudaError_t launch_quant_fp8_block(const void *w, int w_dtype, int64_t N, int64_t K, void *q, float *s,
+                                   cudaStream_t st);
+
 // mode 0: adaln (bf16 y), 1: adaln_quant, 2: gated residual + adaln_quant
 cudaError_t launch_ln_row(int mode, const void *x, const void *y, const void *gate, const void *shift,
                           const void *scale, int64_t B, int64_t L, int64_t D, float eps, void *out_bf16, int8_t *q,

@@ -138,4 +138,57 @@ cudaError_t launch_quant_act(const void *x, int64_t ldx, int x_dtype, int64_t M,
     }
 }
 
+// ---------------------------------------------------------------------------------------------------
+// FP8 weight quantization per 128x128 block (hy_nomas/pixelumm.py:77-82): s = max(absmax, 1e-4) / 448 and
+// codes e4m3(w / s). One CTA per block, 8 warps x 16 rows; lane l holds columns [4l, 4l+4) of its rows, so
+// the block stays in registers between the absmax and the conversion (one HBM read, coalesced rows).
+template <typename TIn>
+__global__ void __launch_bounds__(256) k_quant_fp8_block(const TIn *__restrict__ w, int64_t K, uint8_t *__restrict__ q,
+                                                         float *__restrict__ s) {
+    __shared__ float red[8];
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const int64_t row0 = (int64_t)blockIdx.y * 128 + warp * 16;
+    const int64_t col = (int64_t)blockIdx.x * 128 + lane * 4;
+    float v[16][4];
+    float peak = 0.0f;
+#pragma unroll
+    for (int r = 0; r < 16; ++r) {
+        const TIn *src = w + (row0 + r) * K + col;
+        if constexpr (sizeof(TIn) == 4) {
+            const float4 f = *reinterpret_cast<const float4 *>(src);
+            v[r][0] = f.x; v[r][1] = f.y; v[r][2] = f.z; v[r][3] = f.w;
+        } else {
+            const uint2 u = *reinterpret_cast<const uint2 *>(src);
+            v[r][0] = bf16_lo(u.x); v[r][1] = bf16_hi(u.x); v[r][2] = bf16_lo(u.y); v[r][3] = bf16_hi(u.y);
+        }
+#pragma unroll
+        for (int j = 0; j < 4; ++j) peak = fmaxf(peak, fabsf(v[r][j]));
+    }
+    peak = warp_max_xor(peak, 32);
+    if (lane == 0) red[warp] = peak;
+    __syncthreads();
+    peak = red[0];
+#pragma unroll
+    for (int i = 1; i < 8; ++i) peak = fmaxf(peak, red[i]);
+    const float sc = __fdiv_rn(fmaxf(peak, 1e-4f), 448.0f);
+#pragma unroll
+    for (int r = 0; r < 16; ++r) {
+        const uint32_t lo = pack2_e4m3(__fdiv_rn(v[r][0], sc), __fdiv_rn(v[r][1], sc));
+        const uint32_t hi = pack2_e4m3(__fdiv_rn(v[r][2], sc), __fdiv_rn(v[r][3], sc));
+        *reinterpret_cast<uint32_t *>(q + (row0 + r) * K + col) = lo | (hi << 16);
+    }
+    if (threadIdx.x == 0) s[(int64_t)blockIdx.y * gridDim.x + blockIdx.x] = sc;
+}
+
+cudaError_t launch_quant_fp8_block(const void *w, int w_dtype, int64_t N, int64_t K, void *q, float *s,
+                                   cudaStream_t st) {
+    dim3 grid((unsigned)(K / 128), (unsigned)(N / 128));
+    if (w_dtype == 2)
+        k_quant_fp8_block<float><<<grid, 256, 0, st>>>(static_cast<const float *>(w), K, static_cast<uint8_t *>(q), s);
+    else
+        k_quant_fp8_block<__nv_bfloat16><<<grid, 256, 0, st>>>(static_cast<const __nv_bfloat16 *>(w), K,
+                                                               static_cast<uint8_t *>(q), s);
+    return cudaGetLastError();
+}
+
 } // namespace hn

@@ -39,6 +39,7 @@ SIGNATURES = {
     "hn_gated_residual_adaln_quant": [_V, _V, _V, _V, _V, _I64, _I64, _I64, _F32, _V, _V, _V, _I64, _I64, _V],
     "hn_pixelumm_qk": [_V, _I64, _V, _V, _V, _V, _I64, _I64, _I64, _F32, _V, _V],
     "hn_quantize_kv": [_V, _I64, _I64, _V, _V, _V],
+    "hn_quantize_fp8_block": [_V, _I32, _I64, _I64, _V, _V, _V],
 }
 
 
@@ -63,7 +64,12 @@ def last_error():
     return lib.hn_last_error().decode(errors="replace")
 
 
+calls = 0   # library calls made by this process (each launches at most one kernel); read by bench.py
+
+
 def check(rc, what):
+    global calls
+    calls += 1
     if rc != HN_OK:
         raise RuntimeError(f"{what} failed with {STATUS.get(rc, rc)}: {last_error()}")
 

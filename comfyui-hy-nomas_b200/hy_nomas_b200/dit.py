@@ -1,0 +1,207 @@
+"""Synthetic Hy-Nomas-style DiT on the B200 kernels: one block and the multi-block denoise step.
+
+The block is the image stream of the reference's `DoubleStreamBlock` on its fused int8 path
+(hy_nomas/model.py:246-286, with `MLP.forward_int8` model.py:79-86 and `Modulate` model.py:303-311):
+
+    shift1, scale1, gate1, shift2, scale2, gate2 = Modulate(vec)          int8 linear of silu(vec)
+    qa, sa  = adaln_quant(x, shift1, scale1)                              LN + modulate + int8 quant
+    q, k, v = block_gemm(qa, sa, W_q / W_k / W_v)                         one GEMM for q|k, one for v
+    q, k    = qk_norm_rope(q), qk_norm_rope(k)                            one launch for both
+    attn    = scaled_dot_product_attention(q, K, V)                       torch SDPA, unchanged
+    x       = gated_residual(x, proj(attn), gate1)                        proj = quantize + GEMM
+    qh, sh  = block_gemm(adaln_quant(x, shift2, scale2), W_fc1, "gelu_quant")
+    x       = gated_residual(x, block_gemm(qh, sh, W_fc2), gate2)
+
+Two launches are merged where the result is identical: q and k come from one GEMM over the concatenated
+weights (every output column is computed independently, so the values do not change), and the first
+residual is fused with the second LayerNorm/quantization (`gated_residual_adaln_quant`, bit-identical to the
+two kernels in sequence). Under sequence parallelism (`SequenceParallel`) each rank runs the block on its own
+tokens and K/V are all-gathered; the k and v kernels write straight into the rank's slice of the gather
+buffers.
+
+Weights are random and seeded (there is no checkpoint offline): int8 codes uniform in [-127, 127] with
+per-output-channel fp32 scales, scaled so each linear preserves the activations' variance, and bf16 biases
+N(0, 0.02). The RMSNorm weights are ones, as `RMSNorm.__init__` creates them (model.py:95).
+
+`ops` is the compute seam: the default `CudaOps` calls libhynomas_b200.so for every op except attention;
+host-side tests pass a CPU object with the same methods to check the orchestration (shards, gathers) on gloo.
+"""
+import math
+from dataclasses import dataclass
+
+import torch
+import torch.nn.functional as F
+
+from . import fused, kernels
+from .sequence_parallel import SequenceParallel
+
+
+@dataclass(frozen=True)
+class DiTConfig:
+    hidden: int = 4096
+    heads: int = 32
+    mlp_ratio: int = 4
+    blocks: int = 40
+    rope_dims: tuple = (16, 56, 56)
+    theta: float = 10000.0
+    grid: tuple = (23, 22, 40)   # latent frames x patch rows x patch columns = 20240 tokens
+
+    @property
+    def head_dim(self):
+        return self.hidden // self.heads
+
+    @property
+    def tokens(self):
+        t, h, w = self.grid
+        return t * h * w
+
+
+@dataclass
+class QLinear:
+    """An int8 linear: codes [N, K], per-output-channel fp32 scales [N], bf16 bias [N]."""
+    q: torch.Tensor
+    s: torch.Tensor
+    bias: torch.Tensor
+
+
+@dataclass
+class BlockWeights:
+    mod: QLinear     # [6D, D]
+    qk: QLinear      # [2D, D]: the q rows then the k rows
+    v: QLinear       # [D, D]
+    proj: QLinear    # [D, D]
+    fc1: QLinear     # [mlp, D]
+    fc2: QLinear     # [D, mlp]
+    q_norm: torch.Tensor   # bf16 [head_dim]
+    k_norm: torch.Tensor
+
+
+_CODE_STD = math.sqrt((255.0 ** 2 - 1.0) / 12.0)   # std of an integer uniform on [-127, 127]
+
+
+def make_qlinear(n, k, gen, device, gain=1.0):
+    q = torch.randint(-127, 128, (n, k), generator=gen, device=device, dtype=torch.int8)
+    s = (torch.rand(n, generator=gen, device=device) + 0.5) * (gain / (_CODE_STD * math.sqrt(k)))
+    bias = (torch.randn(n, generator=gen, device=device) * 0.02).to(torch.bfloat16)
+    return QLinear(q, s.float().contiguous(), bias)
+
+
+def make_block_weights(cfg, gen, device):
+    d, mlp = cfg.hidden, cfg.hidden * cfg.mlp_ratio
+    ones = torch.ones(cfg.head_dim, dtype=torch.bfloat16, device=device)
+    return BlockWeights(mod=make_qlinear(6 * d, d, gen, device, gain=0.15), qk=make_qlinear(2 * d, d, gen, device),
+                        v=make_qlinear(d, d, gen, device), proj=make_qlinear(d, d, gen, device),
+                        fc1=make_qlinear(mlp, d, gen, device), fc2=make_qlinear(d, mlp, gen, device),
+                        q_norm=ones, k_norm=ones.clone())
+
+
+def rope_freqs(rope_dims, theta, t, h, w, t_offset=0, device=None):
+    """3-D RoPE tables (cos, sin) fp32 [t*h*w, sum(rope_dims)] for the grid [t_offset, t_offset+t) x [0, h) x
+    [0, w): per axis fp32 positions from a linspace, fp32 frequencies theta^(-2i/dim), cos/sin repeated per
+    interleaved pair (hy_nomas/model.py:114-128). Built once per shape; not on the per-step path."""
+    axes = [torch.linspace(s, s + n, n + 1, dtype=torch.float32, device=device)[:n]
+            for s, n in ((t_offset, t), (0, h), (0, w))]
+    grid = torch.meshgrid(*axes, indexing="ij")
+    cos, sin = [], []
+    for dim, pos in zip(rope_dims, grid):
+        freqs = 1.0 / (theta ** (torch.arange(0, dim, 2, device=device)[: dim // 2].float() / dim))
+        angles = torch.outer(pos.reshape(-1), freqs)
+        cos.append(angles.cos().repeat_interleave(2, dim=1))
+        sin.append(angles.sin().repeat_interleave(2, dim=1))
+    return torch.cat(cos, dim=1).contiguous(), torch.cat(sin, dim=1).contiguous()
+
+
+class CudaOps:
+    """The block's ops on libhynomas_b200.so (attention: torch SDPA, as the reference's pytorch backend)."""
+
+    @staticmethod
+    def linear(x2, w):
+        return kernels.block_linear(x2, w.q, w.s, w.bias)
+
+    @staticmethod
+    def adaln_quant(x, shift, scale):
+        return kernels.adaln_quant(x, shift, scale)
+
+    @staticmethod
+    def gemm(qa, sa, w, epilogue=None, out=None):
+        return kernels.block_gemm(qa, sa, w.q, w.s, w.bias, epilogue=epilogue, out=out)
+
+    @staticmethod
+    def qk_norm_rope2(q, k, wq, wk, rope, out):
+        return fused.qk_norm_rope2(q, k, wq, wk, rope, out=out)
+
+    @staticmethod
+    def gated_residual_adaln_quant(x, y, gate, shift, scale):
+        return fused.gated_residual_adaln_quant(x, y, gate, shift, scale)
+
+    @staticmethod
+    def gated_residual(x, y, gate):
+        return fused.gated_residual(x, y, gate)
+
+    @staticmethod
+    def silu(v):
+        return F.silu(v)
+
+    @staticmethod
+    def attention(q, k, v):
+        """q [B, Lq, H, D], k/v [B, Lk, H, D] -> [B, Lq, H, D] (hy_nomas/model.py:145-151, pytorch backend)."""
+        return F.scaled_dot_product_attention(q.transpose(1, 2), k.transpose(1, 2), v.transpose(1, 2)).transpose(1, 2)
+
+
+def block_forward(cfg, w, x, vec, rope, sp, ops=CudaOps, trace=None):
+    """One block on this rank's tokens. x bf16 [B, l, D] (l = the rank's tokens), vec bf16 [B, D], rope =
+    this rank's rows of the (cos, sin) tables. Returns the block output [B, l, D] bf16. `trace`, when a dict,
+    receives the block's intermediates (for parity tests)."""
+    b, l, d = x.shape
+    h, hd = cfg.heads, cfg.head_dim
+    act = ops.silu(vec)
+    mods = ops.linear(act, w.mod)
+    shift1, scale1, gate1, shift2, scale2, gate2 = mods.chunk(6, dim=-1)
+    qa, sa = ops.adaln_quant(x, shift1, scale1)
+    qk = ops.gemm(qa, sa, w.qk)                                       # [B*l, 2D]
+    q_in = qk[:, :d].view(b, l, h, hd)
+    k_in = qk[:, d:].view(b, l, h, hd)
+    k_full, v_full, k_mine, v_mine = sp.kv_buffers(b, l, h, hd, x.dtype, x.device)
+    q_out = torch.empty((b, l, h, hd), dtype=x.dtype, device=x.device)
+    ops.qk_norm_rope2(q_in, k_in, w.q_norm, w.k_norm, rope, out=(q_out, k_mine))
+    gather_k = sp.all_gather_async(k_full, k_mine)
+    ops.gemm(qa, sa, w.v, out=v_mine.view(b * l, d))
+    gather_v = sp.all_gather_async(v_full, v_mine)
+    sp.wait(gather_k, gather_v)
+    attn = ops.attention(q_out, k_full, v_full).reshape(b * l, d)
+    proj = ops.linear(attn, w.proj).view(b, l, d)
+    x1, qa2, sa2 = ops.gated_residual_adaln_quant(x, proj, gate1, shift2, scale2)
+    qh, sh = ops.gemm(qa2, sa2, w.fc1, epilogue="gelu_quant")
+    y = ops.gemm(qh, sh, w.fc2).view(b, l, d)
+    out = ops.gated_residual(x1, y, gate2)
+    if trace is not None:
+        trace.update(act=act, mods=mods, qa=qa, sa=sa, qk=qk, q=q_out, k_full=k_full.clone(), v_full=v_full.clone(),
+                     attn=attn, proj=proj, x1=x1, qa2=qa2, sa2=sa2, qh=qh, sh=sh, y=y, out=out)
+    return out
+
+
+class SyntheticDiT:
+    """`cfg.blocks` random-init blocks over a `cfg.grid` token sequence, sequence-parallel over `sp`'s ranks.
+
+    Every rank builds the same weights (same seed; weights are replicated) and its own rows of the RoPE tables.
+    `forward(x, vec)` takes this rank's tokens [B, l, D] and returns them after all blocks."""
+
+    def __init__(self, cfg=DiTConfig(), device="cuda", seed=0, sp=None, ops=CudaOps):
+        self.cfg = cfg
+        self.device = torch.device(device)
+        self.sp = sp or SequenceParallel()
+        self.ops = ops
+        gen = torch.Generator(device=self.device).manual_seed(seed)
+        self.blocks = [make_block_weights(cfg, gen, self.device) for _ in range(cfg.blocks)]
+        cos, sin = rope_freqs(cfg.rope_dims, cfg.theta, *cfg.grid, device=self.device)
+        lo, hi = self.sp.shard(cfg.tokens)
+        self.rope = (cos[lo:hi].contiguous(), sin[lo:hi].contiguous())
+        self.token_range = (lo, hi)
+
+    def forward(self, x, vec, trace=None):
+        for i, w in enumerate(self.blocks):
+            x = block_forward(self.cfg, w, x, vec, self.rope, self.sp, self.ops,
+                              trace=trace if (trace is not None and i == len(self.blocks) - 1) else None)
+        return x
+
+    __call__ = forward

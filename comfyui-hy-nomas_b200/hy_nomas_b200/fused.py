@@ -79,16 +79,23 @@ def qk_norm_rope(x, weight, rope=None, eps=1e-6):
     return y
 
 
-def qk_norm_rope2(q, k, weight_q, weight_k, rope=None, eps=1e-6):
-    """`qk_norm_rope` of q and k (same shape and token stride) in one launch -> (q_out, k_out)."""
+def qk_norm_rope2(q, k, weight_q, weight_k, rope=None, eps=1e-6, out=None):
+    """`qk_norm_rope` of q and k (same shape and token stride) in one launch -> (q_out, k_out). `out`: optional
+    caller-owned contiguous bf16 [B, L, H, D] pair to write into (e.g. a rank's slice of an all-gather buffer)."""
     _lib.require_cuda(q, k, weight_q, weight_k)
     _bf16(q, k)
     b, l, h, d = q.shape
     q, k = _qk_input(q), _qk_input(k)
     if q.stride(1) != k.stride(1):
         q, k = q.contiguous(), k.contiguous()
-    yq = torch.empty((b, l, h, d), device=q.device, dtype=torch.bfloat16)
-    yk = torch.empty_like(yq)
+    if out is None:
+        yq = torch.empty((b, l, h, d), device=q.device, dtype=torch.bfloat16)
+        yk = torch.empty_like(yq)
+    else:
+        yq, yk = out
+        for y in (yq, yk):
+            if y.shape != (b, l, h, d) or y.dtype != torch.bfloat16 or not y.is_contiguous() or y.device != q.device:
+                raise ValueError(f"qk_norm_rope2: out tensors must be contiguous bf16 [{b}, {l}, {h}, {d}]")
     wq = weight_q.to(torch.bfloat16).contiguous()
     wk = weight_k.to(torch.bfloat16).contiguous()
     cos, sin = _rope_tables(rope, q.device)

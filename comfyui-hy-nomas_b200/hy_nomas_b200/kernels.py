@@ -62,11 +62,14 @@ def _scale_mode(s, rows, k, weight):
     raise ValueError(f"scale shape {tuple(s.shape)} is none of [{rows}, {g}], [{rows}], [{(rows + 127) // 128}, {g}]")
 
 
-def block_gemm(qa, sa, qw, sw, bias=None, out_dtype=torch.bfloat16, kind="int8", epilogue=None):
+def block_gemm(qa, sa, qw, sw, bias=None, out_dtype=torch.bfloat16, kind="int8", epilogue=None, out=None):
     """Block-scaled GEMM on quantized activations (hy_nomas/kernels.py:152-170). With epilogue "gelu_quant"
     returns (int8 [M, N], scales [M, N / 128]) ready for the next int8 linear; otherwise [M, N] in
     `out_dtype` (bf16, fp16, fp32; torch.int32 gives the raw int32 accumulator when both scales are per
-    row and there is no bias)."""
+    row and there is no bias).
+
+    `out` (not in the reference): a caller-owned [M, N] destination with unit column stride (rows may be
+    strided, e.g. a slice of a larger buffer), written instead of a fresh tensor; epilogues None and "gelu"."""
     _lib.require_cuda(qa, sa, qw, sw, bias)
     m, k = qa.shape
     n = qw.shape[0]
@@ -84,10 +87,17 @@ def block_gemm(qa, sa, qw, sw, bias=None, out_dtype=torch.bfloat16, kind="int8",
     if bias is not None and (bias.stride(0) != 1 or bias.data_ptr() % 16):
         bias = bias.contiguous()
     if mode == 2:
+        if out is not None:
+            raise ValueError("block_gemm: `out` is not supported with epilogue 'gelu_quant'")
         out = torch.empty((m, n), device=qa.device, dtype=torch.int8)
         qs, qrs, qgs = _lib.group_scales(m, n // GROUP, qa.device)
     else:
-        out = torch.empty((m, n), device=qa.device, dtype=out_dtype if mode == 0 else torch.bfloat16)
+        want = out_dtype if mode == 0 else torch.bfloat16
+        if out is None:
+            out = torch.empty((m, n), device=qa.device, dtype=want)
+        elif out.shape != (m, n) or out.dtype != want or out.stride(1) != 1 or out.device != qa.device:
+            raise ValueError(f"block_gemm: out must be a {want} [{m}, {n}] tensor with unit column stride on "
+                             f"{qa.device}")
         qs, qrs, qgs = None, 0, 0
     sa_rs, sa_gs = _lib.scale_strides(sa)
     sw_rs, sw_gs = _lib.scale_strides(sw)

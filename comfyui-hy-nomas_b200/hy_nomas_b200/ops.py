@@ -1,9 +1,12 @@
-"""Tencent's per-row x 128-group int8 weight layout - the drop-in for the arithmetic of hy_nomas/ops.py.
+"""Weight layouts - the drop-in for the arithmetic of hy_nomas/ops.py (Tencent's per-row x 128-group int8)
+and of the FP8 128 x 128 block layout of hy_nomas/pixelumm.py.
 
 `quantize_g128` runs the activation quantizer kernel of libhynomas_b200.so on the weight (the same
 absmax/127, round-half-away arithmetic: hy_nomas/ops.py:41-52) and needs a CUDA tensor. `dequantize_g128`
 is the reference's plain tensor expression (hy_nomas/ops.py:55-62), used by block_linear for shapes the
-GEMM does not take (K % 128 != 0). The ComfyUI layout registration and the Linear module of the reference
+GEMM does not take (K % 128 != 0). `quantize_fp8_block` runs the 128 x 128 block e4m3 quantizer
+(hy_nomas/pixelumm.py:77-82); `fp8_block_linear` is the FP8 decoder linear's dispatch (pixelumm.py:147-155),
+taking the [N/128, K/128] block scales directly instead of expanding them per row on every call. The ComfyUI layout registration and the Linear module of the reference
 file are ComfyUI wiring, not part of this path.
 """
 import torch
@@ -40,3 +43,31 @@ def dequantize_g128(qdata, scale, dtype=torch.bfloat16):
     else:
         weight = qdata.float() * scale.repeat_interleave(GROUP, dim=1)[:, :k]
     return weight.to(dtype)
+
+
+def quantize_fp8_block(weight):
+    """fp32/bf16 [N, K] (N, K multiples of 128) -> (float8_e4m3fn [N, K], fp32 block scales [N/128, K/128])."""
+    _lib.require_cuda(weight)
+    n, k = weight.shape
+    w = weight if weight.dtype in (torch.float32, torch.bfloat16) else weight.float()
+    w = w.contiguous()
+    q = torch.empty((n, k), device=w.device, dtype=torch.float8_e4m3fn)
+    s = torch.empty((n // 128, k // 128), device=w.device, dtype=torch.float32)
+    rc = _lib.lib.hn_quantize_fp8_block(_lib.ptr(w), _lib.DTYPE[w.dtype], n, k, _lib.ptr(q), _lib.ptr(s),
+                                        _lib.stream_of(w))
+    _lib.check(rc, "quantize_fp8_block")
+    return q, s
+
+
+def dequantize_fp8_block(qdata, scale, dtype=torch.bfloat16):
+    """fp32 product per 128 x 128 block, one cast to `dtype` (hy_nomas/pixelumm.py:60-63)."""
+    n, k = qdata.shape
+    w = qdata.float().view(n // 128, 128, k // 128, 128) * scale[:, None, :, None]
+    return w.view(n, k).to(dtype)
+
+
+def fp8_block_linear(x, qdata, scale, bias=None):
+    """The FP8 decoder linear (hy_nomas/pixelumm.py:147-155): e4m3 1 x 128 activations against 128 x 128 block
+    weights on the tensor cores, output in x's dtype."""
+    from .kernels import block_linear
+    return block_linear(x, qdata, scale, bias, kind="fp8")

@@ -1,0 +1,62 @@
+"""Sequence parallelism for the DiT step: each rank owns a contiguous token range, weights are replicated, and
+the only exchange is an all-gather of every block's K and V (after QK-norm + RoPE) so each rank's queries
+attend over the whole sequence.
+
+The reference runs one GPU (`sp_size: 1`, docs/upstream/single_gpu_low_mem_inference.yaml:22-23); this module
+is the B200 build's partition of the same block: every per-token op (LayerNorm, quantizers, the linears,
+QK-norm, the residuals) runs on the rank's own rows with no communication, and attention reads the gathered
+K/V. The gathers are issued asynchronously (NCCL on its own stream, or gloo on CPU for host-side tests), so
+K's gather overlaps the V projection.
+
+Rank r owns tokens [r * L / P, (r + 1) * L / P); L must divide evenly (20240 does for P = 1, 2, 4, 8).
+The gather buffers are rank-major, so with batch 1 a rank's K/V rows are one contiguous slice that its own
+kernels write in place and that the all-gather uses as its input.
+"""
+import torch
+import torch.distributed as dist
+
+
+class SequenceParallel:
+    def __init__(self, group=None):
+        self.group = group
+        if dist.is_available() and dist.is_initialized():
+            self.world = dist.get_world_size(group)
+            self.rank = dist.get_rank(group)
+        else:
+            self.world, self.rank = 1, 0
+        self._bufs = {}
+
+    def shard(self, length):
+        """(start, stop) of this rank's tokens in a sequence of `length`."""
+        if length % self.world:
+            raise ValueError(f"sequence length {length} does not split evenly over {self.world} ranks")
+        per = length // self.world
+        return self.rank * per, (self.rank + 1) * per
+
+    def kv_buffers(self, batch, local, heads, head_dim, dtype, device):
+        """Full-sequence K and V buffers [batch, local * world, heads, head_dim] and this rank's slice of each
+        ([batch, local, heads, head_dim], contiguous). Reused across blocks and steps."""
+        if self.world > 1 and batch != 1:
+            raise ValueError("sequence parallelism takes batch 1 (the denoise step's layout)")
+        key = (batch, local, heads, head_dim, dtype, str(device))
+        if key not in self._bufs:
+            total = local * self.world
+            k_full = torch.empty((batch, total, heads, head_dim), dtype=dtype, device=device)
+            v_full = torch.empty_like(k_full)
+            lo = self.rank * local
+            self._bufs[key] = (k_full, v_full, k_full[:, lo:lo + local], v_full[:, lo:lo + local])
+        return self._bufs[key]
+
+    def all_gather_async(self, full, mine):
+        """Start filling `full` with every rank's `mine` (a slice of `full`); returns a handle for `wait`."""
+        if self.world == 1:
+            return None
+        # flat views: the rank-major buffer is `world` equal chunks of the rank slices (NCCL and gloo agree)
+        return dist.all_gather_into_tensor(full.view(-1), mine.view(-1), group=self.group, async_op=True)
+
+    @staticmethod
+    def wait(*handles):
+        """Make the current stream wait for the gathers (device-side; the host does not block)."""
+        for h in handles:
+            if h is not None:
+                h.wait()

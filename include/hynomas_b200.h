@@ -195,6 +195,14 @@ int hn_pixelumm_qk(const void *x, int64_t row_stride, const void *weight_t, cons
  */
 int hn_quantize_kv(const void *x, int64_t rows, int64_t D, int8_t *q, float *s, void *stream);
 
+/*
+ * FP8 weight quantizer per 128 x 128 block (load time of the FP8 decoder linears).
+ * Replaces hy_nomas/pixelumm.py:77-82 (NomasFP8Block128Layout.quantize). w [N, K] contiguous fp32 or bf16
+ * (w_dtype), N % 128 == 0, K % 128 == 0 -> q [N, K] e4m3 bytes = e4m3(w / s) (nearest even), s [N/128, K/128]
+ * fp32 row-major = max(absmax of the block, 1e-4) / 448.
+ */
+int hn_quantize_fp8_block(const void *w, int w_dtype, int64_t N, int64_t K, void *q, float *s, void *stream);
+
 #if defined(__GNUC__)
 #pragma GCC visibility pop
 #endif

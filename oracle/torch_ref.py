@@ -15,6 +15,7 @@ them on the host cores as the CPU baseline. Nothing in the product imports this 
   int8_linear_cpu   hy_nomas/ops.py:175-176 (dequantize + F.linear, the non-CUDA branch)
   fp8_block_*       hy_nomas/pixelumm.py:60-63, 77-82, 154-155
   quantize_kv       hy_nomas/world.py:83-90
+  dit_block_cpu     hy_nomas/model.py:246-286 (DoubleStreamBlock image stream, the non-fused branch)
 """
 import torch
 import torch.nn.functional as F
@@ -111,3 +112,36 @@ def quantize_kv(x):
     scaled = xf / scale
     rounded = torch.where(scaled >= 0, torch.floor(scaled + 0.5), torch.ceil(scaled - 0.5))
     return rounded.clamp_(-127, 127).to(torch.int8), scale
+
+
+def _linear_per_channel(x, ql):
+    """An int8 linear with per-output-channel scales [N], broadcast to the reference's [N, K/128] layout."""
+    n, k = ql.q.shape
+    return int8_linear_cpu(x, ql.q, ql.s[:, None].expand(n, k // GROUP), ql.bias)
+
+
+def dit_block_cpu(x, vec, w, rope, heads, timings=None):
+    """One block on the reference's CPU path: every linear dequantizes its int8 weight and runs F.linear in
+    bf16 (ops.py:175-176), norms/modulation/RoPE are the torch expressions above, attention is SDPA.
+    `w` has the fields of hy_nomas_b200.dit.BlockWeights (q|k rows stacked in `qk`). `timings`, when a dict,
+    gets the attention's seconds under "attention"."""
+    import time
+    b, n, d = x.shape
+    mods = _linear_per_channel(F.silu(vec), w.mod)
+    shift1, scale1, gate1, shift2, scale2, gate2 = mods.chunk(6, dim=-1)
+    x_mod = modulate(layer_norm(x), shift1, scale1).to(x.dtype)
+    qk = _linear_per_channel(x_mod, w.qk)
+    q = qk[..., :d].reshape(b, n, heads, -1)
+    k = qk[..., d:].reshape(b, n, heads, -1)
+    v = _linear_per_channel(x_mod, w.v).view(b, n, heads, -1)
+    q = rms_norm(q, w.q_norm).to(v)
+    k = rms_norm(k, w.k_norm).to(v)
+    q, k = apply_rope(q, *rope), apply_rope(k, *rope)
+    t0 = time.perf_counter()
+    attn = F.scaled_dot_product_attention(q.transpose(1, 2), k.transpose(1, 2), v.transpose(1, 2)).transpose(1, 2)
+    if timings is not None:
+        timings["attention"] = timings.get("attention", 0.0) + time.perf_counter() - t0
+    x = x + _linear_per_channel(attn.reshape(b, n, d), w.proj) * gate1.unsqueeze(1)
+    h = _linear_per_channel(modulate(layer_norm(x), shift2, scale2).to(x.dtype), w.fc1)
+    h = F.gelu(h, approximate="tanh")
+    return x + _linear_per_channel(h, w.fc2) * gate2.unsqueeze(1)

@@ -1,0 +1,66 @@
+"""Worker processes for the sequence-parallel tests (importable by spawned children)."""
+import os
+
+import torch
+
+
+def small_config():
+    from hy_nomas_b200.dit import DiTConfig
+    # 2 heads x 128, hidden 256, 2 blocks, a 2 x 3 x 4 grid = 24 tokens (splits over 1, 2, 4 ranks)
+    return DiTConfig(hidden=256, heads=2, mlp_ratio=4, blocks=2, grid=(2, 3, 4))
+
+
+def inputs(cfg, device="cpu"):
+    gen = torch.Generator().manual_seed(11)
+    x = torch.randn(1, cfg.tokens, cfg.hidden, generator=gen).to(torch.bfloat16)
+    vec = torch.randn(1, cfg.hidden, generator=gen).to(torch.bfloat16)
+    return x.to(device), vec.to(device)
+
+
+def run_model(cfg, sp, ops, device):
+    from hy_nomas_b200.dit import SyntheticDiT
+    model = SyntheticDiT(cfg, device=device, seed=3, sp=sp, ops=ops)
+    x, vec = inputs(cfg, device)
+    lo, hi = model.token_range
+    return model(x[:, lo:hi].contiguous(), vec)
+
+
+def gloo_rank(rank, world, port, out_path):
+    import torch.distributed as dist
+    from dit_oracle_ops import OracleOps
+    from hy_nomas_b200.sequence_parallel import SequenceParallel
+    os.environ["MASTER_ADDR"] = "127.0.0.1"
+    os.environ["MASTER_PORT"] = str(port)
+    dist.init_process_group("gloo", rank=rank, world_size=world)
+    try:
+        cfg = small_config()
+        out = run_model(cfg, SequenceParallel(), OracleOps, "cpu")
+        parts = [torch.empty_like(out) for _ in range(world)]
+        dist.all_gather(parts, out)
+        if rank == 0:
+            torch.save(torch.cat(parts, dim=1), out_path)
+    finally:
+        dist.destroy_process_group()
+
+
+def nccl_rank(rank, world, port, out_path):
+    import datetime
+    import torch.distributed as dist
+    from hy_nomas_b200.sequence_parallel import SequenceParallel
+    os.environ["MASTER_ADDR"] = "127.0.0.1"
+    os.environ["MASTER_PORT"] = str(port)
+    os.environ.setdefault("NCCL_NVLS_ENABLE", "0")
+    torch.cuda.set_device(rank)
+    dist.init_process_group("nccl", rank=rank, world_size=world, device_id=torch.device("cuda", rank),
+                            timeout=datetime.timedelta(seconds=60))
+    try:
+        from hy_nomas_b200.dit import CudaOps
+        cfg = small_config()
+        out = run_model(cfg, SequenceParallel(), CudaOps, f"cuda:{rank}")
+        parts = [torch.empty_like(out) for _ in range(world)]
+        dist.all_gather(parts, out)
+        torch.cuda.synchronize()
+        if rank == 0:
+            torch.save(torch.cat(parts, dim=1).cpu(), out_path)
+    finally:
+        dist.destroy_process_group()

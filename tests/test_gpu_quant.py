@@ -78,3 +78,25 @@ def test_quantize_kv(hn, golden, cuda):
     torch.cuda.synchronize()
     assert np.array_equal(q.cpu().numpy().reshape(d["q"].shape), d["q"])
     assert np.array_equal(f32(s).reshape(d["s"].shape), d["s"])
+
+
+def test_quantize_fp8_block_golden(hn, golden, cuda):
+    """pixelumm.NomasFP8Block128Layout.quantize (pixelumm.py:77-82): e4m3 codes and block scales bit-exact
+    with the reference's own output, and the block dequantization (pixelumm.py:60-63)."""
+    d = golden("block_gemm")
+    q, s = hn.ops.quantize_fp8_block(torch.from_numpy(d["w"]).to(cuda))
+    assert np.array_equal(u8(q), d["fp8_qw"]) and np.array_equal(f32(s), d["fp8_sw_block"])
+    deq = hn.ops.dequantize_fp8_block(q, s)
+    assert np.array_equal(deq.cpu().view(torch.int16).numpy().view(np.uint16), d["fp8_deq_w"])
+
+
+@pytest.mark.parametrize("dtype", [torch.float32, torch.bfloat16])
+def test_quantize_fp8_block_random(hn, oracle, cuda, dtype):
+    gen = torch.Generator().manual_seed(21)
+    w = (torch.randn(384, 640, generator=gen) * 0.02)
+    w[5, 7] = 3.0           # a block whose absmax is one outlier
+    w[256:, 512:] = 0.0     # an all-zero block: scale 1e-4 / 448, codes 0
+    w = w.to(dtype)
+    q, s = hn.ops.quantize_fp8_block(w.to(cuda))
+    qr, sr = oracle.quantize_fp8_block(w.float().numpy())
+    assert np.array_equal(u8(q), qr) and np.array_equal(f32(s), sr)
