@@ -2,27 +2,29 @@
 //
 //   y[m, n] = sum_g sa[m, g] * sw[n, g] * dot_g(qa[m, :], qw[n, :])  (+ bias[n]),  g over 128-wide K groups
 //
-// Design: one persistent CTA per SM, 640 threads (5 warpgroups), one K group (128 bytes of K) per pipeline
-// stage, tiles of 128 rows x BN columns.
-//   warps 0, 2  producers: cp.async.bulk.tensor 2-D loads (128B swizzle, no multicast) of the A tile
-//               [128 x 128 B] (warp 0) and the B tile [BN x 128 B] (warp 2) into a ring of shared-memory
-//               stages; one thread's bulk-tensor requests are serviced in order, so two issuing warps
-//               double the operand rate an SM can draw from L2.
-//   warp 3      when the weight scale varies per group: the BN weight scales of each group into a ring.
+// Design: one persistent CTA per SM, one warpgroup of producers/issuer plus NPART epilogue warpgroups,
+// tiles of 128 rows x BN columns, GPS 128-wide K groups per pipeline stage.
+//   warps 0, 2  producers: cp.async.bulk.tensor 3-D loads (box {128 B, rows, GPS groups}, 128B swizzle, no
+//               multicast) of the A tile (warp 0) and the B tile (warp 2) into a ring of shared-memory
+//               stages; one thread's bulk-tensor requests are serviced in order, so two issuing warps and
+//               two groups per request raise the operand rate an SM draws from L2.
+//   warp 3      scale ring: each group's activation scales for the tile's 128 rows (and the weight scales of
+//               its BN columns when they vary per group) into a ring of shared-memory slots - one bulk copy
+//               per group when the scales are group-major, plain loads otherwise.
 //   warp 1      MMA issuer: owns 512 TMEM columns = NBUF accumulators of BN columns; per K group it issues
 //               4 x tcgen05.mma.kind::{i8,f8f6f4} (M=128, N=BN, K=32) and tcgen05.commit's the stage back
-//               to the producer and the accumulator to the epilogue.
-//   warps 4-19  epilogue: warp w owns TMEM lanes 32*(w%4).. (32 output rows) and column quarter (w-4)/4,
-//               i.e. each thread one row x BN/4 columns; four epilogue warps per SM sub-partition hide
-//               the TMEM-load and FMA latencies of one another.
+//               to the producers and the accumulator to the epilogue.
+//   epilogue    warp w (w >= 4) owns TMEM lanes 32*(w%4).. (32 output rows) and column part (w-4)/4, i.e.
+//               each thread one row x BN/NPART columns.
 // Two tile shapes, by how the scales vary along K:
-//   * per-group scales (PMODE 0, 1): BN = 128, NBUF = 4. For every group the epilogue reads the int32 (or
-//     fp32) partial from TMEM, converts it exactly (int32 + 0x4B400000 reinterpreted, minus 1.5 * 2^23:
-//     exact for |p| < 2^22) and folds it into 32 fp32 accumulators per thread with packed f32x2
-//     multiply / FMA, while the tensor core fills the next three accumulators.
-//   * per-row scales on both sides (PMODE 2): BN = 256, NBUF = 2; the tensor core accumulates all of K in
-//     one accumulator and the epilogue streams it out of TMEM in 32-column chunks, overlapped with the
-//     next tile's MMAs.
+//   * per-group scales (PMODE 0, 1): BN = 128, NBUF = 4, GPS = 2, four epilogue warpgroups (640 threads).
+//     For every group the epilogue reads the int32 (or fp32) partial from TMEM, hands the accumulator
+//     back to the tensor core, converts the partial exactly (int32 + 0x4B400000 reinterpreted, minus
+//     1.5 * 2^23: exact for |p| < 2^22) and folds it into 32 fp32 accumulators per thread with packed
+//     f32x2 multiply / FMA, while the tensor core fills the next three accumulators.
+//   * per-row scales on both sides (PMODE 2): BN = 256, NBUF = 2, GPS = 1, two epilogue warpgroups (384
+//     threads); the tensor core accumulates all of K in one accumulator and the epilogue streams it out of
+//     TMEM in 32-column chunks, overlapped with the next tile's MMAs.
 // After the last group: the per-row weight scale when it was factored out, + bias, then the epilogue of
 // kernels.py:123-137 (cast / GELU / GELU + int8 requantization per 128 columns; the column quarters of
 // a quantization group exchange their absmax through shared memory).
