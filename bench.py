@@ -834,6 +834,8 @@ def run_reference(args, world, rank):
     """The reference's CPU path for the same workload and metric, rank 0 only (other ranks do no work)."""
     if rank != 0:
         return None
+    # all of the host's threads (torchrun sets OMP_NUM_THREADS=1 for its workers)
+    torch.set_num_threads(len(os.sched_getaffinity(0)))
     r = WORKLOADS[args.workload][1](args)
     sample, kind, cores = r.pop("sample"), r.pop("kind"), r.pop("cores")
     line = {"metric": r["metric"], "value": r["value"], "unit": r["unit"], "n_gpus": world, "steps": args.steps,

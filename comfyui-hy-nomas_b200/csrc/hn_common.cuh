@@ -107,6 +107,84 @@ __device__ __forceinline__ float gelu_tanh(float x) {
     return __fmul_rn(__fmul_rn(0.5f, x), __fadd_rn(1.0f, __fsub_rn(__fmul_rn(2.0f, sig), 1.0f)));
 }
 
+__device__ __forceinline__ uint32_t smem_addr(const void *p) { return (uint32_t)__cvta_generic_to_shared(p); }
+
+// ---------------------------------------------------------------------------------------------------
+// packed pairs of fp32 (sm_100 f32x2 instructions, explicit rounding: never contracted)
+
+__device__ __forceinline__ uint64_t x2(float lo, float hi) {
+    uint64_t r;
+    asm("mov.b64 %0, {%1, %2};" : "=l"(r) : "f"(lo), "f"(hi));
+    return r;
+}
+__device__ __forceinline__ void x2_split(uint64_t p, float &lo, float &hi) {
+    asm("mov.b64 {%0, %1}, %2;" : "=f"(lo), "=f"(hi) : "l"(p));
+}
+__device__ __forceinline__ uint64_t x2_add(uint64_t a, uint64_t b) {
+    uint64_t r;
+    asm("add.rn.f32x2 %0, %1, %2;" : "=l"(r) : "l"(a), "l"(b));
+    return r;
+}
+__device__ __forceinline__ uint64_t x2_add_rz(uint64_t a, uint64_t b) {
+    uint64_t r;
+    asm("add.rz.f32x2 %0, %1, %2;" : "=l"(r) : "l"(a), "l"(b));
+    return r;
+}
+__device__ __forceinline__ uint64_t x2_mul(uint64_t a, uint64_t b) {
+    uint64_t r;
+    asm("mul.rn.f32x2 %0, %1, %2;" : "=l"(r) : "l"(a), "l"(b));
+    return r;
+}
+__device__ __forceinline__ uint64_t x2_fma(uint64_t a, uint64_t b, uint64_t c) {
+    uint64_t r;
+    asm("fma.rn.f32x2 %0, %1, %2, %3;" : "=l"(r) : "l"(a), "l"(b), "l"(c));
+    return r;
+}
+__device__ __forceinline__ uint64_t x2_splat(float v) { return x2(v, v); }
+// (lo, hi) -> bf16x2 word (lo in the low half), each rounded to nearest even: the reference's _rbf16
+// (kernels.py:67-71) for finite values, as one conversion instruction
+__device__ __forceinline__ uint32_t bf16x2_rn(float lo, float hi) {
+    uint32_t r;
+    asm("cvt.rn.bf16x2.f32 %0, %1, %2;" : "=r"(r) : "f"(hi), "f"(lo));
+    return r;
+}
+
+// Quotient v / s for a bf16 value v and a quantization scale s > 0, correctly rounded, given rs = RN(1/s):
+// q0 = RN(v * rs) is within an ulp of v / s, the remainder v - q0 * s is exact in one fma, and one more fma
+// corrects q0 (Markstein, IBM J. Res. Dev. 34(1), 1990). The remainder underflows for very small s; the
+// callers take the IEEE division when s < 2^-90. An exhaustive check over every bf16 absmax p and every bf16
+// |v| <= p found the int8 codes (round half away of the quotient) identical to those of RN(v / s), for both
+// signs, with s = RN(p / 127); for e4m3 the sign of a zero quotient is restored by the caller.
+// Pairs of quotients with the same s: ns = (-s, -s), rs2 = (rs, rs).
+__device__ __forceinline__ uint64_t x2_quot(uint64_t v, uint64_t ns, uint64_t rs2) {
+    const uint64_t q0 = x2_mul(v, rs2);
+    const uint64_t rem = x2_fma(q0, ns, v);
+    return x2_fma(rem, rs2, q0);
+}
+
+// int8 code bytes of a pair of quotients, round half away from zero (kernels.py:35): the low byte of each
+// returned word. w = RN(q + copysign(0.5, q)) is the reference's |q| + 0.5 with q's sign (round to nearest is
+// symmetric); a round-toward-zero add of copysign(2^23, q) truncates it to an integer (exact for |w| < 2^23),
+// subtracting that constant back leaves the integer as a float, and adding 1.5 * 2^23 puts it in two's
+// complement in the low byte. |q| <= 127.00001 for the quotients of the quantizers (|v| <= absmax,
+// s = RN(absmax / 127)), so the clamp to +-127 of the reference never binds and is not applied.
+__device__ __forceinline__ void x2_codes(uint64_t q, uint32_t &c_lo, uint32_t &c_hi) {
+    float qlo, qhi;
+    x2_split(q, qlo, qhi);
+    const uint32_t slo = __float_as_uint(qlo) & 0x80000000u, shi = __float_as_uint(qhi) & 0x80000000u;
+    const uint64_t half = x2(__uint_as_float(slo | 0x3F000000u), __uint_as_float(shi | 0x3F000000u));
+    const uint64_t big = x2(__uint_as_float(slo | 0x4B000000u), __uint_as_float(shi | 0x4B000000u));
+    const uint64_t t = x2_add_rz(x2_add(q, half), big);
+    float blo, bhi;
+    x2_split(x2_add(x2_add(t, big ^ 0x8000000080000000ull), x2_splat(12582912.0f)), blo, bhi);
+    c_lo = __float_as_uint(blo);
+    c_hi = __float_as_uint(bhi);
+}
+// four code words (low bytes) -> one word, first argument in the low byte
+__device__ __forceinline__ uint32_t pack4_lowbytes(uint32_t a, uint32_t b, uint32_t c, uint32_t d) {
+    return __byte_perm(__byte_perm(a, b, 0x0040), __byte_perm(c, d, 0x0040), 0x5410);
+}
+
 // ---------------------------------------------------------------------------------------------------
 // vector loads: 8 bf16 / fp16 or 4 fp32 elements -> fp32
 

@@ -16,19 +16,6 @@ namespace hn {
 
 typedef __nv_bfloat16 bf16;
 
-__device__ __forceinline__ void load16_bf16(const bf16 *p, float *v) {
-    Elem<bf16>::load8(p, v);
-    Elem<bf16>::load8(p + 8, v + 8);
-}
-__device__ __forceinline__ void store16_bf16_exact(bf16 *p, const float *v) {
-    uint4 a, b;
-    a.x = pack_bf16_exact(v[0], v[1]); a.y = pack_bf16_exact(v[2], v[3]);
-    a.z = pack_bf16_exact(v[4], v[5]); a.w = pack_bf16_exact(v[6], v[7]);
-    b.x = pack_bf16_exact(v[8], v[9]); b.y = pack_bf16_exact(v[10], v[11]);
-    b.z = pack_bf16_exact(v[12], v[13]); b.w = pack_bf16_exact(v[14], v[15]);
-    reinterpret_cast<uint4 *>(p)[0] = a;
-    reinterpret_cast<uint4 *>(p)[1] = b;
-}
 
 // balanced pairwise tree over WP (power of two) values in index order
 template <int WP> __device__ __forceinline__ float tree_smem(const float *red) {
@@ -43,103 +30,244 @@ template <int WP> __device__ __forceinline__ float tree_smem(const float *red) {
     return t[0];
 }
 
-// MODE 0: y = bf16(modulate(LN(x)))      (K4)
-// MODE 1: codes/scales of rbf16(modulate(LN(x)))   (K3)
-// MODE 2: x' = bf16(x + rbf16(y * gate)); store x'; then MODE 1 on x'   (K6+K3)
+// ---------------------------------------------------------------------------------------------------
+// LayerNorm rows (K3, K4, K6+K3), persistent: MODE 0: y = bf16(modulate(LN(x))); MODE 1: int8 codes/scales
+// of rbf16(modulate(LN(x))); MODE 2: x' = bf16(x + rbf16(y * gate)), stored, then MODE 1 on x'. Each CTA walks rows blockIdx.x, +gridDim.x, ... and prefetches the next row's inputs before reducing
+// the current one; rbf16(1 + scale), shift (and the gate) are formed once per batch item. The thread's 16
+// elements are held as packed pairs so the per-element work runs on the f32x2 pipes:
+//   P[k] = (e[2k], e[2k+8]), Q[k] = (e[2k+1], e[2k+9]),  k = 0..3   (e = the thread's 16 elements)
+// With this pairing the tree of tree16 is vertical pair additions: P[k]+Q[k] = (a[k], a[k+4]) with
+// a[i] = e[2i]+e[2i+1]; (a0,a4)+(a1,a5) = (b0,b2); (a2,a6)+(a3,a7) = (b1,b3); (b0,b2)+(b1,b3) = (c0,c1).
+// bf16 rounding is the cvt.rn.bf16x2 instruction, the quantizer's division the exact fma-corrected quotient
+// of x2_quot, the code the round-half-away of x2_codes. A packed product is never fed straight into a packed
+// addition (measured here: that pair can come out with one rounding, as a fused multiply-add); the sums of
+// products (the squares of the variance, "+ shift") are scalar __fadd_rn.
+
+struct Row16 {
+    uint64_t P[4], Q[4];
+};
+// 8 bf16x2 words (elements 0..15 in order) -> pairs
+__device__ __forceinline__ Row16 row_from_words(const uint32_t *w) {
+    Row16 r;
+#pragma unroll
+    for (int k = 0; k < 4; ++k) {
+        r.P[k] = x2(bf16_lo(w[k]), bf16_lo(w[k + 4]));
+        r.Q[k] = x2(bf16_hi(w[k]), bf16_hi(w[k + 4]));
+    }
+    return r;
+}
+// pairs -> 8 bf16x2 words in element order, each value rounded to nearest even
+__device__ __forceinline__ void words_from_row(const Row16 &r, uint32_t *w) {
+#pragma unroll
+    for (int k = 0; k < 4; ++k) {
+        float p0, p1, q0, q1;
+        x2_split(r.P[k], p0, p1);
+        x2_split(r.Q[k], q0, q1);
+        w[k] = bf16x2_rn(p0, q0);
+        w[k + 4] = bf16x2_rn(p1, q1);
+    }
+}
+__device__ __forceinline__ float row_tree16(const Row16 &r) {
+    const uint64_t a0 = x2_add(r.P[0], r.Q[0]), a1 = x2_add(r.P[1], r.Q[1]);
+    const uint64_t a2 = x2_add(r.P[2], r.Q[2]), a3 = x2_add(r.P[3], r.Q[3]);
+    const uint64_t c = x2_add(x2_add(a0, a1), x2_add(a2, a3));
+    float c0, c1;
+    x2_split(c, c0, c1);
+    return __fadd_rn(c0, c1);
+}
+__device__ __forceinline__ void load_words16(const bf16 *p, uint32_t *w) {
+    const uint4 a = ldg_stream(p), b = ldg_stream(p + 8);
+    w[0] = a.x; w[1] = a.y; w[2] = a.z; w[3] = a.w; w[4] = b.x; w[5] = b.y; w[6] = b.z; w[7] = b.w;
+}
+__device__ __forceinline__ void store_words16(bf16 *p, const uint32_t *w) {
+    reinterpret_cast<uint4 *>(p)[0] = make_uint4(w[0], w[1], w[2], w[3]);
+    reinterpret_cast<uint4 *>(p)[1] = make_uint4(w[4], w[5], w[6], w[7]);
+}
+
 template <int WP, int MODE>
-__global__ void __launch_bounds__(WP * 32) k_ln_row(const bf16 *__restrict__ x, const bf16 *__restrict__ yres,
-                                                   const bf16 *__restrict__ gate, const bf16 *__restrict__ shift,
-                                                   const bf16 *__restrict__ scale, int64_t L, int D, float eps,
-                                                   bf16 *__restrict__ out, int8_t *__restrict__ q,
-                                                   float *__restrict__ s, int64_t s_rs, int64_t s_gs) {
+__global__ void __launch_bounds__(WP * 32, (WP <= 8) ? (MODE == 2 ? 2 : 3) : 1) k_ln_rows(const bf16 *__restrict__ x, const bf16 *__restrict__ yres,
+                                                    const bf16 *__restrict__ gate, const bf16 *__restrict__ shift,
+                                                    const bf16 *__restrict__ scale, int64_t rows, int64_t L, int D,
+                                                    float eps, bf16 *__restrict__ out, int8_t *__restrict__ q,
+                                                    float *__restrict__ s, int64_t s_rs, int64_t s_gs) {
     __shared__ float red1[WP], red2[WP];
     const int t = threadIdx.x, lane = t & 31, warp = t >> 5;
-    const int64_t row = blockIdx.x;
-    const int64_t b = row / L;
-    const int chunks = D >> 4;
-    const bool active = t < chunks;
-    const int64_t off = row * (int64_t)D + 16 * t;
-    const int64_t voff = b * (int64_t)D + 16 * t;
-    float v[16];
-    if (active) {
-        load16_bf16(x + off, v);
-        if (MODE == 2) {
-            float yv[16], gv[16];
-            load16_bf16(yres + off, yv);
-            load16_bf16(gate + voff, gv);
+    const bool active = t < (D >> 4);
+    const float fd = (float)D;
+    // for a power-of-two D, sum / D is the exact product sum * 2^-log2(D)
+    const float inv_d = (D & (D - 1)) == 0 ? __fdiv_rn(1.0f, fd) : 0.0f;
+    int64_t row = blockIdx.x;
+    if (row >= rows) return;
+    // the row's inputs, prefetched one row ahead
+    uint32_t wx[8], wy[8];
 #pragma unroll
-            for (int i = 0; i < 16; ++i) v[i] = rbf16(__fadd_rn(v[i], rbf16(__fmul_rn(yv[i], gv[i]))));
-            store16_bf16_exact(out + off, v);
+    for (int i = 0; i < 8; ++i) { wx[i] = 0u; wy[i] = 0u; }
+    if (active) {
+        load_words16(x + row * (int64_t)D + 16 * t, wx);
+        if (MODE == 2) load_words16(yres + row * (int64_t)D + 16 * t, wy);
+    }
+    int64_t cur_b = -1;
+    Row16 R, SH, G;   // rbf16(1 + scale), shift, gate of the current batch item
+    for (; row < rows; row += gridDim.x) {
+        const int64_t b = row / L;
+        if (b != cur_b) {
+            cur_b = b;
+            uint32_t w[8];
+            if (active) load_words16(scale + b * (int64_t)D + 16 * t, w);
+            else {
+#pragma unroll
+                for (int i = 0; i < 8; ++i) w[i] = 0u;
+            }
+            R = row_from_words(w);
+#pragma unroll
+            for (int k = 0; k < 4; ++k) {
+                float p0, p1, q0, q1;
+                x2_split(x2_add(R.P[k], x2_splat(1.0f)), p0, p1);
+                x2_split(x2_add(R.Q[k], x2_splat(1.0f)), q0, q1);
+                const uint32_t lo = bf16x2_rn(p0, q0), hi = bf16x2_rn(p1, q1);
+                R.P[k] = x2(bf16_lo(lo), bf16_lo(hi));
+                R.Q[k] = x2(bf16_hi(lo), bf16_hi(hi));
+            }
+            if (active) load_words16(shift + b * (int64_t)D + 16 * t, w);
+            SH = row_from_words(w);
+            if (MODE == 2) {
+                if (active) load_words16(gate + b * (int64_t)D + 16 * t, w);
+                G = row_from_words(w);
+            }
         }
-    } else {
+        const int64_t off = row * (int64_t)D + 16 * t;
+        // this row's words; start the next row's loads
+        uint32_t cx[8], cy[8];
 #pragma unroll
-        for (int i = 0; i < 16; ++i) v[i] = 0.0f;
-    }
-    if (t < WP) { red1[t] = 0.0f; red2[t] = 0.0f; }
-    __syncthreads();
-    float part = warp_sum_tree(tree16(v));
-    if (lane == 0) red1[warp] = part;
-    __syncthreads();
-    const float mean = __fdiv_rn(tree_smem<WP>(red1), (float)D);
-    float sq[16];
+        for (int i = 0; i < 8; ++i) { cx[i] = wx[i]; cy[i] = wy[i]; }
+        const int64_t nrow = row + gridDim.x;
+        if (active && nrow < rows) {
+            load_words16(x + nrow * (int64_t)D + 16 * t, wx);
+            if (MODE == 2) load_words16(yres + nrow * (int64_t)D + 16 * t, wy);
+        }
+        Row16 V = row_from_words(cx);
+        if (MODE == 2) {
+            // x' = rbf16(x + rbf16(y * gate)), stored, then normalized
+            const Row16 Y = row_from_words(cy);
+            Row16 YG;
 #pragma unroll
-    for (int i = 0; i < 16; ++i) {
-        v[i] = __fsub_rn(v[i], mean);
-        sq[i] = active ? __fmul_rn(v[i], v[i]) : 0.0f;
-    }
-    part = warp_sum_tree(tree16(sq));
-    if (lane == 0) red2[warp] = part;
-    __syncthreads();
-    const float var = __fdiv_rn(tree_smem<WP>(red2), (float)D);
-    const float rstd = rsqrt_cr(__fadd_rn(var, eps));
-    float sh[16], sc[16];
-    if (active) {
-        load16_bf16(shift + voff, sh);
-        load16_bf16(scale + voff, sc);
-    } else {
+            for (int k = 0; k < 4; ++k) { YG.P[k] = x2_mul(Y.P[k], G.P[k]); YG.Q[k] = x2_mul(Y.Q[k], G.Q[k]); }
+            uint32_t w[8];
+            words_from_row(YG, w);
+            YG = row_from_words(w);
 #pragma unroll
-        for (int i = 0; i < 16; ++i) { sh[i] = 0.0f; sc[i] = 0.0f; }
-    }
+            for (int k = 0; k < 4; ++k) { V.P[k] = x2_add(V.P[k], YG.P[k]); V.Q[k] = x2_add(V.Q[k], YG.Q[k]); }
+            words_from_row(V, w);
+            if (active) store_words16(out + off, w);
+            V = row_from_words(w);
+        }
+        // mean
+        float part = warp_sum_tree(row_tree16(V));
+        if (lane == 0) red1[warp] = part;
+        __syncthreads();
+        const float mean = inv_d != 0.0f ? __fmul_rn(tree_smem<WP>(red1), inv_d) : __fdiv_rn(tree_smem<WP>(red1), fd);
+        // centred values and variance
+        const uint64_t nm = x2_splat(-mean);
+        Row16 C;
+        float sq[16];
 #pragma unroll
-    for (int i = 0; i < 16; ++i) {
-        float n = __fmul_rn(v[i], rstd);
-        float r = rbf16(__fadd_rn(1.0f, sc[i]));
-        v[i] = rbf16(__fadd_rn(__fmul_rn(n, r), sh[i]));
-    }
-    if (MODE == 0) {
-        if (active) store16_bf16_exact(out + off, v);
-        return;
-    }
-    float peak = 0.0f;
+        for (int k = 0; k < 4; ++k) {
+            C.P[k] = x2_add(V.P[k], nm);
+            C.Q[k] = x2_add(V.Q[k], nm);
+            x2_split(active ? x2_mul(C.P[k], C.P[k]) : 0ull, sq[2 * k], sq[2 * k + 8]);
+            x2_split(active ? x2_mul(C.Q[k], C.Q[k]) : 0ull, sq[2 * k + 1], sq[2 * k + 9]);
+        }
+        part = warp_sum_tree(tree16(sq));
+        if (lane == 0) red2[warp] = part;
+        __syncthreads();
+        const float var = inv_d != 0.0f ? __fmul_rn(tree_smem<WP>(red2), inv_d) : __fdiv_rn(tree_smem<WP>(red2), fd);
+        const uint64_t rstd = x2_splat(rsqrt_cr(__fadd_rn(var, eps)));
+        // modulate: rbf16(n * rbf16(1 + scale) + shift)
+        Row16 Z;
 #pragma unroll
-    for (int i = 0; i < 16; ++i) peak = fmaxf(peak, fabsf(v[i]));
-    peak = warp_max_xor(peak, 8);
-    const float qsc = i8_scale(peak);
-    int c[16];
+        for (int k = 0; k < 4; ++k) {
+            float a0, a1, h0, h1;
+            x2_split(x2_mul(x2_mul(C.P[k], rstd), R.P[k]), a0, a1);
+            x2_split(SH.P[k], h0, h1);
+            Z.P[k] = x2(__fadd_rn(a0, h0), __fadd_rn(a1, h1));
+            x2_split(x2_mul(x2_mul(C.Q[k], rstd), R.Q[k]), a0, a1);
+            x2_split(SH.Q[k], h0, h1);
+            Z.Q[k] = x2(__fadd_rn(a0, h0), __fadd_rn(a1, h1));
+        }
+        uint32_t zw[8];
+        words_from_row(Z, zw);
+        if (MODE == 0) {
+            if (active) store_words16(out + off, zw);
+            continue;
+        }
+        // int8 per 128-wide group (8 adjacent lanes): absmax, scale, exact quotient, round half away
+        Z = row_from_words(zw);
+        float peak = 0.0f;
 #pragma unroll
-    for (int i = 0; i < 16; ++i) c[i] = code_i8(__fdiv_rn(v[i], qsc));
-    if (active) {
-        uint4 o;
-        o.x = pack4_i8(c[0], c[1], c[2], c[3]);
-        o.y = pack4_i8(c[4], c[5], c[6], c[7]);
-        o.z = pack4_i8(c[8], c[9], c[10], c[11]);
-        o.w = pack4_i8(c[12], c[13], c[14], c[15]);
-        *reinterpret_cast<uint4 *>(q + off) = o;
-        if ((t & 7) == 0) s[row * s_rs + (int64_t)(t >> 3) * s_gs] = qsc;
+        for (int k = 0; k < 4; ++k) {
+            float a0, a1, b0, b1;
+            x2_split(Z.P[k], a0, a1);
+            x2_split(Z.Q[k], b0, b1);
+            peak = fmaxf(peak, fmaxf(fmaxf(fabsf(a0), fabsf(a1)), fmaxf(fabsf(b0), fabsf(b1))));
+        }
+        peak = warp_max_xor(peak, 8);
+        const float qsc = i8_scale(peak);
+        uint32_t cP[4][2], cQ[4][2];
+        if (qsc >= 0x1p-90f) {
+            const uint64_t ns = x2_splat(-qsc), rs = x2_splat(__fdiv_rn(1.0f, qsc));
+#pragma unroll
+            for (int k = 0; k < 4; ++k) {
+                x2_codes(x2_quot(Z.P[k], ns, rs), cP[k][0], cP[k][1]);
+                x2_codes(x2_quot(Z.Q[k], ns, rs), cQ[k][0], cQ[k][1]);
+            }
+        } else {
+#pragma unroll
+            for (int k = 0; k < 4; ++k) {
+                float a0, a1, b0, b1;
+                x2_split(Z.P[k], a0, a1);
+                x2_split(Z.Q[k], b0, b1);
+                x2_codes(x2(__fdiv_rn(a0, qsc), __fdiv_rn(a1, qsc)), cP[k][0], cP[k][1]);
+                x2_codes(x2(__fdiv_rn(b0, qsc), __fdiv_rn(b1, qsc)), cQ[k][0], cQ[k][1]);
+            }
+        }
+        if (active) {
+            // element 2k -> cP[k][0], 2k+1 -> cQ[k][0], 2k+8 -> cP[k][1], 2k+9 -> cQ[k][1]
+            uint4 o;
+            o.x = pack4_lowbytes(cP[0][0], cQ[0][0], cP[1][0], cQ[1][0]);
+            o.y = pack4_lowbytes(cP[2][0], cQ[2][0], cP[3][0], cQ[3][0]);
+            o.z = pack4_lowbytes(cP[0][1], cQ[0][1], cP[1][1], cQ[1][1]);
+            o.w = pack4_lowbytes(cP[2][1], cQ[2][1], cP[3][1], cQ[3][1]);
+            *reinterpret_cast<uint4 *>(q + off) = o;
+            if ((t & 7) == 0) s[row * s_rs + (int64_t)(t >> 3) * s_gs] = qsc;
+        }
     }
+}
+
+template <int WP, int MODE>
+static void launch_ln_rows_t(const void *x, const void *y, const void *gate, const void *shift, const void *scale,
+                             int64_t rows, int64_t L, int64_t D, float eps, void *out, int8_t *q, float *s,
+                             int64_t s_rs, int64_t s_gs, cudaStream_t st) {
+    auto kern = k_ln_rows<WP, MODE>;
+    static int per_sm = 0;   // resident CTAs per SM for this instantiation (same on every B200)
+    if (per_sm == 0) {
+        int n = 0;
+        if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&n, kern, WP * 32, 0) != cudaSuccess || n < 1) n = 1;
+        per_sm = n;
+    }
+    int64_t grid = (int64_t)num_sms() * per_sm;
+    if (grid > rows) grid = rows;
+    kern<<<(unsigned)grid, WP * 32, 0, st>>>((const bf16 *)x, (const bf16 *)y, (const bf16 *)gate, (const bf16 *)shift,
+                                             (const bf16 *)scale, rows, L, (int)D, eps, (bf16 *)out, q, s, s_rs, s_gs);
 }
 
 template <int WP>
 static void launch_ln_wp(int mode, const void *x, const void *y, const void *gate, const void *shift,
                          const void *scale, int64_t B, int64_t L, int64_t D, float eps, void *out, int8_t *q,
                          float *s, int64_t s_rs, int64_t s_gs, cudaStream_t st) {
-    const int warps = (int)cdiv(D / 16, 32);
-    dim3 grid((unsigned)(B * L)), block(warps * 32);
-    const bf16 *xp = (const bf16 *)x, *yp = (const bf16 *)y, *gp = (const bf16 *)gate;
-    const bf16 *shp = (const bf16 *)shift, *scp = (const bf16 *)scale;
-    if (mode == 0) k_ln_row<WP, 0><<<grid, block, 0, st>>>(xp, yp, gp, shp, scp, L, (int)D, eps, (bf16 *)out, q, s, s_rs, s_gs);
-    else if (mode == 1) k_ln_row<WP, 1><<<grid, block, 0, st>>>(xp, yp, gp, shp, scp, L, (int)D, eps, (bf16 *)out, q, s, s_rs, s_gs);
-    else k_ln_row<WP, 2><<<grid, block, 0, st>>>(xp, yp, gp, shp, scp, L, (int)D, eps, (bf16 *)out, q, s, s_rs, s_gs);
+    const int64_t rows = B * L;
+    if (mode == 0) launch_ln_rows_t<WP, 0>(x, y, gate, shift, scale, rows, L, D, eps, out, q, s, s_rs, s_gs, st);
+    else if (mode == 1) launch_ln_rows_t<WP, 1>(x, y, gate, shift, scale, rows, L, D, eps, out, q, s, s_rs, s_gs, st);
+    else launch_ln_rows_t<WP, 2>(x, y, gate, shift, scale, rows, L, D, eps, out, q, s, s_rs, s_gs, st);
 }
 
 cudaError_t launch_ln_row(int mode, const void *x, const void *y, const void *gate, const void *shift,
