@@ -292,7 +292,8 @@ static int qk_common(const void *x, int64_t row_stride, const void *w, const flo
     REQUIRE((cos == nullptr) == (sin == nullptr), HN_ERR_ARG, "hn_qk_norm_rope: cos and sin must both be given or both NULL");
     REQUIRE(D == 128, HN_ERR_UNSUPPORTED, "hn_qk_norm_rope: head dim %lld (kernels are built for 128)", (long long)D);
     REQUIRE(B > 0 && L >= 0 && H > 0 && row_stride >= H * D, HN_ERR_SHAPE, "hn_qk_norm_rope: bad shape/stride");
-    REQUIRE(al8(x) && row_stride % 4 == 0 && al8(w) && al8(y), HN_ERR_ALIGN, "hn_qk_norm_rope: x/w/y must be 8-byte aligned");
+    REQUIRE(al16(x) && row_stride % 8 == 0 && al16(w) && al16(y), HN_ERR_ALIGN,
+            "hn_qk_norm_rope: x/w/y must be 16-byte aligned with a row stride that is a multiple of 8");
     REQUIRE(cos == nullptr || (al16(cos) && al16(sin)), HN_ERR_ALIGN, "hn_qk_norm_rope: cos/sin must be 16-byte aligned");
     return HN_OK;
 }

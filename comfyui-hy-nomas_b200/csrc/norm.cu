@@ -326,10 +326,12 @@ cudaError_t launch_gated_residual(const void *x, const void *y, const void *gate
 }
 
 // ---------------------------------------------------------------------------------------------------
-// K5 QK-RMSNorm + interleaved RoPE. One warp per token, looping over heads; lane l owns elements
-// [4l, 4l+4) of a 128-wide head = the interleaved pairs (4l, 4l+1) and (4l+2, 4l+3). The even and odd
-// square sums are separate butterfly trees (fused.py:74: sum(xe^2) + sum(xo^2)). The token's cos/sin
-// (16 bytes each per lane) are loaded once and reused for every head and both tensors.
+// K5 QK-RMSNorm + interleaved RoPE (fused.py:65-91), D = 128. One warp per token, four heads at a time:
+// lane l handles head h0 + l/8, elements [16*(l%8), 16*(l%8) + 16) = 8 interleaved (even, odd) pairs, held as
+// packed (even, odd) f32x2 values. The even and odd square sums (fused.py:74, sum(xe^2) + sum(xo^2)) are
+// pairwise trees over the head's 64 evens / odds in index order: three levels inside the lane (8 pairs), then a
+// butterfly over the 8 lanes of the head - both trees at once, as the two halves of a pair. The token's cos/sin
+// for the lane's 16 positions are loaded once and reused for every head and both tensors.
 template <bool ROPE, int NT>
 __global__ void __launch_bounds__(256) k_qk_norm_rope(const bf16 *__restrict__ x0, const bf16 *__restrict__ x1,
                                                       int64_t row_stride, const bf16 *__restrict__ w0,
@@ -337,56 +339,99 @@ __global__ void __launch_bounds__(256) k_qk_norm_rope(const bf16 *__restrict__ x
                                                       const float *__restrict__ sinp, int64_t BL, int64_t L, int H,
                                                       float eps, bf16 *__restrict__ y0, bf16 *__restrict__ y1) {
     const int lane = threadIdx.x & 31;
+    const int sub = lane & 7, hq = lane >> 3;
     const int64_t tok = (int64_t)blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5);
     if (tok >= BL) return;
     const int64_t l = tok % L;
-    float c[4] = {0, 0, 0, 0}, sn[4] = {0, 0, 0, 0};
+    // cos/sin of the lane's 16 positions as (even, odd) pairs; the sine of the even position negated
+    uint64_t C[8], S[8];
     if (ROPE) {
-        float4 cv = *reinterpret_cast<const float4 *>(cosp + l * 128 + 4 * lane);
-        float4 sv = *reinterpret_cast<const float4 *>(sinp + l * 128 + 4 * lane);
-        c[0] = cv.x; c[1] = cv.y; c[2] = cv.z; c[3] = cv.w;
-        sn[0] = sv.x; sn[1] = sv.y; sn[2] = sv.z; sn[3] = sv.w;
+        const float4 *cv = reinterpret_cast<const float4 *>(cosp + l * 128 + 16 * sub);
+        const float4 *sv = reinterpret_cast<const float4 *>(sinp + l * 128 + 16 * sub);
+#pragma unroll
+        for (int i = 0; i < 4; ++i) {
+            const float4 c4 = cv[i], s4 = sv[i];
+            C[2 * i] = x2(c4.x, c4.y);
+            C[2 * i + 1] = x2(c4.z, c4.w);
+            S[2 * i] = x2(s4.x, s4.y);
+            S[2 * i + 1] = x2(s4.z, s4.w);
+        }
     }
+    const float inv_d = 0.0078125f;   // 1/128: ss / 128 is the exact product ss * 2^-7
 #pragma unroll
     for (int tsel = 0; tsel < NT; ++tsel) {
         const bf16 *xs = tsel == 0 ? x0 : x1;
         const bf16 *ws = tsel == 0 ? w0 : w1;
         bf16 *ys = tsel == 0 ? y0 : y1;
-        uint2 wv = *reinterpret_cast<const uint2 *>(ws + 4 * lane);
-        const float we0 = bf16_lo(wv.x), wo0 = bf16_hi(wv.x), we1 = bf16_lo(wv.y), wo1 = bf16_hi(wv.y);
-        const bf16 *xrow = xs + tok * row_stride + 4 * lane;
-        bf16 *yrow = ys + tok * (int64_t)H * 128 + 4 * lane;
+        uint32_t wwords[8];
+        {
+            const uint4 a = *reinterpret_cast<const uint4 *>(ws + 16 * sub);
+            const uint4 b = *reinterpret_cast<const uint4 *>(ws + 16 * sub + 8);
+            wwords[0] = a.x; wwords[1] = a.y; wwords[2] = a.z; wwords[3] = a.w;
+            wwords[4] = b.x; wwords[5] = b.y; wwords[6] = b.z; wwords[7] = b.w;
+        }
+        const bf16 *xrow = xs + tok * row_stride + 16 * sub;
+        bf16 *yrow = ys + tok * (int64_t)H * 128 + 16 * sub;
         for (int h0 = 0; h0 < H; h0 += 4) {
-            uint2 xv[4];
+            const int h = h0 + hq;
+            const bool on = h < H;
+            uint32_t xw[8];
+            if (on) {
+                const uint4 a = ldg_stream(xrow + h * 128), b = ldg_stream(xrow + h * 128 + 8);
+                xw[0] = a.x; xw[1] = a.y; xw[2] = a.z; xw[3] = a.w; xw[4] = b.x; xw[5] = b.y; xw[6] = b.z; xw[7] = b.w;
+            } else {
 #pragma unroll
-            for (int u = 0; u < 4; ++u)
-                if (h0 + u < H) xv[u] = *reinterpret_cast<const uint2 *>(xrow + (h0 + u) * 128);
+                for (int i = 0; i < 8; ++i) xw[i] = 0u;
+            }
+            uint64_t V[8], SQ[8];
 #pragma unroll
-            for (int u = 0; u < 4; ++u) {
-                if (h0 + u >= H) break;
-                const float e0 = bf16_lo(xv[u].x), o0 = bf16_hi(xv[u].x), e1 = bf16_lo(xv[u].y), o1 = bf16_hi(xv[u].y);
-                float se = __fadd_rn(__fmul_rn(e0, e0), __fmul_rn(e1, e1));
-                float so = __fadd_rn(__fmul_rn(o0, o0), __fmul_rn(o1, o1));
-                se = warp_sum_tree(se);
-                so = warp_sum_tree(so);
-                const float r = rsqrt_cr(__fadd_rn(__fdiv_rn(__fadd_rn(se, so), 128.0f), eps));
-                const float ne0 = rbf16(__fmul_rn(rbf16(__fmul_rn(e0, r)), we0));
-                const float no0 = rbf16(__fmul_rn(rbf16(__fmul_rn(o0, r)), wo0));
-                const float ne1 = rbf16(__fmul_rn(rbf16(__fmul_rn(e1, r)), we1));
-                const float no1 = rbf16(__fmul_rn(rbf16(__fmul_rn(o1, r)), wo1));
-                uint2 ov;
-                if (ROPE) {
-                    const float oe0 = __fsub_rn(__fmul_rn(ne0, c[0]), __fmul_rn(no0, sn[0]));
-                    const float oo0 = __fadd_rn(__fmul_rn(no0, c[1]), __fmul_rn(ne0, sn[1]));
-                    const float oe1 = __fsub_rn(__fmul_rn(ne1, c[2]), __fmul_rn(no1, sn[2]));
-                    const float oo1 = __fadd_rn(__fmul_rn(no1, c[3]), __fmul_rn(ne1, sn[3]));
-                    ov.x = pack_bf16_rn(oe0, oo0);
-                    ov.y = pack_bf16_rn(oe1, oo1);
-                } else {
-                    ov.x = pack_bf16_exact(ne0, no0);
-                    ov.y = pack_bf16_exact(ne1, no1);
+            for (int i = 0; i < 8; ++i) {
+                V[i] = x2(bf16_lo(xw[i]), bf16_hi(xw[i]));
+                SQ[i] = x2_mul(V[i], V[i]);
+            }
+            // (sum of even squares, sum of odd squares): tree over the lane's 8 pairs, then over the 8 lanes
+            float se, so;
+            {
+                float a[16];
+#pragma unroll
+                for (int i = 0; i < 8; ++i) x2_split(SQ[i], a[2 * i], a[2 * i + 1]);
+                // scalar first level (a product is not fed straight into a packed addition)
+                uint64_t t[4];
+#pragma unroll
+                for (int i = 0; i < 4; ++i) t[i] = x2(__fadd_rn(a[4 * i], a[4 * i + 2]), __fadd_rn(a[4 * i + 1], a[4 * i + 3]));
+                const uint64_t u = x2_add(x2_add(t[0], t[1]), x2_add(t[2], t[3]));
+                x2_split(u, se, so);
+#pragma unroll
+                for (int o = 1; o < 8; o <<= 1) {
+                    se = __fadd_rn(se, __shfl_xor_sync(0xffffffffu, se, o));
+                    so = __fadd_rn(so, __shfl_xor_sync(0xffffffffu, so, o));
                 }
-                *reinterpret_cast<uint2 *>(yrow + (h0 + u) * 128) = ov;
+            }
+            const float r = rsqrt_cr(__fadd_rn(__fmul_rn(__fadd_rn(se, so), inv_d), eps));
+            const uint64_t r2 = x2_splat(r);
+            uint32_t ow[8];
+#pragma unroll
+            for (int i = 0; i < 8; ++i) {
+                // rbf16(rbf16(x * r) * w)
+                float a0, a1;
+                x2_split(x2_mul(V[i], r2), a0, a1);
+                const uint32_t n1 = bf16x2_rn(a0, a1);
+                x2_split(x2_mul(x2(bf16_lo(n1), bf16_hi(n1)), x2(bf16_lo(wwords[i]), bf16_hi(wwords[i]))), a0, a1);
+                const uint32_t n2 = bf16x2_rn(a0, a1);
+                if (ROPE) {
+                    // (ne*c_e - no*s_e, no*c_o + ne*s_o), the differences and sums rounded separately
+                    const float ne = bf16_lo(n2), no = bf16_hi(n2);
+                    float pc0, pc1, ps0, ps1;
+                    x2_split(x2_mul(x2(ne, no), C[i]), pc0, pc1);
+                    x2_split(x2_mul(x2(no, ne), S[i]), ps0, ps1);
+                    ow[i] = bf16x2_rn(__fsub_rn(pc0, ps0), __fadd_rn(pc1, ps1));
+                } else {
+                    ow[i] = n2;
+                }
+            }
+            if (on) {
+                reinterpret_cast<uint4 *>(yrow + h * 128)[0] = make_uint4(ow[0], ow[1], ow[2], ow[3]);
+                reinterpret_cast<uint4 *>(yrow + h * 128)[1] = make_uint4(ow[4], ow[5], ow[6], ow[7]);
             }
         }
     }

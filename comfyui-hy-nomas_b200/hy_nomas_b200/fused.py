@@ -48,8 +48,8 @@ def adaln(x, shift, scale, eps=1e-6):
 
 def _qk_input(x):
     b, l, h, d = x.shape
-    if x.stride(3) != 1 or x.stride(2) != d or x.stride(0) != l * x.stride(1) or x.stride(1) % 4 or \
-            x.data_ptr() % 8:
+    if x.stride(3) != 1 or x.stride(2) != d or x.stride(0) != l * x.stride(1) or x.stride(1) % 8 or \
+            x.data_ptr() % 16:
         x = x.contiguous()
     return x
 

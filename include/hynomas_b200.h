@@ -150,6 +150,7 @@ int hn_adaln(const void *x, const void *shift, const void *scale, int64_t B, int
  * x: B*L token rows of H heads x D (D == 128), heads contiguous, token row stride `row_stride`
  * elements (>= H*D; e.g. 3*H*D inside a fused qkv buffer); rows of batch b start at b*L*row_stride.
  * weight [D] bf16. cos/sin [L, D] fp32 or both NULL (no RoPE). y [B, L, H, D] bf16 contiguous.
+ * x, weight and y 16-byte aligned, row_stride a multiple of 8; cos/sin 16-byte aligned.
  */
 int hn_qk_norm_rope(const void *x, int64_t row_stride, const void *weight, const float *cos, const float *sin,
                     int64_t B, int64_t L, int64_t H, int64_t D, float eps, void *y, void *stream);
