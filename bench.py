@@ -750,10 +750,12 @@ def workload_elementwise(args, world, rank, stream, pk, sampler):
     e2e_total = sum_over_ranks(step_bytes * args.steps, world)
     h2d = sum(v.numel() * v.element_size() for v in hsets[0].values())
     d2h = sum(v.numel() * v.element_size() for v in outs_h.values())
+    others = other_elementwise_kernels(m, d, h, hd, stream, sets, shift, scale, wq, rope)
     config = {"workload": "dit_elementwise_chain_M20240_D4096 (config 3): adaln_quant, qk_norm_rope2 (q and k, "
                           "3-D RoPE 16/56/56), gated_residual, gated_residual_adaln_quant",
               "M": m, "D": d, "heads": h, "head_dim": hd, "bytes_per_step": step_bytes,
-              "l2": "inputs rotate over 2 sets (each tensor 166 MB > L2)", "parallelism": f"replicas x{world}"}
+              "l2": "inputs rotate over 2 sets (each tensor 166 MB > L2)", "parallelism": f"replicas x{world}",
+              "other_kernels_gbs": others}
     return dict(metric="fused DiT elementwise chain GB/s", value=round(total / (ms * 1e-3) / 1e9, 1), unit="GB/s",
                 ms_per_step=round(ms / args.steps, 4), higher_is_better=True, scaling="weak", dtype="bf16 -> int8",
                 config=config,
@@ -761,6 +763,40 @@ def workload_elementwise(args, world, rank, stream, pk, sampler):
                      "h2d_bytes_per_step": h2d * world, "d2h_bytes_per_step": d2h * world},
                 roofline=roof, gpu_launches=launches * args.steps,
                 cpu_baseline_fn=lambda: cpu_baseline_elementwise(m, d, h, hd))
+
+
+def other_elementwise_kernels(m, d, h, hd, stream, sets, shift, scale, w, rope, iters=20):
+    """The path's remaining bandwidth-bound kernels at the same shapes (not part of the chain's value), GB/s
+    of algorithmic bytes: K1 quantize_activations (int8 and e4m3, per 128 and per token), K4 adaln, K5 on one
+    tensor, K7 pixelumm_qk (the FP8 decoder's QK norm: 32 heads x 128, split T/HW halves)."""
+    from hy_nomas_b200 import fused, kernels
+    flush = torch.empty(2 * L2_BYTES, dtype=torch.uint8, device="cuda")
+    x2d = [s["x"].view(m, d) for s in sets]
+    half = hd // 2
+    wt = torch.ones(half, dtype=torch.bfloat16, device="cuda")
+    whw = torch.ones(half, dtype=torch.bfloat16, device="cuda")
+    cases = {
+        "quantize_activations_int8_g128": (lambda i: kernels.quantize_activations(x2d[i % 2]), m * d * 3 + m * (d // 128) * 4),
+        "quantize_activations_e4m3_g128": (lambda i: kernels.quantize_activations(x2d[i % 2], "fp8"), m * d * 3 + m * (d // 128) * 4),
+        "quantize_activations_int8_token": (lambda i: kernels.quantize_activations(x2d[i % 2], per_token=True), m * d * 3 + m * 4),
+        "adaln": (lambda i: fused.adaln(sets[i % 2]["x"], shift, scale), m * d * 4),
+        "qk_norm_rope_one_tensor": (lambda i: fused.qk_norm_rope(sets[i % 2]["q"], w, rope), 2 * m * h * hd * 2 + 2 * m * hd * 4),
+        "pixelumm_qk": (lambda i: fused.pixelumm_qk(sets[i % 2]["q"], wt, whw, *rope), 2 * m * h * hd * 2 + 2 * m * hd * 4),
+    }
+    res = {}
+    for name, (fn, nbytes) in cases.items():
+        fn(0)
+        times = []
+        for i in range(iters):
+            flush.zero_()
+            a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            a.record(stream)
+            fn(i)
+            b.record(stream)
+            b.synchronize()
+            times.append(a.elapsed_time(b))
+        res[name] = round(nbytes / (statistics.median(times) * 1e-3) / 1e9, 1)
+    return res
 
 
 def cpu_elementwise_chain(rows, d, h, hd, gen):

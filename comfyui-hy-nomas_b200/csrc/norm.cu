@@ -214,7 +214,7 @@ __global__ void __launch_bounds__(WP * 32, (WP <= 8) ? (MODE == 2 ? 2 : 3) : 1) 
         const float qsc = i8_scale(peak);
         uint32_t cP[4][2], cQ[4][2];
         if (qsc >= 0x1p-90f) {
-            const uint64_t ns = x2_splat(-qsc), rs = x2_splat(__fdiv_rn(1.0f, qsc));
+            const uint64_t ns = x2_splat(-qsc), rs = x2_splat(__frcp_rn(qsc));
 #pragma unroll
             for (int k = 0; k < 4; ++k) {
                 x2_codes(x2_quot(Z.P[k], ns, rs), cP[k][0], cP[k][1]);

@@ -5,6 +5,8 @@
 // (two 16-byte loads of bf16), 4 groups per warp. The group absmax is a 3-step xor-shuffle max; each lane
 // writes its 16 codes as one 16-byte store; the first lane of the group writes the fp32 scale.
 // HBM-bound: per element 2 bytes read (bf16) + 1 byte written, plus 4 bytes of scale per 128 elements.
+#include <type_traits>
+
 #include "hn_common.cuh"
 #include "hn_kernels.h"
 
@@ -39,7 +41,35 @@ __global__ void __launch_bounds__(256) k_quant_group(const TIn *__restrict__ x, 
         peak = warp_max_xor(peak, 8);
         float sc;
         uint4 out;
-        if (KIND == 0) {
+        constexpr bool BF16_IN = sizeof(TIn) == 2 && !std::is_same<TIn, __half>::value;
+        const float sc_try = KIND == 0 ? i8_scale(peak) : e4m3_scale(peak);
+        if (BF16_IN && sc_try >= 0x1p-90f) {
+            // bf16 input: the exact fma-corrected quotient (x2_quot), checked exhaustively over bf16 inputs
+            sc = sc_try;
+            const uint64_t ns = x2_splat(-sc), rs = x2_splat(__frcp_rn(sc));
+            if (KIND == 0) {
+                uint32_t c[16];
+#pragma unroll
+                for (int i = 0; i < 8; ++i) x2_codes(x2_quot(x2(v[2 * i], v[2 * i + 1]), ns, rs), c[2 * i], c[2 * i + 1]);
+                out.x = pack4_lowbytes(c[0], c[1], c[2], c[3]);
+                out.y = pack4_lowbytes(c[4], c[5], c[6], c[7]);
+                out.z = pack4_lowbytes(c[8], c[9], c[10], c[11]);
+                out.w = pack4_lowbytes(c[12], c[13], c[14], c[15]);
+            } else {
+                uint32_t h[8];
+#pragma unroll
+                for (int i = 0; i < 8; ++i) {
+                    float q0, q1;
+                    x2_split(x2_quot(x2(v[2 * i], v[2 * i + 1]), ns, rs), q0, q1);
+                    // a zero quotient keeps the sign of its input, as the IEEE quotient does
+                    h[i] = pack2_e4m3(copysignf(q0, v[2 * i]), copysignf(q1, v[2 * i + 1]));
+                }
+                out.x = h[0] | (h[1] << 16);
+                out.y = h[2] | (h[3] << 16);
+                out.z = h[4] | (h[5] << 16);
+                out.w = h[6] | (h[7] << 16);
+            }
+        } else if (KIND == 0) {
             sc = i8_scale(peak);
             int c[16];
 #pragma unroll

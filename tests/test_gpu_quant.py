@@ -100,3 +100,29 @@ def test_quantize_fp8_block_random(hn, oracle, cuda, dtype):
     q, s = hn.ops.quantize_fp8_block(w.to(cuda))
     qr, sr = oracle.quantize_fp8_block(w.float().numpy())
     assert np.array_equal(u8(q), qr) and np.array_equal(f32(s), sr)
+
+
+@pytest.mark.parametrize("kind", ["int8", "fp8"])
+def test_edge_values_bit_exact(hn, oracle, cuda, kind):
+    """Groups that exercise the quantizer's division: all zero, negative zeros, subnormal-range values (the
+    scale falls below 2^-90 and the kernel takes the IEEE division), exact .5 ties of the int8 rounding (peak
+    127 with half-integer values), mixed signs at the group maximum, and values near the bf16 maximum."""
+    g = 128
+    rows = []
+    rows.append(np.zeros(4 * g, np.float32))
+    rows.append(np.full(4 * g, -0.0, np.float32))
+    tiny = np.float32(1e-37) * np.linspace(-1, 1, 4 * g, dtype=np.float32)
+    rows.append(tiny)
+    ties = (np.arange(4 * g, dtype=np.float32) % 255 - 127).astype(np.float32) + 0.5
+    ties[::g] = 127.0
+    rows.append(ties)
+    mixed = np.linspace(-3.0, 3.0, 4 * g, dtype=np.float32)
+    mixed[5] = -3.0
+    rows.append(mixed)
+    rows.append(np.linspace(-3e38, 3e38, 4 * g, dtype=np.float32))
+    rows.append((np.random.default_rng(3).standard_normal(4 * g) * 1e-30).astype(np.float32))
+    x = torch.from_numpy(np.stack(rows)).bfloat16()
+    q, s = hn.kernels.quantize_activations(x.to(cuda), kind)
+    qo, so = oracle.quantize_activations(f32(x), kind)
+    assert np.array_equal(u8(q), qo)
+    assert np.array_equal(f32(s), so)
