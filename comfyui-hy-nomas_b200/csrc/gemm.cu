@@ -437,14 +437,17 @@ __global__ void __launch_bounds__(128 + 128 * NP, 1)
                     const uint32_t rbase = smem_u32(ring);
                     uint32_t bytes = 0;
                     const bool sa_grp = p.sa_mode == 0, sw_grp = PMODE == 0, sw_blk = PMODE == 1 && p.sw_mode == 2;
-                    if (sa_grp && !p.sa_bulk) {
+                    // bulk copies move whole 16-byte units: a tile whose row (column) count is not a multiple
+                    // of 4 - only the last one can be - gathers its scales so nothing past the end is read
+                    const bool sa_bulk = p.sa_bulk && (rows & 3) == 0, sw_bulk = p.sw_bulk && (cols & 3) == 0;
+                    if (sa_grp && !sa_bulk) {
 #pragma unroll
                         for (int i = 0; i < BM / 32; ++i) {
                             const int r = lane + 32 * i;
                             ring[C::RING_SA + r] = r < rows ? p.sa[(int64_t)(m0 + r) * p.sa_rs + (int64_t)g * p.sa_gs] : 0.0f;
                         }
                     }
-                    if (sw_grp && !p.sw_bulk) {
+                    if (sw_grp && !sw_bulk) {
 #pragma unroll
                         for (int i = 0; i < BN / 32; ++i) {
                             const int c = lane + 32 * i;
@@ -457,8 +460,8 @@ __global__ void __launch_bounds__(128 + 128 * NP, 1)
                     }
                     __syncwarp();
                     if (lane == 0) {
-                        const uint32_t sa_bytes = (sa_grp && p.sa_bulk) ? (uint32_t)(((rows + 3) & ~3) * 4) : 0u;
-                        const uint32_t sw_bytes = (sw_grp && p.sw_bulk) ? (uint32_t)(((cols + 3) & ~3) * 4) : 0u;
+                        const uint32_t sa_bytes = (sa_grp && sa_bulk) ? (uint32_t)(rows * 4) : 0u;
+                        const uint32_t sw_bytes = (sw_grp && sw_bulk) ? (uint32_t)(cols * 4) : 0u;
                         bytes = sa_bytes + sw_bytes;
                         const uint32_t fb = bar_sfull + 8 * slot;
                         if (bytes) mbar_arrive_tx(fb, bytes);
@@ -866,11 +869,11 @@ cudaError_t launch_block_gemm(const GemmArgs &a, cudaStream_t st, const char **m
     const int esz = (a.epilogue == 2) ? 1 : (a.out_dtype == 0 || a.out_dtype == 1) ? 2 : 4;
     p.vec_store = ((reinterpret_cast<uintptr_t>(a.out) % 16) == 0 && (a.ldo * esz) % 16 == 0) ? 1 : 0;
     p.sw_vec = (reinterpret_cast<uintptr_t>(a.sw) % 16) == 0 && a.sw_rs == 1 ? 1 : 0;
-    // bulk copies of one group's scales: group-major, 16-byte aligned rows, and a row count that is a
-    // multiple of 4 so no copy reads past the last row
-    p.sa_bulk = (a.sa_mode == 0 && a.sa_rs == 1 && a.sa_gs % 4 == 0 && a.M % 4 == 0 &&
+    // bulk copies of one group's scales: group-major with 16-byte aligned group rows (a tile with a row
+    // count that is not a multiple of 4 gathers instead, in the kernel)
+    p.sa_bulk = (a.sa_mode == 0 && a.sa_rs == 1 && a.sa_gs % 4 == 0 &&
                  reinterpret_cast<uintptr_t>(a.sa) % 16 == 0) ? 1 : 0;
-    p.sw_bulk = (a.sw_mode == 0 && a.sw_rs == 1 && a.sw_gs % 4 == 0 && a.N % 4 == 0 &&
+    p.sw_bulk = (a.sw_mode == 0 && a.sw_rs == 1 && a.sw_gs % 4 == 0 &&
                  reinterpret_cast<uintptr_t>(a.sw) % 16 == 0) ? 1 : 0;
     int grid = num_sms();
     if (grid > p.num_tiles) grid = p.num_tiles;
