@@ -884,6 +884,11 @@ def run_reference(args, world, rank):
 
 
 def main():
+    # the JSON line goes to the real stdout; everything else written to file descriptor 1 (NCCL's version
+    # banner, library messages) is redirected to stderr so stdout carries exactly one line
+    json_out = os.fdopen(os.dup(1), "w")
+    sys.stdout.flush()
+    os.dup2(2, 1)
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
     ap.add_argument("--steps", type=int, default=None, help="timed steps (default: 10 for dit, 50 otherwise; "
@@ -901,7 +906,7 @@ def main():
         if args.impl == "reference":
             line = run_reference(args, world, rank)
             if line is not None:
-                print(json.dumps(line), flush=True)
+                print(json.dumps(line), file=json_out, flush=True)
             return
         pk = peaks()
         stream = torch.cuda.current_stream()
@@ -919,7 +924,7 @@ def main():
                     "roofline": res["roofline"], "gpu_launches": res["gpu_launches"], "clocks": sampler.result}
             if world == 1 and cpu_fn is not None and not args.no_cpu_baseline:
                 line["cpu_baseline"] = cpu_fn()
-            print(json.dumps(line), flush=True)
+            print(json.dumps(line), file=json_out, flush=True)
     finally:
         if world > 1:
             dist.destroy_process_group()

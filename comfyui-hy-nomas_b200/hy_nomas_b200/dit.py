@@ -5,8 +5,8 @@ The block is the image stream of the reference's `DoubleStreamBlock` on its fuse
 
     shift1, scale1, gate1, shift2, scale2, gate2 = Modulate(vec)          int8 linear of silu(vec)
     qa, sa  = adaln_quant(x, shift1, scale1)                              LN + modulate + int8 quant
-    q, k, v = block_gemm(qa, sa, W_q / W_k / W_v)                         one GEMM for q|k, one for v
-    q, k    = qk_norm_rope(q), qk_norm_rope(k)                            one launch for both
+    q, k, v = block_gemm(qa, sa, W_q / W_k / W_v)                         one GEMM for v, one for q|k
+    q, k    = qk_norm_rope(q), qk_norm_rope(k)                            one launch for both (one GPU)
     attn    = scaled_dot_product_attention(q, K, V)                       torch SDPA, unchanged
     x       = gated_residual(x, proj(attn), gate1)                        proj = quantize + GEMM
     qh, sh  = block_gemm(adaln_quant(x, shift2, scale2), W_fc1, "gelu_quant")
@@ -131,6 +131,10 @@ class CudaOps:
         return fused.qk_norm_rope2(q, k, wq, wk, rope, out=out)
 
     @staticmethod
+    def qk_norm_rope(x, w, rope, out):
+        return fused.qk_norm_rope(x, w, rope, out=out)
+
+    @staticmethod
     def gated_residual_adaln_quant(x, y, gate, shift, scale):
         return fused.gated_residual_adaln_quant(x, y, gate, shift, scale)
 
@@ -158,15 +162,22 @@ def block_forward(cfg, w, x, vec, rope, sp, ops=CudaOps, trace=None):
     mods = ops.linear(act, w.mod)
     shift1, scale1, gate1, shift2, scale2, gate2 = mods.chunk(6, dim=-1)
     qa, sa = ops.adaln_quant(x, shift1, scale1)
+    k_full, v_full, k_mine, v_mine = sp.kv_buffers(b, l, h, hd, x.dtype, x.device)
+    # v first, so its all-gather runs under the q|k GEMM; k is normalized before q, so its gather runs under
+    # q's normalization (with one rank the gathers are no-ops and the order changes nothing)
+    ops.gemm(qa, sa, w.v, out=v_mine.view(b * l, d))
+    gather_v = sp.all_gather_async(v_full, v_mine)
     qk = ops.gemm(qa, sa, w.qk)                                       # [B*l, 2D]
     q_in = qk[:, :d].view(b, l, h, hd)
     k_in = qk[:, d:].view(b, l, h, hd)
-    k_full, v_full, k_mine, v_mine = sp.kv_buffers(b, l, h, hd, x.dtype, x.device)
     q_out = torch.empty((b, l, h, hd), dtype=x.dtype, device=x.device)
-    ops.qk_norm_rope2(q_in, k_in, w.q_norm, w.k_norm, rope, out=(q_out, k_mine))
-    gather_k = sp.all_gather_async(k_full, k_mine)
-    ops.gemm(qa, sa, w.v, out=v_mine.view(b * l, d))
-    gather_v = sp.all_gather_async(v_full, v_mine)
+    if sp.world > 1:
+        ops.qk_norm_rope(k_in, w.k_norm, rope, out=k_mine)
+        gather_k = sp.all_gather_async(k_full, k_mine)
+        ops.qk_norm_rope(q_in, w.q_norm, rope, out=q_out)
+    else:
+        ops.qk_norm_rope2(q_in, k_in, w.q_norm, w.k_norm, rope, out=(q_out, k_mine))
+        gather_k = None
     sp.wait(gather_k, gather_v)
     attn = ops.attention(q_out, k_full, v_full).reshape(b * l, d)
     proj = ops.linear(attn, w.proj).view(b, l, d)

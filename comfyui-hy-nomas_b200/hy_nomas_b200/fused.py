@@ -63,14 +63,20 @@ def _rope_tables(rope, device):
     return cos, sin
 
 
-def qk_norm_rope(x, weight, rope=None, eps=1e-6):
+def qk_norm_rope(x, weight, rope=None, eps=1e-6, out=None):
     """x [B, L, H, D] bf16 (rows may be strided, heads contiguous), weight [D] -> RMSNorm(x) * weight, then RoPE
-    with (cos, sin) [L, D] fp32 when given. Returns a contiguous [B, L, H, D] bf16 tensor."""
+    with (cos, sin) [L, D] fp32 when given. Returns a contiguous [B, L, H, D] bf16 tensor (`out`, when given:
+    a caller-owned contiguous bf16 tensor of that shape)."""
     _lib.require_cuda(x, weight)
     _bf16(x)
     b, l, h, d = x.shape
     x = _qk_input(x)
-    y = torch.empty((b, l, h, d), device=x.device, dtype=torch.bfloat16)
+    if out is None:
+        y = torch.empty((b, l, h, d), device=x.device, dtype=torch.bfloat16)
+    else:
+        y = out
+        if y.shape != (b, l, h, d) or y.dtype != torch.bfloat16 or not y.is_contiguous() or y.device != x.device:
+            raise ValueError(f"qk_norm_rope: out must be a contiguous bf16 [{b}, {l}, {h}, {d}] tensor")
     w = weight.to(torch.bfloat16).contiguous()
     cos, sin = _rope_tables(rope, x.device)
     rc = _lib.lib.hn_qk_norm_rope(_lib.ptr(x), x.stride(1), _lib.ptr(w), _lib.ptr(cos), _lib.ptr(sin), b, l, h, d,

@@ -61,6 +61,12 @@ class OracleOps:
         return out
 
     @staticmethod
+    def qk_norm_rope(x, w, rope, out):
+        rp = None if rope is None else (_np(rope[0]), _np(rope[1]))
+        out.copy_(_bf16(O.qk_norm_rope(_np(x), _np(w), rp)))
+        return out
+
+    @staticmethod
     def gated_residual_adaln_quant(x, y, gate, shift, scale):
         xo, q, s = O.gated_residual_adaln_quant(_np(x), _np(y), _np(gate), _np(shift), _np(scale))
         return _bf16(xo), torch.from_numpy(q), torch.from_numpy(s)
