@@ -456,52 +456,115 @@ cudaError_t launch_qk_norm_rope(int ntensors, const void *x0, const void *x1, in
 }
 
 // ---------------------------------------------------------------------------------------------------
-// K7 PixelUMM q/k prep (D == 128). Lane l owns elements [4l, 4l+4): lanes 0-15 the T half (t0 = lanes
-// 0-7, t1 = lanes 8-15), lanes 16-31 the HW half (h0, h1, w0, w1 in 4-lane quarters). Rotate-half
-// partners are lane ^ 8 (T) and lane ^ 4 (HW).
+// K7 PixelUMM q/k prep (fused.py:131-175, D == 128): a head is [t0 | t1 | h0 | h1 | w0 | w1] of 32, 32, 16, 16,
+// 16, 16 elements; t0/t1, h0/h1 and w0/w1 are rotate-half partners. One warp per token, four heads at a time,
+// 8 lanes per head: lane s (0..7) holds t0[4s..4s+4), t1[4s..4s+4) and h0/h1/w0/w1[2s..2s+2), so every
+// rotation partner is in the same lane. The sums of squares - pairwise trees in index order over t0 and t1
+// (32 each) and over h0, h1, w0, w1 (16 each) - are an in-lane first level (or two) and a butterfly over the
+// head's 8 lanes; the norms combine them as (sum t0^2 + sum t1^2) and ((h0 + h1) + w0) + w1 (fused.py:155-160).
+__device__ __forceinline__ float sum8_lanes(float v) {
+#pragma unroll
+    for (int o = 1; o < 8; o <<= 1) v = __fadd_rn(v, __shfl_xor_sync(0xffffffffu, v, o));
+    return v;
+}
+
 __global__ void __launch_bounds__(256) k_pixelumm_qk(const bf16 *__restrict__ x, int64_t row_stride,
                                                      const bf16 *__restrict__ wt, const bf16 *__restrict__ whw,
                                                      const float *__restrict__ cosp, const float *__restrict__ sinp,
                                                      int64_t N, int H, float eps, bf16 *__restrict__ y) {
-    const int lane = threadIdx.x & 31;
+    const int lane = threadIdx.x & 31, sub = lane & 7, hq = lane >> 3;
     const int64_t tok = (int64_t)blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5);
     if (tok >= N) return;
-    const bool tpart = lane < 16;
-    const bool first = tpart ? (lane < 8) : ((lane & 4) == 0);
-    const int partner = tpart ? (lane ^ 8) : (lane ^ 4);
-    uint2 wv = *reinterpret_cast<const uint2 *>(tpart ? (wt + 4 * lane) : (whw + 4 * lane - 64));
-    const float w[4] = {bf16_lo(wv.x), bf16_hi(wv.x), bf16_lo(wv.y), bf16_hi(wv.y)};
-    float4 cv = *reinterpret_cast<const float4 *>(cosp + tok * 128 + 4 * lane);
-    float4 sv = *reinterpret_cast<const float4 *>(sinp + tok * 128 + 4 * lane);
-    const float c[4] = {cv.x, cv.y, cv.z, cv.w}, sn[4] = {sv.x, sv.y, sv.z, sv.w};
-    for (int h = 0; h < H; ++h) {
-        uint2 xv = *reinterpret_cast<const uint2 *>(x + tok * row_stride + (int64_t)h * 128 + 4 * lane);
-        const float v[4] = {bf16_lo(xv.x), bf16_hi(xv.x), bf16_lo(xv.y), bf16_hi(xv.y)};
-        float s4 = __fadd_rn(__fadd_rn(__fmul_rn(v[0], v[0]), __fmul_rn(v[1], v[1])),
-                             __fadd_rn(__fmul_rn(v[2], v[2]), __fmul_rn(v[3], v[3])));
-        s4 = __fadd_rn(s4, __shfl_xor_sync(0xffffffffu, s4, 1));
-        s4 = __fadd_rn(s4, __shfl_xor_sync(0xffffffffu, s4, 2));   // 16-element sums
-        float s8 = __fadd_rn(s4, __shfl_xor_sync(0xffffffffu, s4, 4));   // 32-element sums (T lanes)
-        float st = __fadd_rn(s8, __shfl_xor_sync(0xffffffffu, s8, 8));   // sum(t0^2) + sum(t1^2)
-        const float sh0 = __shfl_sync(0xffffffffu, s4, 16), sh1 = __shfl_sync(0xffffffffu, s4, 20);
-        const float sw0 = __shfl_sync(0xffffffffu, s4, 24), sw1 = __shfl_sync(0xffffffffu, s4, 28);
-        const float shw = __fadd_rn(__fadd_rn(__fadd_rn(sh0, sh1), sw0), sw1);
-        const float sum = __shfl_sync(0xffffffffu, st, 0);
-        const float r = rsqrt_cr(__fadd_rn(__fdiv_rn(tpart ? sum : shw, 64.0f), eps));
-        float a[4], p[4];
+    // this lane's positions inside a head: T at [4s, 4s+4) and 32 + [4s, 4s+4); HW quarters at 64/80/96/112 + [2s, 2s+2)
+    const int pt0 = 4 * sub, pt1 = 32 + 4 * sub, ph0 = 64 + 2 * sub, ph1 = 80 + 2 * sub, pw0 = 96 + 2 * sub, pw1 = 112 + 2 * sub;
+    // weights (wt over the T half [0, 64), whw over the HW half) and the token's cos/sin at the same positions
+    float wgt[16], cs[16], sn[16];
+    {
+        const uint2 a = *reinterpret_cast<const uint2 *>(wt + pt0), b = *reinterpret_cast<const uint2 *>(wt + pt1);
+        wgt[0] = bf16_lo(a.x); wgt[1] = bf16_hi(a.x); wgt[2] = bf16_lo(a.y); wgt[3] = bf16_hi(a.y);
+        wgt[4] = bf16_lo(b.x); wgt[5] = bf16_hi(b.x); wgt[6] = bf16_lo(b.y); wgt[7] = bf16_hi(b.y);
+        const int ph[4] = {ph0, ph1, pw0, pw1};
 #pragma unroll
-        for (int i = 0; i < 4; ++i) a[i] = __fmul_rn(__fmul_rn(v[i], r), w[i]);
+        for (int q = 0; q < 4; ++q) {
+            const uint32_t w2 = *reinterpret_cast<const uint32_t *>(whw + ph[q] - 64);
+            wgt[8 + 2 * q] = bf16_lo(w2);
+            wgt[9 + 2 * q] = bf16_hi(w2);
+        }
+        const float *cb = cosp + tok * 128, *sb = sinp + tok * 128;
+        const float4 c0 = *reinterpret_cast<const float4 *>(cb + pt0), c1 = *reinterpret_cast<const float4 *>(cb + pt1);
+        const float4 s0 = *reinterpret_cast<const float4 *>(sb + pt0), s1 = *reinterpret_cast<const float4 *>(sb + pt1);
+        cs[0] = c0.x; cs[1] = c0.y; cs[2] = c0.z; cs[3] = c0.w; cs[4] = c1.x; cs[5] = c1.y; cs[6] = c1.z; cs[7] = c1.w;
+        sn[0] = s0.x; sn[1] = s0.y; sn[2] = s0.z; sn[3] = s0.w; sn[4] = s1.x; sn[5] = s1.y; sn[6] = s1.z; sn[7] = s1.w;
 #pragma unroll
-        for (int i = 0; i < 4; ++i) p[i] = __shfl_sync(0xffffffffu, a[i], partner);
-        float o[4];
+        for (int q = 0; q < 4; ++q) {
+            const float2 c2 = *reinterpret_cast<const float2 *>(cb + ph[q]);
+            const float2 s2 = *reinterpret_cast<const float2 *>(sb + ph[q]);
+            cs[8 + 2 * q] = c2.x; cs[9 + 2 * q] = c2.y;
+            sn[8 + 2 * q] = s2.x; sn[9 + 2 * q] = s2.y;
+        }
+    }
+    for (int h0 = 0; h0 < H; h0 += 4) {
+        const int h = h0 + hq;
+        const bool on = h < H;
+        const bf16 *xr = x + tok * row_stride + (int64_t)h * 128;
+        float v[16];
+        if (on) {
+            const uint2 a = *reinterpret_cast<const uint2 *>(xr + pt0), b = *reinterpret_cast<const uint2 *>(xr + pt1);
+            v[0] = bf16_lo(a.x); v[1] = bf16_hi(a.x); v[2] = bf16_lo(a.y); v[3] = bf16_hi(a.y);
+            v[4] = bf16_lo(b.x); v[5] = bf16_hi(b.x); v[6] = bf16_lo(b.y); v[7] = bf16_hi(b.y);
+            const int ph[4] = {ph0, ph1, pw0, pw1};
 #pragma unroll
-        for (int i = 0; i < 4; ++i)
-            o[i] = first ? __fsub_rn(__fmul_rn(a[i], c[i]), __fmul_rn(p[i], sn[i]))
-                         : __fadd_rn(__fmul_rn(a[i], c[i]), __fmul_rn(p[i], sn[i]));
-        uint2 ov;
-        ov.x = pack_bf16_rn(o[0], o[1]);
-        ov.y = pack_bf16_rn(o[2], o[3]);
-        *reinterpret_cast<uint2 *>(y + (tok * H + h) * 128 + 4 * lane) = ov;
+            for (int q = 0; q < 4; ++q) {
+                const uint32_t w2 = *reinterpret_cast<const uint32_t *>(xr + ph[q]);
+                v[8 + 2 * q] = bf16_lo(w2);
+                v[9 + 2 * q] = bf16_hi(w2);
+            }
+        } else {
+#pragma unroll
+            for (int i = 0; i < 16; ++i) v[i] = 0.0f;
+        }
+        // squares; the in-lane levels of each pairwise tree, then the 8-lane butterflies
+        float sq[16];
+#pragma unroll
+        for (int i = 0; i < 16; ++i) sq[i] = __fmul_rn(v[i], v[i]);
+        const float t0 = sum8_lanes(__fadd_rn(__fadd_rn(sq[0], sq[1]), __fadd_rn(sq[2], sq[3])));
+        const float t1 = sum8_lanes(__fadd_rn(__fadd_rn(sq[4], sq[5]), __fadd_rn(sq[6], sq[7])));
+        const float a0 = sum8_lanes(__fadd_rn(sq[8], sq[9]));
+        const float a1 = sum8_lanes(__fadd_rn(sq[10], sq[11]));
+        const float a2 = sum8_lanes(__fadd_rn(sq[12], sq[13]));
+        const float a3 = sum8_lanes(__fadd_rn(sq[14], sq[15]));
+        const float st = __fadd_rn(t0, t1);
+        const float shw = __fadd_rn(__fadd_rn(__fadd_rn(a0, a1), a2), a3);
+        // / 64 (half of D) is the exact product * 2^-6
+        const float rt = rsqrt_cr(__fadd_rn(__fmul_rn(st, 0.015625f), eps));
+        const float rhw = rsqrt_cr(__fadd_rn(__fmul_rn(shw, 0.015625f), eps));
+        float n[16];
+#pragma unroll
+        for (int i = 0; i < 16; ++i) n[i] = __fmul_rn(__fmul_rn(v[i], i < 8 ? rt : rhw), wgt[i]);
+        float o[16];
+        // T: (t0*c - t1*s, t1*c + t0*s) for positions i (t0) and 32 + i (t1)
+#pragma unroll
+        for (int i = 0; i < 4; ++i) {
+            o[i] = __fsub_rn(__fmul_rn(n[i], cs[i]), __fmul_rn(n[4 + i], sn[i]));
+            o[4 + i] = __fadd_rn(__fmul_rn(n[4 + i], cs[4 + i]), __fmul_rn(n[i], sn[4 + i]));
+        }
+        // HW: h0/h1 (slots 8-9 / 10-11) and w0/w1 (slots 12-13 / 14-15)
+#pragma unroll
+        for (int i = 0; i < 2; ++i) {
+            o[8 + i] = __fsub_rn(__fmul_rn(n[8 + i], cs[8 + i]), __fmul_rn(n[10 + i], sn[8 + i]));
+            o[10 + i] = __fadd_rn(__fmul_rn(n[10 + i], cs[10 + i]), __fmul_rn(n[8 + i], sn[10 + i]));
+            o[12 + i] = __fsub_rn(__fmul_rn(n[12 + i], cs[12 + i]), __fmul_rn(n[14 + i], sn[12 + i]));
+            o[14 + i] = __fadd_rn(__fmul_rn(n[14 + i], cs[14 + i]), __fmul_rn(n[12 + i], sn[14 + i]));
+        }
+        if (on) {
+            bf16 *yr = y + (tok * H + h) * 128;
+            *reinterpret_cast<uint2 *>(yr + pt0) = make_uint2(bf16x2_rn(o[0], o[1]), bf16x2_rn(o[2], o[3]));
+            *reinterpret_cast<uint2 *>(yr + pt1) = make_uint2(bf16x2_rn(o[4], o[5]), bf16x2_rn(o[6], o[7]));
+            *reinterpret_cast<uint32_t *>(yr + ph0) = bf16x2_rn(o[8], o[9]);
+            *reinterpret_cast<uint32_t *>(yr + ph1) = bf16x2_rn(o[10], o[11]);
+            *reinterpret_cast<uint32_t *>(yr + pw0) = bf16x2_rn(o[12], o[13]);
+            *reinterpret_cast<uint32_t *>(yr + pw1) = bf16x2_rn(o[14], o[15]);
+        }
     }
 }
 

@@ -116,11 +116,31 @@ __global__ void __launch_bounds__(256) k_quant_row(const TIn *__restrict__ x, in
     peak = 0.0f;
     for (int w = 0; w < (int)(blockDim.x >> 5); ++w) peak = fmaxf(peak, red[w]);
     const float sc = KIND == 0 ? i8_scale(peak) : e4m3_scale(peak);
+    // bf16 input: the exact fma-corrected quotient (as in k_quant_group)
+    constexpr bool BF16_IN = sizeof(TIn) == 2 && !std::is_same<TIn, __half>::value;
+    const bool fast = BF16_IN && sc >= 0x1p-90f;
+    const uint64_t ns = x2_splat(-sc), rs = x2_splat(__frcp_rn(sc));
     for (int64_t c = (int64_t)threadIdx.x * 8; c < K; c += (int64_t)blockDim.x * 8) {
         float v[8];
         Elem<TIn>::load8(row + c, v);
         uint2 out;
-        if (KIND == 0) {
+        if (fast && KIND == 0) {
+            uint32_t cc[8];
+#pragma unroll
+            for (int i = 0; i < 4; ++i) x2_codes(x2_quot(x2(v[2 * i], v[2 * i + 1]), ns, rs), cc[2 * i], cc[2 * i + 1]);
+            out.x = pack4_lowbytes(cc[0], cc[1], cc[2], cc[3]);
+            out.y = pack4_lowbytes(cc[4], cc[5], cc[6], cc[7]);
+        } else if (fast) {
+            uint32_t h[4];
+#pragma unroll
+            for (int i = 0; i < 4; ++i) {
+                float q0, q1;
+                x2_split(x2_quot(x2(v[2 * i], v[2 * i + 1]), ns, rs), q0, q1);
+                h[i] = pack2_e4m3(copysignf(q0, v[2 * i]), copysignf(q1, v[2 * i + 1]));
+            }
+            out.x = h[0] | (h[1] << 16);
+            out.y = h[2] | (h[3] << 16);
+        } else if (KIND == 0) {
             int cc[8];
 #pragma unroll
             for (int i = 0; i < 8; ++i) cc[i] = code_i8(__fdiv_rn(v[i], sc));

@@ -126,3 +126,20 @@ def test_edge_values_bit_exact(hn, oracle, cuda, kind):
     qo, so = oracle.quantize_activations(f32(x), kind)
     assert np.array_equal(u8(q), qo)
     assert np.array_equal(f32(s), so)
+
+
+@pytest.mark.parametrize("kind", ["int8", "fp8"])
+def test_per_token_edge_rows(hn, oracle, cuda, kind):
+    """Per-token quantization of the edge rows (zeros, negative zeros, subnormal-range values, .5 ties, values
+    near the bf16 maximum) over a 1024-wide row: codes and scales bit-exact with the oracle."""
+    k = 1024
+    rows = [np.zeros(k, np.float32), np.full(k, -0.0, np.float32),
+            np.float32(1e-37) * np.linspace(-1, 1, k, dtype=np.float32),
+            (np.arange(k, dtype=np.float32) % 255 - 127).astype(np.float32) + 0.5,
+            np.linspace(-3e38, 3e38, k, dtype=np.float32)]
+    rows[3][0] = 127.0
+    x = torch.from_numpy(np.stack(rows)).bfloat16()
+    q, s = hn.kernels.quantize_activations(x.to(cuda), kind, per_token=True)
+    qo, so = oracle.quantize_activations(f32(x), kind, per_row=True)
+    assert np.array_equal(u8(q), qo)
+    assert np.array_equal(f32(s).reshape(-1), so.reshape(-1))
