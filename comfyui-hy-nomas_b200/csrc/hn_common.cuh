@@ -107,8 +107,6 @@ __device__ __forceinline__ float gelu_tanh(float x) {
     return __fmul_rn(__fmul_rn(0.5f, x), __fadd_rn(1.0f, __fsub_rn(__fmul_rn(2.0f, sig), 1.0f)));
 }
 
-__device__ __forceinline__ uint32_t smem_addr(const void *p) { return (uint32_t)__cvta_generic_to_shared(p); }
-
 // ---------------------------------------------------------------------------------------------------
 // packed pairs of fp32 (sm_100 f32x2 instructions, explicit rounding: never contracted)
 
