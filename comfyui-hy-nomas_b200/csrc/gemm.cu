@@ -8,20 +8,25 @@
 //               multicast) of the A tile (warp 0) and the B tile (warp 2) into a ring of shared-memory
 //               stages; one thread's bulk-tensor requests are serviced in order, so two issuing warps and
 //               two groups per request raise the operand rate an SM draws from L2.
-//   warp 3      scale ring: each group's activation scales for the tile's 128 rows (and the weight scales of
-//               its BN columns when they vary per group) into a ring of shared-memory slots - one bulk copy
-//               per group when the scales are group-major, plain loads otherwise.
+//   warp 3      scale ring: per pair of K groups, both groups' activation scales for the tile's 128 rows
+//               (and the weight scales of its BN columns when they vary per group) into two shared-memory
+//               slots that complete on one barrier - bulk copies when the scales are group-major, plain
+//               loads otherwise.
 //   warp 1      MMA issuer: owns 512 TMEM columns = NBUF accumulators of BN columns; per K group it issues
 //               4 x tcgen05.mma.kind::{i8,f8f6f4} (M=128, N=BN, K=32) and tcgen05.commit's the stage back
-//               to the producers and the accumulator to the epilogue.
+//               to the producers and the accumulator (per-group modes: the pair of accumulators) to the
+//               epilogue.
 //   epilogue    warp w (w >= 4) owns TMEM lanes 32*(w%4).. (32 output rows) and column part (w-4)/4, i.e.
 //               each thread one row x BN/NPART columns.
 // Two tile shapes, by how the scales vary along K:
 //   * per-group scales (PMODE 0, 1): BN = 128, NBUF = 4, GPS = 2, four epilogue warpgroups (640 threads).
-//     For every group the epilogue reads the int32 (or fp32) partial from TMEM, hands the accumulator
-//     back to the tensor core, converts the partial exactly (int32 + 0x4B400000 reinterpreted, minus
-//     1.5 * 2^23: exact for |p| < 2^22) and folds it into 32 fp32 accumulators per thread with packed
-//     f32x2 multiply / FMA, while the tensor core fills the next three accumulators.
+//     The four accumulators form two pairs, one pair per stage (two K groups): every handover - operands
+//     in, pair to the epilogue, pair back, scales in, scale slots back - is one barrier per pair, since
+//     each barrier round trip drains the tensor pipe's short queue. For every group the epilogue reads
+//     the int32 (or fp32) partial from TMEM, hands the pair back after its second read, converts the
+//     partial exactly (int32 + 0x4B400000 reinterpreted, minus 1.5 * 2^23: exact for |p| < 2^22) and
+//     folds it into 32 fp32 accumulators per thread with packed f32x2 multiply / FMA, while the tensor
+//     core fills the other pair.
 //   * per-row scales on both sides (PMODE 2): BN = 256, NBUF = 2, GPS = 1, two epilogue warpgroups (384
 //     threads); the tensor core accumulates all of K in one accumulator and the epilogue streams it out of
 //     TMEM in 32-column chunks, overlapped with the next tile's MMAs.
@@ -60,7 +65,7 @@ namespace gemm {
 
 constexpr int BM = 128, BK = 128;
 constexpr int EPI_WARP0 = 4;  // warpgroup 0: producers, MMA issuer, scale ring; epilogue warpgroups follow
-constexpr int SW_SLOTS = 8;   // scale-ring depth (groups the scale producer runs ahead)
+constexpr int SW_SLOTS = 8;   // scale-ring depth in groups (SW_SLOTS / 2 pair slots the producer runs ahead)
 // K groups per pipeline stage (and per TMA request) for the 128-wide and the 256-wide tile
 constexpr int GPS_NARROW = 2, GPS_WIDE = 1;
 // epilogue warpgroups (column parts of a tile row): the per-group promotion modes hand every 128-column
@@ -420,64 +425,72 @@ __global__ void __launch_bounds__(128 + 128 * NP, 1)
         }
     } else if (warp == 3) {
         // ------------------------------------------------------------------ scale ring (PMODE 0, 1)
-        // Per K group: the activation scales of the tile's rows, the weight scales of its columns (group
-        // mode) or of its 128-column blocks (block mode). Group-major scales arrive by bulk copies that
-        // complete on the slot's barrier; other layouts are gathered with plain loads.
+        // Per pair of K groups (one pipeline stage): the activation scales of the tile's rows, the weight
+        // scales of its columns (group mode) or of its 128-column blocks (block mode), for both groups, in two
+        // consecutive slots that complete on one barrier. Group-major scales arrive by bulk copies; other
+        // layouts are gathered with plain loads.
         if (PMODE != 2) {
-            int slot = 0, issued = 0;
+            static_assert(PMODE == 2 || GPS == 2, "per-group promotion hands over K groups in pairs (GPS == 2)");
+            int ps = 0, issued = 0;
             uint32_t sphase = 0;
             bool ok = true;
             for (int tile = blockIdx.x; tile < p.num_tiles && ok; tile += gridDim.x) {
                 const int m0 = (tile / p.n_blocks) * BM, n0 = (tile % p.n_blocks) * BN;
                 const int rows = min(BM, p.M - m0), cols = min(BN, p.N - n0);
-                for (int g = 0; g < G; ++g) {
-                    ok = warp_wait(lane, bar_sempty + 8 * slot, sphase ^ 1, abort_flag, WAIT_NS);
+                for (int g0 = 0; g0 < G; g0 += 2) {
+                    ok = warp_wait(lane, bar_sempty + 8 * ps, sphase ^ 1, abort_flag, WAIT_NS);
                     if (!ok) break;
-                    float *ring = sw_s + slot * C::RING_FLOATS;
-                    const uint32_t rbase = smem_u32(ring);
-                    uint32_t bytes = 0;
+                    const int ng = min(2, G - g0);
                     const bool sa_grp = p.sa_mode == 0, sw_grp = PMODE == 0, sw_blk = PMODE == 1 && p.sw_mode == 2;
                     // bulk copies move whole 16-byte units: a tile whose row (column) count is not a multiple
                     // of 4 - only the last one can be - gathers its scales so nothing past the end is read
                     const bool sa_bulk = p.sa_bulk && (rows & 3) == 0, sw_bulk = p.sw_bulk && (cols & 3) == 0;
-                    if (sa_grp && !sa_bulk) {
+                    for (int gi = 0; gi < ng; ++gi) {
+                        const int g = g0 + gi;
+                        float *ring = sw_s + (2 * ps + gi) * C::RING_FLOATS;
+                        if (sa_grp && !sa_bulk) {
 #pragma unroll
-                        for (int i = 0; i < BM / 32; ++i) {
-                            const int r = lane + 32 * i;
-                            ring[C::RING_SA + r] = r < rows ? p.sa[(int64_t)(m0 + r) * p.sa_rs + (int64_t)g * p.sa_gs] : 0.0f;
+                            for (int i = 0; i < BM / 32; ++i) {
+                                const int r = lane + 32 * i;
+                                ring[C::RING_SA + r] = r < rows ? p.sa[(int64_t)(m0 + r) * p.sa_rs + (int64_t)g * p.sa_gs] : 0.0f;
+                            }
                         }
-                    }
-                    if (sw_grp && !sw_bulk) {
+                        if (sw_grp && !sw_bulk) {
 #pragma unroll
-                        for (int i = 0; i < BN / 32; ++i) {
-                            const int c = lane + 32 * i;
-                            ring[C::RING_SW + c] = c < cols ? p.sw[(int64_t)(n0 + c) * p.sw_rs + (int64_t)g * p.sw_gs] : 0.0f;
+                            for (int i = 0; i < BN / 32; ++i) {
+                                const int c = lane + 32 * i;
+                                ring[C::RING_SW + c] = c < cols ? p.sw[(int64_t)(n0 + c) * p.sw_rs + (int64_t)g * p.sw_gs] : 0.0f;
+                            }
                         }
-                    }
-                    if (sw_blk && lane < BN / 128) {
-                        const int nb = n0 / 128 + lane;
-                        ring[C::RING_SB + lane] = (nb * 128 < p.N) ? p.sw[(int64_t)nb * p.sw_rs + (int64_t)g * p.sw_gs] : 0.0f;
+                        if (sw_blk && lane < BN / 128) {
+                            const int nb = n0 / 128 + lane;
+                            ring[C::RING_SB + lane] = (nb * 128 < p.N) ? p.sw[(int64_t)nb * p.sw_rs + (int64_t)g * p.sw_gs] : 0.0f;
+                        }
                     }
                     __syncwarp();
                     if (lane == 0) {
                         const uint32_t sa_bytes = (sa_grp && sa_bulk) ? (uint32_t)(rows * 4) : 0u;
                         const uint32_t sw_bytes = (sw_grp && sw_bulk) ? (uint32_t)(cols * 4) : 0u;
-                        bytes = sa_bytes + sw_bytes;
-                        const uint32_t fb = bar_sfull + 8 * slot;
+                        const uint32_t bytes = (uint32_t)ng * (sa_bytes + sw_bytes);
+                        const uint32_t fb = bar_sfull + 8 * ps;
                         if (bytes) mbar_arrive_tx(fb, bytes);
                         else mbar_arrive(fb);
-                        if (sa_bytes) bulk_load(rbase + 4 * C::RING_SA, p.sa + (int64_t)g * p.sa_gs + m0, sa_bytes, fb);
-                        if (sw_bytes) bulk_load(rbase + 4 * C::RING_SW, p.sw + (int64_t)g * p.sw_gs + n0, sw_bytes, fb);
+                        for (int gi = 0; gi < ng; ++gi) {
+                            const int g = g0 + gi;
+                            const uint32_t rbase = smem_u32(sw_s + (2 * ps + gi) * C::RING_FLOATS);
+                            if (sa_bytes) bulk_load(rbase + 4 * C::RING_SA, p.sa + (int64_t)g * p.sa_gs + m0, sa_bytes, fb);
+                            if (sw_bytes) bulk_load(rbase + 4 * C::RING_SW, p.sw + (int64_t)g * p.sw_gs + n0, sw_bytes, fb);
+                        }
                     }
                     ++issued;
-                    if (++slot == SW_SLOTS) { slot = 0; sphase ^= 1; }
+                    if (++ps == SW_SLOTS / 2) { ps = 0; sphase ^= 1; }
                 }
             }
             // drain: the last bulk copies land before the CTA can exit
-            int st = slot;
+            int st = ps;
             uint32_t ph = sphase;
-            for (int i = 0; i < SW_SLOTS && i < issued; ++i) {
-                if (--st < 0) { st = SW_SLOTS - 1; ph ^= 1; }
+            for (int i = 0; i < SW_SLOTS / 2 && i < issued; ++i) {
+                if (--st < 0) { st = SW_SLOTS / 2 - 1; ph ^= 1; }
                 volatile int never = 0;
                 if (lane == 0) mbar_wait(bar_sfull + 8 * st, ph, &never, 100000000ull);
             }
@@ -502,30 +515,30 @@ __global__ void __launch_bounds__(128 + 128 * NP, 1)
             for (int g0 = 0; g0 < G && ok; g0 += GPS) {
                 ok = warp_wait(lane, bar_full + 8 * stage, phase, abort_flag, WAIT_NS);
                 if (!ok) break;
+                if (PMODE != 2) {
+                    // per-group promotion: the stage's two groups go to the two accumulators of TMEM pair tb
+                    // (NBUF / 2 pairs), handed over with one barrier each way
+                    ok = warp_wait(lane, bar_tempty + 8 * tb, tphase ^ 1, abort_flag, WAIT_NS);
+                    if (!ok) break;
+                }
                 tc_fence_after();
+                if (lane == 0) {
 #pragma unroll
-                for (int gi = 0; gi < GPS; ++gi) {
-                    const int g = g0 + gi;
-                    if (g >= G) break;
-                    if (PMODE != 2) {
-                        ok = warp_wait(lane, bar_tempty + 8 * tb, tphase ^ 1, abort_flag, WAIT_NS);
-                        if (!ok) break;
-                        tc_fence_after();
-                    }
-                    if (lane == 0) {
-                        const uint32_t d = tmem_base + (uint32_t)(tb * BN);
+                    for (int gi = 0; gi < GPS; ++gi) {
+                        const int g = g0 + gi;
+                        if (g >= G) break;
+                        const uint32_t d = tmem_base + (uint32_t)(((PMODE != 2) ? (2 * tb + gi) : tb) * BN);
                         const uint64_t ad = sdesc(sbase + C::OFF_A + stage * C::A_STAGE + gi * C::A_GROUP);
                         const uint64_t bd = sdesc(sbase + C::OFF_B + stage * C::B_STAGE + gi * C::B_GROUP);
 #pragma unroll
                         for (int k = 0; k < BK / 32; ++k)
                             mma_128xNx32<KIND>(d, ad + 2 * k, bd + 2 * k, idesc,
                                                (PMODE == 2) ? (uint32_t)(g > 0 || k > 0) : (uint32_t)(k > 0));
-                        if (PMODE != 2) mma_commit(bar_tfull + 8 * tb);
                     }
-                    __syncwarp();
-                    if (PMODE != 2) { if (++tb == NBUF) { tb = 0; tphase ^= 1; } }
+                    if (PMODE != 2) mma_commit(bar_tfull + 8 * tb);
                 }
-                if (!ok) break;
+                __syncwarp();
+                if (PMODE != 2) { if (++tb == NBUF / 2) { tb = 0; tphase ^= 1; } }
                 if (lane == 0) mma_commit(bar_empty + 8 * stage);
                 __syncwarp();
                 last_stage = stage;
@@ -568,43 +581,52 @@ __global__ void __launch_bounds__(128 + 128 * NP, 1)
 #pragma unroll
                 for (int i = 0; i < CPT / 2; ++i) acc[i] = 0ull;
                 const float sa_row = (p.sa_mode == 1) ? p.sa[(int64_t)mm * p.sa_rs] : 0.0f;
-                for (int g = 0; g < G; ++g) {
+                for (int g0 = 0; g0 < G; g0 += 2) {
+                    // one pair of K groups: its scales (pair slot ps) and its two accumulators (TMEM pair tb)
+                    const int ng = min(2, G - g0);
                     ok = warp_wait(lane, bar_sfull + 8 * slot, sphase, abort_flag, WAIT_NS);
                     if (!ok) break;
-                    const float *ring = sw_s + slot * C::RING_FLOATS;
-                    const float sa_g = (p.sa_mode == 0) ? ring[C::RING_SA + row] : sa_row;
-                    float s = sa_g;
-                    if (PMODE == 1 && p.sw_mode == 2)
-                        s = (ncol0 < p.N) ? __fmul_rn(sa_g, ring[C::RING_SB + (hf * CPT) / 128]) : 0.0f;
-                    const uint64_t s2 = pk(s, s);
                     ok = warp_wait(lane, bar_tfull + 8 * tb, tphase, abort_flag, WAIT_NS);
                     if (!ok) break;
                     tc_fence_after();
-                    // move this group's partials out of TMEM and hand the accumulator straight back to the
-                    // tensor core, then fold them in from registers
-                    uint32_t r[CPT];
+                    // group by group: the partials out of TMEM (after the pair's last read the pair goes back to the
+                    // tensor core), then folded in from registers
 #pragma unroll
-                    for (int c = 0; c < CPT / 32; ++c)
-                        tmem_ld32(lane_addr + (uint32_t)(tb * BN + hf * CPT + 32 * c), *reinterpret_cast<uint32_t(*)[32]>(r + 32 * c));
-                    tc_fence_before();
-                    __syncwarp();
-                    if (lane == 0) mbar_arrive(bar_tempty + 8 * tb);
-                    const float *sws = ring + C::RING_SW + hf * CPT;
+                    for (int gi = 0; gi < 2; ++gi) {
+                        if (gi >= ng) break;
+                        uint32_t r[CPT];
 #pragma unroll
-                    for (int j = 0; j < CPT; j += 4) {
-                        if (PMODE == 0) {
-                            const float4 w4 = *reinterpret_cast<const float4 *>(sws + j);
-                            promote_gen<KIND>(acc[j / 2], r[j], r[j + 1], s2, pk(w4.x, w4.y));
-                            promote_gen<KIND>(acc[j / 2 + 1], r[j + 2], r[j + 3], s2, pk(w4.z, w4.w));
-                        } else {
-                            promote_row<KIND>(acc[j / 2], r[j], r[j + 1], s2);
-                            promote_row<KIND>(acc[j / 2 + 1], r[j + 2], r[j + 3], s2);
+                        for (int c = 0; c < CPT / 32; ++c)
+                            tmem_ld32(lane_addr + (uint32_t)((2 * tb + gi) * BN + hf * CPT + 32 * c),
+                                      *reinterpret_cast<uint32_t(*)[32]>(r + 32 * c));
+                        if (gi == ng - 1) {
+                            tc_fence_before();
+                            __syncwarp();
+                            if (lane == 0) mbar_arrive(bar_tempty + 8 * tb);
+                        }
+                        const float *ring = sw_s + (2 * slot + gi) * C::RING_FLOATS;
+                        const float sa_g = (p.sa_mode == 0) ? ring[C::RING_SA + row] : sa_row;
+                        float s = sa_g;
+                        if (PMODE == 1 && p.sw_mode == 2)
+                            s = (ncol0 < p.N) ? __fmul_rn(sa_g, ring[C::RING_SB + (hf * CPT) / 128]) : 0.0f;
+                        const uint64_t s2 = pk(s, s);
+                        const float *sws = ring + C::RING_SW + hf * CPT;
+#pragma unroll
+                        for (int j = 0; j < CPT; j += 4) {
+                            if (PMODE == 0) {
+                                const float4 w4 = *reinterpret_cast<const float4 *>(sws + j);
+                                promote_gen<KIND>(acc[j / 2], r[j], r[j + 1], s2, pk(w4.x, w4.y));
+                                promote_gen<KIND>(acc[j / 2 + 1], r[j + 2], r[j + 3], s2, pk(w4.z, w4.w));
+                            } else {
+                                promote_row<KIND>(acc[j / 2], r[j], r[j + 1], s2);
+                                promote_row<KIND>(acc[j / 2 + 1], r[j + 2], r[j + 3], s2);
+                            }
                         }
                     }
                     __syncwarp();
                     if (lane == 0) mbar_arrive(bar_sempty + 8 * slot);
-                    if (++tb == NBUF) { tb = 0; tphase ^= 1; }
-                    if (++slot == SW_SLOTS) { slot = 0; sphase ^= 1; }
+                    if (++tb == NBUF / 2) { tb = 0; tphase ^= 1; }
+                    if (++slot == SW_SLOTS / 2) { slot = 0; sphase ^= 1; }
                 }
                 if (!ok) break;
                 float v[CPT];
