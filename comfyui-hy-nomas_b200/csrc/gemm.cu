@@ -10,8 +10,8 @@
 //               two groups per request raise the operand rate an SM draws from L2.
 //   warp 3      scale ring: per pair of K groups, both groups' activation scales for the tile's 128 rows
 //               (and the weight scales of its BN columns when they vary per group) into two shared-memory
-//               slots that complete on one barrier - bulk copies when the scales are group-major, plain
-//               loads otherwise.
+//               slots that complete on one barrier - bulk copies when the scales are group-major, 4-byte
+//               cp.async copies otherwise, several pairs in flight either way.
 //   warp 1      MMA issuer: owns 512 TMEM columns = NBUF accumulators of BN columns; per K group it issues
 //               4 x tcgen05.mma.kind::{i8,f8f6f4} (M=128, N=BN, K=32) and tcgen05.commit's the stage back
 //               to the producers and the accumulator (per-group modes: the pair of accumulators) to the
@@ -174,6 +174,17 @@ __device__ __forceinline__ void bulk_load(uint32_t dst, const void *src, uint32_
     asm volatile("cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];"
                  ::"r"(dst), "l"(src), "r"(bytes), "r"(bar)
                  : "memory");
+}
+
+// 4-byte asynchronous copy global -> shared; `valid` false writes zero and reads nothing (src-size 0)
+__device__ __forceinline__ void cp_async4(uint32_t dst, const float *src, bool valid) {
+    asm volatile("cp.async.ca.shared.global [%0], [%1], 4, %2;" ::"r"(dst), "l"(src), "r"(valid ? 4 : 0) : "memory");
+}
+
+// the mbarrier receives one arrival when this thread's earlier cp.async copies have landed (the pending count
+// is raised now and lowered then, so the barrier's expected count is unchanged)
+__device__ __forceinline__ void cp_async_arrive(uint32_t bar) {
+    asm volatile("cp.async.mbarrier.arrive.shared::cta.b64 [%0];" ::"r"(bar) : "memory");
 }
 
 __device__ __forceinline__ void tma_load_3d(const CUtensorMap *map, uint32_t dst, uint32_t bar, int row, int group) {
@@ -428,7 +439,7 @@ __global__ void __launch_bounds__(128 + 128 * NP, 1)
         // Per pair of K groups (one pipeline stage): the activation scales of the tile's rows, the weight
         // scales of its columns (group mode) or of its 128-column blocks (block mode), for both groups, in two
         // consecutive slots that complete on one barrier. Group-major scales arrive by bulk copies; other
-        // layouts are gathered with plain loads.
+        // layouts are gathered with 4-byte cp.async copies.
         if (PMODE != 2) {
             static_assert(PMODE == 2 || GPS == 2, "per-group promotion hands over K groups in pairs (GPS == 2)");
             int ps = 0, issued = 0;
@@ -445,28 +456,36 @@ __global__ void __launch_bounds__(128 + 128 * NP, 1)
                     // bulk copies move whole 16-byte units: a tile whose row (column) count is not a multiple
                     // of 4 - only the last one can be - gathers its scales so nothing past the end is read
                     const bool sa_bulk = p.sa_bulk && (rows & 3) == 0, sw_bulk = p.sw_bulk && (cols & 3) == 0;
+                    // gathers are cp.async copies that complete on the pair's barrier, so the warp moves on to
+                    // the next pair without waiting for their latency
                     for (int gi = 0; gi < ng; ++gi) {
                         const int g = g0 + gi;
-                        float *ring = sw_s + (2 * ps + gi) * C::RING_FLOATS;
+                        const uint32_t rbase = smem_u32(sw_s + (2 * ps + gi) * C::RING_FLOATS);
                         if (sa_grp && !sa_bulk) {
 #pragma unroll
                             for (int i = 0; i < BM / 32; ++i) {
                                 const int r = lane + 32 * i;
-                                ring[C::RING_SA + r] = r < rows ? p.sa[(int64_t)(m0 + r) * p.sa_rs + (int64_t)g * p.sa_gs] : 0.0f;
+                                const bool v = r < rows;
+                                cp_async4(rbase + 4 * (C::RING_SA + r),
+                                          v ? p.sa + (int64_t)(m0 + r) * p.sa_rs + (int64_t)g * p.sa_gs : p.sa, v);
                             }
                         }
                         if (sw_grp && !sw_bulk) {
 #pragma unroll
                             for (int i = 0; i < BN / 32; ++i) {
                                 const int c = lane + 32 * i;
-                                ring[C::RING_SW + c] = c < cols ? p.sw[(int64_t)(n0 + c) * p.sw_rs + (int64_t)g * p.sw_gs] : 0.0f;
+                                const bool v = c < cols;
+                                cp_async4(rbase + 4 * (C::RING_SW + c),
+                                          v ? p.sw + (int64_t)(n0 + c) * p.sw_rs + (int64_t)g * p.sw_gs : p.sw, v);
                             }
                         }
                         if (sw_blk && lane < BN / 128) {
                             const int nb = n0 / 128 + lane;
-                            ring[C::RING_SB + lane] = (nb * 128 < p.N) ? p.sw[(int64_t)nb * p.sw_rs + (int64_t)g * p.sw_gs] : 0.0f;
+                            const bool v = nb * 128 < p.N;
+                            cp_async4(rbase + 4 * (C::RING_SB + lane), v ? p.sw + (int64_t)nb * p.sw_rs + (int64_t)g * p.sw_gs : p.sw, v);
                         }
                     }
+                    if ((sa_grp && !sa_bulk) || (sw_grp && !sw_bulk) || sw_blk) cp_async_arrive(bar_sfull + 8 * ps);
                     __syncwarp();
                     if (lane == 0) {
                         const uint32_t sa_bytes = (sa_grp && sa_bulk) ? (uint32_t)(rows * 4) : 0u;
