@@ -605,6 +605,17 @@ __global__ void __launch_bounds__(128 + 128 * NP, 1)
                     const int ng = min(2, G - g0);
                     ok = warp_wait(lane, bar_sfull + 8 * slot, sphase, abort_flag, WAIT_NS);
                     if (!ok) break;
+                    // (row-scale mode) the pair's scales into registers before the accumulators are waited for,
+                    // so the shared-memory latency hides behind the wait
+                    float s_pair[2] = {0.0f, 0.0f};
+#pragma unroll
+                    for (int gi = 0; gi < 2 && PMODE == 1; ++gi) {
+                        const float *ring = sw_s + (2 * slot + gi) * C::RING_FLOATS;
+                        const float sa_g = (p.sa_mode == 0) ? ring[C::RING_SA + row] : sa_row;
+                        s_pair[gi] = sa_g;
+                        if (p.sw_mode == 2)
+                            s_pair[gi] = (ncol0 < p.N) ? __fmul_rn(sa_g, ring[C::RING_SB + (hf * CPT) / 128]) : 0.0f;
+                    }
                     ok = warp_wait(lane, bar_tfull + 8 * tb, tphase, abort_flag, WAIT_NS);
                     if (!ok) break;
                     tc_fence_after();
@@ -624,11 +635,8 @@ __global__ void __launch_bounds__(128 + 128 * NP, 1)
                             if (lane == 0) mbar_arrive(bar_tempty + 8 * tb);
                         }
                         const float *ring = sw_s + (2 * slot + gi) * C::RING_FLOATS;
-                        const float sa_g = (p.sa_mode == 0) ? ring[C::RING_SA + row] : sa_row;
-                        float s = sa_g;
-                        if (PMODE == 1 && p.sw_mode == 2)
-                            s = (ncol0 < p.N) ? __fmul_rn(sa_g, ring[C::RING_SB + (hf * CPT) / 128]) : 0.0f;
-                        const uint64_t s2 = pk(s, s);
+                        const float s_g = (PMODE == 1) ? s_pair[gi] : ((p.sa_mode == 0) ? ring[C::RING_SA + row] : sa_row);
+                        const uint64_t s2 = pk(s_g, s_g);
                         const float *sws = ring + C::RING_SW + hf * CPT;
 #pragma unroll
                         for (int j = 0; j < CPT; j += 4) {
