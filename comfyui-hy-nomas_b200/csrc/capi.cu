@@ -69,6 +69,8 @@ static int check_arch() {
     return HN_OK;
 }
 
+int g_gemm_sm_reserve = 0;
+
 int num_sms() {
     int dev = 0;
     if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= MAX_DEV) return 148;
@@ -120,6 +122,12 @@ extern "C" {
 const char *hn_last_error(void) { return t_last_error.c_str(); }
 
 int hn_abi_version(void) { return HN_ABI_VERSION; }
+
+int hn_set_gemm_sm_reserve(int n) {
+    if (n < 0 || n > 64) return fail(HN_ERR_ARG, "hn_set_gemm_sm_reserve: n must be in [0, 64]");
+    hn::g_gemm_sm_reserve = n;
+    return HN_OK;
+}
 
 int hn_num_sms(void) {
     int n = 0;

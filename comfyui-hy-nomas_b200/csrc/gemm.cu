@@ -924,7 +924,7 @@ cudaError_t launch_block_gemm(const GemmArgs &a, cudaStream_t st, const char **m
                  reinterpret_cast<uintptr_t>(a.sa) % 16 == 0) ? 1 : 0;
     p.sw_bulk = (a.sw_mode == 0 && a.sw_rs == 1 && a.sw_gs % 4 == 0 &&
                  reinterpret_cast<uintptr_t>(a.sw) % 16 == 0) ? 1 : 0;
-    int grid = num_sms();
+    int grid = num_sms() - g_gemm_sm_reserve;
     if (grid > p.num_tiles) grid = p.num_tiles;
     if (a.kind == 0) {
         if (pmode == 0) return launch_epi<0, 0, 128, GPS_NARROW, NPART_NARROW>(a.epilogue, ma, mb, p, grid, st);

@@ -26,6 +26,7 @@ _V, _I64, _I32, _F32, _U32 = ctypes.c_void_p, ctypes.c_int64, ctypes.c_int, ctyp
 SIGNATURES = {
     "hn_abi_version": [],
     "hn_num_sms": [],
+    "hn_set_gemm_sm_reserve": [ctypes.c_int],
     "hn_device_error": [_V, ctypes.POINTER(ctypes.c_int)],
     "hn_selftest_wait_timeout": [_U32, _V],
     "hn_quant_act": [_V, _I64, _I32, _I64, _I64, _I32, _I32, _V, _I64, _V, _I64, _I64, _V],

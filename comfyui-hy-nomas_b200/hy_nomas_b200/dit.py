@@ -27,6 +27,7 @@ N(0, 0.02). The RMSNorm weights are ones, as `RMSNorm.__init__` creates them (mo
 host-side tests pass a CPU object with the same methods to check the orchestration (shards, gathers) on gloo.
 """
 import math
+import os
 from dataclasses import dataclass
 
 import torch
@@ -34,6 +35,9 @@ import torch.nn.functional as F
 
 from . import fused, kernels
 from .sequence_parallel import SequenceParallel
+
+# SMs each GEMM leaves free under sequence parallelism (HN_SP_GEMM_SM_RESERVE overrides)
+SP_GEMM_SM_RESERVE = 0
 
 
 @dataclass(frozen=True)
@@ -208,6 +212,11 @@ class SyntheticDiT:
         lo, hi = self.sp.shard(cfg.tokens)
         self.rope = (cos[lo:hi].contiguous(), sin[lo:hi].contiguous())
         self.token_range = (lo, hi)
+        if self.sp.world > 1 and self.device.type == "cuda":
+            # the GEMMs leave SMs to the K/V all-gathers, which run on their own stream under the q|k GEMM
+            from . import _lib
+            n = int(os.environ.get("HN_SP_GEMM_SM_RESERVE", str(SP_GEMM_SM_RESERVE)))
+            _lib.check(_lib.lib.hn_set_gemm_sm_reserve(n), "hn_set_gemm_sm_reserve")
 
     def forward(self, x, vec, trace=None):
         for i, w in enumerate(self.blocks):

@@ -77,6 +77,13 @@ int hn_abi_version(void);
 int hn_num_sms(void);
 
 /*
+ * Leave `n` SMs without a GEMM CTA in later hn_block_gemm launches of this process (default 0), so that
+ * kernels on other streams - the K/V all-gathers of sequence parallelism - run beside a GEMM instead of
+ * after it. 0 <= n <= 64. No reference counterpart: the reference runs one GPU.
+ */
+int hn_set_gemm_sm_reserve(int n);
+
+/*
  * Device error word written by bounded waits inside the kernels (0 = none). Synchronizes `stream`,
  * copies the word to *code_host and clears it. Returns HN_ERR_TIMEOUT if a wait timed out.
  */

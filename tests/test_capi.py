@@ -37,6 +37,12 @@ def test_abi_version_and_no_device(hn):
     assert n == (torch.cuda.get_device_properties(0).multi_processor_count if torch.cuda.is_available() else 0)
 
 
+def test_gemm_sm_reserve_range(hn):
+    L = hn.lib.lib
+    assert L.hn_set_gemm_sm_reserve(-1) == 5 and L.hn_set_gemm_sm_reserve(65) == 5
+    assert L.hn_set_gemm_sm_reserve(16) == 0 and L.hn_set_gemm_sm_reserve(0) == 0
+
+
 FAKE = ctypes.c_void_p(0x10000)   # never dereferenced: every call below fails validation first
 
 
