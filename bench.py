@@ -768,13 +768,15 @@ def workload_elementwise(args, world, rank, stream, pk, sampler):
 def other_elementwise_kernels(m, d, h, hd, stream, sets, shift, scale, w, rope, iters=20):
     """The path's remaining bandwidth-bound kernels at the same shapes (not part of the chain's value), GB/s
     of algorithmic bytes: K1 quantize_activations (int8 and e4m3, per 128 and per token), K4 adaln, K5 on one
-    tensor, K7 pixelumm_qk (the FP8 decoder's QK norm: 32 heads x 128, split T/HW halves)."""
-    from hy_nomas_b200 import fused, kernels
+    tensor, K7 pixelumm_qk (the FP8 decoder's QK norm: 32 heads x 128, split T/HW halves), and the int8 KV
+    cache: quantize_kv, dequantize_kv and K5 with the KV quantizer fused (the cache pass)."""
+    from hy_nomas_b200 import fused, kernels, world
     flush = torch.empty(2 * L2_BYTES, dtype=torch.uint8, device="cuda")
     x2d = [s["x"].view(m, d) for s in sets]
     half = hd // 2
     wt = torch.ones(half, dtype=torch.bfloat16, device="cuda")
     whw = torch.ones(half, dtype=torch.bfloat16, device="cuda")
+    kv = [world.quantize_kv(s["q"].view(m, h, hd)) for s in sets]
     cases = {
         "quantize_activations_int8_g128": (lambda i: kernels.quantize_activations(x2d[i % 2]), m * d * 3 + m * (d // 128) * 4),
         "quantize_activations_e4m3_g128": (lambda i: kernels.quantize_activations(x2d[i % 2], "fp8"), m * d * 3 + m * (d // 128) * 4),
@@ -782,6 +784,10 @@ def other_elementwise_kernels(m, d, h, hd, stream, sets, shift, scale, w, rope, 
         "adaln": (lambda i: fused.adaln(sets[i % 2]["x"], shift, scale), m * d * 4),
         "qk_norm_rope_one_tensor": (lambda i: fused.qk_norm_rope(sets[i % 2]["q"], w, rope), 2 * m * h * hd * 2 + 2 * m * hd * 4),
         "pixelumm_qk": (lambda i: fused.pixelumm_qk(sets[i % 2]["q"], wt, whw, *rope), 2 * m * h * hd * 2 + 2 * m * hd * 4),
+        "quantize_kv": (lambda i: world.quantize_kv(sets[i % 2]["q"].view(m, h, hd)), m * h * hd * 3 + m * h * 4),
+        "dequantize_kv": (lambda i: world.dequantize_kv(*kv[i % 2]), m * h * hd * 3 + m * h * 4),
+        "qk_norm_rope_kv": (lambda i: fused.qk_norm_rope_kv(sets[i % 2]["q"], w, rope),
+                            m * h * hd * 5 + m * h * 4 + 2 * m * hd * 4),
     }
     res = {}
     for name, (fn, nbytes) in cases.items():

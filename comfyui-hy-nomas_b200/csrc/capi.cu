@@ -313,8 +313,22 @@ int hn_qk_norm_rope(const void *x, int64_t row_stride, const void *weight, const
     if (L == 0) return HN_OK;
     CHECK_ARCH();
     return launched(launch_qk_norm_rope(1, x, nullptr, row_stride, weight, nullptr, cos, sin, B, L, H, eps, y, nullptr,
-                                        (cudaStream_t)stream),
+                                        nullptr, nullptr, (cudaStream_t)stream),
                     "hn_qk_norm_rope launch");
+}
+
+int hn_qk_norm_rope_kv(const void *x, int64_t row_stride, const void *weight, const float *cos, const float *sin,
+                       int64_t B, int64_t L, int64_t H, int64_t D, float eps, void *y, int8_t *q, float *s,
+                       void *stream) {
+    int rc = qk_common(x, row_stride, weight, cos, sin, B, L, H, D, y);
+    if (rc) return rc;
+    REQUIRE(q && s, HN_ERR_ARG, "hn_qk_norm_rope_kv: null pointer");
+    REQUIRE(al16(q) && (reinterpret_cast<uintptr_t>(s) & 3) == 0, HN_ERR_ALIGN, "hn_qk_norm_rope_kv: misaligned buffer");
+    if (L == 0) return HN_OK;
+    CHECK_ARCH();
+    return launched(launch_qk_norm_rope(1, x, nullptr, row_stride, weight, nullptr, cos, sin, B, L, H, eps, y, nullptr,
+                                        q, s, (cudaStream_t)stream),
+                    "hn_qk_norm_rope_kv launch");
 }
 
 int hn_qk_norm_rope2(const void *xq, const void *xk, int64_t row_stride, const void *wq, const void *wk,
@@ -326,7 +340,8 @@ int hn_qk_norm_rope2(const void *xq, const void *xk, int64_t row_stride, const v
     if (rc) return rc;
     if (L == 0) return HN_OK;
     CHECK_ARCH();
-    return launched(launch_qk_norm_rope(2, xq, xk, row_stride, wq, wk, cos, sin, B, L, H, eps, yq, yk, (cudaStream_t)stream),
+    return launched(launch_qk_norm_rope(2, xq, xk, row_stride, wq, wk, cos, sin, B, L, H, eps, yq, yk, nullptr, nullptr,
+                                        (cudaStream_t)stream),
                     "hn_qk_norm_rope2 launch");
 }
 
@@ -346,6 +361,16 @@ int hn_pixelumm_qk(const void *x, int64_t row_stride, const void *weight_t, cons
 int hn_quantize_kv(const void *x, int64_t rows, int64_t D, int8_t *q, float *s, void *stream) {
     REQUIRE(D > 0 && D % 128 == 0, HN_ERR_SHAPE, "hn_quantize_kv: need D %% 128 == 0");
     return hn_quant_act(x, D, HN_DTYPE_BF16, rows, D, HN_KIND_INT8, D == 128 ? 0 : 1, q, D, s, 1, 1, stream);
+}
+
+int hn_dequantize_kv(const int8_t *q, const float *s, int64_t rows, int64_t D, void *y, void *stream) {
+    REQUIRE(q && s && y, HN_ERR_ARG, "hn_dequantize_kv: null pointer");
+    REQUIRE(rows >= 0 && D > 0 && D % 16 == 0, HN_ERR_SHAPE, "hn_dequantize_kv: need D %% 16 == 0 (D=%lld)", (long long)D);
+    REQUIRE(al16(q) && al16(y) && (reinterpret_cast<uintptr_t>(s) & 3) == 0, HN_ERR_ALIGN,
+            "hn_dequantize_kv: misaligned buffer");
+    if (rows == 0) return HN_OK;
+    CHECK_ARCH();
+    return launched(launch_dequant_kv(q, s, rows, D, y, (cudaStream_t)stream), "hn_dequantize_kv launch");
 }
 
 int hn_quantize_fp8_block(const void *w, int w_dtype, int64_t N, int64_t K, void *q, float *s, void *stream) {

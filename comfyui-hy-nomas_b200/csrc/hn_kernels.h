@@ -26,7 +26,9 @@ cudaError_t launch_gated_residual(const void *x, const void *y, const void *gate
 
 cudaError_t launch_qk_norm_rope(int ntensors, const void *x0, const void *x1, int64_t row_stride, const void *w0,
                                 const void *w1, const float *cos, const float *sin, int64_t B, int64_t L, int64_t H,
-                                float eps, void *y0, void *y1, cudaStream_t st);
+                                float eps, void *y0, void *y1, int8_t *q8, float *s8, cudaStream_t st);
+
+cudaError_t launch_dequant_kv(const int8_t *q, const float *s, int64_t rows, int64_t D, void *y, cudaStream_t st);
 
 cudaError_t launch_pixelumm_qk(const void *x, int64_t row_stride, const void *wt, const void *whw, const float *cos,
                                const float *sin, int64_t N, int64_t H, float eps, void *y, cudaStream_t st);

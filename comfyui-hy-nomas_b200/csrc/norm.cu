@@ -332,12 +332,17 @@ cudaError_t launch_gated_residual(const void *x, const void *y, const void *gate
 // pairwise trees over the head's 64 evens / odds in index order: three levels inside the lane (8 pairs), then a
 // butterfly over the 8 lanes of the head - both trees at once, as the two halves of a pair. The token's cos/sin
 // for the lane's 16 positions are loaded once and reused for every head and both tensors.
-template <bool ROPE, int NT>
+//
+// Q8: the last tensor's output is also quantized for an int8 KV cache (world.py:83-90 applied to it): per
+// (token, head) absmax over the head's 128 bf16 outputs (8 lanes), scale absmax/127 (1 for an all-zero head),
+// codes rounded half away from zero; q8 [BL, H, 128] int8, s8 [BL * H] fp32.
+template <bool ROPE, int NT, bool Q8>
 __global__ void __launch_bounds__(256) k_qk_norm_rope(const bf16 *__restrict__ x0, const bf16 *__restrict__ x1,
                                                       int64_t row_stride, const bf16 *__restrict__ w0,
                                                       const bf16 *__restrict__ w1, const float *__restrict__ cosp,
                                                       const float *__restrict__ sinp, int64_t BL, int64_t L, int H,
-                                                      float eps, bf16 *__restrict__ y0, bf16 *__restrict__ y1) {
+                                                      float eps, bf16 *__restrict__ y0, bf16 *__restrict__ y1,
+                                                      int8_t *__restrict__ q8, float *__restrict__ s8) {
     const int lane = threadIdx.x & 31;
     const int sub = lane & 7, hq = lane >> 3;
     const int64_t tok = (int64_t)blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5);
@@ -433,25 +438,54 @@ __global__ void __launch_bounds__(256) k_qk_norm_rope(const bf16 *__restrict__ x
                 reinterpret_cast<uint4 *>(yrow + h * 128)[0] = make_uint4(ow[0], ow[1], ow[2], ow[3]);
                 reinterpret_cast<uint4 *>(yrow + h * 128)[1] = make_uint4(ow[4], ow[5], ow[6], ow[7]);
             }
+            if (Q8 && tsel == NT - 1) {
+                float peak = 0.0f;
+#pragma unroll
+                for (int i = 0; i < 8; ++i) peak = fmaxf(peak, fmaxf(fabsf(bf16_lo(ow[i])), fabsf(bf16_hi(ow[i]))));
+#pragma unroll
+                for (int o = 1; o < 8; o <<= 1) peak = fmaxf(peak, __shfl_xor_sync(0xffffffffu, peak, o));
+                const float qsc = i8_scale(peak);
+                uint32_t c[16];
+                if (qsc >= 0x1p-90f) {
+                    const uint64_t ns = x2_splat(-qsc), rs = x2_splat(__frcp_rn(qsc));
+#pragma unroll
+                    for (int i = 0; i < 8; ++i) x2_codes(x2_quot(x2(bf16_lo(ow[i]), bf16_hi(ow[i])), ns, rs), c[2 * i], c[2 * i + 1]);
+                } else {
+#pragma unroll
+                    for (int i = 0; i < 8; ++i)
+                        x2_codes(x2(__fdiv_rn(bf16_lo(ow[i]), qsc), __fdiv_rn(bf16_hi(ow[i]), qsc)), c[2 * i], c[2 * i + 1]);
+                }
+                if (on) {
+                    *reinterpret_cast<uint4 *>(q8 + (tok * H + h) * 128 + 16 * sub) =
+                        make_uint4(pack4_lowbytes(c[0], c[1], c[2], c[3]), pack4_lowbytes(c[4], c[5], c[6], c[7]),
+                                   pack4_lowbytes(c[8], c[9], c[10], c[11]), pack4_lowbytes(c[12], c[13], c[14], c[15]));
+                    if (sub == 0) s8[tok * H + h] = qsc;
+                }
+            }
         }
     }
 }
 
 cudaError_t launch_qk_norm_rope(int ntensors, const void *x0, const void *x1, int64_t row_stride, const void *w0,
                                 const void *w1, const float *cos, const float *sin, int64_t B, int64_t L, int64_t H,
-                                float eps, void *y0, void *y1, cudaStream_t st) {
+                                float eps, void *y0, void *y1, int8_t *q8, float *s8, cudaStream_t st) {
     const int64_t BL = B * L;
     dim3 grid((unsigned)cdiv(BL, 8)), block(256);
     const bf16 *a = (const bf16 *)x0, *b = (const bf16 *)x1, *wa = (const bf16 *)w0, *wb = (const bf16 *)w1;
     bf16 *ya = (bf16 *)y0, *yb = (bf16 *)y1;
     const bool rope = cos != nullptr;
-    if (ntensors == 1) {
-        if (rope) k_qk_norm_rope<true, 1><<<grid, block, 0, st>>>(a, b, row_stride, wa, wb, cos, sin, BL, L, (int)H, eps, ya, yb);
-        else k_qk_norm_rope<false, 1><<<grid, block, 0, st>>>(a, b, row_stride, wa, wb, cos, sin, BL, L, (int)H, eps, ya, yb);
+#define HN_QK(R, N, Q) k_qk_norm_rope<R, N, Q><<<grid, block, 0, st>>>(a, b, row_stride, wa, wb, cos, sin, BL, L, (int)H, eps, ya, yb, q8, s8)
+    if (q8 != nullptr) {
+        if (ntensors == 1) { if (rope) HN_QK(true, 1, true); else HN_QK(false, 1, true); }
+        else { if (rope) HN_QK(true, 2, true); else HN_QK(false, 2, true); }
+    } else if (ntensors == 1) {
+        if (rope) HN_QK(true, 1, false);
+        else HN_QK(false, 1, false);
     } else {
-        if (rope) k_qk_norm_rope<true, 2><<<grid, block, 0, st>>>(a, b, row_stride, wa, wb, cos, sin, BL, L, (int)H, eps, ya, yb);
-        else k_qk_norm_rope<false, 2><<<grid, block, 0, st>>>(a, b, row_stride, wa, wb, cos, sin, BL, L, (int)H, eps, ya, yb);
+        if (rope) HN_QK(true, 2, false);
+        else HN_QK(false, 2, false);
     }
+#undef HN_QK
     return cudaGetLastError();
 }
 

@@ -230,6 +230,42 @@ __global__ void __launch_bounds__(256) k_quant_fp8_block(const TIn *__restrict__
     if (threadIdx.x == 0) s[(int64_t)blockIdx.y * gridDim.x + blockIdx.x] = sc;
 }
 
+// int8 KV dequantizer (world.py:93-94): y = bf16(float(q) * s) per (token, head) row of D codes. Each thread
+// turns 16 codes (one 16-byte load) into 16 bf16 (two 16-byte stores). HBM-bound: 1 byte read + 2 bytes
+// written per element, plus 4 bytes of scale per row.
+__global__ void __launch_bounds__(256) k_dequant_kv(const int8_t *__restrict__ q, const float *__restrict__ s,
+                                                    int64_t rows, int64_t D, __nv_bfloat16 *__restrict__ y) {
+    const int64_t per_row = D >> 4;
+    const int64_t n = rows * per_row;
+    for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < n; i += (int64_t)gridDim.x * blockDim.x) {
+        const int64_t row = i / per_row;
+        const uint4 c = ldg_stream(reinterpret_cast<const uint4 *>(q) + i);
+        const float sc = __ldg(s + row);
+        const uint32_t cw[4] = {c.x, c.y, c.z, c.w};
+        uint32_t o[8];
+#pragma unroll
+        for (int w = 0; w < 4; ++w) {
+            float f[4];
+#pragma unroll
+            for (int b = 0; b < 4; ++b) f[b] = __fmul_rn((float)(int8_t)((cw[w] >> (8 * b)) & 0xFFu), sc);
+            o[2 * w] = bf16x2_rn(f[0], f[1]);
+            o[2 * w + 1] = bf16x2_rn(f[2], f[3]);
+        }
+        uint4 *dst = reinterpret_cast<uint4 *>(y) + 2 * i;
+        dst[0] = make_uint4(o[0], o[1], o[2], o[3]);
+        dst[1] = make_uint4(o[4], o[5], o[6], o[7]);
+    }
+}
+
+cudaError_t launch_dequant_kv(const int8_t *q, const float *s, int64_t rows, int64_t D, void *y, cudaStream_t st) {
+    const int64_t n = rows * (D >> 4);
+    int64_t grid = cdiv(n, 256);
+    const int64_t cap = (int64_t)num_sms() * 8;
+    if (grid > cap) grid = cap;
+    k_dequant_kv<<<(unsigned)grid, 256, 0, st>>>(q, s, rows, D, (__nv_bfloat16 *)y);
+    return cudaGetLastError();
+}
+
 cudaError_t launch_quant_fp8_block(const void *w, int w_dtype, int64_t N, int64_t K, void *q, float *s,
                                    cudaStream_t st) {
     dim3 grid((unsigned)(K / 128), (unsigned)(N / 128));

@@ -40,6 +40,8 @@ SIGNATURES = {
     "hn_gated_residual_adaln_quant": [_V, _V, _V, _V, _V, _I64, _I64, _I64, _F32, _V, _V, _V, _I64, _I64, _V],
     "hn_pixelumm_qk": [_V, _I64, _V, _V, _V, _V, _I64, _I64, _I64, _F32, _V, _V],
     "hn_quantize_kv": [_V, _I64, _I64, _V, _V, _V],
+    "hn_dequantize_kv": [_V, _V, _I64, _I64, _V, _V],
+    "hn_qk_norm_rope_kv": [_V, _I64, _V, _V, _V, _I64, _I64, _I64, _I64, _F32, _V, _V, _V, _V],
     "hn_quantize_fp8_block": [_V, _I32, _I64, _I64, _V, _V, _V],
 }
 

@@ -85,6 +85,29 @@ def qk_norm_rope(x, weight, rope=None, eps=1e-6, out=None):
     return y
 
 
+def qk_norm_rope_kv(x, weight, rope=None, eps=1e-6, out=None):
+    """`qk_norm_rope` for the cache pass: returns (y, q, s) where y is qk_norm_rope's output and (q, s) is
+    world.quantize_kv(y) from the same launch - int8 [B, L, H, D] and fp32 [B, L, H, 1] per (token, head)."""
+    _lib.require_cuda(x, weight)
+    _bf16(x)
+    b, l, h, d = x.shape
+    x = _qk_input(x)
+    if out is None:
+        y = torch.empty((b, l, h, d), device=x.device, dtype=torch.bfloat16)
+    else:
+        y = out
+        if y.shape != (b, l, h, d) or y.dtype != torch.bfloat16 or not y.is_contiguous() or y.device != x.device:
+            raise ValueError(f"qk_norm_rope_kv: out must be a contiguous bf16 [{b}, {l}, {h}, {d}] tensor")
+    q = torch.empty((b, l, h, d), device=x.device, dtype=torch.int8)
+    s = torch.empty((b, l, h, 1), device=x.device, dtype=torch.float32)
+    w = weight.to(torch.bfloat16).contiguous()
+    cos, sin = _rope_tables(rope, x.device)
+    rc = _lib.lib.hn_qk_norm_rope_kv(_lib.ptr(x), x.stride(1), _lib.ptr(w), _lib.ptr(cos), _lib.ptr(sin), b, l, h, d,
+                                     eps, _lib.ptr(y), _lib.ptr(q), _lib.ptr(s), _lib.stream_of(x))
+    _lib.check(rc, "qk_norm_rope_kv")
+    return y, q, s
+
+
 def qk_norm_rope2(q, k, weight_q, weight_k, rope=None, eps=1e-6, out=None):
     """`qk_norm_rope` of q and k (same shape and token stride) in one launch -> (q_out, k_out). `out`: optional
     caller-owned contiguous bf16 [B, L, H, D] pair to write into (e.g. a rank's slice of an all-gather buffer)."""

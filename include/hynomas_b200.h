@@ -204,6 +204,22 @@ int hn_pixelumm_qk(const void *x, int64_t row_stride, const void *weight_t, cons
 int hn_quantize_kv(const void *x, int64_t rows, int64_t D, int8_t *q, float *s, void *stream);
 
 /*
+ * int8 KV dequantizer: y = bf16(float(q) * s) with s per (token, head) row.
+ * Replaces hy_nomas/world.py:93-94 (dequantize_kv), as called per layer on history load (world.py:197-204).
+ * q [rows, D] int8, s [rows] fp32 -> y [rows, D] bf16; D % 16 == 0; q and y 16-byte aligned.
+ */
+int hn_dequantize_kv(const int8_t *q, const float *s, int64_t rows, int64_t D, void *y, void *stream);
+
+/*
+ * K5 for the cache pass: hn_qk_norm_rope, and the same output quantized for the int8 KV cache in the same
+ * launch - hy_nomas/world.py:83-90 (quantize_kv) applied to y, fused so y is not read back.
+ * Arguments as hn_qk_norm_rope, plus q [B, L, H, D] int8 (16-byte aligned) and s [B*L*H] fp32.
+ */
+int hn_qk_norm_rope_kv(const void *x, int64_t row_stride, const void *weight, const float *cos, const float *sin,
+                       int64_t B, int64_t L, int64_t H, int64_t D, float eps, void *y, int8_t *q, float *s,
+                       void *stream);
+
+/*
  * FP8 weight quantizer per 128 x 128 block (load time of the FP8 decoder linears).
  * Replaces hy_nomas/pixelumm.py:77-82 (NomasFP8Block128Layout.quantize). w [N, K] contiguous fp32 or bf16
  * (w_dtype), N % 128 == 0, K % 128 == 0 -> q [N, K] e4m3 bytes = e4m3(w / s) (nearest even), s [N/128, K/128]

@@ -426,6 +426,13 @@ void or_quantize_kv(const float *x, int64_t rows, int64_t D, int8_t *q, float *s
     }
 }
 
+/* hy_nomas/world.py:93-94 (dequantize_kv): bf16(float(q) * s), s per row of D codes; y holds the bf16 values
+ * as fp32. */
+void or_dequantize_kv(const int8_t *q, const float *s, int64_t rows, int64_t D, float *y) {
+    for (int64_t r = 0; r < rows; ++r)
+        for (int64_t i = 0; i < D; ++i) y[r * D + i] = rbf16((float)q[r * D + i] * s[r]);
+}
+
 /* ---------------------------------------------------------------------------------------------------
  * Helpers the tests use: bf16 rounding of fp32 arrays, and the Markstein-corrected quotient that the
  * quantizers may use in place of a division (checked here against IEEE division on the CPU).

@@ -67,6 +67,7 @@ def lib():
             "or_qk_norm_rope": [p, p, p, p, i64, i64, i64, i64, f32, p],
             "or_pixelumm_qk": [p, p, p, p, p, i64, i64, i64, f32, p],
             "or_quantize_kv": [p, i64, i64, p, p],
+            "or_dequantize_kv": [p, p, i64, i64, p],
             "or_round_bf16": [p, i64, p],
             "or_expf_array": [p, i64, p],
             "or_gelu_array": [p, i64, p],
@@ -282,3 +283,13 @@ def quantize_kv(x):
     s = np.empty((l, h, 1), dtype=np.float32)
     lib().or_quantize_kv(_ptr(x), l * h, d, _ptr(q), _ptr(s))
     return q, s
+
+
+def dequantize_kv(q, s):
+    """hy_nomas/world.py:93-94. int8 [..., D] and float32 scales [..., 1] -> bf16 values as float32 [..., D]."""
+    q = np.ascontiguousarray(q, dtype=np.int8)
+    s = np.ascontiguousarray(s, dtype=np.float32)
+    d = q.shape[-1]
+    y = np.empty(q.shape, dtype=np.float32)
+    lib().or_dequantize_kv(_ptr(q), _ptr(s), q.size // d, d, _ptr(y))
+    return y

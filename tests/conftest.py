@@ -46,12 +46,13 @@ def hn():
     import hy_nomas_b200.fused as fused
     import hy_nomas_b200.kernels as kernels
     import hy_nomas_b200.ops as ops
+    import hy_nomas_b200.world as world
     from hy_nomas_b200 import _lib
 
     class NS:
         pass
     ns = NS()
-    ns.kernels, ns.fused, ns.ops, ns.lib = kernels, fused, ops, _lib
+    ns.kernels, ns.fused, ns.ops, ns.world, ns.lib = kernels, fused, ops, world, _lib
     return ns
 
 

@@ -17,7 +17,7 @@ How the reference is run on a machine without a GPU or ComfyUI:
     saturation at +-448, i.e. cvt.rn.satfinite). Every other interpreter operation is untouched
     (numpy float32 arithmetic: IEEE division, 1/np.sqrt for tl.rsqrt, numpy's exp, numpy's sum order);
   * its torch reference functions (model.layer_norm / modulate / RMSNorm / rope_freqs / apply_rope,
-    ops.quantize_g128 / dequantize_g128, pixelumm's FP8 block layout, world.quantize_kv) run on CPU with
+    ops.quantize_g128 / dequantize_g128, pixelumm's FP8 block layout, world.quantize_kv / dequantize_kv) run on CPU with
     the `comfy` and `comfy_kitchen` modules stubbed (they are not on this path's arithmetic).
 All inputs are seeded (torch.Generator, seeds below). bf16 arrays are stored as uint16 bit patterns,
 e4m3 codes as uint8 bytes.
@@ -252,7 +252,8 @@ def main():
     x = randn(12, 4, 128, scale=2.0).bfloat16()
     x[0, 0] = 0.0
     qk, sk = world.quantize_kv(x)
-    np.savez_compressed(os.path.join(OUT, "quantize_kv.npz"), x=bits(x), q=qk.numpy(), s=sk.numpy())
+    yk = world.dequantize_kv(qk, sk)   # world.py:93-94
+    np.savez_compressed(os.path.join(OUT, "quantize_kv.npz"), x=bits(x), q=qk.numpy(), s=sk.numpy(), y=bits(yk))
     print("golden vectors written to", OUT)
 
 

@@ -120,6 +120,28 @@ def test_reference_qk_norm_rope(hn, cuda):
     assert ((got.float() - ref.float()).norm() / ref.float().norm()).item() < 1e-3
 
 
+@pytest.mark.parametrize("rope", [True, False])
+def test_qk_norm_rope_kv_cache_pass(hn, oracle, cuda, rope):
+    """The cache pass: qk_norm_rope's output and world.quantize_kv of it from one launch, against the oracle's
+    qk_norm_rope then quantize_kv, on a strided k slice of a fused qkv buffer, with an all-zero head."""
+    from oracle import torch_ref
+    b, l, h, d = 1, 2 * 3 * 4, 8, 128
+    qkv = (torch.randn(b, l, 3 * h * d, generator=torch.Generator().manual_seed(9)) * 3).bfloat16()
+    qkv[0, 5, h * d + 2 * d: h * d + 3 * d] = 0            # token 5, head 2 of k: zero -> scale 1
+    k = qkv.to(cuda)[..., h * d: 2 * h * d].view(b, l, h, d)
+    w = (torch.rand(d) + 0.5).bfloat16().to(cuda)
+    cos, sin = torch_ref.rope_freqs([16, 56, 56], 10000, 2, 3, 4)
+    tables = (cos.to(cuda), sin.to(cuda)) if rope else None
+    y, q8, s8 = hn.fused.qk_norm_rope_kv(k, w, tables)
+    assert torch.equal(y, hn.fused.qk_norm_rope(k, w, tables))
+    ref = oracle.qk_norm_rope(f32(k.contiguous()), f32(w), (cos.numpy(), sin.numpy()) if rope else None)
+    assert np.array_equal(bits16(y), oracle.bf16_bits(ref))
+    rq, rs = oracle.quantize_kv(oracle.round_bf16(ref).reshape(b * l, h, d))
+    assert np.array_equal(q8.cpu().numpy().reshape(b * l, h, d), rq)
+    assert np.array_equal(f32(s8).reshape(b * l, h, 1), rs)
+    assert f32(s8).reshape(b * l, h)[5, 2] == 1.0
+
+
 def test_qk_norm_rope_strided_qkv_and_pair(hn, oracle, cuda):
     """q/k as column slices of a fused [L, 3 * H * D] qkv buffer (token stride 3HD), one and two per launch,
     with BASELINE's 3-D RoPE (t,h,w axes 16/56/56, theta 10000)."""

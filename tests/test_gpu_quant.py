@@ -80,6 +80,30 @@ def test_quantize_kv(hn, golden, cuda):
     assert np.array_equal(f32(s).reshape(d["s"].shape), d["s"])
 
 
+def test_world_kv_golden(hn, golden, cuda):
+    """hy_nomas/world.py:83-94 through the package's world module: codes, scales and the dequantized bf16,
+    bit-exact with the reference's own outputs."""
+    d = golden("quantize_kv")
+    x = bf16_from_bits(d["x"], cuda)
+    q, s = hn.world.quantize_kv(x)
+    assert np.array_equal(q.cpu().numpy(), d["q"]) and np.array_equal(f32(s), d["s"])
+    y = hn.world.dequantize_kv(torch.from_numpy(d["q"]).to(cuda), torch.from_numpy(d["s"]).to(cuda))
+    assert np.array_equal(y.cpu().view(torch.int16).numpy().view(np.uint16), d["y"])
+
+
+@pytest.mark.parametrize("rows,d", [(1, 128), (37, 128), (4096 * 4, 128), (300, 256), (3, 16)])
+def test_dequantize_kv_random(hn, oracle, cuda, rows, d):
+    gen = torch.Generator().manual_seed(rows + d)
+    q = torch.randint(-127, 128, (rows, d), generator=gen, dtype=torch.int8)
+    q[0, :4] = torch.tensor([-127, 127, 0, -1], dtype=torch.int8)
+    s = torch.rand(rows, 1, generator=gen) * 0.05
+    s[-1] = 1.0                                        # an all-zero head's scale
+    y = hn.world.dequantize_kv(q.to(cuda), s.to(cuda))
+    torch.cuda.synchronize()
+    ref = oracle.dequantize_kv(q.numpy(), s.numpy())
+    assert np.array_equal(y.cpu().view(torch.int16).numpy().view(np.uint16), oracle.bf16_bits(ref))
+
+
 def test_quantize_fp8_block_golden(hn, golden, cuda):
     """pixelumm.NomasFP8Block128Layout.quantize (pixelumm.py:77-82): e4m3 codes and block scales bit-exact
     with the reference's own output, and the block dequantization (pixelumm.py:60-63)."""

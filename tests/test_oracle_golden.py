@@ -123,3 +123,9 @@ def test_quantize_kv(oracle, golden):
     d = golden("quantize_kv")  # world.py:83-90
     q, s = oracle.quantize_kv(bf(d["x"]))
     assert np.array_equal(q, d["q"]) and np.array_equal(s, d["s"])
+
+
+def test_dequantize_kv(oracle, golden):
+    d = golden("quantize_kv")  # world.py:93-94, on the reference's own codes and scales
+    y = oracle.dequantize_kv(d["q"], d["s"])
+    assert np.array_equal(oracle.bf16_bits(y), d["y"])
