@@ -472,8 +472,9 @@ def _time_kernel(fn, stream, flush, iters):
 
 
 def gemm_variants(m, n, k, stream, iters=20):
-    """Context for the roofline (not the headline): the GEMM kernel alone in each scale mode, and cuBLASLt's
-    int8 GEMM (torch._int_mm, no scaling) on the same shape."""
+    """Context for the roofline (not the headline): the GEMM kernel alone in each scale mode, config 1's literal
+    linear (per-token round-half-even quantization of x, then the per-token x per-channel GEMM, timed together),
+    and cuBLASLt's int8 GEMM (torch._int_mm, no scaling) on the same shape."""
     from hy_nomas_b200 import kernels
     gen = torch.Generator().manual_seed(99)
     dev = torch.device("cuda")
@@ -483,10 +484,16 @@ def gemm_variants(m, n, k, stream, iters=20):
     sa_r = (torch.rand(m, generator=gen) * 0.02).to(dev)
     sw_g = (torch.rand(n, k // 128, generator=gen) * 4e-3).to(dev)
     sw_r = (torch.rand(n, generator=gen) * 4e-3).to(dev)
+    x = torch.randn(m, k, generator=gen).bfloat16().to(dev)
     flush = torch.empty(2 * L2_BYTES, dtype=torch.uint8, device=dev)
+
+    def literal_config1():
+        qt, st = kernels.quantize_activations(x, per_token=True, round_half_even=True)
+        return kernels.block_gemm(qt, st, qw, sw_r)
     cases = {"a_group_w_group_rowmajor": lambda: kernels.block_gemm(qa, sa_g, qw, sw_g),
              "a_group_w_channel": lambda: kernels.block_gemm(qa, sa_g, qw, sw_r),
              "a_token_w_channel": lambda: kernels.block_gemm(qa, sa_r, qw, sw_r),
+             "quantize_token_rne_and_gemm": literal_config1,
              "cublaslt_int8_int32": lambda: torch._int_mm(qa, qw.t())}
     res = {}
     for name, fn in cases.items():

@@ -158,9 +158,13 @@ int hn_selftest_wait_timeout(uint32_t timeout_us, void *stream) {
     return launched(launch_wait_selftest(timeout_us, static_cast<cudaStream_t>(stream)), "wait self-test launch");
 }
 
-int hn_quant_act(const void *x, int64_t ldx, int x_dtype, int64_t M, int64_t K, int kind, int per_row, void *q,
+int hn_quant_act(const void *x, int64_t ldx, int x_dtype, int64_t M, int64_t K, int kind, int flags, void *q,
                  int64_t ldq, float *s, int64_t s_rs, int64_t s_gs, void *stream) {
     REQUIRE(x && q && s, HN_ERR_ARG, "hn_quant_act: null pointer");
+    REQUIRE((flags & ~(HN_QUANT_PER_ROW | HN_QUANT_ROUND_HALF_EVEN)) == 0, HN_ERR_ARG, "hn_quant_act: unknown flags %d", flags);
+    REQUIRE(!(flags & HN_QUANT_ROUND_HALF_EVEN) || kind == HN_KIND_INT8, HN_ERR_ARG,
+            "hn_quant_act: round-half-even applies to int8 codes (e4m3 always rounds to nearest even)");
+    const bool per_row = (flags & HN_QUANT_PER_ROW) != 0;
     REQUIRE(x_dtype == HN_DTYPE_BF16 || x_dtype == HN_DTYPE_FP16 || x_dtype == HN_DTYPE_FP32, HN_ERR_ARG,
             "hn_quant_act: x_dtype %d not bf16/fp16/fp32", x_dtype);
     REQUIRE(kind == HN_KIND_INT8 || kind == HN_KIND_FP8E4M3, HN_ERR_ARG, "hn_quant_act: unknown kind %d", kind);
@@ -174,7 +178,7 @@ int hn_quant_act(const void *x, int64_t ldx, int x_dtype, int64_t M, int64_t K, 
             "hn_quant_act: x/q must be 16-byte aligned with 16-byte row pitch");
     if (M == 0) return HN_OK;
     CHECK_ARCH();
-    return launched(launch_quant_act(x, ldx, x_dtype, M, K, kind, per_row, q, ldq, s, s_rs, s_gs, (cudaStream_t)stream),
+    return launched(launch_quant_act(x, ldx, x_dtype, M, K, kind, flags, q, ldq, s, s_rs, s_gs, (cudaStream_t)stream),
                     "hn_quant_act launch");
 }
 

@@ -52,6 +52,12 @@ __device__ __forceinline__ int code_i8(float y) {
     r = fminf(fmaxf(r, -127.0f), 127.0f);
     return (int)r;
 }
+// round half to even (cvt.rni), clamp +-127: the per-token int8 codes of BASELINE config 1 ("round-half-even"),
+// an option beside the reference's half-away rounding
+__device__ __forceinline__ int code_i8_rne(float y) {
+    const int r = __float2int_rn(y);
+    return r > 127 ? 127 : (r < -127 ? -127 : r);
+}
 __device__ __forceinline__ uint32_t pack4_i8(int a, int b, int c, int d) {
     return (uint32_t)(a & 0xFF) | ((uint32_t)(b & 0xFF) << 8) | ((uint32_t)(c & 0xFF) << 16) |
            ((uint32_t)(d & 0xFF) << 24);

@@ -10,7 +10,7 @@ namespace hn {
 int num_sms();  // SM count of the current device (cached per device)
 extern int g_gemm_sm_reserve;  // SMs the GEMM leaves free for kernels on other streams (hn_set_gemm_sm_reserve)
 
-cudaError_t launch_quant_act(const void *x, int64_t ldx, int x_dtype, int64_t M, int64_t K, int kind, int per_row,
+cudaError_t launch_quant_act(const void *x, int64_t ldx, int x_dtype, int64_t M, int64_t K, int kind, int flags,
                              void *q, int64_t ldq, float *s, int64_t s_rs, int64_t s_gs, cudaStream_t st);
 
 cudaError_t launch_quant_fp8_block(const void *w, int w_dtype, int64_t N, int64_t K, void *q, float *s,

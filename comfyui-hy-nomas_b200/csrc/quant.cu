@@ -12,7 +12,8 @@
 
 namespace hn {
 
-template <typename TIn, int KIND>
+// RNE (int8 only): codes rounded half to even instead of half away from zero.
+template <typename TIn, int KIND, bool RNE>
 __global__ void __launch_bounds__(256) k_quant_group(const TIn *__restrict__ x, int64_t ldx, int64_t M, int64_t G,
                                                      uint8_t *__restrict__ q, int64_t ldq, float *__restrict__ s,
                                                      int64_t s_rs, int64_t s_gs) {
@@ -47,7 +48,20 @@ __global__ void __launch_bounds__(256) k_quant_group(const TIn *__restrict__ x, 
             // bf16 input: the exact fma-corrected quotient (x2_quot), checked exhaustively over bf16 inputs
             sc = sc_try;
             const uint64_t ns = x2_splat(-sc), rs = x2_splat(__frcp_rn(sc));
-            if (KIND == 0) {
+            if (KIND == 0 && RNE) {
+                int c[16];
+#pragma unroll
+                for (int i = 0; i < 8; ++i) {
+                    float q0, q1;
+                    x2_split(x2_quot(x2(v[2 * i], v[2 * i + 1]), ns, rs), q0, q1);
+                    c[2 * i] = code_i8_rne(q0);
+                    c[2 * i + 1] = code_i8_rne(q1);
+                }
+                out.x = pack4_i8(c[0], c[1], c[2], c[3]);
+                out.y = pack4_i8(c[4], c[5], c[6], c[7]);
+                out.z = pack4_i8(c[8], c[9], c[10], c[11]);
+                out.w = pack4_i8(c[12], c[13], c[14], c[15]);
+            } else if (KIND == 0) {
                 uint32_t c[16];
 #pragma unroll
                 for (int i = 0; i < 8; ++i) x2_codes(x2_quot(x2(v[2 * i], v[2 * i + 1]), ns, rs), c[2 * i], c[2 * i + 1]);
@@ -73,7 +87,7 @@ __global__ void __launch_bounds__(256) k_quant_group(const TIn *__restrict__ x, 
             sc = i8_scale(peak);
             int c[16];
 #pragma unroll
-            for (int i = 0; i < 16; ++i) c[i] = code_i8(__fdiv_rn(v[i], sc));
+            for (int i = 0; i < 16; ++i) c[i] = RNE ? code_i8_rne(__fdiv_rn(v[i], sc)) : code_i8(__fdiv_rn(v[i], sc));
             out.x = pack4_i8(c[0], c[1], c[2], c[3]);
             out.y = pack4_i8(c[4], c[5], c[6], c[7]);
             out.z = pack4_i8(c[8], c[9], c[10], c[11]);
@@ -95,96 +109,158 @@ __global__ void __launch_bounds__(256) k_quant_group(const TIn *__restrict__ x, 
     }
 }
 
-// Per-row (per-token) variant: one CTA per row, two passes over the row (the second hits L1/L2).
-template <typename TIn, int KIND>
+// 8 elements of a row -> 8 codes (int8 bytes or e4m3 bytes) for scale `sc`; `fast`: bf16 input with the
+// exact fma-corrected quotient (as in k_quant_group), else IEEE division.
+template <int KIND, bool RNE>
+__device__ __forceinline__ uint2 quant_chunk8(const float (&v)[8], float sc, bool fast, uint64_t ns, uint64_t rs) {
+    uint2 out;
+    if (fast && KIND == 0 && RNE) {
+        int cc[8];
+#pragma unroll
+        for (int i = 0; i < 4; ++i) {
+            float q0, q1;
+            x2_split(x2_quot(x2(v[2 * i], v[2 * i + 1]), ns, rs), q0, q1);
+            cc[2 * i] = code_i8_rne(q0);
+            cc[2 * i + 1] = code_i8_rne(q1);
+        }
+        out.x = pack4_i8(cc[0], cc[1], cc[2], cc[3]);
+        out.y = pack4_i8(cc[4], cc[5], cc[6], cc[7]);
+    } else if (fast && KIND == 0) {
+        uint32_t cc[8];
+#pragma unroll
+        for (int i = 0; i < 4; ++i) x2_codes(x2_quot(x2(v[2 * i], v[2 * i + 1]), ns, rs), cc[2 * i], cc[2 * i + 1]);
+        out.x = pack4_lowbytes(cc[0], cc[1], cc[2], cc[3]);
+        out.y = pack4_lowbytes(cc[4], cc[5], cc[6], cc[7]);
+    } else if (fast) {
+        uint32_t h[4];
+#pragma unroll
+        for (int i = 0; i < 4; ++i) {
+            float q0, q1;
+            x2_split(x2_quot(x2(v[2 * i], v[2 * i + 1]), ns, rs), q0, q1);
+            h[i] = pack2_e4m3(copysignf(q0, v[2 * i]), copysignf(q1, v[2 * i + 1]));
+        }
+        out.x = h[0] | (h[1] << 16);
+        out.y = h[2] | (h[3] << 16);
+    } else if (KIND == 0) {
+        int cc[8];
+#pragma unroll
+        for (int i = 0; i < 8; ++i) cc[i] = RNE ? code_i8_rne(__fdiv_rn(v[i], sc)) : code_i8(__fdiv_rn(v[i], sc));
+        out.x = pack4_i8(cc[0], cc[1], cc[2], cc[3]);
+        out.y = pack4_i8(cc[4], cc[5], cc[6], cc[7]);
+    } else {
+        uint32_t h[4];
+#pragma unroll
+        for (int i = 0; i < 4; ++i) h[i] = pack2_e4m3(__fdiv_rn(v[2 * i], sc), __fdiv_rn(v[2 * i + 1], sc));
+        out.x = h[0] | (h[1] << 16);
+        out.y = h[2] | (h[3] << 16);
+    }
+    return out;
+}
+
+// Per-row (per-token) variant: one CTA of 256 threads per row. NCH > 0: the row stays in registers, NCH chunks
+// of 8 elements per thread (chunk c at elements [8c, 8c + 8), thread t holding chunks t, t + 256, ...: one HBM
+// pass, coalesced 16-byte loads); NCH == 0 (rows longer than 16384): two passes, the second from L2.
+template <typename TIn, int KIND, bool RNE, int NCH>
 __global__ void __launch_bounds__(256) k_quant_row(const TIn *__restrict__ x, int64_t ldx, int64_t K,
                                                    uint8_t *__restrict__ q, int64_t ldq, float *__restrict__ s,
                                                    int64_t s_rs) {
     __shared__ float red[8];
     const int64_t m = blockIdx.x;
     const TIn *row = x + m * ldx;
+    const int64_t nch = K >> 3;
+    float v[NCH > 0 ? NCH : 1][8];
     float peak = 0.0f;
-    for (int64_t c = (int64_t)threadIdx.x * 8; c < K; c += (int64_t)blockDim.x * 8) {
-        float v[8];
-        Elem<TIn>::load8(row + c, v);
+    if (NCH > 0) {
 #pragma unroll
-        for (int i = 0; i < 8; ++i) peak = fmaxf(peak, fabsf(v[i]));
+        for (int i = 0; i < (NCH > 0 ? NCH : 1); ++i) {
+            const int64_t c = threadIdx.x + (int64_t)i * 256;
+            if (c < nch) Elem<TIn>::load8(row + 8 * c, v[i]);
+            else {
+#pragma unroll
+                for (int j = 0; j < 8; ++j) v[i][j] = 0.0f;
+            }
+#pragma unroll
+            for (int j = 0; j < 8; ++j) peak = fmaxf(peak, fabsf(v[i][j]));
+        }
+    } else {
+        for (int64_t c = threadIdx.x; c < nch; c += 256) {
+            float w[8];
+            Elem<TIn>::load8(row + 8 * c, w);
+#pragma unroll
+            for (int j = 0; j < 8; ++j) peak = fmaxf(peak, fabsf(w[j]));
+        }
     }
     peak = warp_max_xor(peak, 32);
     if ((threadIdx.x & 31) == 0) red[threadIdx.x >> 5] = peak;
     __syncthreads();
     peak = 0.0f;
-    for (int w = 0; w < (int)(blockDim.x >> 5); ++w) peak = fmaxf(peak, red[w]);
+#pragma unroll
+    for (int w = 0; w < 8; ++w) peak = fmaxf(peak, red[w]);
     const float sc = KIND == 0 ? i8_scale(peak) : e4m3_scale(peak);
-    // bf16 input: the exact fma-corrected quotient (as in k_quant_group)
     constexpr bool BF16_IN = sizeof(TIn) == 2 && !std::is_same<TIn, __half>::value;
     const bool fast = BF16_IN && sc >= 0x1p-90f;
     const uint64_t ns = x2_splat(-sc), rs = x2_splat(__frcp_rn(sc));
-    for (int64_t c = (int64_t)threadIdx.x * 8; c < K; c += (int64_t)blockDim.x * 8) {
-        float v[8];
-        Elem<TIn>::load8(row + c, v);
-        uint2 out;
-        if (fast && KIND == 0) {
-            uint32_t cc[8];
+    if (NCH > 0) {
 #pragma unroll
-            for (int i = 0; i < 4; ++i) x2_codes(x2_quot(x2(v[2 * i], v[2 * i + 1]), ns, rs), cc[2 * i], cc[2 * i + 1]);
-            out.x = pack4_lowbytes(cc[0], cc[1], cc[2], cc[3]);
-            out.y = pack4_lowbytes(cc[4], cc[5], cc[6], cc[7]);
-        } else if (fast) {
-            uint32_t h[4];
-#pragma unroll
-            for (int i = 0; i < 4; ++i) {
-                float q0, q1;
-                x2_split(x2_quot(x2(v[2 * i], v[2 * i + 1]), ns, rs), q0, q1);
-                h[i] = pack2_e4m3(copysignf(q0, v[2 * i]), copysignf(q1, v[2 * i + 1]));
-            }
-            out.x = h[0] | (h[1] << 16);
-            out.y = h[2] | (h[3] << 16);
-        } else if (KIND == 0) {
-            int cc[8];
-#pragma unroll
-            for (int i = 0; i < 8; ++i) cc[i] = code_i8(__fdiv_rn(v[i], sc));
-            out.x = pack4_i8(cc[0], cc[1], cc[2], cc[3]);
-            out.y = pack4_i8(cc[4], cc[5], cc[6], cc[7]);
-        } else {
-            uint32_t h[4];
-#pragma unroll
-            for (int i = 0; i < 4; ++i) h[i] = pack2_e4m3(__fdiv_rn(v[2 * i], sc), __fdiv_rn(v[2 * i + 1], sc));
-            out.x = h[0] | (h[1] << 16);
-            out.y = h[2] | (h[3] << 16);
+        for (int i = 0; i < (NCH > 0 ? NCH : 1); ++i) {
+            const int64_t c = threadIdx.x + (int64_t)i * 256;
+            if (c < nch) *reinterpret_cast<uint2 *>(q + m * ldq + 8 * c) = quant_chunk8<KIND, RNE>(v[i], sc, fast, ns, rs);
         }
-        *reinterpret_cast<uint2 *>(q + m * ldq + c) = out;
+    } else {
+        for (int64_t c = threadIdx.x; c < nch; c += 256) {
+            float w[8];
+            Elem<TIn>::load8(row + 8 * c, w);
+            *reinterpret_cast<uint2 *>(q + m * ldq + 8 * c) = quant_chunk8<KIND, RNE>(w, sc, fast, ns, rs);
+        }
     }
     if (threadIdx.x == 0) s[m * s_rs] = sc;
 }
 
+template <typename TIn, int KIND, bool RNE>
+static void launch_quant_row(const TIn *x, int64_t ldx, int64_t M, int64_t K, uint8_t *q, int64_t ldq, float *s,
+                             int64_t s_rs, cudaStream_t st) {
+    dim3 grid((unsigned)M), block(256);
+    switch (cdiv(K / 8, 256)) {
+    case 1: k_quant_row<TIn, KIND, RNE, 1><<<grid, block, 0, st>>>(x, ldx, K, q, ldq, s, s_rs); break;
+    case 2: k_quant_row<TIn, KIND, RNE, 2><<<grid, block, 0, st>>>(x, ldx, K, q, ldq, s, s_rs); break;
+    case 3: k_quant_row<TIn, KIND, RNE, 3><<<grid, block, 0, st>>>(x, ldx, K, q, ldq, s, s_rs); break;
+    case 4: k_quant_row<TIn, KIND, RNE, 4><<<grid, block, 0, st>>>(x, ldx, K, q, ldq, s, s_rs); break;
+    case 5: case 6: k_quant_row<TIn, KIND, RNE, 6><<<grid, block, 0, st>>>(x, ldx, K, q, ldq, s, s_rs); break;
+    case 7: case 8: k_quant_row<TIn, KIND, RNE, 8><<<grid, block, 0, st>>>(x, ldx, K, q, ldq, s, s_rs); break;
+    default: k_quant_row<TIn, KIND, RNE, 0><<<grid, block, 0, st>>>(x, ldx, K, q, ldq, s, s_rs); break;
+    }
+}
+
+// flags: bit 0 one scale per row, bit 1 int8 codes rounded half to even
 template <typename TIn>
-static cudaError_t launch_quant_t(const void *x, int64_t ldx, int64_t M, int64_t K, int kind, int per_row, void *q,
+static cudaError_t launch_quant_t(const void *x, int64_t ldx, int64_t M, int64_t K, int kind, int flags, void *q,
                                   int64_t ldq, float *s, int64_t s_rs, int64_t s_gs, cudaStream_t st) {
     const TIn *xp = static_cast<const TIn *>(x);
     uint8_t *qp = static_cast<uint8_t *>(q);
-    if (per_row) {
-        dim3 grid((unsigned)M), block(256);
-        if (kind == 0) k_quant_row<TIn, 0><<<grid, block, 0, st>>>(xp, ldx, K, qp, ldq, s, s_rs);
-        else k_quant_row<TIn, 1><<<grid, block, 0, st>>>(xp, ldx, K, qp, ldq, s, s_rs);
+    const bool rne = kind == 0 && (flags & 2);
+    if (flags & 1) {
+        if (rne) launch_quant_row<TIn, 0, true>(xp, ldx, M, K, qp, ldq, s, s_rs, st);
+        else if (kind == 0) launch_quant_row<TIn, 0, false>(xp, ldx, M, K, qp, ldq, s, s_rs, st);
+        else launch_quant_row<TIn, 1, false>(xp, ldx, M, K, qp, ldq, s, s_rs, st);
     } else {
         const int64_t G = K / 128;
         const int64_t warps = cdiv(M * G, 4);
         int64_t blocks = cdiv(warps, 8);
         const int64_t cap = (int64_t)num_sms() * 16;
         if (blocks > cap) blocks = cap;
-        if (kind == 0) k_quant_group<TIn, 0><<<(unsigned)blocks, 256, 0, st>>>(xp, ldx, M, G, qp, ldq, s, s_rs, s_gs);
-        else k_quant_group<TIn, 1><<<(unsigned)blocks, 256, 0, st>>>(xp, ldx, M, G, qp, ldq, s, s_rs, s_gs);
+        if (rne) k_quant_group<TIn, 0, true><<<(unsigned)blocks, 256, 0, st>>>(xp, ldx, M, G, qp, ldq, s, s_rs, s_gs);
+        else if (kind == 0) k_quant_group<TIn, 0, false><<<(unsigned)blocks, 256, 0, st>>>(xp, ldx, M, G, qp, ldq, s, s_rs, s_gs);
+        else k_quant_group<TIn, 1, false><<<(unsigned)blocks, 256, 0, st>>>(xp, ldx, M, G, qp, ldq, s, s_rs, s_gs);
     }
     return cudaGetLastError();
 }
 
-cudaError_t launch_quant_act(const void *x, int64_t ldx, int x_dtype, int64_t M, int64_t K, int kind, int per_row,
+cudaError_t launch_quant_act(const void *x, int64_t ldx, int x_dtype, int64_t M, int64_t K, int kind, int flags,
                              void *q, int64_t ldq, float *s, int64_t s_rs, int64_t s_gs, cudaStream_t st) {
     switch (x_dtype) {
-    case 0: return launch_quant_t<__nv_bfloat16>(x, ldx, M, K, kind, per_row, q, ldq, s, s_rs, s_gs, st);
-    case 1: return launch_quant_t<__half>(x, ldx, M, K, kind, per_row, q, ldq, s, s_rs, s_gs, st);
-    default: return launch_quant_t<float>(x, ldx, M, K, kind, per_row, q, ldq, s, s_rs, s_gs, st);
+    case 0: return launch_quant_t<__nv_bfloat16>(x, ldx, M, K, kind, flags, q, ldq, s, s_rs, s_gs, st);
+    case 1: return launch_quant_t<__half>(x, ldx, M, K, kind, flags, q, ldq, s, s_rs, s_gs, st);
+    default: return launch_quant_t<float>(x, ldx, M, K, kind, flags, q, ldq, s, s_rs, s_gs, st);
     }
 }
 

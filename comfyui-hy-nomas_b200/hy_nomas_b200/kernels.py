@@ -25,9 +25,10 @@ def _aligned(t):
     return t.data_ptr() % 16 == 0 and (t.stride(0) * t.element_size()) % 16 == 0 and t.stride(-1) == 1
 
 
-def quantize_activations(x, kind="int8", per_token=False):
+def quantize_activations(x, kind="int8", per_token=False, round_half_even=False):
     """x [M, K] (K % 128 == 0) -> codes [M, K] and fp32 scales [M, K / 128] (hy_nomas/kernels.py:45-54).
-    `per_token=True`: one scale per row, scales [M, 1]."""
+    `per_token=True`: one scale per row, scales [M, 1]. `round_half_even=True` (int8): codes rounded half to
+    even instead of the reference's half away from zero - BASELINE config 1's per-token wording."""
     _lib.require_cuda(x)
     m, k = x.shape
     if x.dtype not in (torch.bfloat16, torch.float16, torch.float32):
@@ -41,9 +42,9 @@ def quantize_activations(x, kind="int8", per_token=False):
         srs, sgs = 1, 1
     else:
         s, srs, sgs = _lib.group_scales(m, k // GROUP, x.device)
-    rc = _lib.lib.hn_quant_act(_lib.ptr(x), x.stride(0), _lib.DTYPE[x.dtype], m, k, _lib.KIND[kind],
-                               1 if per_token else 0, _lib.ptr(q), q.stride(0), _lib.ptr(s), srs, sgs,
-                               _lib.stream_of(x))
+    flags = (1 if per_token else 0) | (2 if round_half_even else 0)
+    rc = _lib.lib.hn_quant_act(_lib.ptr(x), x.stride(0), _lib.DTYPE[x.dtype], m, k, _lib.KIND[kind], flags,
+                               _lib.ptr(q), q.stride(0), _lib.ptr(s), srs, sgs, _lib.stream_of(x))
     _lib.check(rc, "quantize_activations")
     return q, s
 

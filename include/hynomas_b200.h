@@ -105,10 +105,15 @@ int hn_selftest_wait_timeout(uint32_t timeout_us, void *stream);
  *   scales s: one per (row, group) at s[m * s_rs + g * s_gs].
  * int8: s = peak > 0 ? peak/127 : 1, q = round-half-away(x/s) clamped to +-127.
  * e4m3: s = max(peak, 1e-12)/448, q = e4m3(x/s) round-to-nearest-even, saturating.
- * `per_row` != 0 uses one group spanning all K (per-token scale s[m * s_rs]) - the per-token
- * quantization that BASELINE config 1 names; no counterpart in the reference.
+ * `flags` (0 = the reference's quantizer):
+ *   HN_QUANT_PER_ROW: one group spanning all K (per-token scale s[m * s_rs]) - the per-token quantization
+ *     that BASELINE config 1 names; no counterpart in the reference.
+ *   HN_QUANT_ROUND_HALF_EVEN (int8 only): codes rounded half to even instead of half away from zero
+ *     (config 1's wording); no counterpart in the reference.
  */
-int hn_quant_act(const void *x, int64_t ldx, int x_dtype, int64_t M, int64_t K, int kind, int per_row,
+#define HN_QUANT_PER_ROW 1
+#define HN_QUANT_ROUND_HALF_EVEN 2
+int hn_quant_act(const void *x, int64_t ldx, int x_dtype, int64_t M, int64_t K, int kind, int flags,
                  void *q, int64_t ldq, float *s, int64_t s_rs, int64_t s_gs, void *stream);
 
 /*

@@ -46,6 +46,15 @@ static inline int8_t code_i8(float y) {
     return (int8_t)(int)r;
 }
 
+/* round half to even, clamp to +-127: the per-token codes of BASELINE config 1 ("round-half-even"), offered
+ * beside the reference's rounding; nearbyintf rounds to nearest even in the default rounding mode */
+static inline int8_t code_i8_rne(float y) {
+    float r = nearbyintf(y);
+    if (r < -127.0f) r = -127.0f;
+    if (r > 127.0f) r = 127.0f;
+    return (int8_t)(int)r;
+}
+
 /* fp32 -> float8_e4m3fn byte, round to nearest even, saturating to +-448 (the .satfinite conversion the
  * GPU path uses, equal to torch's .to(float8_e4m3fn) for |x| < 464). */
 uint8_t or_e4m3_from_f32(float x) {
@@ -136,7 +145,8 @@ float or_gelu_tanh(float x) {
 
 /* ---------------------------------------------------------------------------------------------------
  * K1 - hy_nomas/kernels.py:22-42 (_quantize_kernel). x fp32 [M, K] (the bf16 input widened exactly);
- * kind 0: int8, 1: e4m3. group = 128, or K for the per-token variant (one scale per row).
+ * kind 0: int8, 1: e4m3, 2: int8 with codes rounded half to even. group = 128, or K for the per-token
+ * variant (one scale per row).
  */
 void or_quant_act(const float *x, int64_t M, int64_t K, int kind, int64_t group, uint8_t *q, float *s) {
     int64_t G = K / group;
@@ -146,9 +156,10 @@ void or_quant_act(const float *x, int64_t M, int64_t K, int kind, int64_t group,
             float peak = 0.0f;
             for (int64_t i = 0; i < group; ++i) peak = fmaxf(peak, fabsf(v[i]));
             float scale;
-            if (kind == 0) {
+            if (kind == 0 || kind == 2) {
                 scale = (peak > 0.0f) ? peak / 127.0f : 1.0f;
-                for (int64_t i = 0; i < group; ++i) q[m * K + g * group + i] = (uint8_t)code_i8(v[i] / scale);
+                for (int64_t i = 0; i < group; ++i)
+                    q[m * K + g * group + i] = (uint8_t)(kind == 0 ? code_i8(v[i] / scale) : code_i8_rne(v[i] / scale));
             } else {
                 scale = fmaxf(peak, 1e-12f) / 448.0f;
                 for (int64_t i = 0; i < group; ++i) q[m * K + g * group + i] = or_e4m3_from_f32(v[i] / scale);

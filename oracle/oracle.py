@@ -141,15 +141,17 @@ def gelu_tanh(x):
 # the path
 
 
-def quantize_activations(x, kind="int8", per_row=False):
+def quantize_activations(x, kind="int8", per_row=False, round_half_even=False):
     """hy_nomas/kernels.py:45-54. x float32 [M, K] -> (codes uint8 [M, K] (int8 bits or e4m3 bytes),
-    scales float32 [M, K/128] or [M, 1] per row)."""
+    scales float32 [M, K/128] or [M, 1] per row). round_half_even: int8 codes rounded half to even (BASELINE
+    config 1's wording) instead of the reference's half away from zero."""
     x = _f32(x)
     m, k = x.shape
     group = k if per_row else GROUP
     q = np.empty((m, k), dtype=np.uint8)
     s = np.empty((m, k // group), dtype=np.float32)
-    lib().or_quant_act(_ptr(x), m, k, 0 if kind == "int8" else 1, group, _ptr(q), _ptr(s))
+    code = (2 if round_half_even else 0) if kind == "int8" else 1
+    lib().or_quant_act(_ptr(x), m, k, code, group, _ptr(q), _ptr(s))
     return q, s
 
 

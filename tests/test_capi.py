@@ -54,6 +54,8 @@ def test_validation_errors_before_launch(hn):
     assert L.hn_quant_act(FAKE, 128, 9, 4, 128, 0, 0, FAKE, 128, FAKE, 1, 1, None) == 5      # dtype
     assert L.hn_quant_act(ctypes.c_void_p(0x10008), 128, 0, 4, 128, 0, 0, FAKE, 128, FAKE, 1, 1, None) == 2
     assert L.hn_quant_act(FAKE, 256, 0, 4, 256, 0, 0, FAKE, 256, FAKE, 1, 2, None) == 1      # scale strides alias
+    assert L.hn_quant_act(FAKE, 128, 0, 4, 128, 0, 4, FAKE, 128, FAKE, 1, 1, None) == 5      # unknown flag
+    assert L.hn_quant_act(FAKE, 128, 0, 4, 128, 1, 2, FAKE, 128, FAKE, 1, 1, None) == 5      # RNE on e4m3
     args = dict(qa=FAKE, lda=256, sa=FAKE, sars=2, sags=1, sam=0, qw=FAKE, ldw=256, sw=FAKE, swrs=2, swgs=1, swm=0,
                 bias=None, bd=0, out=FAKE, ldo=256, od=0, qs=None, qsrs=0, qsgs=0, M=64, N=256, K=256, kind=0, epi=0)
 

@@ -44,8 +44,12 @@ def test_strided_rows(hn, oracle, cuda):
 
 
 @pytest.mark.parametrize("kind", ["int8", "fp8"])
-def test_per_token(hn, oracle, cuda, kind):
-    x = (torch.randn(100, 4096, generator=torch.Generator().manual_seed(3)) * 2).bfloat16()
+@pytest.mark.parametrize("k", [128, 384, 3072, 4096, 16384, 20480])
+def test_per_token(hn, oracle, cuda, kind, k):
+    """Row lengths covering every per-row kernel shape: one to eight register chunks per thread (partial last
+    chunk rows at 384 and 3072) and the two-pass form beyond 16384."""
+    rows = 100 if k <= 4096 else 12
+    x = (torch.randn(rows, k, generator=torch.Generator().manual_seed(3)) * 2).bfloat16()
     q, s = hn.kernels.quantize_activations(x.to(cuda), kind, per_token=True)
     qo, so = oracle.quantize_activations(f32(x), kind, per_row=True)
     assert np.array_equal(u8(q), qo) and np.array_equal(f32(s), so)
@@ -167,3 +171,26 @@ def test_per_token_edge_rows(hn, oracle, cuda, kind):
     qo, so = oracle.quantize_activations(f32(x), kind, per_row=True)
     assert np.array_equal(u8(q), qo)
     assert np.array_equal(f32(s).reshape(-1), so.reshape(-1))
+
+
+@pytest.mark.parametrize("per_token", [False, True])
+@pytest.mark.parametrize("dtype", [torch.bfloat16, torch.float32])
+def test_round_half_even_option(hn, oracle, cuda, per_token, dtype):
+    """int8 codes rounded half to even (BASELINE config 1's wording; the reference rounds half away): exact ties
+    at scale 1 and random rows (with a tie row), bf16 (fast quotient) and fp32 (IEEE division) inputs,
+    bit-exact with the oracle; the default stays half away from zero."""
+    import test_oracle_math
+    ties, _ = test_oracle_math.tie_rows()
+    gen = torch.Generator().manual_seed(7)
+    rnd = (torch.randn(30, 512, generator=gen) * 3).numpy()
+    x = np.concatenate([np.pad(ties, ((0, 0), (0, 512 - 128))), rnd]).astype(np.float32)
+    xt = torch.from_numpy(x).to(dtype)
+    xf = xt.float().numpy()
+    for rne in (True, False):
+        q, s = hn.kernels.quantize_activations(xt.to(cuda), "int8", per_token=per_token, round_half_even=rne)
+        qo, so = oracle.quantize_activations(xf, "int8", per_row=per_token, round_half_even=rne)
+        assert np.array_equal(u8(q), qo), rne
+        assert np.array_equal(f32(s).reshape(-1), so.reshape(-1)), rne
+    codes_even = hn.kernels.quantize_activations(xt.to(cuda), "int8", per_token=per_token, round_half_even=True)[0]
+    codes_away = hn.kernels.quantize_activations(xt.to(cuda), "int8", per_token=per_token)[0]
+    assert not torch.equal(codes_even, codes_away)          # the tie rows differ between the two modes

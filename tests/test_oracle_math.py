@@ -51,3 +51,28 @@ def test_e4m3_conversion_matches_torch(oracle):
     import ctypes
     got = np.array([oracle.lib().or_e4m3_from_f32(ctypes.c_float(v)) for v in x[:20000]], dtype=np.uint8)
     assert np.array_equal(got, ref[:20000])
+
+
+def tie_rows():
+    """Rows whose scale is exactly 1 (absmax 127) and whose other values are exact ties k + 0.5, all bf16."""
+    ties = [0.5, -0.5, 1.5, -1.5, 2.5, -2.5, 3.5, 126.5, -126.5, 0.25, 3.75]
+    row = np.zeros(128, dtype=np.float32)
+    row[0] = 127.0
+    row[1:1 + len(ties)] = ties
+    return np.stack([row, -row]), ties
+
+
+def test_round_half_even_option_on_ties(oracle):
+    """Per-token and per-group int8 codes on exact ties: half away from zero (the reference) and half to even
+    (BASELINE config 1's wording)."""
+    x, ties = tie_rows()
+    away = {0.5: 1, 1.5: 2, 2.5: 3, 3.5: 4, 126.5: 127, 0.25: 0, 3.75: 4}
+    even = {0.5: 0, 1.5: 2, 2.5: 2, 3.5: 4, 126.5: 126, 0.25: 0, 3.75: 4}
+    for per_row in (False, True):
+        for rne, table in ((False, away), (True, even)):
+            q, s = oracle.quantize_activations(x, "int8", per_row=per_row, round_half_even=rne)
+            assert np.all(s == 1.0)
+            codes = q.view(np.int8)
+            for i, t in enumerate(ties):
+                want = int(np.sign(t)) * table[abs(t)]
+                assert codes[0, 1 + i] == want and codes[1, 1 + i] == -want, (per_row, rne, t)
