@@ -166,6 +166,12 @@ def block_forward(cfg, w, x, vec, rope, sp, ops=CudaOps, trace=None):
     mods = ops.linear(act, w.mod)
     shift1, scale1, gate1, shift2, scale2, gate2 = mods.chunk(6, dim=-1)
     qa, sa = ops.adaln_quant(x, shift1, scale1)
+    chunks = sp.head_chunks if (sp.world > 1 and h % sp.head_chunks == 0) else 1
+    if chunks > 1:
+        attn, k_full, v_full, qk, q_out = _attention_chunked(cfg, w, qa, sa, rope, sp, ops, b, l, chunks,
+                                                             keep_kv=trace is not None)
+        return _post(cfg, w, x, attn, qa, sa, qk, q_out, k_full, v_full, act, mods, gate1, shift2, scale2, gate2,
+                     ops, trace)
     k_full, v_full, k_mine, v_mine = sp.kv_buffers(b, l, h, hd, x.dtype, x.device)
     # v first, so its all-gather runs under the q|k GEMM; k is normalized before q, so its gather runs under
     # q's normalization (with one rank the gathers are no-ops and the order changes nothing)
@@ -184,6 +190,49 @@ def block_forward(cfg, w, x, vec, rope, sp, ops=CudaOps, trace=None):
         gather_k = None
     sp.wait(gather_k, gather_v)
     attn = ops.attention(q_out, k_full, v_full).reshape(b * l, d)
+    return _post(cfg, w, x, attn, qa, sa, qk, q_out, k_full, v_full, act, mods, gate1, shift2, scale2, gate2, ops,
+                 trace)
+
+
+def _rows(w, lo, hi):
+    """Output rows [lo, hi) of an int8 linear (views)."""
+    return QLinear(w.q[lo:hi], w.s[lo:hi], w.bias[lo:hi])
+
+
+def _attention_chunked(cfg, w, qa, sa, rope, sp, ops, b, l, chunks, keep_kv=False):
+    """Attention with the K/V all-gathers split into `chunks` head groups: every chunk's V projection and K
+    normalization write the rank's slice of that chunk's gather buffers, the gathers are issued as soon as their
+    inputs exist (V's under the q|k GEMM), and chunk c's attention only waits for chunk c's K and V, so the
+    gathers of later chunks run under it. Per head the arithmetic is that of the unchunked path. `keep_kv`:
+    also return the full K and V (for traces), else None."""
+    h, hd = cfg.heads, cfg.head_dim
+    d = h * hd
+    hc = h // chunks
+    bufs = sp.kv_chunk_buffers(b, l, h, hd, chunks, torch.bfloat16, qa.device)
+    gathers_v, gathers_k = [], []
+    for c, (kf, vf, km, vm) in enumerate(bufs):
+        ops.gemm(qa, sa, _rows(w.v, c * hc * hd, (c + 1) * hc * hd), out=vm.view(b * l, hc * hd))
+        gathers_v.append(sp.all_gather_async(vf, vm))
+    qk = ops.gemm(qa, sa, w.qk)                                       # [B*l, 2D]
+    q_in = qk[:, :d].view(b, l, h, hd)
+    k_in = qk[:, d:].view(b, l, h, hd)
+    for c, (kf, vf, km, vm) in enumerate(bufs):
+        ops.qk_norm_rope(k_in[:, :, c * hc:(c + 1) * hc], w.k_norm, rope, out=km)
+        gathers_k.append(sp.all_gather_async(kf, km))
+    q_out = torch.empty((b, l, h, hd), dtype=torch.bfloat16, device=qa.device)
+    ops.qk_norm_rope(q_in, w.q_norm, rope, out=q_out)
+    attn = torch.empty((b, l, h, hd), dtype=torch.bfloat16, device=qa.device)
+    for c, (kf, vf, km, vm) in enumerate(bufs):
+        sp.wait(gathers_k[c], gathers_v[c])
+        attn[:, :, c * hc:(c + 1) * hc] = ops.attention(q_out[:, :, c * hc:(c + 1) * hc], kf, vf)
+    k_full = torch.cat([kf for kf, _, _, _ in bufs], dim=2) if keep_kv else None
+    v_full = torch.cat([vf for _, vf, _, _ in bufs], dim=2) if keep_kv else None
+    return attn.view(b * l, d), k_full, v_full, qk, q_out
+
+
+def _post(cfg, w, x, attn, qa, sa, qk, q_out, k_full, v_full, act, mods, gate1, shift2, scale2, gate2, ops, trace):
+    """The block after attention: projection, gated residual + LN + quant, MLP, gated residual."""
+    b, l, d = x.shape
     proj = ops.linear(attn, w.proj).view(b, l, d)
     x1, qa2, sa2 = ops.gated_residual_adaln_quant(x, proj, gate1, shift2, scale2)
     qh, sh = ops.gemm(qa2, sa2, w.fc1, epilogue="gelu_quant")

@@ -12,18 +12,31 @@ Rank r owns tokens [r * L / P, (r + 1) * L / P); L must divide evenly (20240 doe
 The gather buffers are rank-major, so with batch 1 a rank's K/V rows are one contiguous slice that its own
 kernels write in place and that the all-gather uses as its input.
 """
+import os
+
 import torch
 import torch.distributed as dist
 
+# K/V head chunks per block under sequence parallelism (HN_SP_HEAD_CHUNKS overrides)
+HEAD_CHUNKS = 1
+
 
 class SequenceParallel:
-    def __init__(self, group=None):
+    """`head_chunks` > 1 splits each block's K/V gathers and attention by heads, so that a chunk's attention runs
+    while the next chunk's K is still being gathered (every head's arithmetic is unchanged)."""
+
+    def __init__(self, group=None, head_chunks=None):
         self.group = group
         if dist.is_available() and dist.is_initialized():
             self.world = dist.get_world_size(group)
             self.rank = dist.get_rank(group)
         else:
             self.world, self.rank = 1, 0
+        if head_chunks is None:
+            head_chunks = int(os.environ.get("HN_SP_HEAD_CHUNKS", str(HEAD_CHUNKS)))
+        if head_chunks < 1:
+            raise ValueError(f"head_chunks must be >= 1, got {head_chunks}")
+        self.head_chunks = head_chunks
         self._bufs = {}
 
     def shard(self, length):
@@ -40,12 +53,25 @@ class SequenceParallel:
             raise ValueError("sequence parallelism takes batch 1 (the denoise step's layout)")
         key = (batch, local, heads, head_dim, dtype, str(device))
         if key not in self._bufs:
-            total = local * self.world
-            k_full = torch.empty((batch, total, heads, head_dim), dtype=dtype, device=device)
-            v_full = torch.empty_like(k_full)
-            lo = self.rank * local
-            self._bufs[key] = (k_full, v_full, k_full[:, lo:lo + local], v_full[:, lo:lo + local])
+            self._bufs[key] = self._alloc(batch, local, heads, head_dim, dtype, device)
         return self._bufs[key]
+
+    def kv_chunk_buffers(self, batch, local, heads, head_dim, chunks, dtype, device):
+        """`kv_buffers` per head chunk: a list of `chunks` (k_full, v_full, k_mine, v_mine) tuples, each over
+        heads // chunks heads, so that every chunk's gather has contiguous rank slices."""
+        if self.world > 1 and batch != 1:
+            raise ValueError("sequence parallelism takes batch 1 (the denoise step's layout)")
+        key = ("chunks", chunks, batch, local, heads, head_dim, dtype, str(device))
+        if key not in self._bufs:
+            self._bufs[key] = [self._alloc(batch, local, heads // chunks, head_dim, dtype, device) for _ in range(chunks)]
+        return self._bufs[key]
+
+    def _alloc(self, batch, local, heads, head_dim, dtype, device):
+        total = local * self.world
+        k_full = torch.empty((batch, total, heads, head_dim), dtype=dtype, device=device)
+        v_full = torch.empty_like(k_full)
+        lo = self.rank * local
+        return k_full, v_full, k_full[:, lo:lo + local], v_full[:, lo:lo + local]
 
     def all_gather_async(self, full, mine):
         """Start filling `full` with every rank's `mine` (a slice of `full`); returns a handle for `wait`."""

@@ -25,7 +25,7 @@ def run_model(cfg, sp, ops, device):
     return model(x[:, lo:hi].contiguous(), vec)
 
 
-def gloo_rank(rank, world, port, out_path):
+def gloo_rank(rank, world, port, out_path, head_chunks=1):
     import torch.distributed as dist
     from dit_oracle_ops import OracleOps
     from hy_nomas_b200.sequence_parallel import SequenceParallel
@@ -34,7 +34,7 @@ def gloo_rank(rank, world, port, out_path):
     dist.init_process_group("gloo", rank=rank, world_size=world)
     try:
         cfg = small_config()
-        out = run_model(cfg, SequenceParallel(), OracleOps, "cpu")
+        out = run_model(cfg, SequenceParallel(head_chunks=head_chunks), OracleOps, "cpu")
         parts = [torch.empty_like(out) for _ in range(world)]
         dist.all_gather(parts, out)
         if rank == 0:
@@ -43,7 +43,7 @@ def gloo_rank(rank, world, port, out_path):
         dist.destroy_process_group()
 
 
-def nccl_rank(rank, world, port, out_path):
+def nccl_rank(rank, world, port, out_path, head_chunks=1):
     import datetime
     import torch.distributed as dist
     from hy_nomas_b200.sequence_parallel import SequenceParallel
@@ -56,7 +56,7 @@ def nccl_rank(rank, world, port, out_path):
     try:
         from hy_nomas_b200.dit import CudaOps
         cfg = small_config()
-        out = run_model(cfg, SequenceParallel(), CudaOps, f"cuda:{rank}")
+        out = run_model(cfg, SequenceParallel(head_chunks=head_chunks), CudaOps, f"cuda:{rank}")
         parts = [torch.empty_like(out) for _ in range(world)]
         dist.all_gather(parts, out)
         torch.cuda.synchronize()

@@ -109,8 +109,9 @@ def free_port():
         return s.getsockname()[1]
 
 
-def test_sequence_parallel_two_gpus(hn, cuda, tmp_path):
-    """2 ranks over NCCL (K/V all-gathered) against the same model on one GPU."""
+@pytest.mark.parametrize("head_chunks", [1, 2])
+def test_sequence_parallel_two_gpus(hn, cuda, tmp_path, head_chunks):
+    """2 ranks over NCCL (K/V all-gathered, whole or split by head) against the same model on one GPU."""
     if torch.cuda.device_count() < 2:
         pytest.skip("needs 2 GPUs")
     from hy_nomas_b200.dit import CudaOps
@@ -119,7 +120,7 @@ def test_sequence_parallel_two_gpus(hn, cuda, tmp_path):
     ctx = mp.get_context("spawn")
     port = free_port()
     out_path = os.path.join(tmp_path, "sp.pt")
-    procs = [ctx.Process(target=sp_worker.nccl_rank, args=(r, 2, port, out_path)) for r in range(2)]
+    procs = [ctx.Process(target=sp_worker.nccl_rank, args=(r, 2, port, out_path, head_chunks)) for r in range(2)]
     for p in procs:
         p.start()
     for p in procs:

@@ -42,12 +42,14 @@ def test_shard_ranges():
         sp.shard(20240)
 
 
-@pytest.mark.parametrize("world", [2, 4])
-def test_gloo_matches_single_rank(single_rank, tmp_path, world):
+@pytest.mark.parametrize("world,head_chunks", [(2, 1), (4, 1), (2, 2)])
+def test_gloo_matches_single_rank(single_rank, tmp_path, world, head_chunks):
+    """2 and 4 gloo ranks, and 2 ranks with the K/V gathers split by head, equal the single-rank model."""
     ctx = mp.get_context("spawn")
     port = free_port()
     out_path = os.path.join(tmp_path, "out.pt")
-    procs = [ctx.Process(target=sp_worker.gloo_rank, args=(r, world, port, out_path)) for r in range(world)]
+    procs = [ctx.Process(target=sp_worker.gloo_rank, args=(r, world, port, out_path, head_chunks))
+             for r in range(world)]
     for p in procs:
         p.start()
     for p in procs:
