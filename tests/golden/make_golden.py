@@ -1,7 +1,7 @@
 """Generate the golden vectors of the quantized DiT linear path from the REFERENCE's own code.
 
-Run in a container that has the reference checked out (default /root/reference; override with
-HY_NOMAS_REFERENCE):
+Run where a checkout of the reference repository is available (its directory given by HY_NOMAS_REFERENCE;
+REF below holds the default):
 
     python tests/golden/make_golden.py
 
