@@ -157,19 +157,50 @@ __device__ __forceinline__ uint2 quant_chunk8(const float (&v)[8], float sc, boo
     return out;
 }
 
-// Per-row (per-token) variant: one CTA of 256 threads per row. NCH > 0: the row stays in registers, NCH chunks
-// of 8 elements per thread (chunk c at elements [8c, 8c + 8), thread t holding chunks t, t + 256, ...: one HBM
+// Per-row variant: one CTA of 256 threads per row. NCH > 0: the row stays in registers, NCH chunks of 8
+// elements per thread (chunk c at elements [8c, 8c + 8), thread t holding chunks t, t + 256, ...: one HBM
 // pass, coalesced 16-byte loads); NCH == 0 (rows longer than 16384): two passes, the second from L2.
-template <typename TIn, int KIND, bool RNE, int NCH>
+// GRP: one scale per 128-element group instead of per row - a group is 16 consecutive chunks, i.e. 16
+// consecutive threads for one i, so its absmax is a 16-lane shuffle (registers only, NCH > 0).
+template <typename TIn, int KIND, bool RNE, int NCH, bool GRP = false>
 __global__ void __launch_bounds__(256) k_quant_row(const TIn *__restrict__ x, int64_t ldx, int64_t K,
                                                    uint8_t *__restrict__ q, int64_t ldq, float *__restrict__ s,
-                                                   int64_t s_rs) {
+                                                   int64_t s_rs, int64_t s_gs = 0) {
     __shared__ float red[8];
     const int64_t m = blockIdx.x;
     const TIn *row = x + m * ldx;
     const int64_t nch = K >> 3;
     float v[NCH > 0 ? NCH : 1][8];
     float peak = 0.0f;
+    if (GRP) {
+        static_assert(!GRP || NCH > 0, "grouped scales keep the row in registers");
+        constexpr bool BF16_IN = sizeof(TIn) == 2 && !std::is_same<TIn, __half>::value;
+#pragma unroll
+        for (int i = 0; i < (NCH > 0 ? NCH : 1); ++i) {
+            const int64_t c = threadIdx.x + (int64_t)i * 256;
+            if (c < nch) Elem<TIn>::load8(row + 8 * c, v[i]);
+            else {
+#pragma unroll
+                for (int j = 0; j < 8; ++j) v[i][j] = 0.0f;
+            }
+        }
+#pragma unroll
+        for (int i = 0; i < (NCH > 0 ? NCH : 1); ++i) {
+            const int64_t c = threadIdx.x + (int64_t)i * 256;
+            float gp = 0.0f;
+#pragma unroll
+            for (int j = 0; j < 8; ++j) gp = fmaxf(gp, fabsf(v[i][j]));
+            gp = warp_max_xor(gp, 16);
+            const float sc = KIND == 0 ? i8_scale(gp) : e4m3_scale(gp);
+            const bool fast = BF16_IN && sc >= 0x1p-90f;
+            const uint64_t ns = x2_splat(-sc), rs = x2_splat(__frcp_rn(sc));
+            if (c < nch) {
+                *reinterpret_cast<uint2 *>(q + m * ldq + 8 * c) = quant_chunk8<KIND, RNE>(v[i], sc, fast, ns, rs);
+                if ((c & 15) == 0) s[m * s_rs + (c >> 4) * s_gs] = sc;
+            }
+        }
+        return;
+    }
     if (NCH > 0) {
 #pragma unroll
         for (int i = 0; i < (NCH > 0 ? NCH : 1); ++i) {
@@ -216,6 +247,21 @@ __global__ void __launch_bounds__(256) k_quant_row(const TIn *__restrict__ x, in
     if (threadIdx.x == 0) s[m * s_rs] = sc;
 }
 
+// grouped scales, rows of up to 16384 elements (NCH <= 8); false when the row is longer
+template <typename TIn, int KIND, bool RNE>
+static bool launch_quant_group_rows(const TIn *x, int64_t ldx, int64_t M, int64_t K, uint8_t *q, int64_t ldq,
+                                    float *s, int64_t s_rs, int64_t s_gs, cudaStream_t st) {
+    dim3 grid((unsigned)M), block(256);
+    switch (cdiv(K / 8, 256)) {
+    case 1: k_quant_row<TIn, KIND, RNE, 1, true><<<grid, block, 0, st>>>(x, ldx, K, q, ldq, s, s_rs, s_gs); return true;
+    case 2: k_quant_row<TIn, KIND, RNE, 2, true><<<grid, block, 0, st>>>(x, ldx, K, q, ldq, s, s_rs, s_gs); return true;
+    case 3: case 4: k_quant_row<TIn, KIND, RNE, 4, true><<<grid, block, 0, st>>>(x, ldx, K, q, ldq, s, s_rs, s_gs); return true;
+    case 5: case 6: case 7: case 8:
+        k_quant_row<TIn, KIND, RNE, 8, true><<<grid, block, 0, st>>>(x, ldx, K, q, ldq, s, s_rs, s_gs); return true;
+    default: return false;
+    }
+}
+
 template <typename TIn, int KIND, bool RNE>
 static void launch_quant_row(const TIn *x, int64_t ldx, int64_t M, int64_t K, uint8_t *q, int64_t ldq, float *s,
                              int64_t s_rs, cudaStream_t st) {
@@ -242,6 +288,11 @@ static cudaError_t launch_quant_t(const void *x, int64_t ldx, int64_t M, int64_t
         if (rne) launch_quant_row<TIn, 0, true>(xp, ldx, M, K, qp, ldq, s, s_rs, st);
         else if (kind == 0) launch_quant_row<TIn, 0, false>(xp, ldx, M, K, qp, ldq, s, s_rs, st);
         else launch_quant_row<TIn, 1, false>(xp, ldx, M, K, qp, ldq, s, s_rs, st);
+    } else if (M >= 2 * num_sms() && K >= 2048 &&
+               (rne ? launch_quant_group_rows<TIn, 0, true>(xp, ldx, M, K, qp, ldq, s, s_rs, s_gs, st)
+                    : kind == 0 ? launch_quant_group_rows<TIn, 0, false>(xp, ldx, M, K, qp, ldq, s, s_rs, s_gs, st)
+                                : launch_quant_group_rows<TIn, 1, false>(xp, ldx, M, K, qp, ldq, s, s_rs, s_gs, st))) {
+        // one CTA per row (enough rows to fill the GPU, and a row that occupies every thread)
     } else {
         const int64_t G = K / 128;
         const int64_t warps = cdiv(M * G, 4);

@@ -194,3 +194,31 @@ def test_round_half_even_option(hn, oracle, cuda, per_token, dtype):
     codes_even = hn.kernels.quantize_activations(xt.to(cuda), "int8", per_token=per_token, round_half_even=True)[0]
     codes_away = hn.kernels.quantize_activations(xt.to(cuda), "int8", per_token=per_token)[0]
     assert not torch.equal(codes_even, codes_away)          # the tie rows differ between the two modes
+
+
+@pytest.mark.parametrize("k", [384, 2048, 3072, 4096, 16384, 20480])
+@pytest.mark.parametrize("kind,rne", [("int8", False), ("int8", True), ("fp8", False)])
+def test_group_scales_one_cta_per_row(hn, oracle, cuda, k, kind, rne):
+    """Enough rows for the one-CTA-per-row group quantizer (rows of 2048 to 16384 in registers; shorter and
+    longer rows on the grid-stride kernel), strided rows, outlier channels and a zero row: codes and scales
+    bit-exact."""
+    m = 2 * torch.cuda.get_device_properties(0).multi_processor_count + 3
+    gen = torch.Generator().manual_seed(k + (7 if rne else 0))
+    base = (torch.randn(m, k + 128, generator=gen) * 3).bfloat16()
+    base[:, torch.randperm(k, generator=gen)[: max(1, k // 64)]] *= 20
+    base[5] = 0
+    x = base[:, :k]
+    q, s = hn.kernels.quantize_activations(base.to(cuda)[:, :k], kind, round_half_even=rne)
+    qo, so = oracle.quantize_activations(f32(x), kind, round_half_even=rne)
+    assert np.array_equal(u8(q), qo)
+    assert np.array_equal(f32(s), so)
+
+
+def test_quantize_kv_many_heads(hn, oracle, cuda):
+    """world.quantize_kv at a DiT-like size (32 heads of 128 per token) against the oracle."""
+    gen = torch.Generator().manual_seed(17)
+    x = (torch.randn(700, 32, 128, generator=gen) * 2).bfloat16()
+    x[3, 4] = 0
+    q, s = hn.world.quantize_kv(x.to(cuda))
+    qo, so = oracle.quantize_kv(f32(x))
+    assert np.array_equal(q.cpu().numpy(), qo) and np.array_equal(f32(s), so)
