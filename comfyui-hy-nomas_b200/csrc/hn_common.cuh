@@ -73,8 +73,8 @@ __device__ __forceinline__ float i8_scale(float peak) { return peak > 0.0f ? __f
 __device__ __forceinline__ float e4m3_scale(float peak) { return __fdiv_rn(fmaxf(peak, 1e-12f), 448.0f); }
 
 // 1/sqrt(v) with both steps correctly rounded (the tl.rsqrt of the reference, evaluated as the Triton
-// interpreter evaluates it).
-__device__ __forceinline__ float rsqrt_cr(float v) { return __fdiv_rn(1.0f, __fsqrt_rn(v)); }
+// interpreter evaluates it). The correctly rounded reciprocal RN(1/s) is the correctly rounded quotient 1/s.
+__device__ __forceinline__ float rsqrt_cr(float v) { return __frcp_rn(__fsqrt_rn(v)); }
 
 // ---------------------------------------------------------------------------------------------------
 // exp / GELU (hy_nomas/kernels.py:74-77). exp_cw: Cody & Waite (1980) reduction x = k*ln2 + r with the
@@ -168,21 +168,18 @@ __device__ __forceinline__ uint64_t x2_quot(uint64_t v, uint64_t ns, uint64_t rs
 
 // int8 code bytes of a pair of quotients, round half away from zero (kernels.py:35): the low byte of each
 // returned word. w = RN(q + copysign(0.5, q)) is the reference's |q| + 0.5 with q's sign (round to nearest is
-// symmetric); a round-toward-zero add of copysign(2^23, q) truncates it to an integer (exact for |w| < 2^23),
-// subtracting that constant back leaves the integer as a float, and adding 1.5 * 2^23 puts it in two's
-// complement in the low byte. |q| <= 127.00001 for the quotients of the quantizers (|v| <= absmax,
-// s = RN(absmax / 127)), so the clamp to +-127 of the reference never binds and is not applied.
+// symmetric); the conversion cvt.rzi.s32.f32 truncates it to the integer, whose two's complement low byte is
+// the code. |q| <= 127.00001 for the quotients of the quantizers (|v| <= absmax, s = RN(absmax / 127)), so the
+// clamp to +-127 of the reference never binds and is not applied.
 __device__ __forceinline__ void x2_codes(uint64_t q, uint32_t &c_lo, uint32_t &c_hi) {
     float qlo, qhi;
     x2_split(q, qlo, qhi);
-    const uint32_t slo = __float_as_uint(qlo) & 0x80000000u, shi = __float_as_uint(qhi) & 0x80000000u;
-    const uint64_t half = x2(__uint_as_float(slo | 0x3F000000u), __uint_as_float(shi | 0x3F000000u));
-    const uint64_t big = x2(__uint_as_float(slo | 0x4B000000u), __uint_as_float(shi | 0x4B000000u));
-    const uint64_t t = x2_add_rz(x2_add(q, half), big);
-    float blo, bhi;
-    x2_split(x2_add(x2_add(t, big ^ 0x8000000080000000ull), x2_splat(12582912.0f)), blo, bhi);
-    c_lo = __float_as_uint(blo);
-    c_hi = __float_as_uint(bhi);
+    const uint64_t half = x2(__uint_as_float((__float_as_uint(qlo) & 0x80000000u) | 0x3F000000u),
+                             __uint_as_float((__float_as_uint(qhi) & 0x80000000u) | 0x3F000000u));
+    float wlo, whi;
+    x2_split(x2_add(q, half), wlo, whi);
+    c_lo = (uint32_t)__float2int_rz(wlo);
+    c_hi = (uint32_t)__float2int_rz(whi);
 }
 // four code words (low bytes) -> one word, first argument in the low byte
 __device__ __forceinline__ uint32_t pack4_lowbytes(uint32_t a, uint32_t b, uint32_t c, uint32_t d) {

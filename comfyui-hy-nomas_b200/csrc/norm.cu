@@ -336,6 +336,9 @@ cudaError_t launch_gated_residual(const void *x, const void *y, const void *gate
 // Q8: the last tensor's output is also quantized for an int8 KV cache (world.py:83-90 applied to it): per
 // (token, head) absmax over the head's 128 bf16 outputs (8 lanes), scale absmax/127 (1 for an all-zero head),
 // codes rounded half away from zero; q8 [BL, H, 128] int8, s8 [BL * H] fp32.
+//
+// The warp walks (tensor, group of four heads) as one sequence, two groups per step: the two groups' loads,
+// reductions and rsqrt chains are independent, so they overlap inside the warp.
 template <bool ROPE, int NT, bool Q8>
 __global__ void __launch_bounds__(256) k_qk_norm_rope(const bf16 *__restrict__ x0, const bf16 *__restrict__ x1,
                                                       int64_t row_stride, const bf16 *__restrict__ w0,
@@ -348,7 +351,7 @@ __global__ void __launch_bounds__(256) k_qk_norm_rope(const bf16 *__restrict__ x
     const int64_t tok = (int64_t)blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5);
     if (tok >= BL) return;
     const int64_t l = tok % L;
-    // cos/sin of the lane's 16 positions as (even, odd) pairs; the sine of the even position negated
+    // cos/sin of the lane's 16 positions as (even, odd) pairs
     uint64_t C[8], S[8];
     if (ROPE) {
         const float4 *cv = reinterpret_cast<const float4 *>(cosp + l * 128 + 16 * sub);
@@ -363,106 +366,116 @@ __global__ void __launch_bounds__(256) k_qk_norm_rope(const bf16 *__restrict__ x
         }
     }
     const float inv_d = 0.0078125f;   // 1/128: ss / 128 is the exact product ss * 2^-7
+    const int ng = (H + 3) >> 2;          // groups of four heads per tensor
+    const int nit = NT * ng;
+    // step `it` = tensor it / ng, heads 4 * (it % ng) + 0..3; this lane's head h, off (h >= H) past the last head
+    struct Group {
+        int ts, h;
+        bool on;
+        uint32_t xw[8], ww[8];
+    };
+    auto load_group = [&](int it, Group &g) {
+        g.ts = (NT == 2 && it >= ng) ? 1 : 0;
+        g.h = 4 * (it - g.ts * ng) + hq;
+        g.on = g.h < H;
+        if (g.on) {
+            const bf16 *p = (g.ts ? x1 : x0) + tok * row_stride + 16 * sub + g.h * 128;
+            const uint4 a = ldg_stream(p), b = ldg_stream(p + 8);
+            g.xw[0] = a.x; g.xw[1] = a.y; g.xw[2] = a.z; g.xw[3] = a.w;
+            g.xw[4] = b.x; g.xw[5] = b.y; g.xw[6] = b.z; g.xw[7] = b.w;
+            const bf16 *ws = (g.ts ? w1 : w0) + 16 * sub;
+            const uint4 c = *reinterpret_cast<const uint4 *>(ws), d = *reinterpret_cast<const uint4 *>(ws + 8);
+            g.ww[0] = c.x; g.ww[1] = c.y; g.ww[2] = c.z; g.ww[3] = c.w;
+            g.ww[4] = d.x; g.ww[5] = d.y; g.ww[6] = d.z; g.ww[7] = d.w;
+        } else {
 #pragma unroll
-    for (int tsel = 0; tsel < NT; ++tsel) {
-        const bf16 *xs = tsel == 0 ? x0 : x1;
-        const bf16 *ws = tsel == 0 ? w0 : w1;
-        bf16 *ys = tsel == 0 ? y0 : y1;
-        uint32_t wwords[8];
-        {
-            const uint4 a = *reinterpret_cast<const uint4 *>(ws + 16 * sub);
-            const uint4 b = *reinterpret_cast<const uint4 *>(ws + 16 * sub + 8);
-            wwords[0] = a.x; wwords[1] = a.y; wwords[2] = a.z; wwords[3] = a.w;
-            wwords[4] = b.x; wwords[5] = b.y; wwords[6] = b.z; wwords[7] = b.w;
+            for (int i = 0; i < 8; ++i) { g.xw[i] = 0u; g.ww[i] = 0u; }
         }
-        const bf16 *xrow = xs + tok * row_stride + 16 * sub;
-        bf16 *yrow = ys + tok * (int64_t)H * 128 + 16 * sub;
-        for (int h0 = 0; h0 < H; h0 += 4) {
-            const int h = h0 + hq;
-            const bool on = h < H;
-            uint32_t xw[8];
-            if (on) {
-                const uint4 a = ldg_stream(xrow + h * 128), b = ldg_stream(xrow + h * 128 + 8);
-                xw[0] = a.x; xw[1] = a.y; xw[2] = a.z; xw[3] = a.w; xw[4] = b.x; xw[5] = b.y; xw[6] = b.z; xw[7] = b.w;
+    };
+    // rbf16(rbf16(x * r) * w), then the rotation; stores y (and the int8 codes of the last tensor for Q8)
+    auto process = [&](const Group &g) {
+        uint64_t V[8], SQ[8];
+#pragma unroll
+        for (int i = 0; i < 8; ++i) {
+            V[i] = x2(bf16_lo(g.xw[i]), bf16_hi(g.xw[i]));
+            SQ[i] = x2_mul(V[i], V[i]);
+        }
+        // (sum of even squares, sum of odd squares): tree over the lane's 8 pairs, then over the 8 lanes
+        float se, so;
+        {
+            float a[16];
+#pragma unroll
+            for (int i = 0; i < 8; ++i) x2_split(SQ[i], a[2 * i], a[2 * i + 1]);
+            // scalar first level (a product is not fed straight into a packed addition)
+            uint64_t t[4];
+#pragma unroll
+            for (int i = 0; i < 4; ++i) t[i] = x2(__fadd_rn(a[4 * i], a[4 * i + 2]), __fadd_rn(a[4 * i + 1], a[4 * i + 3]));
+            const uint64_t u = x2_add(x2_add(t[0], t[1]), x2_add(t[2], t[3]));
+            x2_split(u, se, so);
+#pragma unroll
+            for (int o = 1; o < 8; o <<= 1) {
+                se = __fadd_rn(se, __shfl_xor_sync(0xffffffffu, se, o));
+                so = __fadd_rn(so, __shfl_xor_sync(0xffffffffu, so, o));
+            }
+        }
+        const float r = rsqrt_cr(__fadd_rn(__fmul_rn(__fadd_rn(se, so), inv_d), eps));
+        const uint64_t r2 = x2_splat(r);
+        uint32_t ow[8];
+#pragma unroll
+        for (int i = 0; i < 8; ++i) {
+            float a0, a1;
+            x2_split(x2_mul(V[i], r2), a0, a1);
+            const uint32_t n1 = bf16x2_rn(a0, a1);
+            x2_split(x2_mul(x2(bf16_lo(n1), bf16_hi(n1)), x2(bf16_lo(g.ww[i]), bf16_hi(g.ww[i]))), a0, a1);
+            const uint32_t n2 = bf16x2_rn(a0, a1);
+            if (ROPE) {
+                // (ne*c_e - no*s_e, no*c_o + ne*s_o), the differences and sums rounded separately
+                const float ne = bf16_lo(n2), no = bf16_hi(n2);
+                float pc0, pc1, ps0, ps1;
+                x2_split(x2_mul(x2(ne, no), C[i]), pc0, pc1);
+                x2_split(x2_mul(x2(no, ne), S[i]), ps0, ps1);
+                ow[i] = bf16x2_rn(__fsub_rn(pc0, ps0), __fadd_rn(pc1, ps1));
+            } else {
+                ow[i] = n2;
+            }
+        }
+        bf16 *yrow = (g.ts == 0 ? y0 : y1) + tok * (int64_t)H * 128 + 16 * sub + g.h * 128;
+        if (g.on) {
+            reinterpret_cast<uint4 *>(yrow)[0] = make_uint4(ow[0], ow[1], ow[2], ow[3]);
+            reinterpret_cast<uint4 *>(yrow)[1] = make_uint4(ow[4], ow[5], ow[6], ow[7]);
+        }
+        if (Q8 && g.ts == NT - 1) {
+            float peak = 0.0f;
+#pragma unroll
+            for (int i = 0; i < 8; ++i) peak = fmaxf(peak, fmaxf(fabsf(bf16_lo(ow[i])), fabsf(bf16_hi(ow[i]))));
+#pragma unroll
+            for (int o = 1; o < 8; o <<= 1) peak = fmaxf(peak, __shfl_xor_sync(0xffffffffu, peak, o));
+            const float qsc = i8_scale(peak);
+            uint32_t c[16];
+            if (qsc >= 0x1p-90f) {
+                const uint64_t ns = x2_splat(-qsc), rs = x2_splat(__frcp_rn(qsc));
+#pragma unroll
+                for (int i = 0; i < 8; ++i) x2_codes(x2_quot(x2(bf16_lo(ow[i]), bf16_hi(ow[i])), ns, rs), c[2 * i], c[2 * i + 1]);
             } else {
 #pragma unroll
-                for (int i = 0; i < 8; ++i) xw[i] = 0u;
+                for (int i = 0; i < 8; ++i)
+                    x2_codes(x2(__fdiv_rn(bf16_lo(ow[i]), qsc), __fdiv_rn(bf16_hi(ow[i]), qsc)), c[2 * i], c[2 * i + 1]);
             }
-            uint64_t V[8], SQ[8];
-#pragma unroll
-            for (int i = 0; i < 8; ++i) {
-                V[i] = x2(bf16_lo(xw[i]), bf16_hi(xw[i]));
-                SQ[i] = x2_mul(V[i], V[i]);
-            }
-            // (sum of even squares, sum of odd squares): tree over the lane's 8 pairs, then over the 8 lanes
-            float se, so;
-            {
-                float a[16];
-#pragma unroll
-                for (int i = 0; i < 8; ++i) x2_split(SQ[i], a[2 * i], a[2 * i + 1]);
-                // scalar first level (a product is not fed straight into a packed addition)
-                uint64_t t[4];
-#pragma unroll
-                for (int i = 0; i < 4; ++i) t[i] = x2(__fadd_rn(a[4 * i], a[4 * i + 2]), __fadd_rn(a[4 * i + 1], a[4 * i + 3]));
-                const uint64_t u = x2_add(x2_add(t[0], t[1]), x2_add(t[2], t[3]));
-                x2_split(u, se, so);
-#pragma unroll
-                for (int o = 1; o < 8; o <<= 1) {
-                    se = __fadd_rn(se, __shfl_xor_sync(0xffffffffu, se, o));
-                    so = __fadd_rn(so, __shfl_xor_sync(0xffffffffu, so, o));
-                }
-            }
-            const float r = rsqrt_cr(__fadd_rn(__fmul_rn(__fadd_rn(se, so), inv_d), eps));
-            const uint64_t r2 = x2_splat(r);
-            uint32_t ow[8];
-#pragma unroll
-            for (int i = 0; i < 8; ++i) {
-                // rbf16(rbf16(x * r) * w)
-                float a0, a1;
-                x2_split(x2_mul(V[i], r2), a0, a1);
-                const uint32_t n1 = bf16x2_rn(a0, a1);
-                x2_split(x2_mul(x2(bf16_lo(n1), bf16_hi(n1)), x2(bf16_lo(wwords[i]), bf16_hi(wwords[i]))), a0, a1);
-                const uint32_t n2 = bf16x2_rn(a0, a1);
-                if (ROPE) {
-                    // (ne*c_e - no*s_e, no*c_o + ne*s_o), the differences and sums rounded separately
-                    const float ne = bf16_lo(n2), no = bf16_hi(n2);
-                    float pc0, pc1, ps0, ps1;
-                    x2_split(x2_mul(x2(ne, no), C[i]), pc0, pc1);
-                    x2_split(x2_mul(x2(no, ne), S[i]), ps0, ps1);
-                    ow[i] = bf16x2_rn(__fsub_rn(pc0, ps0), __fadd_rn(pc1, ps1));
-                } else {
-                    ow[i] = n2;
-                }
-            }
-            if (on) {
-                reinterpret_cast<uint4 *>(yrow + h * 128)[0] = make_uint4(ow[0], ow[1], ow[2], ow[3]);
-                reinterpret_cast<uint4 *>(yrow + h * 128)[1] = make_uint4(ow[4], ow[5], ow[6], ow[7]);
-            }
-            if (Q8 && tsel == NT - 1) {
-                float peak = 0.0f;
-#pragma unroll
-                for (int i = 0; i < 8; ++i) peak = fmaxf(peak, fmaxf(fabsf(bf16_lo(ow[i])), fabsf(bf16_hi(ow[i]))));
-#pragma unroll
-                for (int o = 1; o < 8; o <<= 1) peak = fmaxf(peak, __shfl_xor_sync(0xffffffffu, peak, o));
-                const float qsc = i8_scale(peak);
-                uint32_t c[16];
-                if (qsc >= 0x1p-90f) {
-                    const uint64_t ns = x2_splat(-qsc), rs = x2_splat(__frcp_rn(qsc));
-#pragma unroll
-                    for (int i = 0; i < 8; ++i) x2_codes(x2_quot(x2(bf16_lo(ow[i]), bf16_hi(ow[i])), ns, rs), c[2 * i], c[2 * i + 1]);
-                } else {
-#pragma unroll
-                    for (int i = 0; i < 8; ++i)
-                        x2_codes(x2(__fdiv_rn(bf16_lo(ow[i]), qsc), __fdiv_rn(bf16_hi(ow[i]), qsc)), c[2 * i], c[2 * i + 1]);
-                }
-                if (on) {
-                    *reinterpret_cast<uint4 *>(q8 + (tok * H + h) * 128 + 16 * sub) =
-                        make_uint4(pack4_lowbytes(c[0], c[1], c[2], c[3]), pack4_lowbytes(c[4], c[5], c[6], c[7]),
-                                   pack4_lowbytes(c[8], c[9], c[10], c[11]), pack4_lowbytes(c[12], c[13], c[14], c[15]));
-                    if (sub == 0) s8[tok * H + h] = qsc;
-                }
+            if (g.on) {
+                *reinterpret_cast<uint4 *>(q8 + (tok * H + g.h) * 128 + 16 * sub) =
+                    make_uint4(pack4_lowbytes(c[0], c[1], c[2], c[3]), pack4_lowbytes(c[4], c[5], c[6], c[7]),
+                               pack4_lowbytes(c[8], c[9], c[10], c[11]), pack4_lowbytes(c[12], c[13], c[14], c[15]));
+                if (sub == 0) s8[tok * H + g.h] = qsc;
             }
         }
+    };
+    for (int it = 0; it < nit; it += 2) {
+        // the second group of the last step is off when nit is odd (its heads lie past H)
+        Group ga, gb;
+        load_group(it, ga);
+        load_group(it + 1, gb);
+        process(ga);
+        process(gb);
     }
 }
 
