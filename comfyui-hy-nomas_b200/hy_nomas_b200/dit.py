@@ -156,14 +156,16 @@ class CudaOps:
         return F.scaled_dot_product_attention(q.transpose(1, 2), k.transpose(1, 2), v.transpose(1, 2)).transpose(1, 2)
 
 
-def block_forward(cfg, w, x, vec, rope, sp, ops=CudaOps, trace=None):
+def block_forward(cfg, w, x, vec, rope, sp, ops=CudaOps, trace=None, mods=None):
     """One block on this rank's tokens. x bf16 [B, l, D] (l = the rank's tokens), vec bf16 [B, D], rope =
     this rank's rows of the (cos, sin) tables. Returns the block output [B, l, D] bf16. `trace`, when a dict,
-    receives the block's intermediates (for parity tests)."""
+    receives the block's intermediates (for parity tests). `mods`: this block's Modulate(vec) output [B, 6D] when
+    the caller computed it already (`SyntheticDiT` does it for all blocks in one GEMM); else computed here."""
     b, l, d = x.shape
     h, hd = cfg.heads, cfg.head_dim
     act = ops.silu(vec)
-    mods = ops.linear(act, w.mod)
+    if mods is None:
+        mods = ops.linear(act, w.mod)
     shift1, scale1, gate1, shift2, scale2, gate2 = mods.chunk(6, dim=-1)
     qa, sa = ops.adaln_quant(x, shift1, scale1)
     chunks = sp.head_chunks if (sp.world > 1 and h % sp.head_chunks == 0) else 1
@@ -257,6 +259,16 @@ class SyntheticDiT:
         self.ops = ops
         gen = torch.Generator(device=self.device).manual_seed(seed)
         self.blocks = [make_block_weights(cfg, gen, self.device) for _ in range(cfg.blocks)]
+        # Every block's Modulate reads the same vec (model.py:247), so the blocks' [6D, D] modulation weights are
+        # stacked into one [blocks * 6D, D] linear and each block keeps a row view of it: one quantization of
+        # silu(vec) and one GEMM give all blocks' shift/scale/gate per step. Each output column is computed
+        # independently, so every block's values are those of its own linear.
+        self.mod_all = QLinear(torch.cat([bw.mod.q for bw in self.blocks]),
+                               torch.cat([bw.mod.s for bw in self.blocks]),
+                               torch.cat([bw.mod.bias for bw in self.blocks]))
+        n6 = 6 * cfg.hidden
+        for i, bw in enumerate(self.blocks):
+            bw.mod = _rows(self.mod_all, i * n6, (i + 1) * n6)
         cos, sin = rope_freqs(cfg.rope_dims, cfg.theta, *cfg.grid, device=self.device)
         lo, hi = self.sp.shard(cfg.tokens)
         self.rope = (cos[lo:hi].contiguous(), sin[lo:hi].contiguous())
@@ -267,10 +279,17 @@ class SyntheticDiT:
             n = int(os.environ.get("HN_SP_GEMM_SM_RESERVE", str(SP_GEMM_SM_RESERVE)))
             _lib.check(_lib.lib.hn_set_gemm_sm_reserve(n), "hn_set_gemm_sm_reserve")
 
+    def modulations(self, vec):
+        """All blocks' Modulate(vec) in one launch pair (quantize + GEMM): [B, blocks * 6D] bf16."""
+        return self.ops.linear(self.ops.silu(vec), self.mod_all)
+
     def forward(self, x, vec, trace=None):
+        mods = self.modulations(vec)
+        n6 = 6 * self.cfg.hidden
         for i, w in enumerate(self.blocks):
             x = block_forward(self.cfg, w, x, vec, self.rope, self.sp, self.ops,
-                              trace=trace if (trace is not None and i == len(self.blocks) - 1) else None)
+                              trace=trace if (trace is not None and i == len(self.blocks) - 1) else None,
+                              mods=mods[:, i * n6:(i + 1) * n6])
         return x
 
     __call__ = forward

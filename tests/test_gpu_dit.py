@@ -103,6 +103,28 @@ def test_block_end_to_end(block_run):
     assert np.isfinite(out.float().numpy()).all()
 
 
+def test_batched_modulations_bit_exact(hn, cuda):
+    """SyntheticDiT stacks every block's [6D, D] modulation weights and runs one quantize + GEMM per step for all
+    blocks (they share vec, model.py:247): each block's slice equals its own linear bit for bit, and the
+    whole multi-block forward (which uses the batched path) equals the block-by-block chain."""
+    from hy_nomas_b200.dit import DiTConfig, SyntheticDiT, block_forward
+    cfg = DiTConfig(hidden=256, heads=2, mlp_ratio=4, blocks=3, grid=(1, 4, 10))
+    model = SyntheticDiT(cfg, device=cuda, seed=3)
+    g = torch.Generator().manual_seed(4)
+    x = torch.randn(1, cfg.tokens, cfg.hidden, generator=g).to(torch.bfloat16).to(cuda)
+    vec = torch.randn(1, cfg.hidden, generator=g).to(torch.bfloat16).to(cuda)
+    mods = model.modulations(vec)
+    n6 = 6 * cfg.hidden
+    assert mods.shape == (1, cfg.blocks * n6)
+    y = x
+    for i, w in enumerate(model.blocks):
+        own = model.ops.linear(model.ops.silu(vec), w.mod)
+        assert same(mods[:, i * n6:(i + 1) * n6], own)
+        y = block_forward(cfg, w, y, vec, model.rope, model.sp)
+    assert same(model(x, vec), y)
+    torch.cuda.synchronize()
+
+
 def free_port():
     with socket.socket() as s:
         s.bind(("127.0.0.1", 0))
