@@ -285,6 +285,30 @@ __device__ __forceinline__ void promote_row(uint64_t &acc, uint32_t p0, uint32_t
             : "r"(p0), "r"(p1), "l"(s2));
 }
 
+// int8 codes of CPT bf16-valued GELU outputs v(0..CPT-1) of one row's 128-column quantization group, scale sc = RN(peak /
+// 127) (kernels.py:131-135): the quotients v / sc by the exact fma-corrected reciprocal of x2_quot (exact for bf16
+// values |v| <= peak, checked exhaustively over the bf16 domain; IEEE division below 2^-90), rounded half away
+// from zero, 16 codes per 16-byte store.
+template <int CPT, typename V> __device__ __forceinline__ void store_codes(int8_t *qrow, V v, float sc) {
+    const bool fast = sc >= 0x1p-90f;
+    const uint64_t ns = x2_splat(-sc), rs = x2_splat(fast ? __frcp_rn(sc) : 1.0f);
+#pragma unroll
+    for (int j = 0; j < CPT; j += 16) {
+        uint32_t c[16];
+        if (fast) {
+#pragma unroll
+            for (int i = 0; i < 8; ++i) x2_codes(x2_quot(x2(v(j + 2 * i), v(j + 2 * i + 1)), ns, rs), c[2 * i], c[2 * i + 1]);
+        } else {
+#pragma unroll
+            for (int i = 0; i < 8; ++i)
+                x2_codes(x2(__fdiv_rn(v(j + 2 * i), sc), __fdiv_rn(v(j + 2 * i + 1), sc)), c[2 * i], c[2 * i + 1]);
+        }
+        *reinterpret_cast<uint4 *>(qrow + j) =
+            make_uint4(pack4_lowbytes(c[0], c[1], c[2], c[3]), pack4_lowbytes(c[4], c[5], c[6], c[7]),
+                       pack4_lowbytes(c[8], c[9], c[10], c[11]), pack4_lowbytes(c[12], c[13], c[14], c[15]));
+    }
+}
+
 __device__ __forceinline__ float acc_lo(uint64_t a) { F2 v; v.u = a; return v.f[0]; }
 __device__ __forceinline__ float acc_hi(uint64_t a) { F2 v; v.u = a; return v.f[1]; }
 
@@ -709,16 +733,7 @@ __global__ void __launch_bounds__(128 + 128 * NP, 1)
                     const float sc = i8_scale(peak);
                     if (row_ok && full_cols) {
                         int8_t *qrow = static_cast<int8_t *>(p.out) + (int64_t)m * p.ldo + ncol0;
-#pragma unroll
-                        for (int j = 0; j < CPT; j += 16) {
-                            uint4 o;
-                            uint32_t *ow = &o.x;
-#pragma unroll
-                            for (int w = 0; w < 4; ++w)
-                                ow[w] = pack4_i8(code_i8(__fdiv_rn(v[j + 4 * w], sc)), code_i8(__fdiv_rn(v[j + 4 * w + 1], sc)),
-                                                 code_i8(__fdiv_rn(v[j + 4 * w + 2], sc)), code_i8(__fdiv_rn(v[j + 4 * w + 3], sc)));
-                            *reinterpret_cast<uint4 *>(qrow + j) = o;
-                        }
+                        store_codes<CPT>(qrow, [&](int j) { return v[j]; }, sc);
                         if (hf % C::PARTS_PER_GROUP == 0) p.qs[(int64_t)m * p.qs_rs + (int64_t)(ncol0 >> 7) * p.qs_gs] = sc;
                     }
                 } else if (row_ok) {
@@ -805,18 +820,7 @@ __global__ void __launch_bounds__(128 + 128 * NP, 1)
                 if (EPI == 2 && row_ok && full_cols) {
                     const float sc = i8_scale(peak);
                     int8_t *qrow = static_cast<int8_t *>(p.out) + (int64_t)m * p.ldo + ncol0;
-#pragma unroll
-                    for (int j = 0; j < CPT; j += 16) {
-                        uint4 o;
-                        uint32_t *ow = &o.x;
-#pragma unroll
-                        for (int w = 0; w < 4; ++w) {
-                            const uint32_t a = hpk[(j + 4 * w) / 2], b2 = hpk[(j + 4 * w) / 2 + 1];
-                            ow[w] = pack4_i8(code_i8(__fdiv_rn(bf16_lo(a), sc)), code_i8(__fdiv_rn(bf16_hi(a), sc)),
-                                             code_i8(__fdiv_rn(bf16_lo(b2), sc)), code_i8(__fdiv_rn(bf16_hi(b2), sc)));
-                        }
-                        *reinterpret_cast<uint4 *>(qrow + j) = o;
-                    }
+                    store_codes<CPT>(qrow, [&](int j) { return j & 1 ? bf16_hi(hpk[j >> 1]) : bf16_lo(hpk[j >> 1]); }, sc);
                     if (hf % C::PARTS_PER_GROUP == 0) p.qs[(int64_t)m * p.qs_rs + (int64_t)(ncol0 >> 7) * p.qs_gs] = sc;
                 }
             }

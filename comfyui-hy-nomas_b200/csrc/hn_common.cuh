@@ -109,7 +109,7 @@ __device__ __forceinline__ float gelu_tanh(float x) {
     float x3 = __fmul_rn(__fmul_rn(__fmul_rn(0.044715f, x), x), x);
     float inner = __fmul_rn(0.7978845608028654f, __fadd_rn(x, x3));
     float z = __fmul_rn(2.0f, inner);
-    float sig = __fdiv_rn(1.0f, __fadd_rn(1.0f, exp_cw(-z)));
+    float sig = __frcp_rn(__fadd_rn(1.0f, exp_cw(-z)));   // RN(1 / d): the correctly rounded quotient 1 / d
     return __fmul_rn(__fmul_rn(0.5f, x), __fadd_rn(1.0f, __fsub_rn(__fmul_rn(2.0f, sig), 1.0f)));
 }
 
