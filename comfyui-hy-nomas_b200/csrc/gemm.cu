@@ -714,7 +714,7 @@ __global__ void __launch_bounds__(128 + 128 * NP, 1)
                 }
                 if (EPI != 0) {
 #pragma unroll
-                    for (int j = 0; j < CPT; ++j) v[j] = rbf16(gelu_tanh(rbf16(v[j])));
+                    for (int j = 0; j < CPT; j += 2) gelu_bf16_pair(v[j], v[j + 1]);
                 }
                 if (EPI == 2) {
                     // absmax over the 128-column group: this thread's 64 columns + the other half's
@@ -784,7 +784,7 @@ __global__ void __launch_bounds__(128 + 128 * NP, 1)
                     }
                     if (EPI != 0) {
 #pragma unroll
-                        for (int j = 0; j < 32; ++j) v[j] = rbf16(gelu_tanh(rbf16(v[j])));
+                        for (int j = 0; j < 32; j += 2) gelu_bf16_pair(v[j], v[j + 1]);
                     }
                     if (EPI == 2) {
 #pragma unroll

@@ -186,6 +186,15 @@ __device__ __forceinline__ uint32_t pack4_lowbytes(uint32_t a, uint32_t b, uint3
     return __byte_perm(__byte_perm(a, b, 0x0040), __byte_perm(c, d, 0x0040), 0x5410);
 }
 
+// rbf16(gelu_tanh(rbf16(v))) of two finite values (kernels.py:126-127), the bf16 roundings by one cvt.rn.bf16x2 each
+__device__ __forceinline__ void gelu_bf16_pair(float &a, float &b) {
+    uint32_t w = bf16x2_rn(a, b);
+    const float ga = gelu_tanh(bf16_lo(w)), gb = gelu_tanh(bf16_hi(w));
+    w = bf16x2_rn(ga, gb);
+    a = bf16_lo(w);
+    b = bf16_hi(w);
+}
+
 // ---------------------------------------------------------------------------------------------------
 // vector loads: 8 bf16 / fp16 or 4 fp32 elements -> fp32
 

@@ -550,7 +550,9 @@ __global__ void __launch_bounds__(256) k_pixelumm_qk(const bf16 *__restrict__ x,
             sn[8 + 2 * q] = s2.x; sn[9 + 2 * q] = s2.y;
         }
     }
-    for (int h0 = 0; h0 < H; h0 += 4) {
+    // one group of four heads (this lane: head h0 + hq); the loop below runs two groups per step, whose loads,
+    // reductions and rsqrt chains are independent and overlap inside the warp
+    auto process = [&](int h0) {
         const int h = h0 + hq;
         const bool on = h < H;
         const bf16 *xr = x + tok * row_stride + (int64_t)h * 128;
@@ -612,6 +614,10 @@ __global__ void __launch_bounds__(256) k_pixelumm_qk(const bf16 *__restrict__ x,
             *reinterpret_cast<uint32_t *>(yr + pw0) = bf16x2_rn(o[12], o[13]);
             *reinterpret_cast<uint32_t *>(yr + pw1) = bf16x2_rn(o[14], o[15]);
         }
+    };
+    for (int h0 = 0; h0 < H; h0 += 8) {
+        process(h0);
+        process(h0 + 4);   // heads past H are off
     }
 }
 
