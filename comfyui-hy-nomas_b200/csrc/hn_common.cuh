@@ -267,4 +267,12 @@ __device__ __forceinline__ uint64_t globaltimer_ns() {
 
 __host__ __device__ constexpr int64_t cdiv(int64_t a, int64_t b) { return (a + b - 1) / b; }
 
+// a / d for 0 <= a, 0 < d: a shift when d is a power of two, a 32-bit unsigned division when both fit (a few
+// instructions instead of the 64-bit division routine), the 64-bit one otherwise
+__device__ __forceinline__ int64_t div_nonneg(int64_t a, int64_t d) {
+    if ((d & (d - 1)) == 0) return a >> (__ffsll(d) - 1);
+    if (((uint64_t)a | (uint64_t)d) <= 0xFFFFFFFFull) return (int64_t)((uint32_t)a / (uint32_t)d);
+    return a / d;
+}
+
 } // namespace hn

@@ -106,12 +106,12 @@ __global__ void __launch_bounds__(WP * 32, (WP <= 8) ? (MODE == 2 ? 2 : 3) : 1) 
         load_words16(x + row * (int64_t)D + 16 * t, wx);
         if (MODE == 2) load_words16(yres + row * (int64_t)D + 16 * t, wy);
     }
-    int64_t cur_b = -1;
+    int64_t b_end = 0;   // rows [.., b_end) belong to the current batch item (rows only increase)
     Row16 R, SH, G;   // rbf16(1 + scale), shift, gate of the current batch item
     for (; row < rows; row += gridDim.x) {
-        const int64_t b = row / L;
-        if (b != cur_b) {
-            cur_b = b;
+        if (row >= b_end) {
+            const int64_t b = div_nonneg(row, L);
+            b_end = (b + 1) * L;
             uint32_t w[8];
             if (active) load_words16(scale + b * (int64_t)D + 16 * t, w);
             else {
@@ -296,8 +296,8 @@ __global__ void __launch_bounds__(256) k_gated_residual(const bf16 *__restrict__
     const int64_t stride = (int64_t)gridDim.x * blockDim.x;
     for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < nvec; i += stride) {
         const int64_t e = i * 8;
-        const int64_t row = e / D, col = e - row * D;
-        const int64_t b = row / L;
+        const int64_t row = div_nonneg(e, D), col = e - row * D;
+        const int64_t b = div_nonneg(row, L);
         uint4 xv = ldg_stream(x + e), yv = ldg_stream(y + e);
         uint4 gv = *reinterpret_cast<const uint4 *>(gate + b * D + col);
         const uint32_t *xw = &xv.x, *yw = &yv.x, *gw = &gv.x;
@@ -350,7 +350,7 @@ __global__ void __launch_bounds__(256) k_qk_norm_rope(const bf16 *__restrict__ x
     const int sub = lane & 7, hq = lane >> 3;
     const int64_t tok = (int64_t)blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5);
     if (tok >= BL) return;
-    const int64_t l = tok % L;
+    const int64_t l = tok - div_nonneg(tok, L) * L;
     // cos/sin of the lane's 16 positions as (even, odd) pairs
     uint64_t C[8], S[8];
     if (ROPE) {

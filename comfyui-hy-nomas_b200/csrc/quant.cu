@@ -27,7 +27,7 @@ __global__ void __launch_bounds__(256) k_quant_group(const TIn *__restrict__ x, 
         int64_t m = 0, g = 0;
         float v[16];
         if (active) {
-            m = gi / G;
+            m = G == 1 ? gi : div_nonneg(gi, G);
             g = gi - m * G;
             const TIn *p = x + m * ldx + g * 128 + sub * 16;
             Elem<TIn>::load8(p, v);

@@ -163,7 +163,7 @@ def block_forward(cfg, w, x, vec, rope, sp, ops=CudaOps, trace=None, mods=None):
     the caller computed it already (`SyntheticDiT` does it for all blocks in one GEMM); else computed here."""
     b, l, d = x.shape
     h, hd = cfg.heads, cfg.head_dim
-    act = ops.silu(vec)
+    act = ops.silu(vec) if (mods is None or trace is not None) else None
     if mods is None:
         mods = ops.linear(act, w.mod)
     shift1, scale1, gate1, shift2, scale2, gate2 = mods.chunk(6, dim=-1)
