@@ -730,7 +730,7 @@ __global__ void __launch_bounds__(128 + 128 * NP, 1)
                     const int first = hf - hf % C::PARTS_PER_GROUP;
 #pragma unroll
                     for (int o = 0; o < C::PARTS_PER_GROUP; ++o) peak = fmaxf(peak, px_s[(pb * NPART + first + o) * 128 + row]);
-                    const float sc = i8_scale(peak);
+                    const float sc = i8_scale_bf16(peak);   // peak of bf16 GELU outputs
                     if (row_ok && full_cols) {
                         int8_t *qrow = static_cast<int8_t *>(p.out) + (int64_t)m * p.ldo + ncol0;
                         store_codes<CPT>(qrow, [&](int j) { return v[j]; }, sc);
@@ -818,7 +818,7 @@ __global__ void __launch_bounds__(128 + 128 * NP, 1)
                     for (int o = 0; o < C::PARTS_PER_GROUP; ++o) peak = fmaxf(peak, px_s[(pb * NPART + first + o) * 128 + row]);
                 }
                 if (EPI == 2 && row_ok && full_cols) {
-                    const float sc = i8_scale(peak);
+                    const float sc = i8_scale_bf16(peak);   // peak of bf16 GELU outputs
                     int8_t *qrow = static_cast<int8_t *>(p.out) + (int64_t)m * p.ldo + ncol0;
                     store_codes<CPT>(qrow, [&](int j) { return j & 1 ? bf16_hi(hpk[j >> 1]) : bf16_lo(hpk[j >> 1]); }, sc);
                     if (hf % C::PARTS_PER_GROUP == 0) p.qs[(int64_t)m * p.qs_rs + (int64_t)(ncol0 >> 7) * p.qs_gs] = sc;

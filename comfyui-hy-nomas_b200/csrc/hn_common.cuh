@@ -72,6 +72,21 @@ __device__ __forceinline__ float i8_scale(float peak) { return peak > 0.0f ? __f
 // e4m3 scale (kernels.py:39): max(peak, 1e-12) / 448
 __device__ __forceinline__ float e4m3_scale(float peak) { return __fdiv_rn(fmaxf(peak, 1e-12f), 448.0f); }
 
+// RN(p / d) for a scale divisor d (127, 448) and p a bf16 value (or the 1e-12 floor): q0 = RN(p * RN(1/d)), the
+// exact remainder p - q0 * d in one fma, and one more fma corrects q0. tests/division_check.c checks it against
+// the IEEE quotient for every positive finite bf16 p. The same scales as i8_scale / e4m3_scale, for peaks that
+// are absmaxes of bf16 values.
+__device__ __forceinline__ float quot_const(float p, float d, float rd) {
+    const float q0 = __fmul_rn(p, rd);
+    return __fmaf_rn(__fmaf_rn(-q0, d, p), rd, q0);
+}
+__device__ __forceinline__ float i8_scale_bf16(float peak) {
+    return peak > 0.0f ? quot_const(peak, 127.0f, 1.0f / 127.0f) : 1.0f;
+}
+__device__ __forceinline__ float e4m3_scale_bf16(float peak) {
+    return quot_const(fmaxf(peak, 1e-12f), 448.0f, 1.0f / 448.0f);
+}
+
 // 1/sqrt(v) with both steps correctly rounded (the tl.rsqrt of the reference, evaluated as the Triton
 // interpreter evaluates it). The correctly rounded reciprocal RN(1/s) is the correctly rounded quotient 1/s.
 __device__ __forceinline__ float rsqrt_cr(float v) { return __frcp_rn(__fsqrt_rn(v)); }

@@ -211,7 +211,7 @@ __global__ void __launch_bounds__(WP * 32, (WP <= 8) ? (MODE == 2 ? 2 : 3) : 1) 
             peak = fmaxf(peak, fmaxf(fmaxf(fabsf(a0), fabsf(a1)), fmaxf(fabsf(b0), fabsf(b1))));
         }
         peak = warp_max_xor(peak, 8);
-        const float qsc = i8_scale(peak);
+        const float qsc = i8_scale_bf16(peak);   // peak of bf16 values
         uint32_t cP[4][2], cQ[4][2];
         if (qsc >= 0x1p-90f) {
             const uint64_t ns = x2_splat(-qsc), rs = x2_splat(__frcp_rn(qsc));
@@ -450,7 +450,7 @@ __global__ void __launch_bounds__(256) k_qk_norm_rope(const bf16 *__restrict__ x
             for (int i = 0; i < 8; ++i) peak = fmaxf(peak, fmaxf(fabsf(bf16_lo(ow[i])), fabsf(bf16_hi(ow[i]))));
 #pragma unroll
             for (int o = 1; o < 8; o <<= 1) peak = fmaxf(peak, __shfl_xor_sync(0xffffffffu, peak, o));
-            const float qsc = i8_scale(peak);
+            const float qsc = i8_scale_bf16(peak);   // peak of bf16 values
             uint32_t c[16];
             if (qsc >= 0x1p-90f) {
                 const uint64_t ns = x2_splat(-qsc), rs = x2_splat(__frcp_rn(qsc));

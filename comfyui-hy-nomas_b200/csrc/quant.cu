@@ -12,6 +12,14 @@
 
 namespace hn {
 
+// the quantization scale of a group with absmax `peak`: for bf16 input the peak is a bf16 value and the scale
+// comes from the fma-corrected quotient (identical to the IEEE division on that domain), else IEEE division
+template <typename TIn, int KIND> __device__ __forceinline__ float group_scale(float peak) {
+    constexpr bool BF16_IN = sizeof(TIn) == 2 && !std::is_same<TIn, __half>::value;
+    if (BF16_IN) return KIND == 0 ? i8_scale_bf16(peak) : e4m3_scale_bf16(peak);
+    return KIND == 0 ? i8_scale(peak) : e4m3_scale(peak);
+}
+
 // RNE (int8 only): codes rounded half to even instead of half away from zero.
 template <typename TIn, int KIND, bool RNE>
 __global__ void __launch_bounds__(256) k_quant_group(const TIn *__restrict__ x, int64_t ldx, int64_t M, int64_t G,
@@ -43,7 +51,7 @@ __global__ void __launch_bounds__(256) k_quant_group(const TIn *__restrict__ x, 
         float sc;
         uint4 out;
         constexpr bool BF16_IN = sizeof(TIn) == 2 && !std::is_same<TIn, __half>::value;
-        const float sc_try = KIND == 0 ? i8_scale(peak) : e4m3_scale(peak);
+        const float sc_try = group_scale<TIn, KIND>(peak);
         if (BF16_IN && sc_try >= 0x1p-90f) {
             // bf16 input: the exact fma-corrected quotient (x2_quot), checked exhaustively over bf16 inputs
             sc = sc_try;
@@ -191,7 +199,7 @@ __global__ void __launch_bounds__(256) k_quant_row(const TIn *__restrict__ x, in
 #pragma unroll
             for (int j = 0; j < 8; ++j) gp = fmaxf(gp, fabsf(v[i][j]));
             gp = warp_max_xor(gp, 16);
-            const float sc = KIND == 0 ? i8_scale(gp) : e4m3_scale(gp);
+            const float sc = group_scale<TIn, KIND>(gp);
             const bool fast = BF16_IN && sc >= 0x1p-90f;
             const uint64_t ns = x2_splat(-sc), rs = x2_splat(__frcp_rn(sc));
             if (c < nch) {
@@ -227,7 +235,7 @@ __global__ void __launch_bounds__(256) k_quant_row(const TIn *__restrict__ x, in
     peak = 0.0f;
 #pragma unroll
     for (int w = 0; w < 8; ++w) peak = fmaxf(peak, red[w]);
-    const float sc = KIND == 0 ? i8_scale(peak) : e4m3_scale(peak);
+    const float sc = group_scale<TIn, KIND>(peak);
     constexpr bool BF16_IN = sizeof(TIn) == 2 && !std::is_same<TIn, __half>::value;
     const bool fast = BF16_IN && sc >= 0x1p-90f;
     const uint64_t ns = x2_splat(-sc), rs = x2_splat(__frcp_rn(sc));

@@ -5,7 +5,10 @@
  *     s >= 2^-90:  q0 = RN(v * r), r = RN(1 / s);  q = fma(fma(-q0, s, v), r, q0)
  *     otherwise:   q = RN(v / s)
  * This program counts the (p, v) pairs whose int8 code (round half away from zero) or e4m3 byte (nearest even,
- * saturating; zero takes v's sign) differs from the one of the IEEE quotient. Exit status 0 iff none do. */
+ * saturating; zero takes v's sign) differs from the one of the IEEE quotient. It also checks the scales themselves
+ * as the kernels form them for bf16 peaks (hn_common.cuh: quot_const): for every positive finite bf16 p,
+ *     RN(p / d) == fma(fma(-q0, d, p), RN(1 / d), q0),  q0 = RN(p * RN(1 / d)),  d = 127 and (p floored at 1e-12) 448.
+ * Exit status 0 iff nothing differs. */
 #include <math.h>
 #include <stdint.h>
 #include <stdio.h>
@@ -24,7 +27,19 @@ static float fast_quotient(float v, float s, float r) {
     return fmaf(fmaf(-q0, s, v), r, q0);
 }
 
+static float quot_const(float p, float d) {
+    const float rd = 1.0f / d, q0 = p * rd;
+    return fmaf(fmaf(-q0, d, p), rd, q0);
+}
+
 int main(void) {
+    long long bad_scale = 0;
+    for (uint32_t pb = 1; pb < 0x7F80; ++pb) {
+        const float p = from_bits(pb << 16), pe = fmaxf(p, 1e-12f);
+        bad_scale += quot_const(p, 127.0f) != p / 127.0f;
+        bad_scale += quot_const(pe, 448.0f) != pe / 448.0f;
+    }
+    printf("scale mismatches %lld\n", bad_scale);
     long long bad_i8 = 0, bad_e4m3 = 0, pairs = 0;
 #pragma omp parallel for schedule(dynamic, 64) reduction(+ : bad_i8, bad_e4m3, pairs)
     for (uint32_t pb = 1; pb < 0x7F80; ++pb) {
@@ -43,5 +58,5 @@ int main(void) {
         }
     }
     printf("pairs %lld: int8 code mismatches %lld, e4m3 byte mismatches %lld\n", pairs, bad_i8, bad_e4m3);
-    return (bad_i8 || bad_e4m3) ? 1 : 0;
+    return (bad_i8 || bad_e4m3 || bad_scale) ? 1 : 0;
 }

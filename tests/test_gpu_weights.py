@@ -87,3 +87,28 @@ def test_loaded_block_equals_row_major_scales(hn, cuda, loaded):
     b = block_forward(cfg, bw_rm, x, vec, rope, SequenceParallel())
     assert torch.equal(a.view(torch.int16), b.view(torch.int16))
     assert torch.isfinite(a.float()).all()
+
+
+def test_fp8_decoder_linear_from_file(hn, oracle, cuda, tmp_path):
+    """An FP8 decoder linear (pixelumm.py:126-145) written as `fp8_weight` / `fp8_scale`, read back and run by
+    `ops.fp8_block_linear`: the same output as the in-memory tensors bit for bit, and the oracle's block-scaled
+    GEMM on the same 1x128 e4m3 activations within the stated FP8 tolerance (rel-L2 <= 1e-2)."""
+    from hy_nomas_b200 import weights as W
+    from hn_testutil import rel_l2
+    gen = torch.Generator().manual_seed(14)
+    w = torch.randn(384, 512, generator=gen) * 0.02
+    q, s = hn.ops.quantize_fp8_block(w.to(cuda))
+    bias = (torch.randn(384, generator=gen) * 0.02).to(torch.bfloat16)
+    path = str(tmp_path / "decoder_fp8.safetensors")
+    W.write_safetensors(path, {"layers.0.mlp.up_proj.fp8_weight": q, "layers.0.mlp.up_proj.fp8_scale": s,
+                               "layers.0.mlp.up_proj.bias": bias})
+    sd, _ = W.read_safetensors(path)
+    lin = W.fp8_linear(sd, "layers.0.mlp.up_proj.", device=cuda)
+    x = torch.randn(200, 512, generator=gen).to(torch.bfloat16).to(cuda)
+    y = hn.ops.fp8_block_linear(x, lin.q, lin.s, lin.bias)
+    y_mem = hn.ops.fp8_block_linear(x, q, s, bias.to(cuda))
+    assert torch.equal(y.view(torch.int16), y_mem.view(torch.int16))
+    qa, sa = oracle.quantize_activations(x.float().cpu().numpy(), kind="fp8")
+    ref = oracle.block_gemm(qa, sa, q.cpu().view(torch.uint8).numpy(), s.cpu().numpy(), bias.float().numpy(),
+                            kind="fp8", sa_mode="group", sw_mode="block")
+    assert rel_l2(y.float().cpu().numpy(), oracle.round_bf16(ref)) < 1e-2

@@ -1,6 +1,7 @@
 """The quantizers' fast division (hn_common.cuh: x2_quot) gives the same int8 codes and e4m3 bytes as the IEEE
 quotient over the whole bf16 input domain: tests/division_check.c enumerates every bf16 absmax and every bf16
-value within it (1.07e9 pairs, both signs) and compares. CPU only; about 20 s on 8 threads."""
+value within it (1.07e9 pairs, both signs) and compares; it also checks the scales absmax/127 and absmax/448 that
+the kernels form by the same fma-corrected quotient (quot_const) for every bf16 absmax. CPU only; about 20 s on 8 threads."""
 import os
 import subprocess
 
@@ -18,3 +19,4 @@ def test_fast_division_exhaustive(tmp_path):
     r = subprocess.run([exe], capture_output=True, text=True, timeout=900)
     assert r.returncode == 0, r.stdout + r.stderr
     assert "int8 code mismatches 0, e4m3 byte mismatches 0" in r.stdout
+    assert "scale mismatches 0" in r.stdout
