@@ -720,7 +720,7 @@ __global__ void __launch_bounds__(128 + 128 * NP, 1)
                     // absmax over the 128-column group: this thread's 64 columns + the other half's
                     float peak = 0.0f;
 #pragma unroll
-                    for (int j = 0; j < CPT; ++j) peak = fmaxf(peak, fabsf(v[j]));
+                    for (int j = 0; j < CPT; j += 2) peak = absmax3(peak, v[j], v[j + 1]);
                     const int pb = it & 1;
                     px_s[(pb * NPART + hf) * 128 + row] = peak;
                     __syncwarp();
@@ -789,7 +789,7 @@ __global__ void __launch_bounds__(128 + 128 * NP, 1)
                     if (EPI == 2) {
 #pragma unroll
                         for (int j = 0; j < 32; j += 2) {
-                            peak = fmaxf(peak, fmaxf(fabsf(v[j]), fabsf(v[j + 1])));
+                            peak = absmax3(peak, v[j], v[j + 1]);
                             hpk[c * 16 + j / 2] = pack_bf16_exact(v[j], v[j + 1]);
                         }
                     } else if (row_ok) {

@@ -246,6 +246,14 @@ __device__ __forceinline__ uint4 ldg_stream(const void *p) {
     return r;
 }
 
+// max(m, |a|, |b|) in one three-input max (PTX max.abs.f32 with three operands, sm_100); m >= 0. As fmaxf, a NaN
+// input is ignored.
+__device__ __forceinline__ float absmax3(float m, float a, float b) {
+    float r;
+    asm("max.abs.f32 %0, %1, %2, %3;" : "=f"(r) : "f"(m), "f"(a), "f"(b));
+    return r;
+}
+
 // ---------------------------------------------------------------------------------------------------
 // warp reductions
 

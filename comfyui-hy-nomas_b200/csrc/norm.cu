@@ -208,7 +208,7 @@ __global__ void __launch_bounds__(WP * 32, (WP <= 8) ? (MODE == 2 ? 2 : 3) : 1) 
             float a0, a1, b0, b1;
             x2_split(Z.P[k], a0, a1);
             x2_split(Z.Q[k], b0, b1);
-            peak = fmaxf(peak, fmaxf(fmaxf(fabsf(a0), fabsf(a1)), fmaxf(fabsf(b0), fabsf(b1))));
+            peak = absmax3(absmax3(peak, a0, a1), b0, b1);
         }
         peak = warp_max_xor(peak, 8);
         const float qsc = i8_scale_bf16(peak);   // peak of bf16 values
@@ -447,7 +447,7 @@ __global__ void __launch_bounds__(256) k_qk_norm_rope(const bf16 *__restrict__ x
         if (Q8 && g.ts == NT - 1) {
             float peak = 0.0f;
 #pragma unroll
-            for (int i = 0; i < 8; ++i) peak = fmaxf(peak, fmaxf(fabsf(bf16_lo(ow[i])), fabsf(bf16_hi(ow[i]))));
+            for (int i = 0; i < 8; ++i) peak = absmax3(peak, bf16_lo(ow[i]), bf16_hi(ow[i]));
 #pragma unroll
             for (int o = 1; o < 8; o <<= 1) peak = fmaxf(peak, __shfl_xor_sync(0xffffffffu, peak, o));
             const float qsc = i8_scale_bf16(peak);   // peak of bf16 values

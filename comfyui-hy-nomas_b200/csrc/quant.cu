@@ -46,7 +46,7 @@ __global__ void __launch_bounds__(256) k_quant_group(const TIn *__restrict__ x, 
         }
         float peak = 0.0f;
 #pragma unroll
-        for (int i = 0; i < 16; ++i) peak = fmaxf(peak, fabsf(v[i]));
+        for (int i = 0; i < 16; i += 2) peak = absmax3(peak, v[i], v[i + 1]);
         peak = warp_max_xor(peak, 8);
         float sc;
         uint4 out;
@@ -197,7 +197,7 @@ __global__ void __launch_bounds__(256) k_quant_row(const TIn *__restrict__ x, in
             const int64_t c = threadIdx.x + (int64_t)i * 256;
             float gp = 0.0f;
 #pragma unroll
-            for (int j = 0; j < 8; ++j) gp = fmaxf(gp, fabsf(v[i][j]));
+            for (int j = 0; j < 8; j += 2) gp = absmax3(gp, v[i][j], v[i][j + 1]);
             gp = warp_max_xor(gp, 16);
             const float sc = group_scale<TIn, KIND>(gp);
             const bool fast = BF16_IN && sc >= 0x1p-90f;
@@ -219,14 +219,14 @@ __global__ void __launch_bounds__(256) k_quant_row(const TIn *__restrict__ x, in
                 for (int j = 0; j < 8; ++j) v[i][j] = 0.0f;
             }
 #pragma unroll
-            for (int j = 0; j < 8; ++j) peak = fmaxf(peak, fabsf(v[i][j]));
+            for (int j = 0; j < 8; j += 2) peak = absmax3(peak, v[i][j], v[i][j + 1]);
         }
     } else {
         for (int64_t c = threadIdx.x; c < nch; c += 256) {
             float w[8];
             Elem<TIn>::load8(row + 8 * c, w);
 #pragma unroll
-            for (int j = 0; j < 8; ++j) peak = fmaxf(peak, fabsf(w[j]));
+            for (int j = 0; j < 8; j += 2) peak = absmax3(peak, w[j], w[j + 1]);
         }
     }
     peak = warp_max_xor(peak, 32);
@@ -347,7 +347,7 @@ __global__ void __launch_bounds__(256) k_quant_fp8_block(const TIn *__restrict__
             v[r][0] = bf16_lo(u.x); v[r][1] = bf16_hi(u.x); v[r][2] = bf16_lo(u.y); v[r][3] = bf16_hi(u.y);
         }
 #pragma unroll
-        for (int j = 0; j < 4; ++j) peak = fmaxf(peak, fabsf(v[r][j]));
+        for (int j = 0; j < 4; j += 2) peak = absmax3(peak, v[r][j], v[r][j + 1]);
     }
     peak = warp_max_xor(peak, 32);
     if (lane == 0) red[warp] = peak;
