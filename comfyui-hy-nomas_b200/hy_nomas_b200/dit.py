@@ -156,24 +156,28 @@ class CudaOps:
         return F.scaled_dot_product_attention(q.transpose(1, 2), k.transpose(1, 2), v.transpose(1, 2)).transpose(1, 2)
 
 
-def block_forward(cfg, w, x, vec, rope, sp, ops=CudaOps, trace=None, mods=None):
+def block_forward(cfg, w, x, vec, rope, sp, ops=CudaOps, trace=None, mods=None, x_q=None, next_mods=None):
     """One block on this rank's tokens. x bf16 [B, l, D] (l = the rank's tokens), vec bf16 [B, D], rope =
     this rank's rows of the (cos, sin) tables. Returns the block output [B, l, D] bf16. `trace`, when a dict,
     receives the block's intermediates (for parity tests). `mods`: this block's Modulate(vec) output [B, 6D] when
-    the caller computed it already (`SyntheticDiT` does it for all blocks in one GEMM); else computed here."""
+    the caller computed it already (`SyntheticDiT` does it for all blocks in one GEMM); else computed here.
+
+    Chaining blocks: `next_mods` (the next block's modulations) fuses this block's final gated residual with the
+    next block's LN + modulate + int8 quantization (one pass, bit-identical to the two kernels) and makes the
+    return value (out, (qa, sa)); the next block takes that pair as `x_q` instead of quantizing `out` again."""
     b, l, d = x.shape
     h, hd = cfg.heads, cfg.head_dim
     act = ops.silu(vec) if (mods is None or trace is not None) else None
     if mods is None:
         mods = ops.linear(act, w.mod)
     shift1, scale1, gate1, shift2, scale2, gate2 = mods.chunk(6, dim=-1)
-    qa, sa = ops.adaln_quant(x, shift1, scale1)
+    qa, sa = x_q if x_q is not None else ops.adaln_quant(x, shift1, scale1)
     chunks = sp.head_chunks if (sp.world > 1 and h % sp.head_chunks == 0) else 1
     if chunks > 1:
         attn, k_full, v_full, qk, q_out = _attention_chunked(cfg, w, qa, sa, rope, sp, ops, b, l, chunks,
                                                              keep_kv=trace is not None)
         return _post(cfg, w, x, attn, qa, sa, qk, q_out, k_full, v_full, act, mods, gate1, shift2, scale2, gate2,
-                     ops, trace)
+                     ops, trace, next_mods)
     k_full, v_full, k_mine, v_mine = sp.kv_buffers(b, l, h, hd, x.dtype, x.device)
     # v first, so its all-gather runs under the q|k GEMM; k is normalized before q, so its gather runs under
     # q's normalization (with one rank the gathers are no-ops and the order changes nothing)
@@ -193,7 +197,7 @@ def block_forward(cfg, w, x, vec, rope, sp, ops=CudaOps, trace=None, mods=None):
     sp.wait(gather_k, gather_v)
     attn = ops.attention(q_out, k_full, v_full).reshape(b * l, d)
     return _post(cfg, w, x, attn, qa, sa, qk, q_out, k_full, v_full, act, mods, gate1, shift2, scale2, gate2, ops,
-                 trace)
+                 trace, next_mods)
 
 
 def _rows(w, lo, hi):
@@ -232,18 +236,26 @@ def _attention_chunked(cfg, w, qa, sa, rope, sp, ops, b, l, chunks, keep_kv=Fals
     return attn.view(b * l, d), k_full, v_full, qk, q_out
 
 
-def _post(cfg, w, x, attn, qa, sa, qk, q_out, k_full, v_full, act, mods, gate1, shift2, scale2, gate2, ops, trace):
-    """The block after attention: projection, gated residual + LN + quant, MLP, gated residual."""
+def _post(cfg, w, x, attn, qa, sa, qk, q_out, k_full, v_full, act, mods, gate1, shift2, scale2, gate2, ops, trace,
+          next_mods=None):
+    """The block after attention: projection, gated residual + LN + quant, MLP, gated residual (fused with the
+    next block's LN + quant when `next_mods` is given: returns (out, (qa, sa)) then)."""
     b, l, d = x.shape
     proj = ops.linear(attn, w.proj).view(b, l, d)
     x1, qa2, sa2 = ops.gated_residual_adaln_quant(x, proj, gate1, shift2, scale2)
     qh, sh = ops.gemm(qa2, sa2, w.fc1, epilogue="gelu_quant")
     y = ops.gemm(qh, sh, w.fc2).view(b, l, d)
-    out = ops.gated_residual(x1, y, gate2)
+    nxt = None
+    if next_mods is None:
+        out = ops.gated_residual(x1, y, gate2)
+    else:
+        nshift1, nscale1 = next_mods.chunk(6, dim=-1)[:2]
+        out, nqa, nsa = ops.gated_residual_adaln_quant(x1, y, gate2, nshift1, nscale1)
+        nxt = (nqa, nsa)
     if trace is not None:
         trace.update(act=act, mods=mods, qa=qa, sa=sa, qk=qk, q=q_out, k_full=k_full.clone(), v_full=v_full.clone(),
                      attn=attn, proj=proj, x1=x1, qa2=qa2, sa2=sa2, qh=qh, sh=sh, y=y, out=out)
-    return out
+    return out if nxt is None else (out, nxt)
 
 
 class SyntheticDiT:
@@ -286,10 +298,16 @@ class SyntheticDiT:
     def forward(self, x, vec, trace=None):
         mods = self.modulations(vec)
         n6 = 6 * self.cfg.hidden
+        nb = len(self.blocks)
+        x_q = None
         for i, w in enumerate(self.blocks):
-            x = block_forward(self.cfg, w, x, vec, self.rope, self.sp, self.ops,
-                              trace=trace if (trace is not None and i == len(self.blocks) - 1) else None,
-                              mods=mods[:, i * n6:(i + 1) * n6])
+            # every block but the last ends with its residual fused into the next block's LN + quantization
+            last = i == nb - 1
+            r = block_forward(self.cfg, w, x, vec, self.rope, self.sp, self.ops,
+                              trace=trace if (trace is not None and last) else None,
+                              mods=mods[:, i * n6:(i + 1) * n6], x_q=x_q,
+                              next_mods=None if last else mods[:, (i + 1) * n6:(i + 2) * n6])
+            x, x_q = (r, None) if last else r
         return x
 
     __call__ = forward
