@@ -201,11 +201,65 @@ __device__ __forceinline__ uint32_t pack4_lowbytes(uint32_t a, uint32_t b, uint3
     return __byte_perm(__byte_perm(a, b, 0x0040), __byte_perm(c, d, 0x0040), 0x5410);
 }
 
-// rbf16(gelu_tanh(rbf16(v))) of two finite values (kernels.py:126-127), the bf16 roundings by one cvt.rn.bf16x2 each
+// 2^k for an integer k in [-126, 127], as a float
+__device__ __forceinline__ float pow2i(int k) { return __uint_as_float((uint32_t)(k + 127) << 23); }
+
+// exp_cw of a pair, the same operations lane by lane: the products and fused multiply-adds on f32x2 pairs, the
+// per-lane steps (rint, the exponent split, the range cases) scalar
+__device__ __forceinline__ uint64_t exp_cw_x2(uint64_t v) {
+    const float log2e = 0x1.715476p+0f, ln2_hi = 0x1.62e4p-1f, ln2_lo = 0x1.7f7d1cp-20f;
+    float v0, v1, t0, t1;
+    x2_split(v, v0, v1);
+    x2_split(x2_mul(v, x2_splat(log2e)), t0, t1);
+    const float k0f = rintf(t0), k1f = rintf(t1);
+    const uint64_t nk = x2(-k0f, -k1f);
+    uint64_t r = x2_fma(nk, x2_splat(ln2_hi), v);
+    r = x2_fma(nk, x2_splat(ln2_lo), r);
+    uint64_t p = x2_splat(0x1.a01a02p-13f);
+    p = x2_fma(p, r, x2_splat(0x1.6c16c2p-10f));
+    p = x2_fma(p, r, x2_splat(0x1.111112p-7f));
+    p = x2_fma(p, r, x2_splat(0x1.555556p-5f));
+    p = x2_fma(p, r, x2_splat(0x1.555556p-3f));
+    p = x2_fma(p, r, x2_splat(0.5f));
+    p = x2_fma(p, r, x2_splat(1.0f));
+    p = x2_fma(p, r, x2_splat(1.0f));
+    const int k0 = (int)k0f, k1 = (int)k1f;
+    const int h0 = k0 / 2, h1 = k1 / 2;
+    p = x2_mul(p, x2(pow2i(h0), pow2i(h1)));
+    p = x2_mul(p, x2(pow2i(k0 - h0), pow2i(k1 - h1)));
+    float e0, e1;
+    x2_split(p, e0, e1);
+    // the range cases of exp_cw, lane by lane (the pair was computed regardless; its value is not used there)
+    if (v0 != v0) e0 = v0;
+    else if (v0 > 88.7228394f) e0 = __int_as_float(0x7F800000);
+    else if (v0 < -103.972084f) e0 = 0.0f;
+    if (v1 != v1) e1 = v1;
+    else if (v1 > 88.7228394f) e1 = __int_as_float(0x7F800000);
+    else if (v1 < -103.972084f) e1 = 0.0f;
+    return x2(e0, e1);
+}
+
+// rbf16(gelu_tanh(rbf16(v))) of two finite values (kernels.py:126-127): gelu_tanh's operations on an f32x2
+// pair - products on packed multiplies, every addition or subtraction whose operand is a product scalar (a
+// packed product is never fed to a packed addition) - and the bf16 roundings by one cvt.rn.bf16x2 each
 __device__ __forceinline__ void gelu_bf16_pair(float &a, float &b) {
     uint32_t w = bf16x2_rn(a, b);
-    const float ga = gelu_tanh(bf16_lo(w)), gb = gelu_tanh(bf16_hi(w));
-    w = bf16x2_rn(ga, gb);
+    const uint64_t x = x2(bf16_lo(w), bf16_hi(w));
+    const uint64_t x3 = x2_mul(x2_mul(x2_mul(x2_splat(0.044715f), x), x), x);
+    float x0, x1, c0, c1;
+    x2_split(x, x0, x1);
+    x2_split(x3, c0, c1);
+    const uint64_t inner = x2_mul(x2_splat(0.7978845608028654f), x2(__fadd_rn(x0, c0), __fadd_rn(x1, c1)));
+    // exp(-z), z = 2 * inner: the product by -2 is exact and equals -RN(2 * inner)
+    float e0, e1;
+    x2_split(exp_cw_x2(x2_mul(x2_splat(-2.0f), inner)), e0, e1);
+    const uint64_t sig2 = x2_mul(x2_splat(2.0f), x2(__frcp_rn(__fadd_rn(1.0f, e0)), __frcp_rn(__fadd_rn(1.0f, e1))));
+    float s0, s1;
+    x2_split(sig2, s0, s1);
+    const uint64_t t = x2(__fadd_rn(1.0f, __fsub_rn(s0, 1.0f)), __fadd_rn(1.0f, __fsub_rn(s1, 1.0f)));
+    float g0, g1;
+    x2_split(x2_mul(x2_mul(x2_splat(0.5f), x), t), g0, g1);
+    w = bf16x2_rn(g0, g1);
     a = bf16_lo(w);
     b = bf16_hi(w);
 }
