@@ -3,16 +3,16 @@
     python bench.py [--gpus N] [--steps K] [--warmup W] [--workload dit|gemm|fp8|elementwise] [--impl ours|reference]
 
 Workloads (synthetic, seeded; the reference publishes no dataset for this path):
-  dit          (default) BASELINE config 5: one denoise step of a 40-block Hy-Nomas-style DiT (hidden 4096,
+  dit          (default) benchmark config 5: one denoise step of a 40-block Hy-Nomas-style DiT (hidden 4096,
                32 x 128 heads, MLP 16384, adaLN modulation, W8A8 int8 linears with per-channel weight scales),
                L = 20240 tokens, batch 1, sequence-parallel over the ranks (per-block K/V all-gather over
                NCCL). metric: tokens/s of the whole job (strong scaling); roofline: the W8A8 GEMM kernel
                inside the step.
-  gemm         BASELINE config 1: W8A8 int8 linear 4096 x 4096 x 4096 (quantize + GEMM), per-128-group
+  gemm         benchmark config 1: W8A8 int8 linear 4096 x 4096 x 4096 (quantize + GEMM), per-128-group
                activation scales and per-channel weight scales; every rank runs its own copy (replicas).
-  fp8          BASELINE config 2: FP8 e4m3 block-scaled linear, MLP-up 16384 x 4096 at M = 20240 (quantize +
+  fp8          benchmark config 2: FP8 e4m3 block-scaled linear, MLP-up 16384 x 4096 at M = 20240 (quantize +
                GEMM); the config's 12-shape sweep is reported per kernel in `config`.
-  elementwise  BASELINE config 3: the fused elementwise chain at M = 20240, D = 4096 (LN + modulate + int8
+  elementwise  benchmark config 3: the fused elementwise chain at M = 20240, D = 4096 (LN + modulate + int8
                quantize; QK-RMSNorm + 3-D RoPE of q and k; gated residual; residual + LN + quantize).
 
 Timing: W warm-up steps, then exactly K steps between a barrier + cuda.synchronize on both sides, CUDA
@@ -226,7 +226,7 @@ def launch_count(fn):
 
 
 def make_int8_weight(n, k, gen, device, per_channel=True):
-    """Random int8 codes uniform in [-127, 127] and per-output-channel scales U[1e-3, 5e-3] (BASELINE config
+    """Random int8 codes uniform in [-127, 127] and per-output-channel scales U[1e-3, 5e-3] (benchmark config
     1), broadcast to the reference's [N, K/128] layout when per_channel is False."""
     q = torch.randint(-127, 128, (n, k), generator=gen, dtype=torch.int8)
     s = torch.rand(n, generator=gen) * 4e-3 + 1e-3
@@ -236,7 +236,7 @@ def make_int8_weight(n, k, gen, device, per_channel=True):
 
 
 def outlier_activations(m, k, gen):
-    """x ~ N(0, 1) with 1% of the channels scaled x20."""
+    """x ~ N(0, 1) with 1% of the channels scaled x20 (benchmark config 1)."""
     x = torch.randn(m, k, generator=gen)
     x[:, torch.randperm(k, generator=gen)[: max(1, k // 100)]] *= 20.0
     return x.bfloat16()

@@ -52,8 +52,8 @@ __device__ __forceinline__ int code_i8(float y) {
     r = fminf(fmaxf(r, -127.0f), 127.0f);
     return (int)r;
 }
-// round half to even (cvt.rni), clamp +-127: the per-token int8 codes of BASELINE config 1 ("round-half-even"),
-// an option beside the reference's half-away rounding
+// round half to even (cvt.rni), clamp +-127: torch.round's convention for per-token int8 codes, an option beside
+// the reference's half-away rounding
 __device__ __forceinline__ int code_i8_rne(float y) {
     const int r = __float2int_rn(y);
     return r > 127 ? 127 : (r < -127 ? -127 : r);

@@ -28,7 +28,7 @@ def _aligned(t):
 def quantize_activations(x, kind="int8", per_token=False, round_half_even=False):
     """x [M, K] (K % 128 == 0) -> codes [M, K] and fp32 scales [M, K / 128] (hy_nomas/kernels.py:45-54).
     `per_token=True`: one scale per row, scales [M, 1]. `round_half_even=True` (int8): codes rounded half to
-    even instead of the reference's half away from zero - BASELINE config 1's per-token wording."""
+    even instead of the reference's half away from zero (torch.round's convention)."""
     _lib.require_cuda(x)
     m, k = x.shape
     if x.dtype not in (torch.bfloat16, torch.float16, torch.float32):

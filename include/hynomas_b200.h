@@ -106,10 +106,10 @@ int hn_selftest_wait_timeout(uint32_t timeout_us, void *stream);
  * int8: s = peak > 0 ? peak/127 : 1, q = round-half-away(x/s) clamped to +-127.
  * e4m3: s = max(peak, 1e-12)/448, q = e4m3(x/s) round-to-nearest-even, saturating.
  * `flags` (0 = the reference's quantizer):
- *   HN_QUANT_PER_ROW: one group spanning all K (per-token scale s[m * s_rs]) - the per-token quantization
- *     that BASELINE config 1 names; no counterpart in the reference.
+ *   HN_QUANT_PER_ROW: one group spanning all K (per-token scale s[m * s_rs]) - per-token dynamic activation
+ *     quantization, the usual W8A8 convention; no counterpart in the reference.
  *   HN_QUANT_ROUND_HALF_EVEN (int8 only): codes rounded half to even instead of half away from zero
- *     (config 1's wording); no counterpart in the reference.
+ *     (torch.round's convention); no counterpart in the reference.
  */
 #define HN_QUANT_PER_ROW 1
 #define HN_QUANT_ROUND_HALF_EVEN 2

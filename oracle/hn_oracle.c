@@ -46,8 +46,8 @@ static inline int8_t code_i8(float y) {
     return (int8_t)(int)r;
 }
 
-/* round half to even, clamp to +-127: the per-token codes of BASELINE config 1 ("round-half-even"), offered
- * beside the reference's rounding; nearbyintf rounds to nearest even in the default rounding mode */
+/* round half to even, clamp to +-127: torch.round's convention for per-token codes, offered beside the
+ * reference's rounding; nearbyintf rounds to nearest even in the default rounding mode */
 static inline int8_t code_i8_rne(float y) {
     float r = nearbyintf(y);
     if (r < -127.0f) r = -127.0f;

@@ -143,8 +143,8 @@ def gelu_tanh(x):
 
 def quantize_activations(x, kind="int8", per_row=False, round_half_even=False):
     """hy_nomas/kernels.py:45-54. x float32 [M, K] -> (codes uint8 [M, K] (int8 bits or e4m3 bytes),
-    scales float32 [M, K/128] or [M, 1] per row). round_half_even: int8 codes rounded half to even (BASELINE
-    config 1's wording) instead of the reference's half away from zero."""
+    scales float32 [M, K/128] or [M, 1] per row). round_half_even: int8 codes rounded half to even (torch.round's
+    convention) instead of the reference's half away from zero."""
     x = _f32(x)
     m, k = x.shape
     group = k if per_row else GROUP

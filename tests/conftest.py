@@ -21,7 +21,7 @@ GOLDEN = os.path.join(ROOT, "tests", "golden")
 
 def pytest_configure(config):
     config.addinivalue_line("markers", "gpu: needs a B200 (sm_100a) GPU; runs the CUDA path through the C ABI")
-    config.addinivalue_line("markers", "slow: full-size (BASELINE shape) property checks")
+    config.addinivalue_line("markers", "slow: full-size (benchmark shape) property checks")
 
 
 @pytest.fixture(scope="session")

@@ -144,7 +144,7 @@ def test_qk_norm_rope_kv_cache_pass(hn, oracle, cuda, rope):
 
 def test_qk_norm_rope_strided_qkv_and_pair(hn, oracle, cuda):
     """q/k as column slices of a fused [L, 3 * H * D] qkv buffer (token stride 3HD), one and two per launch,
-    with BASELINE's 3-D RoPE (t,h,w axes 16/56/56, theta 10000)."""
+    with the benchmark's 3-D RoPE (t,h,w axes 16/56/56, theta 10000)."""
     from oracle import torch_ref
     b, l, h, d = 1, 2 * 3 * 4, 32, 128
     qkv = (torch.randn(b, l, 3 * h * d, generator=torch.Generator().manual_seed(4)) * 2).bfloat16().to(cuda)

@@ -161,7 +161,7 @@ def test_block_linear_ragged_k_takes_dequant_path(hn, cuda):
 
 @pytest.mark.slow
 def test_full_size_sampled_rows(hn, oracle, cuda):
-    """BASELINE shapes: M = 20240 tokens, K = N = 4096, per-group scales; 96 sampled rows vs the oracle."""
+    """Benchmark shapes: M = 20240 tokens, K = N = 4096, per-group scales; 96 sampled rows vs the oracle."""
     gen = torch.Generator().manual_seed(7)
     m, n, k = 20240, 4096, 4096
     x = (torch.randn(m, k, generator=gen)).bfloat16().to(cuda)

@@ -176,7 +176,7 @@ def test_per_token_edge_rows(hn, oracle, cuda, kind):
 @pytest.mark.parametrize("per_token", [False, True])
 @pytest.mark.parametrize("dtype", [torch.bfloat16, torch.float32])
 def test_round_half_even_option(hn, oracle, cuda, per_token, dtype):
-    """int8 codes rounded half to even (BASELINE config 1's wording; the reference rounds half away): exact ties
+    """int8 codes rounded half to even (the option beside the reference's half-away rounding): exact ties
     at scale 1 and random rows (with a tie row), bf16 (fast quotient) and fp32 (IEEE division) inputs,
     bit-exact with the oracle; the default stays half away from zero."""
     import test_oracle_math

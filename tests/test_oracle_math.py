@@ -64,7 +64,7 @@ def tie_rows():
 
 def test_round_half_even_option_on_ties(oracle):
     """Per-token and per-group int8 codes on exact ties: half away from zero (the reference) and half to even
-    (BASELINE config 1's wording)."""
+    (the option beside it)."""
     x, ties = tie_rows()
     away = {0.5: 1, 1.5: 2, 2.5: 3, 3.5: 4, 126.5: 127, 0.25: 0, 3.75: 4}
     even = {0.5: 0, 1.5: 2, 2.5: 2, 3.5: 4, 126.5: 126, 0.25: 0, 3.75: 4}
