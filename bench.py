@@ -246,7 +246,10 @@ def outlier_activations(m, k, gen):
 # dit (config 5)
 
 
-DIT_LC = (128, 512)   # token counts of the CPU samples (the fit's two points)
+# the benchmark's DiT (config 5), stated here so the CPU reference arm needs nothing from the product package
+DIT = dict(hidden=4096, heads=32, mlp=16384, blocks=40, rope_dims=(16, 56, 56), theta=10000.0, grid=(23, 22, 40))
+DIT_TOKENS = 23 * 22 * 40
+DIT_WARM_TOKENS = 512   # the CPU arm's extra warm-up blocks run on this many tokens
 
 
 def workload_dit(args, world, rank, stream, pk, sampler):
@@ -259,7 +262,8 @@ def workload_dit(args, world, rank, stream, pk, sampler):
     lo, hi = model.token_range
     L, d = cfg.tokens, cfg.hidden
     gen = torch.Generator(device="cuda").manual_seed(1000)
-    x = torch.randn(1, L, d, generator=gen, device="cuda")[:, lo:hi].to(torch.bfloat16).contiguous()
+    x_full = torch.randn(1, L, d, generator=gen, device="cuda").to(torch.bfloat16)
+    x = x_full[:, lo:hi].contiguous()
     vec = torch.randn(1, d, generator=gen, device="cuda").to(torch.bfloat16)
 
     def step(i):
@@ -297,6 +301,7 @@ def workload_dit(args, world, rank, stream, pk, sampler):
         yh.copy_(y, non_blocking=True)
 
     e2e_ms = timed_steps(e2e_step, args.steps, 1, world, stream)
+    check = sp_output_check(model, x_full, x, vec, world) if world > 1 else None
     tokens = L * args.steps
     value = tokens / (ms * 1e-3)
     int8_peak = 2.0 * pk["bf16_tflops_sustained"]
@@ -307,7 +312,7 @@ def workload_dit(args, world, rank, stream, pk, sampler):
             "unit": "TOPS", "frac": round(achieved / int8_peak, 4),
             "peak_note": f"int8 dense = 2 x {pk['source']} bf16 sustained ({pk['bf16_tflops_sustained']} TFLOP/s); "
                          "the GEMMs run inside a long step",
-            "traffic": traffic_for("dit"), "gemm_ops_per_step_rank": gemm_ops}
+            "traffic": dit_gemm_traffic(cfg, hi - lo), "gemm_ops_per_step_rank": gemm_ops}
     config = {"workload": "dit_step_40x_hidden4096_L20240 (config 5): 40 DiT blocks, SDPA attention, W8A8 linears",
               "model": "synthetic Hy-Nomas-style DiT (random init, seeded)", "global_batch": 1, "seq_len": L,
               "tokens_per_rank": hi - lo, "blocks": cfg.blocks, "hidden": d, "heads": cfg.heads, "mlp": d * cfg.mlp_ratio,
@@ -318,7 +323,12 @@ def workload_dit(args, world, rank, stream, pk, sampler):
                                           "other": round(max(step_ms - gemm_ms - attn_ms, 0.0), 2)},
               "attention_tflops": round(attn_flops / (attn_ms * 1e-3) / 1e12, 1) if attn_ms else None,
               "floor_ms_rank0": {"gemm_at_int8_peak": round(gemm_ops / (int8_peak * 1e12) * 1e3, 2),
-                                 "attention_at_bf16_peak": round(attn_flops / (pk["bf16_tflops_sustained"] * 1e12) * 1e3, 2)}}
+                                 "attention_at_bf16_peak": round(attn_flops / (pk["bf16_tflops_sustained"] * 1e12) * 1e3, 2)},
+              "modulation_gemv": modulation_context(model, vec, stream, pk)}
+    if check is not None:
+        config["sp_output_check"] = check
+    if world == 1 and not args.no_context:
+        config["configs_1_to_3"] = path_context(stream, pk)
     return dict(metric="DiT denoise step tokens/s (40 blocks, 20240 tokens)", value=round(value, 1), unit="tokens/s",
                 ms_per_step=round(step_ms, 3), higher_is_better=True, scaling="strong", dtype="int8 (GEMMs), bf16",
                 config=config,
@@ -326,77 +336,130 @@ def workload_dit(args, world, rank, stream, pk, sampler):
                      "h2d_bytes_per_step": int(sum_over_ranks(xh.numel() * 2 + vh.numel() * 2, world)),
                      "d2h_bytes_per_step": int(sum_over_ranks(yh.numel() * 2, world))},
                 roofline=roof, gpu_launches=launches * args.steps,
-                cpu_baseline_fn=lambda: cpu_baseline_dit(cfg))
+                cpu_baseline_fn=lambda: cpu_baseline_dit())
 
 
-def _cpu_dit_weights(cfg, gen):
-    from hy_nomas_b200.dit import make_block_weights
-    return make_block_weights(cfg, gen, "cpu")
+def sp_output_check(model, x_full, x, vec, world, tol=1e-2):
+    """Every rank also runs the whole sequence on its own GPU (no sequence parallelism, the same weights) and
+    compares its own tokens of that result with the sequence-parallel output: the largest rel-L2 over ranks and
+    the number of ranks whose tokens are bit-identical. Attention over the gathered K/V may pick other kernel
+    tilings for fewer queries, and a few quantization codes downstream can move with it, hence a tolerance."""
+    from hy_nomas_b200.sequence_parallel import SequenceParallel
+    y_sp = model(x, vec)
+    single = model.replica(SequenceParallel(local=True))
+    y_one = single(x_full, vec)
+    lo, hi = model.token_range
+    ref = y_one[:, lo:hi].float()
+    err = (torch.linalg.vector_norm(y_sp.float() - ref) / torch.linalg.vector_norm(ref).clamp_min(1e-30)).item()
+    same = 1.0 if torch.equal(y_sp.view(torch.int16), y_one[:, lo:hi].view(torch.int16)) else 0.0
+    finite = 1.0 if bool(torch.isfinite(y_sp).all()) else 0.0
+    err_max = max_over_ranks(err, world)
+    n_same = int(sum_over_ranks(same, world))
+    n_finite = int(sum_over_ranks(finite, world))
+    del single, y_one
+    torch.cuda.empty_cache()
+    return {"against": "the same tokens computed on one GPU without sequence parallelism, on every rank",
+            "rel_l2_max_over_ranks": float(f"{err_max:.3e}"), "bit_identical_ranks": n_same, "ranks": world,
+            "finite_ranks": n_finite, "tolerance": tol, "pass": bool(err_max <= tol and n_finite == world)}
 
 
-def cpu_dit_sample(cfg, w, lc, gen):
-    """One block of the reference's CPU path on `lc` tokens -> (seconds, attention seconds)."""
-    from hy_nomas_b200.dit import rope_freqs
+def modulation_context(model, vec, stream, pk, iters=10):
+    """The step's stacked modulation linear (every block's Modulate(vec), one [blocks x 6D, D] int8 linear at
+    M = 1): its time and the weight bandwidth it reaches (a GEMV reads every weight byte once)."""
+    flush = torch.empty(2 * L2_BYTES, dtype=torch.uint8, device="cuda")
+    t = _time_kernel(lambda: model.modulations(vec), stream, flush, iters)
+    w = model.mod_all
+    nbytes = w.q.numel() + w.s.numel() * 4 + w.bias.numel() * 2
+    return {"ms": round(t, 4), "weight_bytes": nbytes, "gbs": round(nbytes / (t * 1e-3) / 1e9, 1),
+            "frac_of_hbm": round(nbytes / (t * 1e-3) / 1e9 / pk["hbm_gbs"], 4),
+            "shape": f"1 x {w.q.shape[0]} x {w.q.shape[1]} (quantize + GEMM, timed together)"}
+
+
+def dit_gemm_traffic(cfg, tokens):
+    """DRAM bytes of all GEMM launches of one step on this rank, from the committed per-shape ncu captures
+    (profiles/traffic.json "dit_gemm_shapes": bytes per launch at M = 20240, scaled by tokens / 20240, which
+    holds while each tile streams its own A rows once and the weights are re-read per row band)."""
+    t = traffic_for("dit_gemm_shapes")
+    if not t:
+        return None
+    per_block = sum(t[name] for name in ("v", "qk", "proj", "fc1", "fc2") if name in t)
+    if len([n for n in ("v", "qk", "proj", "fc1", "fc2") if n in t]) != 5:
+        return None
+    return int(per_block * cfg.blocks * tokens / t.get("tokens", 20240))
+
+
+def path_context(stream, pk):
+    """Benchmark configs 1-3 measured in the same run as the DiT step (context for its roofline): the W8A8 GEMM
+    kernel at 4096^3 in every scale mode, the FP8 sweep, and the fused elementwise kernels at M = 20240."""
+    int8_burst = 2.0 * pk["bf16_tflops"]
+    tops = gemm_variants(4096, 4096, 4096, stream)
+    ctx = {"config1_w8a8_4096_kernel": {k: {"tops": v, "frac_of_int8_burst": round(v / int8_burst, 4)}
+                                        if isinstance(v, float) else v for k, v in tops.items()},
+           "config2_fp8_sweep_kernel_tflops": fp8_sweep(stream),
+           "config3_elementwise": elementwise_gbs(stream, pk)}
+    torch.cuda.empty_cache()
+    return ctx
+
+
+def _cpu_block_inputs(tokens, gen):
     from oracle import torch_ref
-    x = torch.randn(1, lc, cfg.hidden, generator=gen).to(torch.bfloat16)
-    vec = torch.randn(1, cfg.hidden, generator=gen).to(torch.bfloat16)
-    cos, sin = rope_freqs(cfg.rope_dims, cfg.theta, *cfg.grid)
-    rope = (cos[:lc], sin[:lc])
+    x = torch.randn(1, tokens, DIT["hidden"], generator=gen).to(torch.bfloat16)
+    vec = torch.randn(1, DIT["hidden"], generator=gen).to(torch.bfloat16)
+    cos, sin = torch_ref.rope_freqs(DIT["rope_dims"], DIT["theta"], *DIT["grid"])
+    return x, vec, (cos[:tokens].contiguous(), sin[:tokens].contiguous())
+
+
+def cpu_dit_block(w, tokens, gen):
+    """One block of the reference's CPU path on `tokens` tokens -> (seconds, attention seconds)."""
+    from oracle import torch_ref
+    x, vec, rope = _cpu_block_inputs(tokens, gen)
     tm = {}
     t0 = time.perf_counter()
-    torch_ref.dit_block_cpu(x, vec, w, rope, cfg.heads, timings=tm)
+    torch_ref.dit_block_cpu(x, vec, w, rope, DIT["heads"], timings=tm)
     return time.perf_counter() - t0, tm.get("attention", 0.0)
 
 
-def dit_extrapolate(cfg, samples):
-    """Fit t(l) = a + b*l (everything but attention: the per-call weight dequantization is the fixed part)
-    and c*l^2 (attention) to the CPU samples, evaluate at the full sequence -> tokens/s of a 40-block step."""
-    (l1, t1, at1), (l2, t2, at2) = samples
-    n1, n2 = t1 - at1, t2 - at2
-    b = max((n2 - n1) / (l2 - l1), 0.0)
-    a = max(n1 - b * l1, 0.0)
-    c = at2 / (l2 * l2)
-    L = cfg.tokens
-    step_s = cfg.blocks * (a + b * L + c * L * L)
-    return L / step_s, step_s
+def _cpu_dit_weights(gen):
+    from oracle import torch_ref
+    return torch_ref.make_block_weights_cpu(DIT["hidden"], DIT["mlp"], DIT["hidden"] // DIT["heads"], gen)
 
 
-def cpu_baseline_dit(cfg, repeats=2):
+def cpu_baseline_dit():
+    """The reference's CPU path on one full-length block (L = 20240: every linear, the norms, RoPE and
+    attention) after one 512-token warm-up block; the 40-block step is 40 x that block."""
     gen = torch.Generator().manual_seed(7)
-    w = _cpu_dit_weights(cfg, gen)
-    samples = []
-    for lc in DIT_LC:
-        cpu_dit_sample(cfg, w, lc, gen)
-        runs = [cpu_dit_sample(cfg, w, lc, gen) for _ in range(repeats)]
-        samples.append((lc, statistics.median(r[0] for r in runs), statistics.median(r[1] for r in runs)))
-    value, step_s = dit_extrapolate(cfg, samples)
+    w = _cpu_dit_weights(gen)
+    cpu_dit_block(w, DIT_WARM_TOKENS, gen)
+    t, ta = cpu_dit_block(w, DIT_TOKENS, gen)
     cores, threads = cpu_threads()
-    return {"value": round(value, 2), "unit": "tokens/s", "cores": threads, "kind": "port",
-            "sample": f"one block of the reference's CPU path (dequantize + bf16 F.linear per linear, torch norms, "
-                      f"RoPE and SDPA) at {DIT_LC[0]} and {DIT_LC[1]} tokens, median of {repeats}; extrapolated to "
-                      f"40 blocks x {cfg.tokens} tokens ({step_s:.0f} s per step) by a + b*L (linears, norms) + "
-                      f"c*L^2 (attention); {threads} threads on {cores} cores"}
+    step_s = DIT["blocks"] * t
+    return {"value": round(DIT_TOKENS / step_s, 2), "unit": "tokens/s", "cores": threads, "kind": "port",
+            "sample": f"one full-length block of the reference's CPU path (dequantize + bf16 F.linear per linear, "
+                      f"torch norms, RoPE and SDPA) at {DIT_TOKENS} tokens: {t:.1f} s ({ta:.1f} s attention); the "
+                      f"step is {DIT['blocks']} such blocks ({step_s:.0f} s); {threads} threads on {cores} cores"}
 
 
 def reference_dit(args):
-    from hy_nomas_b200.dit import DiTConfig
-    cfg = DiTConfig()
+    """Each timed step is one full-length block (L = 20240: every linear, the norms, RoPE and attention) of the
+    reference's CPU path; the 40 blocks of a step are identical in work, so the step takes 40 x the block."""
     gen = torch.Generator().manual_seed(7)
-    w = _cpu_dit_weights(cfg, gen)
-    first = cpu_dit_sample(cfg, w, DIT_LC[0], gen)
+    w = _cpu_dit_weights(gen)
+    # untimed: one full-length block (allocator and page-in at full size), then cheap 512-token blocks
+    cpu_dit_block(w, DIT_TOKENS, gen)
     for _ in range(args.warmup - 1):
-        cpu_dit_sample(cfg, w, DIT_LC[1], gen)
-    runs = [cpu_dit_sample(cfg, w, DIT_LC[1], gen) for _ in range(args.steps)]
-    small = (DIT_LC[0], first[0], first[1])
-    big = (DIT_LC[1], statistics.median(r[0] for r in runs), statistics.median(r[1] for r in runs))
-    value, step_s = dit_extrapolate(cfg, [small, big])
+        cpu_dit_block(w, DIT_WARM_TOKENS, gen)
+    runs = [cpu_dit_block(w, DIT_TOKENS, gen) for _ in range(args.steps)]
+    block_s = sum(r[0] for r in runs) / len(runs)
+    attn_s = sum(r[1] for r in runs) / len(runs)
+    step_s = DIT["blocks"] * block_s
     cores, threads = cpu_threads()
-    sample = (f"each step: one block of the reference's CPU path at {DIT_LC[1]} tokens (a {DIT_LC[0]}-token block "
-              f"fixes the fit), extrapolated to 40 blocks x {cfg.tokens} tokens by a + b*L + c*L^2 "
-              f"({step_s:.0f} s per step); {threads} threads")
-    return dict(metric="DiT denoise step tokens/s (40 blocks, 20240 tokens)", value=round(value, 2), unit="tokens/s",
-                ms_per_step=round(step_s * 1e3, 1), higher_is_better=True, scaling="strong", dtype="bf16 (CPU)",
-                config={"workload": "dit_step_40x_hidden4096_L20240 (config 5)", "seq_len": cfg.tokens},
+    sample = (f"each step: one full-length block of the reference's CPU path at {DIT_TOKENS} tokens "
+              f"({block_s:.1f} s, {attn_s:.1f} s of it attention); a 40-block step is 40 x the block "
+              f"({step_s:.0f} s); {threads} threads")
+    return dict(metric="DiT denoise step tokens/s (40 blocks, 20240 tokens)", value=round(DIT_TOKENS / step_s, 2),
+                unit="tokens/s", ms_per_step=round(step_s * 1e3, 1), higher_is_better=True, scaling="strong",
+                dtype="bf16 (CPU)", config={"workload": "dit_step_40x_hidden4096_L20240 (config 5)", "seq_len": DIT_TOKENS,
+                                            "block_seconds": round(block_s, 3), "blocks": DIT["blocks"]},
                 kind="port", sample=sample, cores=threads)
 
 
@@ -490,7 +553,9 @@ def gemm_variants(m, n, k, stream, iters=20):
     def literal_config1():
         qt, st = kernels.quantize_activations(x, per_token=True, round_half_even=True)
         return kernels.block_gemm(qt, st, qw, sw_r)
+    sw_gm = sw_g.t().contiguous().t()   # [N, K/128] view of group-major storage (the layout weights.py loads)
     cases = {"a_group_w_group_rowmajor": lambda: kernels.block_gemm(qa, sa_g, qw, sw_g),
+             "a_group_w_group_groupmajor": lambda: kernels.block_gemm(qa, sa_g, qw, sw_gm),
              "a_group_w_channel": lambda: kernels.block_gemm(qa, sa_g, qw, sw_r),
              "a_token_w_channel": lambda: kernels.block_gemm(qa, sa_r, qw, sw_r),
              "quantize_token_rne_and_gemm": literal_config1,
@@ -812,10 +877,49 @@ def other_elementwise_kernels(m, d, h, hd, stream, sets, shift, scale, w, rope, 
     return res
 
 
+def elementwise_gbs(stream, pk, iters=20):
+    """Config 3's kernels (and the path's other bandwidth-bound kernels) at M = 20240, D = 4096, 32 x 128 heads,
+    each alone with L2 flushed before every launch: GB/s of algorithmic bytes and the fraction of the measured
+    HBM copy bandwidth."""
+    from hy_nomas_b200 import fused, kernels
+    from hy_nomas_b200.dit import rope_freqs
+    m, d, h, hd = 20240, 4096, 32, 128
+    dev = torch.device("cuda")
+    gen = torch.Generator(device=dev).manual_seed(31)
+    bf = lambda *s, std=1.0: (torch.randn(*s, generator=gen, device=dev) * std).to(torch.bfloat16)  # noqa: E731
+    sets = [dict(x=bf(1, m, d), y=bf(1, m, d), q=bf(1, m, h, hd), k=bf(1, m, h, hd)) for _ in range(2)]
+    shift, scale, gate = bf(1, d, std=0.1), bf(1, d, std=0.1), bf(1, d, std=0.1)
+    wq, wk = bf(hd, std=0.1) + 1, bf(hd, std=0.1) + 1
+    rope = rope_freqs((16, 56, 56), 10000.0, 23, 22, 40, device=dev)
+    nb = elementwise_bytes(m, d, h, hd)
+    flush = torch.empty(2 * L2_BYTES, dtype=torch.uint8, device=dev)
+    chain = {"adaln_quant": lambda i: kernels.adaln_quant(sets[i % 2]["x"], shift, scale),
+             "qk_norm_rope2": lambda i: fused.qk_norm_rope2(sets[i % 2]["q"], sets[i % 2]["k"], wq, wk, rope),
+             "gated_residual": lambda i: fused.gated_residual(sets[i % 2]["x"], sets[i % 2]["y"], gate),
+             "gated_residual_adaln_quant": lambda i: fused.gated_residual_adaln_quant(
+                 sets[i % 2]["x"], sets[i % 2]["y"], gate, shift, scale)}
+    gbs = {}
+    for name, fn in chain.items():
+        fn(0)
+        times = []
+        for i in range(iters):
+            flush.zero_()
+            a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            a.record(stream)
+            fn(i)
+            b.record(stream)
+            b.synchronize()
+            times.append(a.elapsed_time(b))
+        gbs[name] = round(nb[name] / (statistics.median(times) * 1e-3) / 1e9, 1)
+    gbs.update(other_elementwise_kernels(m, d, h, hd, stream, sets, shift, scale, wq, rope, iters))
+    del sets, flush
+    return {name: {"gbs": v, "frac_of_hbm": round(v / pk["hbm_gbs"], 4)} for name, v in gbs.items()}
+
+
 def cpu_elementwise_chain(rows, d, h, hd, gen):
     """The reference's CPU arithmetic for the chain on `rows` tokens (model.py:103-138, 280-284, ops.py:41-52)."""
-    from hy_nomas_b200.dit import rope_freqs
     from oracle import torch_ref
+    rope_freqs = torch_ref.rope_freqs
     bf = lambda *s, std=1.0: (torch.randn(*s, generator=gen) * std).to(torch.bfloat16)  # noqa: E731
     x, y, q, k = bf(1, rows, d), bf(1, rows, d), bf(1, rows, h, hd), bf(1, rows, h, hd)
     shift, scale, gate = bf(1, d, std=0.1), bf(1, d, std=0.1), bf(1, d, std=0.1)
@@ -880,10 +984,12 @@ WORKLOADS = {"dit": (workload_dit, reference_dit), "gemm": (workload_gemm, refer
 
 
 def run_reference(args, world, rank):
-    """The reference's CPU path for the same workload and metric, rank 0 only (other ranks do no work)."""
+    """The reference's CPU path for the same workload and metric, rank 0 only (other ranks do no work and start
+    no process group, so nothing else competes for the host's cores). Nothing of the product package is
+    imported: the reference arm loads only torch and oracle/torch_ref.py."""
     if rank != 0:
         return None
-    # all of the host's threads (torchrun sets OMP_NUM_THREADS=1 for its workers)
+    # all of the host's threads, pinned (torchrun sets OMP_NUM_THREADS=1 for its workers)
     torch.set_num_threads(len(os.sched_getaffinity(0)))
     r = WORKLOADS[args.workload][1](args)
     sample, kind, cores = r.pop("sample"), r.pop("kind"), r.pop("cores")
@@ -910,17 +1016,20 @@ def main():
     ap.add_argument("--workload", default="dit", choices=sorted(WORKLOADS))
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--no-context", action="store_true", help="dit: skip the configs 1-3 kernel measurements")
     args = ap.parse_args()
     args.warmup = max(args.warmup, 3)
     if args.steps is None:
         args.steps = 3 if args.impl == "reference" else (10 if args.workload == "dit" else 50)
+    if args.impl == "reference":
+        # the CPU arm: rank 0 alone works; no GPU and no process group are touched
+        world, rank = int(os.environ.get("WORLD_SIZE", "1")), int(os.environ.get("RANK", "0"))
+        line = run_reference(args, world, rank)
+        if line is not None:
+            print(json.dumps(line), file=json_out, flush=True)
+        return
     world, rank, local = init_dist()
     try:
-        if args.impl == "reference":
-            line = run_reference(args, world, rank)
-            if line is not None:
-                print(json.dumps(line), file=json_out, flush=True)
-            return
         pk = peaks()
         stream = torch.cuda.current_stream()
         props = torch.cuda.get_device_properties(torch.cuda.current_device())

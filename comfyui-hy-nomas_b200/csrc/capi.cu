@@ -8,6 +8,7 @@
 #include <stdio.h>
 #include <string.h>
 
+#include <atomic>
 #include <mutex>
 #include <string>
 
@@ -34,7 +35,7 @@ static int cuda_fail(cudaError_t e, const char *what) {
     return fail(HN_ERR_CUDA, "%s: %s (%s)", what, cudaGetErrorString(e), cudaGetErrorName(e));
 }
 
-constexpr int MAX_DEV = 64;
+constexpr int MAX_DEV = HN_MAX_DEV;
 static int g_sms[MAX_DEV];
 static int g_arch_ok[MAX_DEV];  // 0 unknown, 1 ok, -1 not sm_100
 static std::mutex g_mu;
@@ -69,7 +70,22 @@ static int check_arch() {
     return HN_OK;
 }
 
-int g_gemm_sm_reserve = 0;
+static std::atomic<int> g_gemm_sm_reserve{0};
+int gemm_sm_reserve() { return g_gemm_sm_reserve.load(std::memory_order_relaxed); }
+
+// stream -> error-word slot (slot 0: the NULL stream, and every stream once the table is full)
+static cudaStream_t g_slot_stream[HN_ERR_SLOTS];
+static int g_slots_used = 1;
+
+int err_slot(cudaStream_t st) {
+    if (st == nullptr) return 0;
+    std::lock_guard<std::mutex> lk(g_mu);
+    for (int i = 1; i < g_slots_used; ++i)
+        if (g_slot_stream[i] == st) return i;
+    if (g_slots_used == HN_ERR_SLOTS) return 0;
+    g_slot_stream[g_slots_used] = st;
+    return g_slots_used++;
+}
 
 int num_sms() {
     int dev = 0;
@@ -97,6 +113,29 @@ static bool scale_strides_ok(int64_t rows, int64_t groups, int64_t rs, int64_t g
     return rs >= groups * gs || gs >= rows * rs;
 }
 
+// The device that owns `stream` made current for the duration of an entry point (the caller's current device
+// is put back on exit), so a launch, the SM count and the architecture check all refer to the stream's
+// device whichever device the calling thread had current. The NULL stream keeps the current device.
+struct StreamDevice {
+    int prev = -1;
+    cudaError_t err = cudaSuccess;
+    explicit StreamDevice(void *stream) {
+        if (stream == nullptr) return;
+        int want = 0, cur = 0;
+        err = cudaStreamGetDevice(static_cast<cudaStream_t>(stream), &want);
+        if (err != cudaSuccess) return;
+        err = cudaGetDevice(&cur);
+        if (err != cudaSuccess || cur == want) return;
+        err = cudaSetDevice(want);
+        if (err == cudaSuccess) prev = cur;
+    }
+    ~StreamDevice() {
+        if (prev >= 0) cudaSetDevice(prev);
+    }
+    StreamDevice(const StreamDevice &) = delete;
+    StreamDevice &operator=(const StreamDevice &) = delete;
+};
+
 static int launched(cudaError_t e, const char *what) {
     if (e != cudaSuccess) return cuda_fail(e, what);
     t_last_error.clear();
@@ -107,10 +146,13 @@ static int launched(cudaError_t e, const char *what) {
 
 using namespace hn;
 
-#define CHECK_ARCH()                  \
-    do {                              \
-        int _rc = check_arch();       \
-        if (_rc != HN_OK) return _rc; \
+// the stream's device made current for the rest of the entry point, then the architecture check on it
+#define CHECK_ARCH()                                                                        \
+    StreamDevice _stream_device(stream);                                                    \
+    if (_stream_device.err != cudaSuccess) return cuda_fail(_stream_device.err, "cudaStreamGetDevice"); \
+    do {                                                                                    \
+        int _rc = check_arch();                                                             \
+        if (_rc != HN_OK) return _rc;                                                       \
     } while (0)
 #define REQUIRE(cond, code, ...)                      \
     do {                                              \
@@ -125,9 +167,11 @@ int hn_abi_version(void) { return HN_ABI_VERSION; }
 
 int hn_set_gemm_sm_reserve(int n) {
     if (n < 0 || n > 64) return fail(HN_ERR_ARG, "hn_set_gemm_sm_reserve: n must be in [0, 64]");
-    hn::g_gemm_sm_reserve = n;
+    hn::g_gemm_sm_reserve.store(n, std::memory_order_relaxed);
     return HN_OK;
 }
+
+int hn_get_gemm_sm_reserve(void) { return hn::gemm_sm_reserve(); }
 
 int hn_num_sms(void) {
     int n = 0;
@@ -140,11 +184,13 @@ int hn_num_sms(void) {
 
 int hn_device_error(void *stream, int *code_host) {
     REQUIRE(code_host != nullptr, HN_ERR_ARG, "code_host is NULL");
+    StreamDevice sd(stream);
+    if (sd.err != cudaSuccess) return cuda_fail(sd.err, "cudaStreamGetDevice");
     cudaStream_t st = static_cast<cudaStream_t>(stream);
     cudaError_t e = cudaStreamSynchronize(st);
     if (e != cudaSuccess) return cuda_fail(e, "cudaStreamSynchronize");
     int v = 0;
-    e = read_and_clear_device_error(&v);
+    e = read_and_clear_device_error(err_slot(st), &v);
     if (e != cudaSuccess) return cuda_fail(e, "reading the device error word");
     *code_host = v;
     if (v & HN_DEVERR_TIMEOUT) return fail(HN_ERR_TIMEOUT, "a device-side wait ran past its limit");
@@ -194,6 +240,10 @@ int hn_block_gemm(const void *qa, int64_t lda, const float *sa, int64_t sa_rs, i
     REQUIRE(M >= 0 && N > 0 && K > 0 && K % 128 == 0, HN_ERR_SHAPE,
             "hn_block_gemm: need K %% 128 == 0, N > 0 (M=%lld N=%lld K=%lld)", (long long)M, (long long)N, (long long)K);
     REQUIRE(M < (1LL << 31) && N < (1LL << 31) && K < (1LL << 31), HN_ERR_SHAPE, "hn_block_gemm: dimension too large");
+    // both scales per row: the tensor core sums all of K in one int32 accumulator, |sum| <= K * 128 * 128
+    REQUIRE(!(kind == HN_KIND_INT8 && sa_mode == HN_SCALE_ROW && sw_mode == HN_SCALE_ROW) || K <= HN_ROW_MODE_MAX_K,
+            HN_ERR_SHAPE, "hn_block_gemm: int8 with per-row scales on both sides needs K <= %d (int32 accumulator; K=%lld)",
+            HN_ROW_MODE_MAX_K, (long long)K);
     REQUIRE(lda >= K && ldw >= K && ldo >= N, HN_ERR_SHAPE, "hn_block_gemm: leading dimension too small");
     REQUIRE(sa_mode != HN_SCALE_GROUP || scale_strides_ok(M, K / 128, sa_rs, sa_gs), HN_ERR_SHAPE,
             "hn_block_gemm: activation scale strides overlap");
@@ -221,7 +271,8 @@ int hn_block_gemm(const void *qa, int64_t lda, const float *sa, int64_t sa_rs, i
                 HN_ERR_UNSUPPORTED, "hn_block_gemm: int32 output is the raw int8 accumulator (row scales, no bias)");
     if (bias) REQUIRE(bias_dtype == HN_DTYPE_BF16 || bias_dtype == HN_DTYPE_FP16 || bias_dtype == HN_DTYPE_FP32,
                       HN_ERR_ARG, "hn_block_gemm: bad bias dtype %d", bias_dtype);
-    if (bias && N % 8 == 0) REQUIRE(al16(bias), HN_ERR_ALIGN, "hn_block_gemm: bias must be 16-byte aligned");
+    // the epilogue reads the bias 8 columns at a time with 16-byte loads wherever 8 columns are in range
+    if (bias) REQUIRE(al16(bias), HN_ERR_ALIGN, "hn_block_gemm: bias must be 16-byte aligned");
     if (M == 0) return HN_OK;
     CHECK_ARCH();
     GemmArgs a;
@@ -230,6 +281,7 @@ int hn_block_gemm(const void *qa, int64_t lda, const float *sa, int64_t sa_rs, i
     a.bias = bias; a.bias_dtype = bias_dtype;
     a.out = out; a.ldo = ldo; a.out_dtype = out_dtype; a.qs = qs; a.qs_rs = qs_rs; a.qs_gs = qs_gs;
     a.M = M; a.N = N; a.K = K; a.kind = kind; a.epilogue = epilogue;
+    a.sm_reserve = gemm_sm_reserve();
     const char *msg = nullptr;
     cudaError_t e = launch_block_gemm(a, (cudaStream_t)stream, &msg);
     if (e != cudaSuccess && msg) return fail(HN_ERR_ALIGN, "hn_block_gemm: %s", msg);

@@ -36,8 +36,10 @@
 //
 // Promotion arithmetic (the CPU oracle evaluates the same):
 //   PMODE 0 (sw per row x group):  t = RN(p * sa[m,g]);  acc = fma(t, sw[n,g], acc)
-//   PMODE 1 (sw per row or block):  acc = fma(p, s, acc) with s = sa[m,g] (sw per row, applied at the end)
-//                                   or s = RN(sa[m,g] * swb[n/128,g]) (128x128 weight blocks)
+//   PMODE 1 (sw per row or block):  s = sa[m,g] (sw per row, applied at the end) or s = RN(sa[m,g] *
+//                                   swb[n/128,g]) (128x128 weight blocks); fp8: acc = fma(p, s, acc); int8, with
+//                                   O = 1.5 * 2^23: acc = fma(O + p, s, acc) for even g, fma(O - p, -s, acc) for
+//                                   odd g, then acc = fma(-O, c, acc) with c = RN(...RN(RN(s_0 - s_1) + s_2)...)
 //   PMODE 2 (both per row):         one accumulator over all K; y = RN(RN(float(D) * sa[m]) * sw[n])
 //
 // Every wait on an mbarrier is bounded (globaltimer); on expiry the kernel records HN_DEVERR_TIMEOUT,
@@ -51,14 +53,34 @@
 
 namespace hn {
 
-// Device error word (0 = ok): bounded waits OR in HN_DEVERR_* bits.
-__device__ int g_device_error = 0;
+// Device error words (0 = ok), one per stream slot (err_slot() in capi.cu): a bounded wait that gives up ORs
+// HN_DEVERR_* bits into the word of the stream its kernel was launched on, so a timeout is reported to the
+// reader of that stream only. Each device holds its own copy of the array.
+__device__ int g_device_error[HN_ERR_SLOTS];
 
-cudaError_t read_and_clear_device_error(int *value) {
-    int zero = 0;
-    cudaError_t e = cudaMemcpyFromSymbol(value, g_device_error, sizeof(int));
+cudaError_t device_error_word(int slot, int **ptr) {
+    int dev = 0;
+    cudaError_t e = cudaGetDevice(&dev);
     if (e != cudaSuccess) return e;
-    return cudaMemcpyToSymbol(g_device_error, &zero, sizeof(int));
+    if (dev < 0 || dev >= HN_MAX_DEV) return cudaErrorInvalidDevice;
+    // the array's device address, looked up once per device with that device current (in host code the
+    // symbol name itself is only a host-side stand-in)
+    static int *base[HN_MAX_DEV];
+    if (base[dev] == nullptr) {
+        void *p = nullptr;
+        e = cudaGetSymbolAddress(&p, g_device_error);
+        if (e != cudaSuccess) return e;
+        base[dev] = static_cast<int *>(p);
+    }
+    *ptr = base[dev] + slot;
+    return cudaSuccess;
+}
+
+cudaError_t read_and_clear_device_error(int slot, int *value) {
+    int zero = 0;
+    cudaError_t e = cudaMemcpyFromSymbol(value, g_device_error, sizeof(int), sizeof(int) * slot);
+    if (e != cudaSuccess) return e;
+    return cudaMemcpyToSymbol(g_device_error, &zero, sizeof(int), sizeof(int) * slot);
 }
 
 namespace gemm {
@@ -109,6 +131,7 @@ struct Params {
     const void *bias; int bias_dtype;
     void *out; int64_t ldo; int out_dtype;
     float *qs; int64_t qs_rs, qs_gs;
+    int *err;       // this launch's device error word (its stream's slot)
     int M, N, K, G;
     int n_blocks, num_tiles;
     int vec_store;
@@ -142,7 +165,8 @@ __device__ __forceinline__ bool mbar_try(uint32_t bar, uint32_t parity) {
     return ok != 0;
 }
 // bounded wait: false when the kernel is aborting (this wait timed out, or another role's did)
-__device__ __forceinline__ bool mbar_wait(uint32_t bar, uint32_t parity, volatile int *abort_flag, uint64_t limit_ns) {
+__device__ __forceinline__ bool mbar_wait(uint32_t bar, uint32_t parity, volatile int *abort_flag, uint64_t limit_ns,
+                                          int *err) {
     if (mbar_try(bar, parity)) return true;
     const uint64_t t0 = globaltimer_ns();
     while (true) {
@@ -152,7 +176,7 @@ __device__ __forceinline__ bool mbar_wait(uint32_t bar, uint32_t parity, volatil
         if (*abort_flag) return false;
         if (globaltimer_ns() - t0 > limit_ns) {
             *abort_flag = 1;
-            atomicOr(&g_device_error, HN_DEVERR_TIMEOUT);
+            atomicOr(err, HN_DEVERR_TIMEOUT);
             return false;
         }
     }
@@ -163,9 +187,9 @@ __device__ __forceinline__ bool mbar_wait(uint32_t bar, uint32_t parity, volatil
 // on a completed phase, and 32 lanes polling one barrier serialize. The shuffle also orders the other
 // lanes after the waiting lane's acquire.
 __device__ __forceinline__ bool warp_wait(int lane, uint32_t bar, uint32_t parity, volatile int *abort_flag,
-                                          uint64_t limit_ns) {
+                                          uint64_t limit_ns, int *err) {
     bool ok = true;
-    if (lane == 0) ok = mbar_wait(bar, parity, abort_flag, limit_ns);
+    if (lane == 0) ok = mbar_wait(bar, parity, abort_flag, limit_ns, err);
     return __shfl_sync(0xffffffffu, ok ? 1 : 0, 0) != 0;
 }
 
@@ -266,17 +290,27 @@ __device__ __forceinline__ void promote_gen(uint64_t &acc, uint32_t p0, uint32_t
             : "+l"(acc)
             : "r"(p0), "r"(p1), "l"(sa2), "l"(sw2));
 }
-// acc = fma(conv(p), s2, acc)     (PMODE 1)
-template <int KIND>
+// acc = fma(conv(p), s2, acc)     (PMODE 1; fp8 partials are fp32 already)
+// int8: the conversion offset stays in: an even group adds RN((O + p) * s) - exact O + p, O = 1.5 * 2^23, the
+// integer's bits + 0x4B400000 read as a float - and an odd group RN((O - p) * -s), s2 = (-s, -s), so that the
+// offsets alternate in sign (O * (s_0 - s_1 + s_2 - ...)) and leave once per tile (offset_out); one integer op
+// and half a packed fma per output and group
+template <int KIND, int ODD>
 __device__ __forceinline__ void promote_row(uint64_t &acc, uint32_t p0, uint32_t p1, uint64_t s2) {
-    if (KIND == 0)
+    if (KIND == 0 && ODD == 0)
         asm("{\n\t.reg .b32 a, b;\n\t.reg .b64 f;\n\t"
             "add.s32 a, %1, 0x4B400000;\n\tadd.s32 b, %2, 0x4B400000;\n\t"
             "mov.b64 f, {a, b};\n\t"
-            "add.rn.f32x2 f, f, %4;\n\t"
             "fma.rn.f32x2 %0, f, %3, %0;\n\t}"
             : "+l"(acc)
-            : "r"(p0), "r"(p1), "l"(s2), "l"(pk(-12582912.0f, -12582912.0f)));
+            : "r"(p0), "r"(p1), "l"(s2));
+    else if (KIND == 0)
+        asm("{\n\t.reg .b32 a, b;\n\t.reg .b64 f;\n\t"
+            "sub.s32 a, %4, %1;\n\tsub.s32 b, %4, %2;\n\t"
+            "mov.b64 f, {a, b};\n\t"
+            "fma.rn.f32x2 %0, f, %3, %0;\n\t}"
+            : "+l"(acc)
+            : "r"(p0), "r"(p1), "l"(s2), "r"(0x4B400000u));
     else
         asm("{\n\t.reg .b64 f;\n\t"
             "mov.b64 f, {%1, %2};\n\t"
@@ -433,7 +467,7 @@ __global__ void __launch_bounds__(128 + 128 * NP, 1)
         for (int tile = blockIdx.x; tile < p.num_tiles && ok; tile += gridDim.x) {
             const int m0 = (tile / p.n_blocks) * BM, n0 = (tile % p.n_blocks) * BN;
             for (int g0 = 0; g0 < G; g0 += GPS) {
-                ok = warp_wait(lane, bar_empty + 8 * stage, phase ^ 1, abort_flag, WAIT_NS);
+                ok = warp_wait(lane, bar_empty + 8 * stage, phase ^ 1, abort_flag, WAIT_NS, p.err);
                 if (!ok) break;
                 if (lane == 0) {
                     // a box that runs past the last group is zero-filled and still counts its full bytes
@@ -456,7 +490,7 @@ __global__ void __launch_bounds__(128 + 128 * NP, 1)
         for (int i = 0; i < STAGES && i < issued; ++i) {
             if (--st < 0) { st = STAGES - 1; ph ^= 1; }
             volatile int never = 0;
-            mbar_wait(bar_full + 8 * st, ph, &never, 100000000ull);
+            mbar_wait(bar_full + 8 * st, ph, &never, 100000000ull, p.err);
         }
     } else if (warp == 3) {
         // ------------------------------------------------------------------ scale ring (PMODE 0, 1)
@@ -473,7 +507,7 @@ __global__ void __launch_bounds__(128 + 128 * NP, 1)
                 const int m0 = (tile / p.n_blocks) * BM, n0 = (tile % p.n_blocks) * BN;
                 const int rows = min(BM, p.M - m0), cols = min(BN, p.N - n0);
                 for (int g0 = 0; g0 < G; g0 += 2) {
-                    ok = warp_wait(lane, bar_sempty + 8 * ps, sphase ^ 1, abort_flag, WAIT_NS);
+                    ok = warp_wait(lane, bar_sempty + 8 * ps, sphase ^ 1, abort_flag, WAIT_NS, p.err);
                     if (!ok) break;
                     const int ng = min(2, G - g0);
                     const bool sa_grp = p.sa_mode == 0, sw_grp = PMODE == 0, sw_blk = PMODE == 1 && p.sw_mode == 2;
@@ -535,7 +569,7 @@ __global__ void __launch_bounds__(128 + 128 * NP, 1)
             for (int i = 0; i < SW_SLOTS / 2 && i < issued; ++i) {
                 if (--st < 0) { st = SW_SLOTS / 2 - 1; ph ^= 1; }
                 volatile int never = 0;
-                if (lane == 0) mbar_wait(bar_sfull + 8 * st, ph, &never, 100000000ull);
+                if (lane == 0) mbar_wait(bar_sfull + 8 * st, ph, &never, 100000000ull, p.err);
             }
             __syncwarp();
         }
@@ -551,17 +585,17 @@ __global__ void __launch_bounds__(128 + 128 * NP, 1)
         uint32_t last_phase = 0;
         for (int tile = blockIdx.x; tile < p.num_tiles && ok; tile += gridDim.x) {
             if (PMODE == 2) {
-                ok = warp_wait(lane, bar_tempty + 8 * tb, tphase ^ 1, abort_flag, WAIT_NS);
+                ok = warp_wait(lane, bar_tempty + 8 * tb, tphase ^ 1, abort_flag, WAIT_NS, p.err);
                 if (!ok) break;
                 tc_fence_after();
             }
             for (int g0 = 0; g0 < G && ok; g0 += GPS) {
-                ok = warp_wait(lane, bar_full + 8 * stage, phase, abort_flag, WAIT_NS);
+                ok = warp_wait(lane, bar_full + 8 * stage, phase, abort_flag, WAIT_NS, p.err);
                 if (!ok) break;
                 if (PMODE != 2) {
                     // per-group promotion: the stage's two groups go to the two accumulators of TMEM pair tb
                     // (NBUF / 2 pairs), handed over with one barrier each way
-                    ok = warp_wait(lane, bar_tempty + 8 * tb, tphase ^ 1, abort_flag, WAIT_NS);
+                    ok = warp_wait(lane, bar_tempty + 8 * tb, tphase ^ 1, abort_flag, WAIT_NS, p.err);
                     if (!ok) break;
                 }
                 tc_fence_after();
@@ -597,7 +631,7 @@ __global__ void __launch_bounds__(128 + 128 * NP, 1)
         // drain: the MMAs behind the last commit finish before TMEM is released
         if (last_stage >= 0) {
             volatile int never = 0;
-            mbar_wait(bar_empty + 8 * last_stage, last_phase, &never, 100000000ull);
+            mbar_wait(bar_empty + 8 * last_stage, last_phase, &never, 100000000ull, p.err);
         }
     } else if (warp >= EPI_WARP0) {
         // ------------------------------------------------------------------ epilogue
@@ -623,11 +657,13 @@ __global__ void __launch_bounds__(128 + 128 * NP, 1)
                 uint64_t acc[CPT / 2];
 #pragma unroll
                 for (int i = 0; i < CPT / 2; ++i) acc[i] = 0ull;
+                // int8 row-scale mode: s_0 - s_1 + s_2 - ... of this row's scales, for the conversion offsets
+                float offset_sum = 0.0f;
                 const float sa_row = (p.sa_mode == 1) ? p.sa[(int64_t)mm * p.sa_rs] : 0.0f;
                 for (int g0 = 0; g0 < G; g0 += 2) {
                     // one pair of K groups: its scales (pair slot ps) and its two accumulators (TMEM pair tb)
                     const int ng = min(2, G - g0);
-                    ok = warp_wait(lane, bar_sfull + 8 * slot, sphase, abort_flag, WAIT_NS);
+                    ok = warp_wait(lane, bar_sfull + 8 * slot, sphase, abort_flag, WAIT_NS, p.err);
                     if (!ok) break;
                     // (row-scale mode) the pair's scales into registers before the accumulators are waited for,
                     // so the shared-memory latency hides behind the wait
@@ -640,7 +676,7 @@ __global__ void __launch_bounds__(128 + 128 * NP, 1)
                         if (p.sw_mode == 2)
                             s_pair[gi] = (ncol0 < p.N) ? __fmul_rn(sa_g, ring[C::RING_SB + (hf * CPT) / 128]) : 0.0f;
                     }
-                    ok = warp_wait(lane, bar_tfull + 8 * tb, tphase, abort_flag, WAIT_NS);
+                    ok = warp_wait(lane, bar_tfull + 8 * tb, tphase, abort_flag, WAIT_NS, p.err);
                     if (!ok) break;
                     tc_fence_after();
                     // group by group: the partials out of TMEM (after the pair's last read the pair goes back to the
@@ -660,7 +696,10 @@ __global__ void __launch_bounds__(128 + 128 * NP, 1)
                         }
                         const float *ring = sw_s + (2 * slot + gi) * C::RING_FLOATS;
                         const float s_g = (PMODE == 1) ? s_pair[gi] : ((p.sa_mode == 0) ? ring[C::RING_SA + row] : sa_row);
-                        const uint64_t s2 = pk(s_g, s_g);
+                        // (int8 row-scale mode) an odd group's multiplier is -s: see promote_row
+                        const float s_m = (KIND == 0 && PMODE == 1 && gi == 1) ? -s_g : s_g;
+                        if (KIND == 0 && PMODE == 1) offset_sum = __fadd_rn(offset_sum, s_m);
+                        const uint64_t s2 = pk(s_m, s_m);
                         const float *sws = ring + C::RING_SW + hf * CPT;
 #pragma unroll
                         for (int j = 0; j < CPT; j += 4) {
@@ -668,9 +707,12 @@ __global__ void __launch_bounds__(128 + 128 * NP, 1)
                                 const float4 w4 = *reinterpret_cast<const float4 *>(sws + j);
                                 promote_gen<KIND>(acc[j / 2], r[j], r[j + 1], s2, pk(w4.x, w4.y));
                                 promote_gen<KIND>(acc[j / 2 + 1], r[j + 2], r[j + 3], s2, pk(w4.z, w4.w));
+                            } else if (gi == 0) {
+                                promote_row<KIND, 0>(acc[j / 2], r[j], r[j + 1], s2);
+                                promote_row<KIND, 0>(acc[j / 2 + 1], r[j + 2], r[j + 3], s2);
                             } else {
-                                promote_row<KIND>(acc[j / 2], r[j], r[j + 1], s2);
-                                promote_row<KIND>(acc[j / 2 + 1], r[j + 2], r[j + 3], s2);
+                                promote_row<KIND, 1>(acc[j / 2], r[j], r[j + 1], s2);
+                                promote_row<KIND, 1>(acc[j / 2 + 1], r[j + 2], r[j + 3], s2);
                             }
                         }
                     }
@@ -680,6 +722,12 @@ __global__ void __launch_bounds__(128 + 128 * NP, 1)
                     if (++slot == SW_SLOTS / 2) { slot = 0; sphase ^= 1; }
                 }
                 if (!ok) break;
+                if (KIND == 0 && PMODE == 1) {
+                    // the conversion offsets out: acc = fma(-O, s_0 - s_1 + ..., acc), one rounding
+                    const uint64_t no = pk(-12582912.0f, -12582912.0f), os = pk(offset_sum, offset_sum);
+#pragma unroll
+                    for (int i = 0; i < CPT / 2; ++i) acc[i] = x2_fma(no, os, acc[i]);
+                }
                 float v[CPT];
 #pragma unroll
                 for (int i = 0; i < CPT / 2; ++i) { v[2 * i] = acc_lo(acc[i]); v[2 * i + 1] = acc_hi(acc[i]); }
@@ -725,7 +773,7 @@ __global__ void __launch_bounds__(128 + 128 * NP, 1)
                     px_s[(pb * NPART + hf) * 128 + row] = peak;
                     __syncwarp();
                     if (lane == 0) mbar_arrive(bar_px + 8 * pb);
-                    ok = warp_wait(lane, bar_px + 8 * pb, (it >> 1) & 1, abort_flag, WAIT_NS);
+                    ok = warp_wait(lane, bar_px + 8 * pb, (it >> 1) & 1, abort_flag, WAIT_NS, p.err);
                     if (!ok) break;
                     const int first = hf - hf % C::PARTS_PER_GROUP;
 #pragma unroll
@@ -746,7 +794,7 @@ __global__ void __launch_bounds__(128 + 128 * NP, 1)
                 }
             } else {
                 // ------------------------------------------------ whole-K accumulator, streamed from TMEM
-                ok = warp_wait(lane, bar_tfull + 8 * tb, tphase, abort_flag, WAIT_NS);
+                ok = warp_wait(lane, bar_tfull + 8 * tb, tphase, abort_flag, WAIT_NS, p.err);
                 if (!ok) break;
                 tc_fence_after();
                 const uint32_t tcol = lane_addr + (uint32_t)(tb * BN + hf * CPT);
@@ -811,7 +859,7 @@ __global__ void __launch_bounds__(128 + 128 * NP, 1)
                     px_s[(pb * NPART + hf) * 128 + row] = peak;
                     __syncwarp();
                     if (lane == 0) mbar_arrive(bar_px + 8 * pb);
-                    ok = warp_wait(lane, bar_px + 8 * pb, (it >> 1) & 1, abort_flag, WAIT_NS);
+                    ok = warp_wait(lane, bar_px + 8 * pb, (it >> 1) & 1, abort_flag, WAIT_NS, p.err);
                     if (!ok) break;
                     const int first = hf - hf % C::PARTS_PER_GROUP;
 #pragma unroll
@@ -874,11 +922,17 @@ template <int KIND, int PMODE, int EPI, int BN, int GPS, int NP>
 static cudaError_t launch_t(const CUtensorMap &ma, const CUtensorMap &mb, const Params &p, int grid, cudaStream_t st) {
     using C = Cfg<BN, GPS, NP>;
     auto kern = k_block_gemm<KIND, PMODE, EPI, BN, GPS, NP>;
-    static bool configured = false;  // per instantiation; setting the attribute again is harmless
-    if (!configured) {
-        cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, C::SMEM);
+    // the shared-memory opt-in is a per-device property of the function: set it once per instantiation and
+    // device (setting it twice, e.g. by two threads at once, is harmless)
+    static bool configured[HN_MAX_DEV];
+    int dev = 0;
+    cudaError_t e = cudaGetDevice(&dev);
+    if (e != cudaSuccess) return e;
+    if (dev < 0 || dev >= HN_MAX_DEV) return cudaErrorInvalidDevice;
+    if (!configured[dev]) {
+        e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, C::SMEM);
         if (e != cudaSuccess) return e;
-        configured = true;
+        configured[dev] = true;
     }
     kern<<<grid, C::THREADS, C::SMEM, st>>>(ma, mb, p);
     return cudaGetLastError();
@@ -898,6 +952,9 @@ static cudaError_t launch_epi(int epi, const CUtensorMap &ma, const CUtensorMap 
 
 cudaError_t launch_block_gemm(const GemmArgs &a, cudaStream_t st, const char **msg) {
     using namespace gemm;
+    int *err = nullptr;
+    cudaError_t ee = device_error_word(err_slot(st), &err);
+    if (ee != cudaSuccess) return ee;
     int pmode;
     if (a.sa_mode == 1 && a.sw_mode == 1) pmode = 2;
     else if (a.sw_mode == 0) pmode = 0;
@@ -916,6 +973,7 @@ cudaError_t launch_block_gemm(const GemmArgs &a, cudaStream_t st, const char **m
     p.bias = a.bias; p.bias_dtype = a.bias_dtype;
     p.out = a.out; p.ldo = a.ldo; p.out_dtype = a.out_dtype;
     p.qs = a.qs; p.qs_rs = a.qs_rs; p.qs_gs = a.qs_gs;
+    p.err = err;
     p.M = (int)a.M; p.N = (int)a.N; p.K = (int)a.K; p.G = (int)(a.K / 128);
     p.n_blocks = (int)cdiv(a.N, bn);
     p.num_tiles = (int)(cdiv(a.M, BM) * p.n_blocks);
@@ -928,7 +986,7 @@ cudaError_t launch_block_gemm(const GemmArgs &a, cudaStream_t st, const char **m
                  reinterpret_cast<uintptr_t>(a.sa) % 16 == 0) ? 1 : 0;
     p.sw_bulk = (a.sw_mode == 0 && a.sw_rs == 1 && a.sw_gs % 4 == 0 &&
                  reinterpret_cast<uintptr_t>(a.sw) % 16 == 0) ? 1 : 0;
-    int grid = num_sms() - g_gemm_sm_reserve;
+    int grid = num_sms() - a.sm_reserve;
     if (grid > p.num_tiles) grid = p.num_tiles;
     if (a.kind == 0) {
         if (pmode == 0) return launch_epi<0, 0, 128, GPS_NARROW, NPART_NARROW>(a.epilogue, ma, mb, p, grid, st);
@@ -942,7 +1000,7 @@ cudaError_t launch_block_gemm(const GemmArgs &a, cudaStream_t st, const char **m
 
 // ---------------------------------------------------------------------------------------------------
 // Bounded-wait self-test: one CTA waits on an mbarrier that nothing completes, with a short limit.
-__global__ void k_wait_selftest(uint64_t limit_ns) {
+__global__ void k_wait_selftest(uint64_t limit_ns, int *err) {
     __shared__ __align__(8) uint64_t bar;
     __shared__ int abort_flag;
     if (threadIdx.x == 0) {
@@ -951,12 +1009,15 @@ __global__ void k_wait_selftest(uint64_t limit_ns) {
         asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
     }
     __syncthreads();
-    if (threadIdx.x == 0) gemm::mbar_wait(gemm::smem_u32(&bar), 0, &abort_flag, limit_ns);
+    if (threadIdx.x == 0) gemm::mbar_wait(gemm::smem_u32(&bar), 0, &abort_flag, limit_ns, err);
     __syncthreads();
 }
 
 cudaError_t launch_wait_selftest(uint32_t timeout_us, cudaStream_t st) {
-    k_wait_selftest<<<1, 32, 0, st>>>((uint64_t)timeout_us * 1000ull);
+    int *err = nullptr;
+    cudaError_t e = device_error_word(err_slot(st), &err);
+    if (e != cudaSuccess) return e;
+    k_wait_selftest<<<1, 32, 0, st>>>((uint64_t)timeout_us * 1000ull, err);
     return cudaGetLastError();
 }
 

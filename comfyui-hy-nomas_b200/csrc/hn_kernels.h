@@ -7,8 +7,17 @@
 
 namespace hn {
 
+constexpr int HN_MAX_DEV = 64;     // device indices the library keeps per-device state for
+constexpr int HN_ERR_SLOTS = 64;   // device error words per device: slot 0 = the NULL stream and overflow
+
 int num_sms();  // SM count of the current device (cached per device)
-extern int g_gemm_sm_reserve;  // SMs the GEMM leaves free for kernels on other streams (hn_set_gemm_sm_reserve)
+int gemm_sm_reserve();  // SMs the GEMM leaves free for kernels on other streams (hn_set_gemm_sm_reserve)
+
+// Slot of `st`'s device error word: 0 for the NULL stream, else a slot of its own while fewer than
+// HN_ERR_SLOTS - 1 streams have launched a kernel that waits (later streams share slot 0).
+int err_slot(cudaStream_t st);
+// Device address of slot `slot` of the current device's error-word array.
+cudaError_t device_error_word(int slot, int **ptr);
 
 cudaError_t launch_quant_act(const void *x, int64_t ldx, int x_dtype, int64_t M, int64_t K, int kind, int flags,
                              void *q, int64_t ldq, float *s, int64_t s_rs, int64_t s_gs, cudaStream_t st);
@@ -43,13 +52,14 @@ struct GemmArgs {
     float *qs; int64_t qs_rs, qs_gs;
     int64_t M, N, K;
     int kind, epilogue;
+    int sm_reserve;   // SMs left without a CTA (the grid is num_sms() - sm_reserve persistent CTAs)
 };
 // Returns cudaSuccess, or cudaErrorInvalidValue with *msg set when a TMA descriptor cannot be encoded.
 cudaError_t launch_block_gemm(const GemmArgs &a, cudaStream_t st, const char **msg);
 
 cudaError_t launch_wait_selftest(uint32_t timeout_us, cudaStream_t st);
 
-// read the device error word into *value and clear it (synchronous)
-cudaError_t read_and_clear_device_error(int *value);
+// read slot `slot` of the current device's error words into *value and clear it (synchronous)
+cudaError_t read_and_clear_device_error(int slot, int *value);
 
 } // namespace hn

@@ -3,7 +3,7 @@
 The library is the only compute path: there is no Triton, no torch or CPU fallback. If the shared object
 is missing, importing this module raises; if a call fails, the C status becomes a RuntimeError carrying
 hn_last_error(). Tensors are passed as raw device pointers; every launch goes on torch's current stream
-of the tensor's device.
+of the tensor's device (the library makes that stream's device current for the call).
 """
 import ctypes
 import os
@@ -27,6 +27,7 @@ SIGNATURES = {
     "hn_abi_version": [],
     "hn_num_sms": [],
     "hn_set_gemm_sm_reserve": [ctypes.c_int],
+    "hn_get_gemm_sm_reserve": [],
     "hn_device_error": [_V, ctypes.POINTER(ctypes.c_int)],
     "hn_selftest_wait_timeout": [_U32, _V],
     "hn_quant_act": [_V, _I64, _I32, _I64, _I64, _I32, _I32, _V, _I64, _V, _I64, _I64, _V],
@@ -79,6 +80,14 @@ def check(rc, what):
 
 def ptr(t):
     return None if t is None else ctypes.c_void_p(t.data_ptr())
+
+
+def dense(t):
+    """`t` as a contiguous tensor whose data starts on a 16-byte boundary (the vector and TMA paths of the
+    library need it). Copies only when needed; a contiguous view at an odd offset is copied too, since
+    .contiguous() would hand back the same misaligned pointer."""
+    t = t.contiguous()
+    return t if t.data_ptr() % 16 == 0 else t.clone()
 
 
 def stream_of(t):

@@ -285,17 +285,40 @@ class SyntheticDiT:
         lo, hi = self.sp.shard(cfg.tokens)
         self.rope = (cos[lo:hi].contiguous(), sin[lo:hi].contiguous())
         self.token_range = (lo, hi)
-        if self.sp.world > 1 and self.device.type == "cuda":
-            # the GEMMs leave SMs to the K/V all-gathers, which run on their own stream under the q|k GEMM
-            from . import _lib
-            n = int(os.environ.get("HN_SP_GEMM_SM_RESERVE", str(SP_GEMM_SM_RESERVE)))
-            _lib.check(_lib.lib.hn_set_gemm_sm_reserve(n), "hn_set_gemm_sm_reserve")
+        # SMs the GEMMs leave to the K/V all-gathers under sequence parallelism (applied only while forward runs)
+        self.sm_reserve = int(os.environ.get("HN_SP_GEMM_SM_RESERVE", str(SP_GEMM_SM_RESERVE))) \
+            if (self.sp.world > 1 and self.device.type == "cuda") else 0
+
+    def replica(self, sp):
+        """The same model (weights shared, not copied) over another partition `sp` of the sequence, e.g. the whole
+        sequence on one GPU to check a sequence-parallel run against."""
+        import copy
+        other = copy.copy(self)
+        other.sp = sp
+        cos, sin = rope_freqs(self.cfg.rope_dims, self.cfg.theta, *self.cfg.grid, device=self.device)
+        lo, hi = sp.shard(self.cfg.tokens)
+        other.rope = (cos[lo:hi].contiguous(), sin[lo:hi].contiguous())
+        other.token_range = (lo, hi)
+        other.sm_reserve = 0
+        return other
 
     def modulations(self, vec):
         """All blocks' Modulate(vec) in one launch pair (quantize + GEMM): [B, blocks * 6D] bf16."""
         return self.ops.linear(self.ops.silu(vec), self.mod_all)
 
     def forward(self, x, vec, trace=None):
+        if not self.sm_reserve:
+            return self._forward(x, vec, trace)
+        # the library's SM reserve is process-wide: set it for this step only and put the caller's value back
+        from . import _lib
+        prev = _lib.lib.hn_get_gemm_sm_reserve()
+        _lib.check(_lib.lib.hn_set_gemm_sm_reserve(self.sm_reserve), "hn_set_gemm_sm_reserve")
+        try:
+            return self._forward(x, vec, trace)
+        finally:
+            _lib.lib.hn_set_gemm_sm_reserve(prev)
+
+    def _forward(self, x, vec, trace=None):
         mods = self.modulations(vec)
         n6 = 6 * self.cfg.hidden
         nb = len(self.blocks)

@@ -38,7 +38,7 @@ def adaln(x, shift, scale, eps=1e-6):
     _lib.require_cuda(x, shift, scale)
     _bf16(x, shift, scale)
     b, l, d = x.shape
-    x, shift, scale = x.contiguous(), shift.contiguous(), scale.contiguous()
+    x, shift, scale = _lib.dense(x), _lib.dense(shift), _lib.dense(scale)
     y = torch.empty(x.shape, device=x.device, dtype=x.dtype)
     rc = _lib.lib.hn_adaln(_lib.ptr(x), _lib.ptr(shift), _lib.ptr(scale), b, l, d, eps, _lib.ptr(y),
                            _lib.stream_of(x))
@@ -50,7 +50,7 @@ def _qk_input(x):
     b, l, h, d = x.shape
     if x.stride(3) != 1 or x.stride(2) != d or x.stride(0) != l * x.stride(1) or x.stride(1) % 8 or \
             x.data_ptr() % 16:
-        x = x.contiguous()
+        x = _lib.dense(x)
     return x
 
 
@@ -58,8 +58,8 @@ def _rope_tables(rope, device):
     if rope is None:
         return None, None
     cos, sin = rope
-    cos = cos.to(device=device, dtype=torch.float32).contiguous()
-    sin = sin.to(device=device, dtype=torch.float32).contiguous()
+    cos = _lib.dense(cos.to(device=device, dtype=torch.float32))
+    sin = _lib.dense(sin.to(device=device, dtype=torch.float32))
     return cos, sin
 
 
@@ -77,7 +77,7 @@ def qk_norm_rope(x, weight, rope=None, eps=1e-6, out=None):
         y = out
         if y.shape != (b, l, h, d) or y.dtype != torch.bfloat16 or not y.is_contiguous() or y.device != x.device:
             raise ValueError(f"qk_norm_rope: out must be a contiguous bf16 [{b}, {l}, {h}, {d}] tensor")
-    w = weight.to(torch.bfloat16).contiguous()
+    w = _lib.dense(weight.to(torch.bfloat16))
     cos, sin = _rope_tables(rope, x.device)
     rc = _lib.lib.hn_qk_norm_rope(_lib.ptr(x), x.stride(1), _lib.ptr(w), _lib.ptr(cos), _lib.ptr(sin), b, l, h, d,
                                   eps, _lib.ptr(y), _lib.stream_of(x))
@@ -100,7 +100,7 @@ def qk_norm_rope_kv(x, weight, rope=None, eps=1e-6, out=None):
             raise ValueError(f"qk_norm_rope_kv: out must be a contiguous bf16 [{b}, {l}, {h}, {d}] tensor")
     q = torch.empty((b, l, h, d), device=x.device, dtype=torch.int8)
     s = torch.empty((b, l, h, 1), device=x.device, dtype=torch.float32)
-    w = weight.to(torch.bfloat16).contiguous()
+    w = _lib.dense(weight.to(torch.bfloat16))
     cos, sin = _rope_tables(rope, x.device)
     rc = _lib.lib.hn_qk_norm_rope_kv(_lib.ptr(x), x.stride(1), _lib.ptr(w), _lib.ptr(cos), _lib.ptr(sin), b, l, h, d,
                                      eps, _lib.ptr(y), _lib.ptr(q), _lib.ptr(s), _lib.stream_of(x))
@@ -116,7 +116,7 @@ def qk_norm_rope2(q, k, weight_q, weight_k, rope=None, eps=1e-6, out=None):
     b, l, h, d = q.shape
     q, k = _qk_input(q), _qk_input(k)
     if q.stride(1) != k.stride(1):
-        q, k = q.contiguous(), k.contiguous()
+        q, k = _lib.dense(q), _lib.dense(k)
     if out is None:
         yq = torch.empty((b, l, h, d), device=q.device, dtype=torch.bfloat16)
         yk = torch.empty_like(yq)
@@ -125,8 +125,8 @@ def qk_norm_rope2(q, k, weight_q, weight_k, rope=None, eps=1e-6, out=None):
         for y in (yq, yk):
             if y.shape != (b, l, h, d) or y.dtype != torch.bfloat16 or not y.is_contiguous() or y.device != q.device:
                 raise ValueError(f"qk_norm_rope2: out tensors must be contiguous bf16 [{b}, {l}, {h}, {d}]")
-    wq = weight_q.to(torch.bfloat16).contiguous()
-    wk = weight_k.to(torch.bfloat16).contiguous()
+    wq = _lib.dense(weight_q.to(torch.bfloat16))
+    wk = _lib.dense(weight_k.to(torch.bfloat16))
     cos, sin = _rope_tables(rope, q.device)
     rc = _lib.lib.hn_qk_norm_rope2(_lib.ptr(q), _lib.ptr(k), q.stride(1), _lib.ptr(wq), _lib.ptr(wk), _lib.ptr(cos),
                                    _lib.ptr(sin), b, l, h, d, eps, _lib.ptr(yq), _lib.ptr(yk), _lib.stream_of(q))
@@ -139,7 +139,7 @@ def gated_residual(x, y, gate):
     _lib.require_cuda(x, y, gate)
     _bf16(x, y, gate)
     b, l, d = x.shape
-    x, y, gate = x.contiguous(), y.contiguous(), gate.contiguous()
+    x, y, gate = _lib.dense(x), _lib.dense(y), _lib.dense(gate)
     out = torch.empty(x.shape, device=x.device, dtype=x.dtype)
     rc = _lib.lib.hn_gated_residual(_lib.ptr(x), _lib.ptr(y), _lib.ptr(gate), b, l, d, _lib.ptr(out),
                                     _lib.stream_of(x))
@@ -152,8 +152,8 @@ def gated_residual_adaln_quant(x, y, gate, shift, scale, eps=1e-6):
     _lib.require_cuda(x, y, gate, shift, scale)
     _bf16(x, y, gate, shift, scale)
     b, l, d = x.shape
-    x, y, gate = x.contiguous(), y.contiguous(), gate.contiguous()
-    shift, scale = shift.contiguous(), scale.contiguous()
+    x, y, gate = _lib.dense(x), _lib.dense(y), _lib.dense(gate)
+    shift, scale = _lib.dense(shift), _lib.dense(scale)
     out = torch.empty(x.shape, device=x.device, dtype=x.dtype)
     q = torch.empty((b * l, d), device=x.device, dtype=torch.int8)
     s, srs, sgs = _lib.group_scales(b * l, d // 128, x.device)
@@ -172,12 +172,12 @@ def pixelumm_qk(x, weight_t, weight_hw, cos, sin, eps=1e-6):
     if b != 1:
         raise ValueError("pixelumm_qk: batch must be 1 (the decoder's layout)")
     if x.stride(3) != 1 or x.stride(2) != d or x.stride(1) % 4 or x.data_ptr() % 8:
-        x = x.contiguous()
+        x = _lib.dense(x)
     y = torch.empty((b, n, h, d), device=x.device, dtype=torch.bfloat16)
-    wt = weight_t.to(torch.bfloat16).contiguous()
-    whw = weight_hw.to(torch.bfloat16).contiguous()
-    cos = cos.to(torch.float32).contiguous()
-    sin = sin.to(torch.float32).contiguous()
+    wt = _lib.dense(weight_t.to(torch.bfloat16))
+    whw = _lib.dense(weight_hw.to(torch.bfloat16))
+    cos = _lib.dense(cos.to(torch.float32))
+    sin = _lib.dense(sin.to(torch.float32))
     rc = _lib.lib.hn_pixelumm_qk(_lib.ptr(x), x.stride(1), _lib.ptr(wt), _lib.ptr(whw), _lib.ptr(cos), _lib.ptr(sin),
                                  n, h, d, eps, _lib.ptr(y), _lib.stream_of(x))
     _lib.check(rc, "pixelumm_qk")

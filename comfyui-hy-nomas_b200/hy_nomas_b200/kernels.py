@@ -34,7 +34,7 @@ def quantize_activations(x, kind="int8", per_token=False, round_half_even=False)
     if x.dtype not in (torch.bfloat16, torch.float16, torch.float32):
         x = x.float()
     if not _aligned(x):
-        x = x.contiguous()
+        x = _lib.dense(x)
     dtype = torch.int8 if kind == "int8" else torch.float8_e4m3fn
     q = torch.empty((m, k), device=x.device, dtype=dtype)
     if per_token:
@@ -82,11 +82,11 @@ def block_gemm(qa, sa, qw, sw, bias=None, out_dtype=torch.bfloat16, kind="int8",
     if sw.dtype != torch.float32:
         sw = sw.float()
     if not _aligned(qa):
-        qa = qa.contiguous()
+        qa = _lib.dense(qa)
     if not _aligned(qw):
-        qw = qw.contiguous()
+        qw = _lib.dense(qw)
     if bias is not None and (bias.stride(0) != 1 or bias.data_ptr() % 16):
-        bias = bias.contiguous()
+        bias = _lib.dense(bias)
     if mode == 2:
         if out is not None:
             raise ValueError("block_gemm: `out` is not supported with epilogue 'gelu_quant'")
@@ -120,7 +120,7 @@ def adaln_quant(x, shift, scale, eps=1e-6):
     b, l, d = x.shape
     if x.dtype != torch.bfloat16 or shift.dtype != torch.bfloat16 or scale.dtype != torch.bfloat16:
         raise TypeError("adaln_quant: x, shift and scale must be bf16")
-    x, shift, scale = x.contiguous(), shift.contiguous(), scale.contiguous()
+    x, shift, scale = _lib.dense(x), _lib.dense(shift), _lib.dense(scale)
     q = torch.empty((b * l, d), device=x.device, dtype=torch.int8)
     s, srs, sgs = _lib.group_scales(b * l, d // GROUP, x.device)
     rc = _lib.lib.hn_adaln_quant(_lib.ptr(x), _lib.ptr(shift), _lib.ptr(scale), b, l, d, eps, _lib.ptr(q),
@@ -135,8 +135,6 @@ def block_linear(x, qw, sw, bias=None, kind="int8"):
     _lib.require_cuda(x)
     shape = x.shape
     x2 = x.reshape(-1, shape[-1])
-    if not x2.is_contiguous():
-        x2 = x2.contiguous()
     if shape[-1] % GROUP or x2.shape[0] == 0:
         from .ops import dequantize_g128
         return torch.nn.functional.linear(x, dequantize_g128(qw, sw, x.dtype), bias)

@@ -25,7 +25,7 @@ def quantize_g128(weight):
     w = weight.float()
     if k % GROUP:
         w = F.pad(w, (0, groups * GROUP - k))
-    w = w.contiguous()
+    w = _lib.dense(w)
     q = torch.empty((n, groups * GROUP), device=w.device, dtype=torch.int8)
     s, srs, sgs = _lib.group_scales(n, groups, w.device)
     rc = _lib.lib.hn_quant_act(_lib.ptr(w), w.stride(0), _lib.DTYPE[torch.float32], n, groups * GROUP,
@@ -50,7 +50,7 @@ def quantize_fp8_block(weight):
     _lib.require_cuda(weight)
     n, k = weight.shape
     w = weight if weight.dtype in (torch.float32, torch.bfloat16) else weight.float()
-    w = w.contiguous()
+    w = _lib.dense(w)
     q = torch.empty((n, k), device=w.device, dtype=torch.float8_e4m3fn)
     s = torch.empty((n // 128, k // 128), device=w.device, dtype=torch.float32)
     rc = _lib.lib.hn_quantize_fp8_block(_lib.ptr(w), _lib.DTYPE[w.dtype], n, k, _lib.ptr(q), _lib.ptr(s),

@@ -23,11 +23,14 @@ HEAD_CHUNKS = 1
 
 class SequenceParallel:
     """`head_chunks` > 1 splits each block's K/V gathers and attention by heads, so that a chunk's attention runs
-    while the next chunk's K is still being gathered (every head's arithmetic is unchanged)."""
+    while the next chunk's K is still being gathered (every head's arithmetic is unchanged). `local=True` is a
+    partition of one rank even inside a process group: the whole sequence on this process, no exchange."""
 
-    def __init__(self, group=None, head_chunks=None):
+    def __init__(self, group=None, head_chunks=None, local=False):
         self.group = group
-        if dist.is_available() and dist.is_initialized():
+        if local:
+            self.world, self.rank = 1, 0
+        elif dist.is_available() and dist.is_initialized():
             self.world = dist.get_world_size(group)
             self.rank = dist.get_rank(group)
         else:

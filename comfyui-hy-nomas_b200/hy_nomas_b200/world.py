@@ -16,7 +16,7 @@ def quantize_kv(x):
     if x.dtype != torch.bfloat16:
         raise TypeError(f"quantize_kv: bf16 input expected, got {x.dtype}")
     l, h, d = x.shape
-    x = x.contiguous()
+    x = _lib.dense(x)
     q = torch.empty((l, h, d), device=x.device, dtype=torch.int8)
     s = torch.empty((l, h, 1), device=x.device, dtype=torch.float32)
     rc = _lib.lib.hn_quantize_kv(_lib.ptr(x), l * h, d, _lib.ptr(q), _lib.ptr(s), _lib.stream_of(x))
@@ -31,8 +31,8 @@ def dequantize_kv(q, scale, dtype=torch.bfloat16):
         raise TypeError("dequantize_kv: the kernel writes bf16 (the reference's default dtype)")
     d = q.shape[-1]
     rows = q.numel() // d if d else 0
-    q = q.contiguous()
-    s = scale.to(torch.float32).contiguous()
+    q = _lib.dense(q)
+    s = _lib.dense(scale.to(torch.float32))
     if s.numel() != rows:
         raise ValueError(f"dequantize_kv: {s.numel()} scales for {rows} rows")
     y = torch.empty(q.shape, device=q.device, dtype=torch.bfloat16)

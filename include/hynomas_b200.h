@@ -77,15 +77,21 @@ int hn_abi_version(void);
 int hn_num_sms(void);
 
 /*
- * Leave `n` SMs without a GEMM CTA in later hn_block_gemm launches of this process (default 0), so that
- * kernels on other streams - the K/V all-gathers of sequence parallelism - run beside a GEMM instead of
- * after it. 0 <= n <= 64. No reference counterpart: the reference runs one GPU.
+ * Leave `n` SMs without a GEMM CTA in later hn_block_gemm launches (default 0), so that kernels on other
+ * streams - the K/V all-gathers of sequence parallelism - run beside a GEMM instead of after it.
+ * 0 <= n <= 64. The value is PROCESS-GLOBAL: it applies to every later hn_block_gemm call of every thread
+ * and device until it is set again, so a caller that changes it should put the old value
+ * (hn_get_gemm_sm_reserve) back when done. No reference counterpart: the reference runs one GPU.
  */
 int hn_set_gemm_sm_reserve(int n);
+int hn_get_gemm_sm_reserve(void);
 
 /*
- * Device error word written by bounded waits inside the kernels (0 = none). Synchronizes `stream`,
- * copies the word to *code_host and clears it. Returns HN_ERR_TIMEOUT if a wait timed out.
+ * Device error word of `stream`, written by bounded waits inside the kernels launched on that stream
+ * (0 = none). Synchronizes `stream`, copies its word to *code_host and clears it. Returns HN_ERR_TIMEOUT if
+ * a wait timed out. Each stream that launches a waiting kernel gets a word of its own, per device, up to 63
+ * streams; the NULL stream and any further streams share one word. Call it with the stream's device
+ * current.
  */
 int hn_device_error(void *stream, int *code_host);
 
@@ -126,14 +132,17 @@ int hn_quant_act(const void *x, int64_t ldx, int x_dtype, int64_t M, int64_t K, 
  * sw: sw_mode HN_SCALE_GROUP -> sw[n * sw_rs + g * sw_gs] | HN_SCALE_ROW -> sw[n * sw_rs] |
  *     HN_SCALE_BLOCK -> sw[(n / 128) * sw_rs + g * sw_gs] (one per 128 x 128 weight block).
  * Group scales with unit row stride (group-major) are streamed by bulk copies; others by plain loads.
- * bias: NULL or [N] of bias_dtype (bf16/fp16/fp32).
+ * bias: NULL or [N] of bias_dtype (bf16/fp16/fp32), 16-byte aligned.
  * epilogue HN_EPI_NONE: out [M, N] of out_dtype (bf16/fp16/fp32), ldo.
  *          HN_EPI_GELU: out bf16 = rbf16(gelu_tanh(rbf16(y))).
  *          HN_EPI_GELU_QUANT: out int8 [M, N] codes of the GELU output quantized per row and 128
  *                             columns, scales qs[m * qs_rs + c * qs_gs]. Needs N % 128 == 0.
  * out_dtype HN_DTYPE_INT32 (int8 kind, both scale modes HN_SCALE_ROW, no bias, HN_EPI_NONE): out is the
  * exact int32 accumulator sum_k qa*qw - the raw integer result, no scaling.
+ * int8 with HN_SCALE_ROW on both sides accumulates all of K in one int32 (|sum| <= K * 128 * 128), so it
+ * needs K <= HN_ROW_MODE_MAX_K; the per-group modes accumulate 128 columns at a time and have no such bound.
  */
+#define HN_ROW_MODE_MAX_K 130944
 int hn_block_gemm(const void *qa, int64_t lda, const float *sa, int64_t sa_rs, int64_t sa_gs, int sa_mode,
                   const void *qw, int64_t ldw, const float *sw, int64_t sw_rs, int64_t sw_gs, int sw_mode,
                   const void *bias, int bias_dtype,

@@ -16,7 +16,12 @@ them on the host cores as the CPU baseline. Nothing in the product imports this 
   fp8_block_*       hy_nomas/pixelumm.py:60-63, 77-82, 154-155
   quantize_kv       hy_nomas/world.py:83-90
   dit_block_cpu     hy_nomas/model.py:246-286 (DoubleStreamBlock image stream, the non-fused branch)
+  make_block_weights_cpu  seeded random int8 weights of one synthetic block (the benchmark's shapes), built
+                    here so that the CPU reference arm loads nothing of the product
 """
+import math
+from collections import namedtuple
+
 import torch
 import torch.nn.functional as F
 
@@ -145,3 +150,27 @@ def dit_block_cpu(x, vec, w, rope, heads, timings=None):
     h = _linear_per_channel(modulate(layer_norm(x), shift2, scale2).to(x.dtype), w.fc1)
     h = F.gelu(h, approximate="tanh")
     return x + _linear_per_channel(h, w.fc2) * gate2.unsqueeze(1)
+
+
+QLinearCPU = namedtuple("QLinearCPU", "q s bias")
+BlockWeightsCPU = namedtuple("BlockWeightsCPU", "mod qk v proj fc1 fc2 q_norm k_norm")
+_CODE_STD = math.sqrt((255.0 ** 2 - 1.0) / 12.0)   # std of an integer uniform on [-127, 127]
+
+
+def _qlinear_cpu(n, k, gen, gain=1.0):
+    """int8 codes uniform in [-127, 127], per-output-channel fp32 scales preserving the activations' variance,
+    bf16 bias N(0, 0.02): the distribution the benchmark's synthetic DiT uses."""
+    q = torch.randint(-127, 128, (n, k), generator=gen, dtype=torch.int8)
+    s = (torch.rand(n, generator=gen) + 0.5) * (gain / (_CODE_STD * math.sqrt(k)))
+    bias = (torch.randn(n, generator=gen) * 0.02).to(torch.bfloat16)
+    return QLinearCPU(q, s.float().contiguous(), bias)
+
+
+def make_block_weights_cpu(hidden, mlp, head_dim, gen):
+    """One block's linears ([6D, D] modulation, q|k [2D, D], v, proj, fc1 [mlp, D], fc2 [D, mlp]) and RMSNorm
+    weights (ones, as RMSNorm.__init__ makes them, hy_nomas/model.py:95), on the CPU."""
+    d = hidden
+    ones = torch.ones(head_dim, dtype=torch.bfloat16)
+    return BlockWeightsCPU(mod=_qlinear_cpu(6 * d, d, gen, gain=0.15), qk=_qlinear_cpu(2 * d, d, gen),
+                           v=_qlinear_cpu(d, d, gen), proj=_qlinear_cpu(d, d, gen), fc1=_qlinear_cpu(mlp, d, gen),
+                           fc2=_qlinear_cpu(d, mlp, gen), q_norm=ones, k_norm=ones.clone())

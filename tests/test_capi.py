@@ -40,7 +40,20 @@ def test_abi_version_and_no_device(hn):
 def test_gemm_sm_reserve_range(hn):
     L = hn.lib.lib
     assert L.hn_set_gemm_sm_reserve(-1) == 5 and L.hn_set_gemm_sm_reserve(65) == 5
-    assert L.hn_set_gemm_sm_reserve(16) == 0 and L.hn_set_gemm_sm_reserve(0) == 0
+    assert L.hn_set_gemm_sm_reserve(16) == 0 and L.hn_get_gemm_sm_reserve() == 16
+    assert L.hn_set_gemm_sm_reserve(0) == 0 and L.hn_get_gemm_sm_reserve() == 0
+
+
+def test_dense_realigns_misaligned_views(hn):
+    """A contiguous view at an odd offset keeps its pointer under .contiguous(); dense() copies it to an aligned
+    allocation, so the wrappers never hand the library a misaligned input."""
+    base = torch.arange(64, dtype=torch.bfloat16)
+    view = base[3:3 + 40]
+    assert view.is_contiguous() and view.data_ptr() % 16 != 0
+    d = hn.lib.dense(view)
+    assert d.data_ptr() % 16 == 0 and torch.equal(d, view)
+    aligned = base[8:48]
+    assert hn.lib.dense(aligned).data_ptr() == aligned.data_ptr()
 
 
 FAKE = ctypes.c_void_p(0x10000)   # never dereferenced: every call below fails validation first
@@ -71,6 +84,14 @@ def test_validation_errors_before_launch(hn):
     assert gemm(od=3) == 7                                         # int32 out needs row scales
     assert gemm(lda=100) == 1                                      # lda < K
     assert gemm(qa=ctypes.c_void_p(0x10004)) == 2                  # TMA base alignment
+    # a bias that does not start on a 16-byte boundary is refused for every N (the epilogue reads it with
+    # 16-byte loads wherever 8 columns are in range), also when N % 8 != 0
+    assert gemm(bias=ctypes.c_void_p(0x10002), N=200, ldo=256) == 2
+    assert gemm(bias=ctypes.c_void_p(0x10002), N=256) == 2
+    # int8 with per-row scales on both sides sums all of K in one int32: K * 128 * 128 must stay below 2^31
+    big_k = 130944 + 128
+    assert gemm(sam=1, swm=1, sars=1, swrs=1, K=big_k, lda=big_k, ldw=big_k) == 1
+    assert b"K <= 130944" in L.hn_last_error()
     assert L.hn_adaln_quant(FAKE, FAKE, FAKE, 1, 4, 200, 1e-6, FAKE, FAKE, 1, 1, None) == 1   # D % 128
     assert L.hn_qk_norm_rope(FAKE, 4096, FAKE, FAKE, None, 1, 4, 32, 128, 1e-6, FAKE, None) == 5  # cos w/o sin
     assert L.hn_qk_norm_rope(FAKE, 4096, FAKE, None, None, 1, 4, 32, 64, 1e-6, FAKE, None) == 7   # D != 128

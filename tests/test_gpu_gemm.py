@@ -174,3 +174,58 @@ def test_full_size_sampled_rows(hn, oracle, cuda):
     rows = torch.cat([rows, torch.tensor([0, m - 1])])
     ref = oracle.block_gemm(u8(qa[rows.to(cuda)]), f32(sa[rows.to(cuda)]), u8(qw), f32(sw))
     assert np.array_equal(f32(y[rows.to(cuda)]).view(np.uint32), ref.view(np.uint32))
+
+
+def _outlier_x(m, k, gen, device):
+    """x ~ N(0, 1) with 1% of the channels scaled x20 (benchmark config 1's activations)."""
+    x = torch.randn(m, k, generator=gen, device=device)
+    x[:, torch.randperm(k, generator=gen, device=device)[: max(1, k // 100)]] *= 20.0
+    return x.bfloat16()
+
+
+PIN_SHAPES = [(4096, 4096, 4096), (20240, 4096, 4096), (20240, 8192, 4096), (20240, 16384, 4096),
+              (20240, 4096, 16384)]
+
+
+@pytest.mark.parametrize("m,n,k", PIN_SHAPES)
+def test_benchmarked_modes_pinned_to_reference_layout(hn, cuda, m, n, k):
+    """The DiT and the bench run two scale layouts the reference does not have: per-output-channel weight scales
+    [N] with the reference's per-(token, 128) activation scales (the DiT's linears), and per-token activation
+    scales [M] with per-channel weights (benchmark config 1's wording). Their promotion orders differ from the
+    reference's sum over groups of p_g * sa * sw (hy_nomas/kernels.py:104-120), so each is held, at config-1 and
+    DiT shapes, to the north star's int8 bound against the reference-layout path (group scales [N, K/128] and
+    [M, K/128], the mode pinned to the reference's golden vectors) run on the same codes with the same scales
+    broadcast: rel-L2 <= 2e-3 on the bf16 output. The integer partials are exact at these sizes too: the raw
+    int32 accumulator and the per-group partials summed with unit scales equal cuBLASLt's int8 GEMM."""
+    gen = torch.Generator(device=cuda).manual_seed(m + 7 * n + 3 * k)
+    g = k // 128
+    x = _outlier_x(m, k, gen, cuda)
+    qw = torch.randint(-127, 128, (n, k), generator=gen, device=cuda, dtype=torch.int8)
+    sw_c = torch.rand(n, generator=gen, device=cuda) * 4e-3 + 1e-3
+    sw_g = sw_c[:, None].expand(n, g).contiguous()
+    bias = (torch.randn(n, generator=gen, device=cuda) * 0.02).bfloat16()
+    K = hn.kernels
+
+    def compare(y, ref, what):
+        err = rel_l2(f32(y), f32(ref))
+        mism = (y.view(torch.int16) != ref.view(torch.int16)).float().mean().item()
+        print(f"{what} {m}x{n}x{k}: rel-L2 {err:.2e}, bf16 elements differing {mism:.2%}")
+        assert err <= 2e-3, (what, err)
+
+    # per-(token, 128) activations x per-channel weights (the DiT) vs x group weights [N, K/128]
+    qa, sa = K.quantize_activations(x)
+    compare(K.block_gemm(qa, sa, qw, sw_c, bias), K.block_gemm(qa, sa, qw, sw_g, bias), "a_group x w_channel")
+    # per-token activations x per-channel weights (config 1's wording) vs both broadcast to the group layout
+    qt, st = K.quantize_activations(x, per_token=True)
+    compare(K.block_gemm(qt, st, qw, sw_c, bias), K.block_gemm(qt, st.expand(m, g).contiguous(), qw, sw_g, bias),
+            "a_token x w_channel")
+    no_device_error(hn)
+    # exact integer partials at full size
+    ref = torch._int_mm(qt, qw.t())
+    raw = K.block_gemm(qt, torch.ones(m, device=cuda), qw, torch.ones(n, device=cuda), out_dtype=torch.int32)
+    assert torch.equal(raw, ref)
+    ref = torch._int_mm(qa, qw.t())
+    assert ref.abs().max().item() < 2 ** 24      # every partial sum of the fp32 promotion is then an exact integer
+    unit = K.block_gemm(qa, torch.ones(m, g, device=cuda), qw, torch.ones(n, g, device=cuda), out_dtype=torch.float32)
+    assert torch.equal(unit, ref.float())
+    no_device_error(hn)
