@@ -136,6 +136,27 @@ struct StreamDevice {
     StreamDevice &operator=(const StreamDevice &) = delete;
 };
 
+// The data must live on the launch device: the library enables no peer access, and a kernel handed another
+// device's (or host) memory would fault. Checked on each call's main input before anything is launched.
+static int check_pointer_device(const void *p, const char *what) {
+    cudaPointerAttributes at;
+    cudaError_t e = cudaPointerGetAttributes(&at, p);
+    if (e != cudaSuccess) {
+        cudaGetLastError();
+        return fail(HN_ERR_ARG, "%s: %p is not memory CUDA knows (%s)", what, p, cudaGetErrorString(e));
+    }
+    int dev = -1;
+    e = cudaGetDevice(&dev);
+    if (e != cudaSuccess) return cuda_fail(e, "cudaGetDevice");
+    if (at.type == cudaMemoryTypeManaged) return HN_OK;
+    if (at.type != cudaMemoryTypeDevice)
+        return fail(HN_ERR_ARG, "%s: %p is not device memory", what, p);
+    if (at.device != dev)
+        return fail(HN_ERR_ARG, "%s: the data is on device %d but the launch device is %d (pass a stream of the "
+                    "data's device, or make that device current for the NULL stream)", what, at.device, dev);
+    return HN_OK;
+}
+
 static int launched(cudaError_t e, const char *what) {
     if (e != cudaSuccess) return cuda_fail(e, what);
     t_last_error.clear();
@@ -146,7 +167,16 @@ static int launched(cudaError_t e, const char *what) {
 
 using namespace hn;
 
-// the stream's device made current for the rest of the entry point, then the architecture check on it
+// the stream's device made current for the rest of the entry point, then the architecture check on it, and
+// the check that the main input `ptr` lives on it
+#define CHECK_DEVICE(ptr)                                                                   \
+    StreamDevice _stream_device(stream);                                                    \
+    if (_stream_device.err != cudaSuccess) return cuda_fail(_stream_device.err, "cudaStreamGetDevice"); \
+    do {                                                                                    \
+        int _rc = check_arch();                                                             \
+        if (_rc == HN_OK) _rc = check_pointer_device((ptr), __func__);                      \
+        if (_rc != HN_OK) return _rc;                                                       \
+    } while (0)
 #define CHECK_ARCH()                                                                        \
     StreamDevice _stream_device(stream);                                                    \
     if (_stream_device.err != cudaSuccess) return cuda_fail(_stream_device.err, "cudaStreamGetDevice"); \
@@ -223,7 +253,7 @@ int hn_quant_act(const void *x, int64_t ldx, int x_dtype, int64_t M, int64_t K, 
     REQUIRE(al16(x) && (ldx * dsize(x_dtype)) % 16 == 0 && al16(q) && ldq % 16 == 0, HN_ERR_ALIGN,
             "hn_quant_act: x/q must be 16-byte aligned with 16-byte row pitch");
     if (M == 0) return HN_OK;
-    CHECK_ARCH();
+    CHECK_DEVICE(x);
     return launched(launch_quant_act(x, ldx, x_dtype, M, K, kind, flags, q, ldq, s, s_rs, s_gs, (cudaStream_t)stream),
                     "hn_quant_act launch");
 }
@@ -274,7 +304,7 @@ int hn_block_gemm(const void *qa, int64_t lda, const float *sa, int64_t sa_rs, i
     // the epilogue reads the bias 8 columns at a time with 16-byte loads wherever 8 columns are in range
     if (bias) REQUIRE(al16(bias), HN_ERR_ALIGN, "hn_block_gemm: bias must be 16-byte aligned");
     if (M == 0) return HN_OK;
-    CHECK_ARCH();
+    CHECK_DEVICE(qa);
     GemmArgs a;
     a.qa = qa; a.lda = lda; a.sa = sa; a.sa_rs = sa_rs; a.sa_gs = sa_gs; a.sa_mode = sa_mode;
     a.qw = qw; a.ldw = ldw; a.sw = sw; a.sw_rs = sw_rs; a.sw_gs = sw_gs; a.sw_mode = sw_mode;
@@ -306,7 +336,7 @@ int hn_adaln_quant(const void *x, const void *shift, const void *scale, int64_t 
     REQUIRE(q && s && al16(q), HN_ERR_ARG, "hn_adaln_quant: null or misaligned output");
     REQUIRE(scale_strides_ok(B * L, D / 128, s_rs, s_gs), HN_ERR_SHAPE, "hn_adaln_quant: scale strides overlap");
     if (L == 0) return HN_OK;
-    CHECK_ARCH();
+    CHECK_DEVICE(x);
     return launched(launch_ln_row(1, x, nullptr, nullptr, shift, scale, B, L, D, eps, nullptr, q, s, s_rs, s_gs,
                                   (cudaStream_t)stream),
                     "hn_adaln_quant launch");
@@ -318,7 +348,7 @@ int hn_adaln(const void *x, const void *shift, const void *scale, int64_t B, int
     if (rc) return rc;
     REQUIRE(y && al16(y), HN_ERR_ARG, "hn_adaln: null or misaligned output");
     if (L == 0) return HN_OK;
-    CHECK_ARCH();
+    CHECK_DEVICE(x);
     return launched(launch_ln_row(0, x, nullptr, nullptr, shift, scale, B, L, D, eps, y, nullptr, nullptr, 0, 0,
                                   (cudaStream_t)stream),
                     "hn_adaln launch");
@@ -335,7 +365,7 @@ int hn_gated_residual_adaln_quant(const void *x, const void *y, const void *gate
     REQUIRE(scale_strides_ok(B * L, D / 128, s_rs, s_gs), HN_ERR_SHAPE,
             "hn_gated_residual_adaln_quant: scale strides overlap");
     if (L == 0) return HN_OK;
-    CHECK_ARCH();
+    CHECK_DEVICE(x);
     return launched(launch_ln_row(2, x, y, gate, shift, scale, B, L, D, eps, out, q, s, s_rs, s_gs, (cudaStream_t)stream),
                     "hn_gated_residual_adaln_quant launch");
 }
@@ -346,7 +376,7 @@ int hn_gated_residual(const void *x, const void *y, const void *gate, int64_t B,
     REQUIRE(B > 0 && L >= 0 && D > 0 && D % 8 == 0, HN_ERR_SHAPE, "hn_gated_residual: need D %% 8 == 0");
     REQUIRE(al16(x) && al16(y) && al16(gate) && al16(out), HN_ERR_ALIGN, "hn_gated_residual: buffers must be 16-byte aligned");
     if (L == 0) return HN_OK;
-    CHECK_ARCH();
+    CHECK_DEVICE(x);
     return launched(launch_gated_residual(x, y, gate, B, L, D, out, (cudaStream_t)stream), "hn_gated_residual launch");
 }
 
@@ -367,7 +397,7 @@ int hn_qk_norm_rope(const void *x, int64_t row_stride, const void *weight, const
     int rc = qk_common(x, row_stride, weight, cos, sin, B, L, H, D, y);
     if (rc) return rc;
     if (L == 0) return HN_OK;
-    CHECK_ARCH();
+    CHECK_DEVICE(x);
     return launched(launch_qk_norm_rope(1, x, nullptr, row_stride, weight, nullptr, cos, sin, B, L, H, eps, y, nullptr,
                                         nullptr, nullptr, (cudaStream_t)stream),
                     "hn_qk_norm_rope launch");
@@ -381,7 +411,7 @@ int hn_qk_norm_rope_kv(const void *x, int64_t row_stride, const void *weight, co
     REQUIRE(q && s, HN_ERR_ARG, "hn_qk_norm_rope_kv: null pointer");
     REQUIRE(al16(q) && (reinterpret_cast<uintptr_t>(s) & 3) == 0, HN_ERR_ALIGN, "hn_qk_norm_rope_kv: misaligned buffer");
     if (L == 0) return HN_OK;
-    CHECK_ARCH();
+    CHECK_DEVICE(x);
     return launched(launch_qk_norm_rope(1, x, nullptr, row_stride, weight, nullptr, cos, sin, B, L, H, eps, y, nullptr,
                                         q, s, (cudaStream_t)stream),
                     "hn_qk_norm_rope_kv launch");
@@ -395,7 +425,7 @@ int hn_qk_norm_rope2(const void *xq, const void *xk, int64_t row_stride, const v
     rc = qk_common(xk, row_stride, wk, cos, sin, B, L, H, D, yk);
     if (rc) return rc;
     if (L == 0) return HN_OK;
-    CHECK_ARCH();
+    CHECK_DEVICE(xq);
     return launched(launch_qk_norm_rope(2, xq, xk, row_stride, wq, wk, cos, sin, B, L, H, eps, yq, yk, nullptr, nullptr,
                                         (cudaStream_t)stream),
                     "hn_qk_norm_rope2 launch");
@@ -409,7 +439,7 @@ int hn_pixelumm_qk(const void *x, int64_t row_stride, const void *weight_t, cons
     REQUIRE(al8(x) && row_stride % 4 == 0 && al8(weight_t) && al8(weight_hw) && al16(cos) && al16(sin) && al8(y),
             HN_ERR_ALIGN, "hn_pixelumm_qk: misaligned buffer");
     if (N == 0) return HN_OK;
-    CHECK_ARCH();
+    CHECK_DEVICE(x);
     return launched(launch_pixelumm_qk(x, row_stride, weight_t, weight_hw, cos, sin, N, H, eps, y, (cudaStream_t)stream),
                     "hn_pixelumm_qk launch");
 }
@@ -425,7 +455,7 @@ int hn_dequantize_kv(const int8_t *q, const float *s, int64_t rows, int64_t D, v
     REQUIRE(al16(q) && al16(y) && (reinterpret_cast<uintptr_t>(s) & 3) == 0, HN_ERR_ALIGN,
             "hn_dequantize_kv: misaligned buffer");
     if (rows == 0) return HN_OK;
-    CHECK_ARCH();
+    CHECK_DEVICE(q);
     return launched(launch_dequant_kv(q, s, rows, D, y, (cudaStream_t)stream), "hn_dequantize_kv launch");
 }
 
@@ -438,7 +468,7 @@ int hn_quantize_fp8_block(const void *w, int w_dtype, int64_t N, int64_t K, void
     REQUIRE(N / 128 <= 65535 && K / 128 <= 0x7fffffffLL, HN_ERR_SHAPE, "hn_quantize_fp8_block: too large");
     REQUIRE(al16(w) && al16(q) && (reinterpret_cast<uintptr_t>(s) & 3) == 0, HN_ERR_ALIGN, "hn_quantize_fp8_block: misaligned buffer");
     if (N == 0 || K == 0) return HN_OK;
-    CHECK_ARCH();
+    CHECK_DEVICE(w);
     return launched(launch_quant_fp8_block(w, w_dtype, N, K, q, s, (cudaStream_t)stream), "hn_quantize_fp8_block launch");
 }
 

@@ -36,10 +36,8 @@
 //
 // Promotion arithmetic (the CPU oracle evaluates the same):
 //   PMODE 0 (sw per row x group):  t = RN(p * sa[m,g]);  acc = fma(t, sw[n,g], acc)
-//   PMODE 1 (sw per row or block):  s = sa[m,g] (sw per row, applied at the end) or s = RN(sa[m,g] *
-//                                   swb[n/128,g]) (128x128 weight blocks); fp8: acc = fma(p, s, acc); int8, with
-//                                   O = 1.5 * 2^23: acc = fma(O + p, s, acc) for even g, fma(O - p, -s, acc) for
-//                                   odd g, then acc = fma(-O, c, acc) with c = RN(...RN(RN(s_0 - s_1) + s_2)...)
+//   PMODE 1 (sw per row or block):  acc = fma(p, s, acc) with s = sa[m,g] (sw per row, applied at the end)
+//                                   or s = RN(sa[m,g] * swb[n/128,g]) (128x128 weight blocks)
 //   PMODE 2 (both per row):         one accumulator over all K; y = RN(RN(float(D) * sa[m]) * sw[n])
 //
 // Every wait on an mbarrier is bounded (globaltimer); on expiry the kernel records HN_DEVERR_TIMEOUT,
@@ -290,27 +288,17 @@ __device__ __forceinline__ void promote_gen(uint64_t &acc, uint32_t p0, uint32_t
             : "+l"(acc)
             : "r"(p0), "r"(p1), "l"(sa2), "l"(sw2));
 }
-// acc = fma(conv(p), s2, acc)     (PMODE 1; fp8 partials are fp32 already)
-// int8: the conversion offset stays in: an even group adds RN((O + p) * s) - exact O + p, O = 1.5 * 2^23, the
-// integer's bits + 0x4B400000 read as a float - and an odd group RN((O - p) * -s), s2 = (-s, -s), so that the
-// offsets alternate in sign (O * (s_0 - s_1 + s_2 - ...)) and leave once per tile (offset_out); one integer op
-// and half a packed fma per output and group
-template <int KIND, int ODD>
+// acc = fma(conv(p), s2, acc)     (PMODE 1)
+template <int KIND>
 __device__ __forceinline__ void promote_row(uint64_t &acc, uint32_t p0, uint32_t p1, uint64_t s2) {
-    if (KIND == 0 && ODD == 0)
+    if (KIND == 0)
         asm("{\n\t.reg .b32 a, b;\n\t.reg .b64 f;\n\t"
             "add.s32 a, %1, 0x4B400000;\n\tadd.s32 b, %2, 0x4B400000;\n\t"
             "mov.b64 f, {a, b};\n\t"
+            "add.rn.f32x2 f, f, %4;\n\t"
             "fma.rn.f32x2 %0, f, %3, %0;\n\t}"
             : "+l"(acc)
-            : "r"(p0), "r"(p1), "l"(s2));
-    else if (KIND == 0)
-        asm("{\n\t.reg .b32 a, b;\n\t.reg .b64 f;\n\t"
-            "sub.s32 a, %4, %1;\n\tsub.s32 b, %4, %2;\n\t"
-            "mov.b64 f, {a, b};\n\t"
-            "fma.rn.f32x2 %0, f, %3, %0;\n\t}"
-            : "+l"(acc)
-            : "r"(p0), "r"(p1), "l"(s2), "r"(0x4B400000u));
+            : "r"(p0), "r"(p1), "l"(s2), "l"(pk(-12582912.0f, -12582912.0f)));
     else
         asm("{\n\t.reg .b64 f;\n\t"
             "mov.b64 f, {%1, %2};\n\t"
@@ -657,8 +645,6 @@ __global__ void __launch_bounds__(128 + 128 * NP, 1)
                 uint64_t acc[CPT / 2];
 #pragma unroll
                 for (int i = 0; i < CPT / 2; ++i) acc[i] = 0ull;
-                // int8 row-scale mode: s_0 - s_1 + s_2 - ... of this row's scales, for the conversion offsets
-                float offset_sum = 0.0f;
                 const float sa_row = (p.sa_mode == 1) ? p.sa[(int64_t)mm * p.sa_rs] : 0.0f;
                 for (int g0 = 0; g0 < G; g0 += 2) {
                     // one pair of K groups: its scales (pair slot ps) and its two accumulators (TMEM pair tb)
@@ -696,10 +682,7 @@ __global__ void __launch_bounds__(128 + 128 * NP, 1)
                         }
                         const float *ring = sw_s + (2 * slot + gi) * C::RING_FLOATS;
                         const float s_g = (PMODE == 1) ? s_pair[gi] : ((p.sa_mode == 0) ? ring[C::RING_SA + row] : sa_row);
-                        // (int8 row-scale mode) an odd group's multiplier is -s: see promote_row
-                        const float s_m = (KIND == 0 && PMODE == 1 && gi == 1) ? -s_g : s_g;
-                        if (KIND == 0 && PMODE == 1) offset_sum = __fadd_rn(offset_sum, s_m);
-                        const uint64_t s2 = pk(s_m, s_m);
+                        const uint64_t s2 = pk(s_g, s_g);
                         const float *sws = ring + C::RING_SW + hf * CPT;
 #pragma unroll
                         for (int j = 0; j < CPT; j += 4) {
@@ -707,12 +690,9 @@ __global__ void __launch_bounds__(128 + 128 * NP, 1)
                                 const float4 w4 = *reinterpret_cast<const float4 *>(sws + j);
                                 promote_gen<KIND>(acc[j / 2], r[j], r[j + 1], s2, pk(w4.x, w4.y));
                                 promote_gen<KIND>(acc[j / 2 + 1], r[j + 2], r[j + 3], s2, pk(w4.z, w4.w));
-                            } else if (gi == 0) {
-                                promote_row<KIND, 0>(acc[j / 2], r[j], r[j + 1], s2);
-                                promote_row<KIND, 0>(acc[j / 2 + 1], r[j + 2], r[j + 3], s2);
                             } else {
-                                promote_row<KIND, 1>(acc[j / 2], r[j], r[j + 1], s2);
-                                promote_row<KIND, 1>(acc[j / 2 + 1], r[j + 2], r[j + 3], s2);
+                                promote_row<KIND>(acc[j / 2], r[j], r[j + 1], s2);
+                                promote_row<KIND>(acc[j / 2 + 1], r[j + 2], r[j + 3], s2);
                             }
                         }
                     }
@@ -722,12 +702,6 @@ __global__ void __launch_bounds__(128 + 128 * NP, 1)
                     if (++slot == SW_SLOTS / 2) { slot = 0; sphase ^= 1; }
                 }
                 if (!ok) break;
-                if (KIND == 0 && PMODE == 1) {
-                    // the conversion offsets out: acc = fma(-O, s_0 - s_1 + ..., acc), one rounding
-                    const uint64_t no = pk(-12582912.0f, -12582912.0f), os = pk(offset_sum, offset_sum);
-#pragma unroll
-                    for (int i = 0; i < CPT / 2; ++i) acc[i] = x2_fma(no, os, acc[i]);
-                }
                 float v[CPT];
 #pragma unroll
                 for (int i = 0; i < CPT / 2; ++i) { v[2 * i] = acc_lo(acc[i]); v[2 * i + 1] = acc_hi(acc[i]); }
@@ -952,6 +926,7 @@ static cudaError_t launch_epi(int epi, const CUtensorMap &ma, const CUtensorMap 
 
 cudaError_t launch_block_gemm(const GemmArgs &a, cudaStream_t st, const char **msg) {
     using namespace gemm;
+    if (gemv_applies(a)) return launch_gemv(a, st);
     int *err = nullptr;
     cudaError_t ee = device_error_word(err_slot(st), &err);
     if (ee != cudaSuccess) return ee;

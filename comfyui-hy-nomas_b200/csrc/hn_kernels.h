@@ -57,6 +57,12 @@ struct GemmArgs {
 // Returns cudaSuccess, or cudaErrorInvalidValue with *msg set when a TMA descriptor cannot be encoded.
 cudaError_t launch_block_gemm(const GemmArgs &a, cudaStream_t st, const char **msg);
 
+// int8 calls with at most GEMV_MAX_M activation rows (epilogue none or gelu, weight scales per row or per row x
+// group) run as a weight-streaming GEMV (gemv.cu) with the tile kernel's arithmetic
+constexpr int GEMV_MAX_M = 8;
+bool gemv_applies(const GemmArgs &a);
+cudaError_t launch_gemv(const GemmArgs &a, cudaStream_t st);
+
 cudaError_t launch_wait_selftest(uint32_t timeout_us, cudaStream_t st);
 
 // read slot `slot` of the current device's error words into *value and clear it (synchronous)

@@ -47,6 +47,33 @@ SIGNATURES = {
 }
 
 
+class StreamArg(ctypes.c_void_p):
+    """A cudaStream_t argument that also carries the device of the tensors the call is for."""
+    device = None
+
+
+class _Library:
+    """The loaded library; an entry point whose last argument is a StreamArg runs with that stream's device
+    current. The library itself makes a non-NULL stream's device current, but torch's default stream is the
+    legacy NULL stream, which stands for the current device whichever it is."""
+
+    def __init__(self, cdll):
+        self._cdll = cdll
+
+    def __getattr__(self, name):
+        fn = getattr(self._cdll, name)
+
+        def call(*args):
+            s = args[-1] if args else None
+            if isinstance(s, StreamArg) and s.device is not None and s.device != torch.cuda.current_device():
+                with torch.cuda.device(s.device):
+                    return fn(*args)
+            return fn(*args)
+        call.__name__ = name
+        setattr(self, name, call)
+        return call
+
+
 def _load():
     if not os.path.exists(LIB_PATH):
         raise ImportError(f"{LIB_PATH} is missing: build it with `python -m hy_nomas_b200.build` "
@@ -58,7 +85,7 @@ def _load():
         fn = getattr(lib, name)
         fn.argtypes = args
         fn.restype = ctypes.c_int
-    return lib
+    return _Library(lib)
 
 
 lib = _load()
@@ -91,8 +118,10 @@ def dense(t):
 
 
 def stream_of(t):
-    """torch's current stream on the tensor's device, as a cudaStream_t value."""
-    return ctypes.c_void_p(torch.cuda.current_stream(t.device).cuda_stream)
+    """torch's current stream on the tensor's device, as a cudaStream_t value that remembers that device."""
+    s = StreamArg(torch.cuda.current_stream(t.device).cuda_stream)
+    s.device = t.device.index
+    return s
 
 
 def require_cuda(*tensors):
@@ -121,6 +150,7 @@ def scale_strides(s):
 def device_error(stream=None):
     """Synchronize `stream` and return (and clear) the device error word of the bounded waits."""
     code = ctypes.c_int(0)
-    s = ctypes.c_void_p(stream.cuda_stream if stream is not None else torch.cuda.current_stream().cuda_stream)
-    rc = lib.hn_device_error(s, ctypes.byref(code))
+    stream = stream if stream is not None else torch.cuda.current_stream()
+    with torch.cuda.device(stream.device):     # a NULL stream means the current device: make it the stream's
+        rc = lib.hn_device_error(ctypes.c_void_p(stream.cuda_stream), ctypes.byref(code))
     return rc, code.value

@@ -201,12 +201,8 @@ void or_quantize_fp8_block(const float *w, int64_t N, int64_t K, uint8_t *q, flo
  *   sa group, sw group (kernels.py:115):      t = RN(part*sa[m,g]); acc = fma(t, sw[n,g], acc)
  *        (fma == 0: acc = RN(acc + RN(t*sw[n,g])), the interpreter's / torch's separate roundings)
  *   sa row,   sw group: as above with sa[m,g] = sa[m]
- *   sa group, sw row:  s = sa[m,g]; sa any, sw block: s = RN(sa[m,g] * swb[n/128,g]); then
- *      e4m3: acc = fma(part, s, acc)
- *      int8: the kernel's conversion offset O = 1.5 * 2^23 stays in the product, with alternating sign:
- *            acc = fma(O + part, s, acc) for even g, acc = fma(O - part, -s, acc) for odd g (O +- part exact),
- *            c = RN(c + s) / RN(c - s) likewise, and after the last group acc = fma(-O, c, acc)
- *      sw row: at the end acc = RN(acc * sw[n])
+ *   sa group, sw row:  acc = fma(part, sa[m,g], acc); at the end acc = RN(acc * sw[n])
+ *   sa any,   sw block: acc = fma(part, RN(sa[m,g] * swb[n/128,g]), acc)
  *   sa row,   sw row:  whole-K dot D (int32 exact for int8); acc = RN(RN(RN32(D) * sa[m]) * sw[n])
  * then acc = RN(acc + bias[n]) and the epilogue:
  *   0: out = acc;  1: h = rbf16(gelu(rbf16(acc)));  2: h as in 1, then int8 per row and 128 columns
@@ -235,8 +231,6 @@ void or_block_gemm(const uint8_t *qa, const float *sa, int sa_mode, const uint8_
                 }
                 acc = (d * sa[m]) * sw[n];
             } else {
-                float offset_sum = 0.0f;
-                const float O = 12582912.0f; /* 1.5 * 2^23 */
                 for (int64_t g = 0; g < G; ++g) {
                     float part;
                     if (kind == 0) {
@@ -250,17 +244,11 @@ void or_block_gemm(const uint8_t *qa, const float *sa, int sa_mode, const uint8_
                         part = (float)dd;
                     }
                     float sag = (sa_mode == 0) ? sa[m * G + g] : sa[m];
-                    if (sw_mode == 1 || sw_mode == 2) {
-                        float s = (sw_mode == 2) ? sag * sw[(n / 128) * G + g] : sag;
-                        if (kind != 0) {
-                            acc = fmaf(part, s, acc);
-                        } else if ((g & 1) == 0) {
-                            acc = fmaf(O + part, s, acc);
-                            offset_sum = offset_sum + s;
-                        } else {
-                            acc = fmaf(O - part, -s, acc);
-                            offset_sum = offset_sum - s;
-                        }
+                    if (sw_mode == 2) {
+                        float s = sag * sw[(n / 128) * G + g];
+                        acc = fmaf(part, s, acc);
+                    } else if (sw_mode == 1) {
+                        acc = fmaf(part, sag, acc);
                     } else {
                         float t = part * sag;
                         float swg = sw[n * G + g];
@@ -268,7 +256,6 @@ void or_block_gemm(const uint8_t *qa, const float *sa, int sa_mode, const uint8_
                         else acc = acc + t * swg;
                     }
                 }
-                if (kind == 0 && (sw_mode == 1 || sw_mode == 2)) acc = fmaf(-O, offset_sum, acc);
                 if (sw_mode == 1) acc = acc * sw[n];
             }
             if (bias) acc = acc + bias[n];

@@ -1,9 +1,8 @@
 """Generate the golden vectors of the quantized DiT linear path from the REFERENCE's own code.
 
-Run where a checkout of the reference repository is available (its directory given by HY_NOMAS_REFERENCE;
-REF below holds the default):
+Run where a checkout of the reference repository is available, its directory given by HY_NOMAS_REFERENCE:
 
-    python tests/golden/make_golden.py
+    HY_NOMAS_REFERENCE=<checkout> python tests/golden/make_golden.py
 
 It writes tests/golden/*.npz. Nothing at test time reads the reference: the tests only read these files.
 
@@ -32,8 +31,15 @@ os.environ["TRITON_INTERPRET"] = "1"
 import numpy as np  # noqa: E402
 import torch  # noqa: E402
 
-REF = os.environ.get("HY_NOMAS_REFERENCE", "/root/reference")
 OUT = os.path.dirname(os.path.abspath(__file__))
+
+
+def reference_dir():
+    """The reference checkout, from HY_NOMAS_REFERENCE (no default: the scripts never guess a path)."""
+    ref = os.environ.get("HY_NOMAS_REFERENCE")
+    if not ref or not os.path.isdir(os.path.join(ref, "hy_nomas")):
+        raise SystemExit("set HY_NOMAS_REFERENCE to a checkout of the ComfyUI-Hy-Nomas repository")
+    return ref
 
 
 def _stub_comfy():
@@ -103,7 +109,7 @@ def bits(t):
 def main():
     _stub_comfy()
     _fix_interpreter_casts()
-    sys.path.insert(0, REF)
+    sys.path.insert(0, reference_dir())
     from hy_nomas import fused, kernels, model, ops, pixelumm, world  # noqa: E402
 
     gen = torch.Generator().manual_seed(0)

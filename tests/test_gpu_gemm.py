@@ -229,3 +229,40 @@ def test_benchmarked_modes_pinned_to_reference_layout(hn, cuda, m, n, k):
     unit = K.block_gemm(qa, torch.ones(m, g, device=cuda), qw, torch.ones(n, g, device=cuda), out_dtype=torch.float32)
     assert torch.equal(unit, ref.float())
     no_device_error(hn)
+
+
+@pytest.mark.parametrize("m", [1, 2, 3, 5, 8])
+@pytest.mark.parametrize("sa_mode,sw_mode", [("group", "group"), ("group", "row"), ("row", "row"), ("row", "group")])
+@pytest.mark.parametrize("k,epi", [(128, None), (640, None), (4096, None), (640, "gelu")])
+def test_few_rows_gemv_matches_tile_kernel(hn, oracle, cuda, m, sa_mode, sw_mode, k, epi):
+    """int8 calls with at most 8 activation rows (the stacked modulation linear runs at M = 1) take the weight-
+    streaming GEMV; it evaluates the tile kernel's promotion operation by operation, so its outputs equal the
+    tile kernel's on the same rows (reached by padding the call past 8 rows) and the oracle's, bit for bit."""
+    gen = torch.Generator().manual_seed(m * 1000 + k)
+    n, g = 1000, k // 128
+    qa, qw = rand_codes(gen, 16, k), rand_codes(gen, n, k)
+    sa = torch.rand(16, g, generator=gen) * 0.02 + 1e-3 if sa_mode == "group" else torch.rand(16, generator=gen) * 0.02
+    sw = torch.rand(n, g, generator=gen) * 4e-3 + 1e-3 if sw_mode == "group" else torch.rand(n, generator=gen) * 4e-3 + 1e-3
+    bias = (torch.randn(n, generator=gen) * 0.1).bfloat16()
+    dev = lambda t: t.to(cuda)  # noqa: E731
+    K = hn.kernels
+    few = K.block_gemm(dev(qa[:m]), dev(sa[:m]), dev(qw), dev(sw), dev(bias), epilogue=epi)
+    tile = K.block_gemm(dev(qa), dev(sa), dev(qw), dev(sw), dev(bias), epilogue=epi)[:m]
+    few32 = K.block_gemm(dev(qa[:m]), dev(sa[:m]), dev(qw), dev(sw), dev(bias), out_dtype=torch.float32) \
+        if epi is None else None
+    no_device_error(hn)
+    assert torch.equal(few.view(torch.int16).cpu(), tile.view(torch.int16).cpu())
+    if few32 is not None:
+        ref = oracle.block_gemm(qa[:m].numpy(), sa[:m].numpy(), qw.numpy(), sw.numpy(), bias.float().numpy(),
+                                sa_mode=sa_mode, sw_mode=sw_mode)
+        assert np.array_equal(f32(few32).view(np.uint32), ref.view(np.uint32))
+
+
+def test_few_rows_gemv_raw_int32(hn, cuda):
+    gen = torch.Generator().manual_seed(3)
+    qa, qw = rand_codes(gen, 3, 1152, lo=-128), rand_codes(gen, 777, 1152, lo=-128)
+    out = hn.kernels.block_gemm(qa.to(cuda), torch.ones(3, device=cuda), qw.to(cuda), torch.ones(777, device=cuda),
+                                out_dtype=torch.int32)
+    no_device_error(hn)
+    ref = qa.long() @ qw.long().t()
+    assert torch.equal(out.cpu().long(), ref)
