@@ -327,6 +327,8 @@ def workload_dit(args, world, rank, stream, pk, sampler):
               "modulation_gemv": modulation_context(model, vec, stream, pk)}
     if check is not None:
         config["sp_output_check"] = check
+    if not args.no_context:
+        config["segment2_with_int8_history"] = segment2_context(model, vec, world, stream)
     if world == 1 and not args.no_context:
         config["configs_1_to_3"] = path_context(stream, pk)
     return dict(metric="DiT denoise step tokens/s (40 blocks, 20240 tokens)", value=round(value, 1), unit="tokens/s",
@@ -361,6 +363,37 @@ def sp_output_check(model, x_full, x, vec, world, tol=1e-2):
     return {"against": "the same tokens computed on one GPU without sequence parallelism, on every rank",
             "rel_l2_max_over_ranks": float(f"{err_max:.3e}"), "bit_identical_ranks": n_same, "ranks": world,
             "finite_ranks": n_finite, "tolerance": tol, "pass": bool(err_max <= tol and n_finite == world)}
+
+
+def segment2_context(model, vec, world, stream, steps=5, history_frames=18):
+    """The world model's second segment (hy_nomas/model.py:199-209, world.py:197-204): the 23 latent frames of the
+    benchmark grid split into 18 frames of history and 5 current frames. A cache pass over the history frames
+    (every block's K quantized inside the QK-norm kernel, V by the KV quantizer) writes the int8 K/V cache of
+    each block - on every rank the whole history, as a world's staged history is replicated. The timed step
+    runs the 5 current frames (sharded over the ranks), each block dequantizing its history into the front of
+    its K/V buffers and attending over history + current."""
+    from hy_nomas_b200.sequence_parallel import SequenceParallel
+    t, gh, gw = model.cfg.grid
+    d = model.cfg.hidden
+    cache_model = model.replica(sp=SequenceParallel(local=True), grid=(history_frames, gh, gw), t_offset=0)
+    gen = torch.Generator(device="cuda").manual_seed(2000)
+    xh = torch.randn(1, cache_model.cfg.tokens, d, generator=gen, device="cuda").to(torch.bfloat16)
+    history = []
+    cache_model(xh, vec, capture=history)
+    del xh, cache_model
+    seg = model.replica(grid=(t - history_frames, gh, gw), t_offset=history_frames)
+    lo, hi = seg.token_range
+    x = torch.randn(1, seg.cfg.tokens, d, generator=gen, device="cuda").to(torch.bfloat16)[:, lo:hi].contiguous()
+    ms = timed_steps(lambda i: seg(x, vec, history=history), steps, 3, world, stream)
+    lh = history[0][0].shape[0]
+    hist_bytes = sum(c[0].numel() + c[2].numel() + 4 * (c[1].numel() + c[3].numel()) for c in history)
+    del history
+    torch.cuda.empty_cache()
+    return {"current_tokens": seg.cfg.tokens, "history_tokens": lh, "ms_per_step": round(ms / steps, 3),
+            "current_tokens_per_s": round(seg.cfg.tokens * steps / (ms * 1e-3), 1),
+            "int8_history_bytes": hist_bytes,
+            "note": "40 blocks; every block attends over its dequantized int8 history followed by the current "
+                    "tokens' K/V; the history is built by a cache pass on each rank"}
 
 
 def modulation_context(model, vec, stream, pk, iters=10):

@@ -3,9 +3,8 @@
 // With one to a few activation rows the 128-row tensor-core tile does 1/128 of useful work and the linear is a
 // read of the weight matrix: hy_nomas/model.py:247's Modulate(vec) is one such call per block (M = batch = 1),
 // and the DiT step stacks all blocks' modulation weights into one [blocks * 6D, D] linear. Here one warp streams
-// one weight row (output column n) with 16-byte non-allocating loads, 512 bytes per warp step, the loads of four
-// steps issued together: lane l holds bytes [16 l, 16 l + 16) of a step, so the 8 lanes of octet j hold K group
-// 4 i + j of step i. The group's
+// one weight row (output column n) with 16-byte non-allocating loads, 512 bytes per warp step: lane l holds bytes
+// [16 l, 16 l + 16) of a step, so the 8 lanes of octet j hold K group 4 i + j of step i. The group's
 // integer dot for each activation row is dp4a over the lane's 16 bytes and a 3-step butterfly in the octet; the
 // four groups of a step are then folded in group order by every lane (4 shuffles), with the same fp32 operations
 // as the tile kernel's epilogue (gemm.cu), so both produce identical bits:
@@ -51,7 +50,9 @@ __global__ void __launch_bounds__(32 * WARPS) k_gemv(const Params p) {
     const int64_t warp0 = (int64_t)blockIdx.x * WARPS + (threadIdx.x >> 5);
     const int64_t nwarps = (int64_t)gridDim.x * WARPS;
     const int steps = (p.K + 511) / 512;
-    constexpr int U = 4;          // 512-byte steps whose weight loads are issued together
+    // one 512-byte step's loads at a time: with the registers of deeper unrolling fewer warps are resident and
+    // the kernel was slower (1.13-1.17 ms against 1.07 ms at M = 1 for 983040 x 4096 weights)
+    constexpr int U = 1;
     for (int64_t n = warp0; n < p.N; n += nwarps) {
         const int8_t *wrow = p.qw + n * p.ldw;
         float acc[MM];
@@ -146,23 +147,34 @@ __global__ void __launch_bounds__(32 * WARPS) k_gemv(const Params p) {
     }
 }
 
-template <int MM, int PMODE>
-static cudaError_t launch_m(const Params &p, int epi, cudaStream_t st) {
-    // enough warps in flight to cover HBM latency: 8 resident CTAs of 8 warps per SM, grid-stride over rows
-    int64_t grid = (int64_t)num_sms() * 8;
+template <int MM, int PMODE, int EPI>
+static cudaError_t launch_e(const Params &p, cudaStream_t st) {
+    auto kern = k_gemv<MM, PMODE, EPI>;
+    // every CTA resident at once (grid = SMs x resident CTAs per SM), grid-stride over the weight rows: a larger
+    // grid would leave the rows of its non-resident CTAs to a second, partial wave
+    static int per_sm = 0;
+    if (per_sm == 0) {
+        int n = 0;
+        if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&n, kern, 32 * WARPS, 0) != cudaSuccess || n < 1) n = 1;
+        per_sm = n;
+    }
+    int64_t grid = (int64_t)num_sms() * per_sm;
     const int64_t need = (p.N + WARPS - 1) / WARPS;
     if (grid > need) grid = need;
-    if (epi == 1) k_gemv<MM, PMODE, 1><<<(unsigned)grid, 32 * WARPS, 0, st>>>(p);
-    else k_gemv<MM, PMODE, 0><<<(unsigned)grid, 32 * WARPS, 0, st>>>(p);
+    kern<<<(unsigned)grid, 32 * WARPS, 0, st>>>(p);
     return cudaGetLastError();
+}
+
+template <int MM, int PMODE>
+static cudaError_t launch_m(const Params &p, int epi, cudaStream_t st) {
+    return epi == 1 ? launch_e<MM, PMODE, 1>(p, st) : launch_e<MM, PMODE, 0>(p, st);
 }
 
 template <int PMODE>
 static cudaError_t launch_p(const Params &p, int epi, cudaStream_t st) {
+    static_assert(GEMV_MAX_M == 2, "instantiations cover M = 1 and 2");
     if (p.M <= 1) return launch_m<1, PMODE>(p, epi, st);
-    if (p.M <= 2) return launch_m<2, PMODE>(p, epi, st);
-    if (p.M <= 4) return launch_m<4, PMODE>(p, epi, st);
-    return launch_m<GEMV_MAX_M, PMODE>(p, epi, st);
+    return launch_m<2, PMODE>(p, epi, st);
 }
 
 } // namespace gemv

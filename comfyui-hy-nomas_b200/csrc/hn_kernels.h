@@ -58,8 +58,10 @@ struct GemmArgs {
 cudaError_t launch_block_gemm(const GemmArgs &a, cudaStream_t st, const char **msg);
 
 // int8 calls with at most GEMV_MAX_M activation rows (epilogue none or gelu, weight scales per row or per row x
-// group) run as a weight-streaming GEMV (gemv.cu) with the tile kernel's arithmetic
-constexpr int GEMV_MAX_M = 8;
+// group) run as a weight-streaming GEMV (gemv.cu) with the tile kernel's arithmetic. Above 2 rows the GEMV's
+// per-row folding makes it slower than the tile kernel (measured: 2.87 ms at 4 rows of 983040 x 4096 weights,
+// against ~1.8 ms for the tile kernel at any row count up to 128)
+constexpr int GEMV_MAX_M = 2;
 bool gemv_applies(const GemmArgs &a);
 cudaError_t launch_gemv(const GemmArgs &a, cudaStream_t st);
 

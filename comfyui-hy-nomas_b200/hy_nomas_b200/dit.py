@@ -33,7 +33,7 @@ from dataclasses import dataclass
 import torch
 import torch.nn.functional as F
 
-from . import fused, kernels
+from . import fused, kernels, world
 from .sequence_parallel import SequenceParallel
 
 # SMs each GEMM leaves free under sequence parallelism (HN_SP_GEMM_SM_RESERVE overrides)
@@ -49,6 +49,7 @@ class DiTConfig:
     rope_dims: tuple = (16, 56, 56)
     theta: float = 10000.0
     grid: tuple = (23, 22, 40)   # latent frames x patch rows x patch columns = 20240 tokens
+    t_offset: int = 0            # frame index of the first latent frame (RoPE positions; > 0 after history)
 
     @property
     def head_dim(self):
@@ -143,6 +144,20 @@ class CudaOps:
         return fused.gated_residual_adaln_quant(x, y, gate, shift, scale)
 
     @staticmethod
+    def qk_norm_rope_kv(x, w, rope, out):
+        """QK-norm + RoPE into `out`, and its int8 KV-cache codes and scales from the same launch."""
+        _, q, s = fused.qk_norm_rope_kv(x, w, rope, out=out)
+        return q, s
+
+    @staticmethod
+    def quantize_kv(x):
+        return world.quantize_kv(x)
+
+    @staticmethod
+    def dequantize_kv(q, s, out):
+        return world.dequantize_kv(q, s, out=out)
+
+    @staticmethod
     def gated_residual(x, y, gate):
         return fused.gated_residual(x, y, gate)
 
@@ -156,7 +171,8 @@ class CudaOps:
         return F.scaled_dot_product_attention(q.transpose(1, 2), k.transpose(1, 2), v.transpose(1, 2)).transpose(1, 2)
 
 
-def block_forward(cfg, w, x, vec, rope, sp, ops=CudaOps, trace=None, mods=None, x_q=None, next_mods=None):
+def block_forward(cfg, w, x, vec, rope, sp, ops=CudaOps, trace=None, mods=None, x_q=None, next_mods=None,
+                  history=None, capture=None):
     """One block on this rank's tokens. x bf16 [B, l, D] (l = the rank's tokens), vec bf16 [B, D], rope =
     this rank's rows of the (cos, sin) tables. Returns the block output [B, l, D] bf16. `trace`, when a dict,
     receives the block's intermediates (for parity tests). `mods`: this block's Modulate(vec) output [B, 6D] when
@@ -164,7 +180,15 @@ def block_forward(cfg, w, x, vec, rope, sp, ops=CudaOps, trace=None, mods=None, 
 
     Chaining blocks: `next_mods` (the next block's modulations) fuses this block's final gated residual with the
     next block's LN + modulate + int8 quantization (one pass, bit-identical to the two kernels) and makes the
-    return value (out, (qa, sa)); the next block takes that pair as `x_q` instead of quantizing `out` again."""
+    return value (out, (qa, sa)); the next block takes that pair as `x_q` instead of quantizing `out` again.
+
+    The segment history (hy_nomas/model.py:199-209, world.py:197-204): `history` = (hk_q, hk_s, hv_q, hv_s), this
+    block's int8 K/V cache of earlier frames, codes [Lh, H, D] and scales [Lh, H, 1] (world.quantize_kv's
+    format, the same on every rank). They are dequantized straight into the first Lh positions of the K/V
+    buffers, ahead of the current tokens', and the current tokens attend over history + current as the
+    reference's torch.cat([hk, k]) does. `capture`, when a list, receives this block's int8 cache of the rank's
+    own tokens (kq, ks, vq, vs): K quantized inside the QK-norm + RoPE kernel, V by the KV quantizer - the cache
+    pass that writes the history of a finished segment."""
     b, l, d = x.shape
     h, hd = cfg.heads, cfg.head_dim
     act = ops.silu(vec) if (mods is None or trace is not None) else None
@@ -173,12 +197,20 @@ def block_forward(cfg, w, x, vec, rope, sp, ops=CudaOps, trace=None, mods=None, 
     shift1, scale1, gate1, shift2, scale2, gate2 = mods.chunk(6, dim=-1)
     qa, sa = x_q if x_q is not None else ops.adaln_quant(x, shift1, scale1)
     chunks = sp.head_chunks if (sp.world > 1 and h % sp.head_chunks == 0) else 1
+    if (history is not None or capture is not None) and chunks > 1:
+        raise NotImplementedError("history and capture take the unchunked K/V exchange (head_chunks = 1)")
     if chunks > 1:
         attn, k_full, v_full, qk, q_out = _attention_chunked(cfg, w, qa, sa, rope, sp, ops, b, l, chunks,
                                                              keep_kv=trace is not None)
         return _post(cfg, w, x, attn, qa, sa, qk, q_out, k_full, v_full, act, mods, gate1, shift2, scale2, gate2,
                      ops, trace, next_mods)
-    k_full, v_full, k_mine, v_mine = sp.kv_buffers(b, l, h, hd, x.dtype, x.device)
+    lh = 0 if history is None else history[0].shape[0]
+    k_full, v_full, k_mine, v_mine = sp.kv_buffers(b, l, h, hd, x.dtype, x.device, prefix=lh)
+    if history is not None:
+        hk_q, hk_s, hv_q, hv_s = history
+        for bi in range(b):
+            ops.dequantize_kv(hk_q, hk_s, out=k_full[bi, :lh])
+            ops.dequantize_kv(hv_q, hv_s, out=v_full[bi, :lh])
     # v first, so its all-gather runs under the q|k GEMM; k is normalized before q, so its gather runs under
     # q's normalization (with one rank the gathers are no-ops and the order changes nothing)
     ops.gemm(qa, sa, w.v, out=v_mine.view(b * l, d))
@@ -187,7 +219,13 @@ def block_forward(cfg, w, x, vec, rope, sp, ops=CudaOps, trace=None, mods=None, 
     q_in = qk[:, :d].view(b, l, h, hd)
     k_in = qk[:, d:].view(b, l, h, hd)
     q_out = torch.empty((b, l, h, hd), dtype=x.dtype, device=x.device)
-    if sp.world > 1:
+    if capture is not None:
+        kq, ks = ops.qk_norm_rope_kv(k_in, w.k_norm, rope, out=k_mine)
+        gather_k = sp.all_gather_async(k_full, k_mine)
+        ops.qk_norm_rope(q_in, w.q_norm, rope, out=q_out)
+        vq, vs = ops.quantize_kv(v_mine.reshape(b * l, h, hd))
+        capture.append((kq.reshape(b * l, h, hd), ks.reshape(b * l, h, 1), vq, vs))
+    elif sp.world > 1:
         ops.qk_norm_rope(k_in, w.k_norm, rope, out=k_mine)
         gather_k = sp.all_gather_async(k_full, k_mine)
         ops.qk_norm_rope(q_in, w.q_norm, rope, out=q_out)
@@ -281,7 +319,7 @@ class SyntheticDiT:
         n6 = 6 * cfg.hidden
         for i, bw in enumerate(self.blocks):
             bw.mod = _rows(self.mod_all, i * n6, (i + 1) * n6)
-        cos, sin = rope_freqs(cfg.rope_dims, cfg.theta, *cfg.grid, device=self.device)
+        cos, sin = rope_freqs(cfg.rope_dims, cfg.theta, *cfg.grid, t_offset=cfg.t_offset, device=self.device)
         lo, hi = self.sp.shard(cfg.tokens)
         self.rope = (cos[lo:hi].contiguous(), sin[lo:hi].contiguous())
         self.token_range = (lo, hi)
@@ -289,36 +327,43 @@ class SyntheticDiT:
         self.sm_reserve = int(os.environ.get("HN_SP_GEMM_SM_RESERVE", str(SP_GEMM_SM_RESERVE))) \
             if (self.sp.world > 1 and self.device.type == "cuda") else 0
 
-    def replica(self, sp):
-        """The same model (weights shared, not copied) over another partition `sp` of the sequence, e.g. the whole
-        sequence on one GPU to check a sequence-parallel run against."""
+    def replica(self, sp=None, grid=None, t_offset=None):
+        """The same model (weights shared, not copied) over another partition `sp` of the sequence (e.g. the whole
+        sequence on one GPU, to check a sequence-parallel run against) and/or another token grid starting at
+        frame `t_offset` (e.g. a later segment, or the frames of its history)."""
         import copy
+        import dataclasses
         other = copy.copy(self)
-        other.sp = sp
-        cos, sin = rope_freqs(self.cfg.rope_dims, self.cfg.theta, *self.cfg.grid, device=self.device)
-        lo, hi = sp.shard(self.cfg.tokens)
+        other.sp = sp = sp or self.sp
+        changes = {k: v for k, v in (("grid", grid), ("t_offset", t_offset)) if v is not None}
+        other.cfg = dataclasses.replace(self.cfg, **changes)
+        other.sm_reserve = self.sm_reserve if sp is self.sp else 0
+        cos, sin = rope_freqs(other.cfg.rope_dims, other.cfg.theta, *other.cfg.grid, t_offset=other.cfg.t_offset,
+                              device=self.device)
+        lo, hi = sp.shard(other.cfg.tokens)
         other.rope = (cos[lo:hi].contiguous(), sin[lo:hi].contiguous())
         other.token_range = (lo, hi)
-        other.sm_reserve = 0
         return other
 
     def modulations(self, vec):
         """All blocks' Modulate(vec) in one launch pair (quantize + GEMM): [B, blocks * 6D] bf16."""
         return self.ops.linear(self.ops.silu(vec), self.mod_all)
 
-    def forward(self, x, vec, trace=None):
+    def forward(self, x, vec, trace=None, history=None, capture=None):
+        """This rank's tokens after all blocks. `history`: one (hk_q, hk_s, hv_q, hv_s) int8 cache per block (see
+        block_forward); `capture`, when a list, receives one such cache per block for this rank's tokens."""
         if not self.sm_reserve:
-            return self._forward(x, vec, trace)
+            return self._forward(x, vec, trace, history, capture)
         # the library's SM reserve is process-wide: set it for this step only and put the caller's value back
         from . import _lib
         prev = _lib.lib.hn_get_gemm_sm_reserve()
         _lib.check(_lib.lib.hn_set_gemm_sm_reserve(self.sm_reserve), "hn_set_gemm_sm_reserve")
         try:
-            return self._forward(x, vec, trace)
+            return self._forward(x, vec, trace, history, capture)
         finally:
             _lib.lib.hn_set_gemm_sm_reserve(prev)
 
-    def _forward(self, x, vec, trace=None):
+    def _forward(self, x, vec, trace=None, history=None, capture=None):
         mods = self.modulations(vec)
         n6 = 6 * self.cfg.hidden
         nb = len(self.blocks)
@@ -329,7 +374,8 @@ class SyntheticDiT:
             r = block_forward(self.cfg, w, x, vec, self.rope, self.sp, self.ops,
                               trace=trace if (trace is not None and last) else None,
                               mods=mods[:, i * n6:(i + 1) * n6], x_q=x_q,
-                              next_mods=None if last else mods[:, (i + 1) * n6:(i + 2) * n6])
+                              next_mods=None if last else mods[:, (i + 1) * n6:(i + 2) * n6],
+                              history=None if history is None else history[i], capture=capture)
             x, x_q = (r, None) if last else r
         return x
 

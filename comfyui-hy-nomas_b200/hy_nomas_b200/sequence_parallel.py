@@ -49,14 +49,15 @@ class SequenceParallel:
         per = length // self.world
         return self.rank * per, (self.rank + 1) * per
 
-    def kv_buffers(self, batch, local, heads, head_dim, dtype, device):
-        """Full-sequence K and V buffers [batch, local * world, heads, head_dim] and this rank's slice of each
-        ([batch, local, heads, head_dim], contiguous). Reused across blocks and steps."""
+    def kv_buffers(self, batch, local, heads, head_dim, dtype, device, prefix=0):
+        """Full-sequence K and V buffers [batch, prefix + local * world, heads, head_dim] and this rank's slice of
+        each ([batch, local, heads, head_dim], contiguous, at prefix + rank * local). The first `prefix` tokens
+        hold the segment history's keys and values (replicated on every rank). Reused across blocks and steps."""
         if self.world > 1 and batch != 1:
             raise ValueError("sequence parallelism takes batch 1 (the denoise step's layout)")
-        key = (batch, local, heads, head_dim, dtype, str(device))
+        key = (batch, local, heads, head_dim, dtype, str(device), prefix)
         if key not in self._bufs:
-            self._bufs[key] = self._alloc(batch, local, heads, head_dim, dtype, device)
+            self._bufs[key] = self._alloc(batch, local, heads, head_dim, dtype, device, prefix)
         return self._bufs[key]
 
     def kv_chunk_buffers(self, batch, local, heads, head_dim, chunks, dtype, device):
@@ -69,19 +70,23 @@ class SequenceParallel:
             self._bufs[key] = [self._alloc(batch, local, heads // chunks, head_dim, dtype, device) for _ in range(chunks)]
         return self._bufs[key]
 
-    def _alloc(self, batch, local, heads, head_dim, dtype, device):
-        total = local * self.world
+    def _alloc(self, batch, local, heads, head_dim, dtype, device, prefix=0):
+        total = prefix + local * self.world
         k_full = torch.empty((batch, total, heads, head_dim), dtype=dtype, device=device)
         v_full = torch.empty_like(k_full)
-        lo = self.rank * local
+        lo = prefix + self.rank * local
         return k_full, v_full, k_full[:, lo:lo + local], v_full[:, lo:lo + local]
 
     def all_gather_async(self, full, mine):
-        """Start filling `full` with every rank's `mine` (a slice of `full`); returns a handle for `wait`."""
+        """Start filling `full`'s ranks' part (everything after its history prefix) with every rank's `mine` (a
+        slice of `full`); returns a handle for `wait`."""
         if self.world == 1:
             return None
-        # flat views: the rank-major buffer is `world` equal chunks of the rank slices (NCCL and gloo agree)
-        return dist.all_gather_into_tensor(full.view(-1), mine.view(-1), group=self.group, async_op=True)
+        prefix = full.shape[1] - mine.shape[1] * self.world
+        ranks_part = full[:, prefix:]
+        # flat views: the rank-major part is `world` equal chunks of the rank slices (NCCL and gloo agree); with
+        # batch 1 it is one contiguous range
+        return dist.all_gather_into_tensor(ranks_part.view(-1), mine.view(-1), group=self.group, async_op=True)
 
     @staticmethod
     def wait(*handles):

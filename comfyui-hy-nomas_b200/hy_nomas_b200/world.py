@@ -24,8 +24,10 @@ def quantize_kv(x):
     return q, s
 
 
-def dequantize_kv(q, scale, dtype=torch.bfloat16):
-    """int8 [..., D] codes and fp32 scales [..., 1] -> bf16(float(q) * scale) (hy_nomas/world.py:93-94)."""
+def dequantize_kv(q, scale, dtype=torch.bfloat16, out=None):
+    """int8 [..., D] codes and fp32 scales [..., 1] -> bf16(float(q) * scale) (hy_nomas/world.py:93-94).
+    `out` (not in the reference): a caller-owned contiguous bf16 tensor with q's number of elements, e.g. the
+    history part of a block's K or V buffer, written instead of a fresh tensor."""
     _lib.require_cuda(q, scale)
     if dtype != torch.bfloat16:
         raise TypeError("dequantize_kv: the kernel writes bf16 (the reference's default dtype)")
@@ -35,7 +37,13 @@ def dequantize_kv(q, scale, dtype=torch.bfloat16):
     s = _lib.dense(scale.to(torch.float32))
     if s.numel() != rows:
         raise ValueError(f"dequantize_kv: {s.numel()} scales for {rows} rows")
-    y = torch.empty(q.shape, device=q.device, dtype=torch.bfloat16)
+    if out is None:
+        y = torch.empty(q.shape, device=q.device, dtype=torch.bfloat16)
+    elif out.dtype != torch.bfloat16 or not out.is_contiguous() or out.numel() != q.numel() or out.device != q.device \
+            or out.data_ptr() % 16:
+        raise ValueError("dequantize_kv: out must be a contiguous, 16-byte aligned bf16 tensor of q's size on q's device")
+    else:
+        y = out
     rc = _lib.lib.hn_dequantize_kv(_lib.ptr(q), _lib.ptr(s), rows, d, _lib.ptr(y), _lib.stream_of(q))
     _lib.check(rc, "dequantize_kv")
     return y

@@ -72,6 +72,24 @@ class OracleOps:
         return _bf16(xo), torch.from_numpy(q), torch.from_numpy(s)
 
     @staticmethod
+    def qk_norm_rope_kv(x, w, rope, out):
+        """QK-norm + RoPE into `out`, then the KV quantizer of world.quantize_kv on that output."""
+        OracleOps.qk_norm_rope(x, w, rope, out)
+        b, l, h, d = out.shape
+        return OracleOps.quantize_kv(out.reshape(b * l, h, d))
+
+    @staticmethod
+    def quantize_kv(x):
+        q, s = O.quantize_kv(_np(x).reshape(-1, x.shape[-2], x.shape[-1]))
+        return torch.from_numpy(q).reshape(x.shape), torch.from_numpy(s).reshape(*x.shape[:-1], 1)
+
+    @staticmethod
+    def dequantize_kv(q, s, out):
+        y = O.dequantize_kv(q.cpu().numpy().reshape(-1, q.shape[-1]), _np(s).reshape(-1))
+        out.copy_(_bf16(y).reshape(out.shape))
+        return out
+
+    @staticmethod
     def gated_residual(x, y, gate):
         return _bf16(O.round_bf16(O.gated_residual(_np(x), _np(y), _np(gate))))
 

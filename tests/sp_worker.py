@@ -17,15 +17,31 @@ def inputs(cfg, device="cpu"):
     return x.to(device), vec.to(device)
 
 
-def run_model(cfg, sp, ops, device):
+def history(cfg, tokens, device="cpu"):
+    """A seeded int8 K/V history of `tokens` earlier tokens for every block: codes in [-127, 127] and scales
+    (the same on every rank, as a world's staged history is)."""
+    gen = torch.Generator().manual_seed(21)
+    h, d = cfg.heads, cfg.head_dim
+    caches = []
+    for _ in range(cfg.blocks):
+        part = []
+        for _kv in range(2):
+            part.append(torch.randint(-127, 128, (tokens, h, d), generator=gen, dtype=torch.int8).to(device))
+            part.append((torch.rand(tokens, h, 1, generator=gen) * 0.04 + 0.01).to(device))
+        caches.append(tuple(part))
+    return caches
+
+
+def run_model(cfg, sp, ops, device, history_tokens=0):
     from hy_nomas_b200.dit import SyntheticDiT
     model = SyntheticDiT(cfg, device=device, seed=3, sp=sp, ops=ops)
     x, vec = inputs(cfg, device)
     lo, hi = model.token_range
-    return model(x[:, lo:hi].contiguous(), vec)
+    hist = history(cfg, history_tokens, device) if history_tokens else None
+    return model(x[:, lo:hi].contiguous(), vec, history=hist)
 
 
-def gloo_rank(rank, world, port, out_path, head_chunks=1):
+def gloo_rank(rank, world, port, out_path, head_chunks=1, history_tokens=0):
     import torch.distributed as dist
     from dit_oracle_ops import OracleOps
     from hy_nomas_b200.sequence_parallel import SequenceParallel
@@ -34,7 +50,7 @@ def gloo_rank(rank, world, port, out_path, head_chunks=1):
     dist.init_process_group("gloo", rank=rank, world_size=world)
     try:
         cfg = small_config()
-        out = run_model(cfg, SequenceParallel(head_chunks=head_chunks), OracleOps, "cpu")
+        out = run_model(cfg, SequenceParallel(head_chunks=head_chunks), OracleOps, "cpu", history_tokens)
         parts = [torch.empty_like(out) for _ in range(world)]
         dist.all_gather(parts, out)
         if rank == 0:

@@ -155,3 +155,62 @@ def test_sequence_parallel_two_gpus(hn, cuda, tmp_path, head_chunks):
     got = torch.load(out_path)
     assert got.shape == single.shape
     assert rel_l2(got.float().numpy(), single.float().numpy()) < 1e-2
+
+
+@pytest.fixture(scope="module")
+def history_run(hn, oracle, cuda):
+    """One block over 200 current tokens with a 120-token int8 K/V history (the segment-2 layout: earlier frames
+    as int8 cache, hy_nomas/model.py:199-209), on the GPU, with its trace and the cache it captures."""
+    from hy_nomas_b200.dit import block_forward, make_block_weights, rope_freqs
+    from hy_nomas_b200.sequence_parallel import SequenceParallel
+    cfg = small_cfg()
+    gen = torch.Generator(device=cuda).manual_seed(9)
+    w = make_block_weights(cfg, gen, cuda)
+    rope = rope_freqs(cfg.rope_dims, cfg.theta, *cfg.grid, t_offset=3, device=cuda)
+    g = torch.Generator().manual_seed(10)
+    x = torch.randn(1, cfg.tokens, cfg.hidden, generator=g).to(torch.bfloat16).to(cuda)
+    vec = torch.randn(1, cfg.hidden, generator=g).to(torch.bfloat16).to(cuda)
+    hist = sp_worker.history(cfg.__class__(**{**cfg.__dict__, "blocks": 1}), 120, cuda)[0]
+    trace, cap = {}, []
+    out = block_forward(cfg, w, x, vec, rope, SequenceParallel(), trace=trace, history=hist, capture=cap)
+    torch.cuda.synchronize()
+    rc, code = hn.lib.device_error()
+    assert rc == 0 and code == 0
+    cpu = lambda t: t.cpu() if torch.is_tensor(t) else t  # noqa: E731
+    return (cfg, to_cpu_weights(w), x.cpu(), vec.cpu(), (rope[0].cpu(), rope[1].cpu()),
+            tuple(cpu(t) for t in hist), {k: cpu(v) for k, v in trace.items()}, out.cpu(), [tuple(map(cpu, c)) for c in cap])
+
+
+def test_history_dequantized_into_the_kv_prefix(history_run):
+    """The history's K and V, dequantized by the int8-KV kernel straight into the first 120 positions of the K/V
+    buffers, equal the oracle's dequantize_kv (world.py:93-94) bit for bit; the current tokens follow."""
+    cfg, w, x, vec, rope, hist, t, out, cap = history_run
+    hk_q, hk_s, hv_q, hv_s = hist
+    lh = hk_q.shape[0]
+    assert t["k_full"].shape[1] == lh + cfg.tokens
+    ref_k = OracleOps.dequantize_kv(hk_q, hk_s, torch.empty(lh, cfg.heads, cfg.head_dim, dtype=torch.bfloat16))
+    ref_v = OracleOps.dequantize_kv(hv_q, hv_s, torch.empty(lh, cfg.heads, cfg.head_dim, dtype=torch.bfloat16))
+    assert same(t["k_full"][0, :lh], ref_k) and same(t["v_full"][0, :lh], ref_v)
+
+
+def test_history_attention_and_block_within_tolerance(history_run):
+    from hy_nomas_b200.dit import block_forward
+    from hy_nomas_b200.sequence_parallel import SequenceParallel
+    cfg, w, x, vec, rope, hist, t, out, cap = history_run
+    b, l, d = x.shape
+    ref = OracleOps.attention(t["q"], t["k_full"], t["v_full"]).reshape(b * l, d)
+    assert rel_l2(t["attn"].float().numpy(), ref.float().numpy()) < 1e-2
+    full = block_forward(cfg, w, x, vec, rope, SequenceParallel(), ops=OracleOps, history=hist)
+    assert rel_l2(out.float().numpy(), full.float().numpy()) < 2e-2
+
+
+def test_capture_equals_kv_quantizer_on_gpu(history_run):
+    """The cache pass on the GPU: the K codes and scales come out of the QK-norm + RoPE kernel (fused quantizer)
+    and V's from the KV quantizer, equal to the oracle's world.quantize_kv of the block's own K and V."""
+    cfg, w, x, vec, rope, hist, t, out, cap = history_run
+    kq, ks, vq, vs = cap[0]
+    lh, l, h, d = hist[0].shape[0], cfg.tokens, cfg.heads, cfg.head_dim
+    k_ref = OracleOps.quantize_kv(t["k_full"][0, lh:].reshape(l, h, d))
+    v_ref = OracleOps.quantize_kv(t["v_full"][0, lh:].reshape(l, h, d))
+    assert torch.equal(kq, k_ref[0]) and torch.equal(ks.reshape(l, h, 1), k_ref[1])
+    assert torch.equal(vq, v_ref[0]) and torch.equal(vs.reshape(l, h, 1), v_ref[1])

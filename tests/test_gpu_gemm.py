@@ -231,13 +231,14 @@ def test_benchmarked_modes_pinned_to_reference_layout(hn, cuda, m, n, k):
     no_device_error(hn)
 
 
-@pytest.mark.parametrize("m", [1, 2, 3, 5, 8])
+@pytest.mark.parametrize("m", [1, 2, 3])
 @pytest.mark.parametrize("sa_mode,sw_mode", [("group", "group"), ("group", "row"), ("row", "row"), ("row", "group")])
 @pytest.mark.parametrize("k,epi", [(128, None), (640, None), (4096, None), (640, "gelu")])
 def test_few_rows_gemv_matches_tile_kernel(hn, oracle, cuda, m, sa_mode, sw_mode, k, epi):
-    """int8 calls with at most 8 activation rows (the stacked modulation linear runs at M = 1) take the weight-
+    """int8 calls with at most 2 activation rows (the stacked modulation linear runs at M = 1) take the weight-
     streaming GEMV; it evaluates the tile kernel's promotion operation by operation, so its outputs equal the
-    tile kernel's on the same rows (reached by padding the call past 8 rows) and the oracle's, bit for bit."""
+    tile kernel's on the same rows (reached by padding the call to 16 rows) and the oracle's, bit for bit
+    (m = 3 is the first row count past the GEMV)."""
     gen = torch.Generator().manual_seed(m * 1000 + k)
     n, g = 1000, k // 128
     qa, qw = rand_codes(gen, 16, k), rand_codes(gen, n, k)

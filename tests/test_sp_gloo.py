@@ -62,3 +62,46 @@ def test_gloo_matches_single_rank(single_rank, tmp_path, world, head_chunks):
     got = torch.load(out_path)
     assert got.shape == single_rank.shape
     assert torch.equal(got.view(torch.int16), single_rank.view(torch.int16))
+
+
+def test_gloo_with_history_matches_single_rank(hn, oracle, tmp_path):
+    """With a replicated int8 K/V history (every block's attention runs over the dequantized history followed by
+    the gathered current tokens), 2 gloo ranks equal the single-rank model bit for bit."""
+    from hy_nomas_b200.sequence_parallel import SequenceParallel
+    single = sp_worker.run_model(sp_worker.small_config(), SequenceParallel(), OracleOps, "cpu", history_tokens=12)
+    ctx = mp.get_context("spawn")
+    port = free_port()
+    out_path = os.path.join(tmp_path, "out.pt")
+    procs = [ctx.Process(target=sp_worker.gloo_rank, args=(r, 2, port, out_path, 1, 12)) for r in range(2)]
+    for p in procs:
+        p.start()
+    for p in procs:
+        p.join(timeout=240)
+    codes = [p.exitcode for p in procs]
+    for p in procs:
+        if p.is_alive():
+            p.kill()
+    assert codes == [0, 0], codes
+    got = torch.load(out_path)
+    assert torch.equal(got.view(torch.int16), single.view(torch.int16))
+    no_hist = sp_worker.run_model(sp_worker.small_config(), SequenceParallel(), OracleOps, "cpu")
+    assert not torch.equal(no_hist.view(torch.int16), single.view(torch.int16))   # the history is attended to
+
+
+def test_capture_is_the_kv_quantizer_of_the_block_kv(hn, oracle):
+    """The cache pass: each block's captured (kq, ks, vq, vs) equals world.quantize_kv of the K and V the block
+    attended with (K after QK-norm + RoPE)."""
+    from hy_nomas_b200.dit import block_forward, make_block_weights, rope_freqs
+    from hy_nomas_b200.sequence_parallel import SequenceParallel
+    cfg = sp_worker.small_config()
+    w = make_block_weights(cfg, torch.Generator().manual_seed(8), "cpu")
+    x, vec = sp_worker.inputs(cfg)
+    rope = rope_freqs(cfg.rope_dims, cfg.theta, *cfg.grid)
+    trace, cap = {}, []
+    block_forward(cfg, w, x, vec, rope, SequenceParallel(), ops=OracleOps, trace=trace, capture=cap)
+    kq, ks, vq, vs = cap[0]
+    l, h, d = cfg.tokens, cfg.heads, cfg.head_dim
+    k_ref = OracleOps.quantize_kv(trace["k_full"].reshape(l, h, d))
+    v_ref = OracleOps.quantize_kv(trace["v_full"].reshape(l, h, d))
+    assert torch.equal(kq, k_ref[0]) and torch.equal(ks, k_ref[1])
+    assert torch.equal(vq, v_ref[0]) and torch.equal(vs, v_ref[1])
