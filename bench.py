@@ -1,6 +1,7 @@
 """Benchmark of the quantized DiT linear path on B200 - one JSON line on rank 0.
 
-    python bench.py [--gpus N] [--steps K] [--warmup W] [--workload dit|gemm|fp8|elementwise] [--impl ours|reference]
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--workload dit|dit_gemms|gemm|fp8|elementwise]
+                    [--impl ours|reference]
 
 Workloads (synthetic, seeded; the reference publishes no dataset for this path):
   dit          (default) benchmark config 5: one denoise step of a 40-block Hy-Nomas-style DiT (hidden 4096,
@@ -8,6 +9,8 @@ Workloads (synthetic, seeded; the reference publishes no dataset for this path):
                L = 20240 tokens, batch 1, sequence-parallel over the ranks (per-block K/V all-gather over
                NCCL). metric: tokens/s of the whole job (strong scaling); roofline: the W8A8 GEMM kernel
                inside the step.
+  dit_gemms    benchmark config 4's linears: the block's five W8A8 GEMMs at M = 20240 (v, q|k, proj, fc1 with
+               the GELU + requantization epilogue, fc2); metric TOPS; the profiling target of their ncu summary.
   gemm         benchmark config 1: W8A8 int8 linear 4096 x 4096 x 4096 (quantize + GEMM), per-128-group
                activation scales and per-channel weight scales; every rank runs its own copy (replicas).
   fp8          benchmark config 2: FP8 e4m3 block-scaled linear, MLP-up 16384 x 4096 at M = 20240 (quantize +
@@ -497,6 +500,112 @@ def reference_dit(args):
 
 
 # --------------------------------------------------------------------------------------------------------
+# dit_gemms (config 4's linears)
+
+
+DIT_GEMM_SHAPES = [("v", 4096, 4096, None), ("qk", 8192, 4096, None), ("proj", 4096, 4096, None),
+                   ("fc1", 16384, 4096, "gelu_quant"), ("fc2", 4096, 16384, None)]
+
+
+def workload_dit_gemms(args, world, rank, stream, pk, sampler):
+    """Benchmark config 4's W8A8 linears at the block's shapes, M = 20240 tokens: v, q|k, proj and fc1 (GELU +
+    int8 requantization epilogue) on the block's int8 activations, fc2 on fc1's codes - one step is the five
+    GEMM launches of a block (8.15 Top). Weights: int8 codes with per-output-channel scales, as the DiT's."""
+    from hy_nomas_b200 import kernels
+    m = 20240
+    dev = torch.device("cuda")
+    gen = torch.Generator(device=dev).manual_seed(4242 + rank)
+    x = torch.randn(m, 4096, generator=gen, device=dev).to(torch.bfloat16)
+    qa, sa = kernels.quantize_activations(x)
+    ws = {}
+    for name, n, k, _ in DIT_GEMM_SHAPES:
+        q = torch.randint(-127, 128, (n, k), generator=gen, device=dev, dtype=torch.int8)
+        s = (torch.rand(n, generator=gen, device=dev) + 0.5) / (73.6 * k ** 0.5)
+        ws[name] = (q, s, (torch.randn(n, generator=gen, device=dev) * 0.02).to(torch.bfloat16))
+    h_q, h_s = kernels.block_gemm(qa, sa, *ws["fc1"], epilogue="gelu_quant")
+    ops = {name: 2.0 * m * n * k for name, n, k, _ in DIT_GEMM_SHAPES}
+    timers = {name: KernelTimer(stream) for name in ops}
+
+    def step(i):
+        for name, n, k, epi in DIT_GEMM_SHAPES:
+            a, sa_ = (h_q, h_s) if name == "fc2" else (qa, sa)
+            timers[name].wrap(lambda: kernels.block_gemm(a, sa_, *ws[name], epilogue=epi), ops[name])
+
+    ms = timed_steps(step, args.steps, args.warmup, world, stream, sampler)
+    for t in timers.values():
+        t.active = True
+    timed_steps(step, args.steps, 0, world, stream)
+    per = {name: round(ops[name] / (timers[name].mean_ms() * 1e-3) / 1e12, 1) for name in ops}
+    launches = launch_count(lambda: step(0))
+    step_ops = sum(ops.values())
+    total = sum_over_ranks(step_ops * args.steps, world)
+    # e2e: the block's activations from pinned host memory, quantized and run through the five linears by the
+    # public API (fc2 on fc1's requantized output), fc2's output read back
+    xh = x.cpu().pin_memory()
+    yh = torch.empty((m, 4096), dtype=torch.bfloat16).pin_memory()
+
+    def e2e_step(i):
+        xd = xh.to(dev, non_blocking=True)
+        a, sa_ = kernels.quantize_activations(xd)
+        for name in ("v", "qk", "proj"):
+            kernels.block_gemm(a, sa_, *ws[name])
+        hq, hs = kernels.block_gemm(a, sa_, *ws["fc1"], epilogue="gelu_quant")
+        yh.copy_(kernels.block_gemm(hq, hs, *ws["fc2"]), non_blocking=True)
+
+    e2e_ms = timed_steps(e2e_step, args.steps, 1, world, stream)
+    peak = 2.0 * pk["bf16_tflops"]
+    achieved = step_ops / (sum(t.mean_ms() for t in timers.values()) * 1e-3) / 1e12
+    traffic = traffic_for("dit_gemm_shapes")
+    roof = {"kernel": "hn::gemm::k_block_gemm<int8, group activation scales, per-channel weights> (the five)",
+            "bound": "tensor", "achieved": round(achieved, 1), "peak": round(peak, 1), "unit": "TOPS",
+            "frac": round(achieved / peak, 4),
+            "peak_note": f"int8 dense = 2 x {pk['source']} bf16 burst ({pk['bf16_tflops']} TFLOP/s)",
+            "traffic": sum(traffic[n] for n in ops) if traffic else None}
+    config = {"workload": "dit_block_linears_M20240 (config 4): v, q|k, proj, fc1 (GELU + requant), fc2",
+              "M": m, "shapes": {name: f"{n}x{k}" for name, n, k, _ in DIT_GEMM_SHAPES}, "per_shape_tops": per,
+              "activation_scales": "per token x 128 channels", "weight_scales": "per output channel",
+              "l2": "weights 16.8-67 MB per shape and activations 83-331 MB stream between reuses",
+              "parallelism": f"replicas x{world}"}
+    return dict(metric="W8A8 GEMM TOPS (DiT block linears)", value=round(total / (ms * 1e-3) / 1e12, 2), unit="TOPS",
+                ms_per_step=round(ms / args.steps, 4), higher_is_better=True, scaling="weak", dtype="int8",
+                config=config,
+                e2e={"value": round(total / (e2e_ms * 1e-3) / 1e12, 2), "unit": "TOPS",
+                     "h2d_bytes_per_step": xh.numel() * 2 * world, "d2h_bytes_per_step": yh.numel() * 2 * world},
+                roofline=roof, gpu_launches=launches * args.steps,
+                cpu_baseline_fn=lambda: cpu_baseline_gemm(4096, 4096, 4096))
+
+
+def reference_dit_gemms(args):
+    """The reference's CPU path for the block's five linears on 256 of the 20240 rows per step (dequantize +
+    bf16 F.linear each, ops.py:175-176)."""
+    from oracle import torch_ref
+    rows = 256
+    gen = torch.Generator().manual_seed(5)
+    lin = {}
+    for name, n, k, _ in DIT_GEMM_SHAPES:
+        x, q, s, bias = cpu_gemm_sample(rows, n, k, gen)
+        lin[name] = (x, q, s, bias)
+
+    def run():
+        for name, *_ in DIT_GEMM_SHAPES:
+            torch_ref.int8_linear_cpu(*lin[name])
+    for _ in range(args.warmup):
+        run()
+    t0 = time.perf_counter()
+    for _ in range(args.steps):
+        run()
+    dt = time.perf_counter() - t0
+    ops = sum(2.0 * rows * n * k for _, n, k, _ in DIT_GEMM_SHAPES)
+    cores, threads = cpu_threads()
+    return dict(metric="W8A8 GEMM TOPS (DiT block linears)", value=round(ops * args.steps / dt / 1e12, 4), unit="TOPS",
+                ms_per_step=round(dt / args.steps * 1e3, 3), higher_is_better=True, scaling="weak", dtype="int8",
+                kind="port", cores=threads,
+                config={"workload": "dit_block_linears_M20240 (config 4)", "M": 20240},
+                sample=f"{rows} of 20240 rows per step for each of the five linears (dequantize_g128 + bf16 F.linear, "
+                       f"{threads} threads)")
+
+
+# --------------------------------------------------------------------------------------------------------
 # gemm (config 1)
 
 
@@ -882,6 +991,8 @@ def other_elementwise_kernels(m, d, h, hd, stream, sets, shift, scale, w, rope, 
     wt = torch.ones(half, dtype=torch.bfloat16, device="cuda")
     whw = torch.ones(half, dtype=torch.bfloat16, device="cuda")
     kv = [world.quantize_kv(s["q"].view(m, h, hd)) for s in sets]
+    dec_w = torch.ones(d, dtype=torch.bfloat16, device="cuda")
+    gu = [torch.randn(m, 2 * 12288, device="cuda").to(torch.bfloat16) for _ in range(2)]
     cases = {
         "quantize_activations_int8_g128": (lambda i: kernels.quantize_activations(x2d[i % 2]), m * d * 3 + m * (d // 128) * 4),
         "quantize_activations_e4m3_g128": (lambda i: kernels.quantize_activations(x2d[i % 2], "fp8"), m * d * 3 + m * (d // 128) * 4),
@@ -893,6 +1004,12 @@ def other_elementwise_kernels(m, d, h, hd, stream, sets, shift, scale, w, rope, 
         "dequantize_kv": (lambda i: world.dequantize_kv(*kv[i % 2]), m * h * hd * 3 + m * h * 4),
         "qk_norm_rope_kv": (lambda i: fused.qk_norm_rope_kv(sets[i % 2]["q"], w, rope),
                             m * h * hd * 5 + m * h * 4 + 2 * m * hd * 4),
+        # the PixelUMM decoder fusions at its shapes (hidden 4096, intermediate 12288): RMSNorm + e4m3 quantizer,
+        # and silu(gate) * up + e4m3 quantizer over the halves of a [M, 2 x 12288] gate|up output
+        "decoder_rmsnorm_quant_e4m3": (lambda i: fused.rmsnorm_quant(x2d[i % 2], dec_w, 1e-6, "fp8"),
+                                       m * d * 3 + m * (d // 128) * 4 + d * 2),
+        "decoder_silu_mul_quant_e4m3": (lambda i: fused.silu_mul_quant(gu[i % 2][:, :12288], gu[i % 2][:, 12288:], "fp8"),
+                                        m * 12288 * 5 + m * 96 * 4),
     }
     res = {}
     for name, (fn, nbytes) in cases.items():
@@ -1012,7 +1129,8 @@ def reference_elementwise(args):
 # --------------------------------------------------------------------------------------------------------
 
 
-WORKLOADS = {"dit": (workload_dit, reference_dit), "gemm": (workload_gemm, reference_gemm),
+WORKLOADS = {"dit": (workload_dit, reference_dit), "dit_gemms": (workload_dit_gemms, reference_dit_gemms),
+             "gemm": (workload_gemm, reference_gemm),
              "fp8": (workload_fp8, reference_fp8), "elementwise": (workload_elementwise, reference_elementwise)}
 
 

@@ -459,6 +459,37 @@ int hn_dequantize_kv(const int8_t *q, const float *s, int64_t rows, int64_t D, v
     return launched(launch_dequant_kv(q, s, rows, D, y, (cudaStream_t)stream), "hn_dequantize_kv launch");
 }
 
+int hn_rmsnorm_quant(const void *x, int64_t ldx, const void *weight, int64_t rows, int64_t D, float eps, int kind,
+                     void *q, int64_t ldq, float *s, int64_t s_rs, int64_t s_gs, void *stream) {
+    REQUIRE(x && weight && q && s, HN_ERR_ARG, "hn_rmsnorm_quant: null pointer");
+    REQUIRE(kind == HN_KIND_INT8 || kind == HN_KIND_FP8E4M3, HN_ERR_ARG, "hn_rmsnorm_quant: unknown kind %d", kind);
+    REQUIRE(rows >= 0 && D > 0 && D % 128 == 0 && D <= 16384, HN_ERR_SHAPE,
+            "hn_rmsnorm_quant: need D %% 128 == 0 and D <= 16384 (D=%lld)", (long long)D);
+    REQUIRE(rows < (1LL << 31) && ldx >= D && ldq >= D, HN_ERR_SHAPE, "hn_rmsnorm_quant: bad rows or leading dimension");
+    REQUIRE(scale_strides_ok(rows, D / 128, s_rs, s_gs), HN_ERR_SHAPE, "hn_rmsnorm_quant: scale strides overlap");
+    REQUIRE(al16(x) && ldx % 8 == 0 && al16(weight) && al16(q) && ldq % 16 == 0, HN_ERR_ALIGN,
+            "hn_rmsnorm_quant: x/weight/q must be 16-byte aligned with 16-byte row pitches");
+    if (rows == 0) return HN_OK;
+    CHECK_DEVICE(x);
+    return launched(launch_rmsnorm_quant(x, ldx, weight, rows, D, eps, kind, q, ldq, s, s_rs, s_gs, (cudaStream_t)stream),
+                    "hn_rmsnorm_quant launch");
+}
+
+int hn_silu_mul_quant(const void *g, int64_t ldg, const void *u, int64_t ldu, int64_t rows, int64_t I, int kind,
+                      void *q, int64_t ldq, float *s, int64_t s_rs, int64_t s_gs, void *stream) {
+    REQUIRE(g && u && q && s, HN_ERR_ARG, "hn_silu_mul_quant: null pointer");
+    REQUIRE(kind == HN_KIND_INT8 || kind == HN_KIND_FP8E4M3, HN_ERR_ARG, "hn_silu_mul_quant: unknown kind %d", kind);
+    REQUIRE(rows >= 0 && I > 0 && I % 128 == 0, HN_ERR_SHAPE, "hn_silu_mul_quant: need I %% 128 == 0 (I=%lld)", (long long)I);
+    REQUIRE(ldg >= I && ldu >= I && ldq >= I, HN_ERR_SHAPE, "hn_silu_mul_quant: leading dimension too small");
+    REQUIRE(scale_strides_ok(rows, I / 128, s_rs, s_gs), HN_ERR_SHAPE, "hn_silu_mul_quant: scale strides overlap");
+    REQUIRE(al16(g) && al16(u) && ldg % 8 == 0 && ldu % 8 == 0 && al16(q) && ldq % 16 == 0, HN_ERR_ALIGN,
+            "hn_silu_mul_quant: g/u/q must be 16-byte aligned with 16-byte row pitches");
+    if (rows == 0) return HN_OK;
+    CHECK_DEVICE(g);
+    return launched(launch_silu_mul_quant(g, ldg, u, ldu, rows, I, kind, q, ldq, s, s_rs, s_gs, (cudaStream_t)stream),
+                    "hn_silu_mul_quant launch");
+}
+
 int hn_quantize_fp8_block(const void *w, int w_dtype, int64_t N, int64_t K, void *q, float *s, void *stream) {
     REQUIRE(w && q && s, HN_ERR_ARG, "hn_quantize_fp8_block: null pointer");
     REQUIRE(w_dtype == HN_DTYPE_FP32 || w_dtype == HN_DTYPE_BF16, HN_ERR_ARG,

@@ -39,6 +39,12 @@ cudaError_t launch_qk_norm_rope(int ntensors, const void *x0, const void *x1, in
 
 cudaError_t launch_dequant_kv(const int8_t *q, const float *s, int64_t rows, int64_t D, void *y, cudaStream_t st);
 
+// decoder.cu: kind 0 int8, 1 e4m3 codes
+cudaError_t launch_rmsnorm_quant(const void *x, int64_t ldx, const void *w, int64_t rows, int64_t D, float eps,
+                                 int kind, void *q, int64_t ldq, float *s, int64_t s_rs, int64_t s_gs, cudaStream_t st);
+cudaError_t launch_silu_mul_quant(const void *g, int64_t ldg, const void *u, int64_t ldu, int64_t rows, int64_t I,
+                                  int kind, void *q, int64_t ldq, float *s, int64_t s_rs, int64_t s_gs, cudaStream_t st);
+
 cudaError_t launch_pixelumm_qk(const void *x, int64_t row_stride, const void *wt, const void *whw, const float *cos,
                                const float *sin, int64_t N, int64_t H, float eps, void *y, cudaStream_t st);
 

@@ -117,54 +117,6 @@ __global__ void __launch_bounds__(256) k_quant_group(const TIn *__restrict__ x, 
     }
 }
 
-// 8 elements of a row -> 8 codes (int8 bytes or e4m3 bytes) for scale `sc`; `fast`: bf16 input with the
-// exact fma-corrected quotient (as in k_quant_group), else IEEE division.
-template <int KIND, bool RNE>
-__device__ __forceinline__ uint2 quant_chunk8(const float (&v)[8], float sc, bool fast, uint64_t ns, uint64_t rs) {
-    uint2 out;
-    if (fast && KIND == 0 && RNE) {
-        int cc[8];
-#pragma unroll
-        for (int i = 0; i < 4; ++i) {
-            float q0, q1;
-            x2_split(x2_quot(x2(v[2 * i], v[2 * i + 1]), ns, rs), q0, q1);
-            cc[2 * i] = code_i8_rne(q0);
-            cc[2 * i + 1] = code_i8_rne(q1);
-        }
-        out.x = pack4_i8(cc[0], cc[1], cc[2], cc[3]);
-        out.y = pack4_i8(cc[4], cc[5], cc[6], cc[7]);
-    } else if (fast && KIND == 0) {
-        uint32_t cc[8];
-#pragma unroll
-        for (int i = 0; i < 4; ++i) x2_codes(x2_quot(x2(v[2 * i], v[2 * i + 1]), ns, rs), cc[2 * i], cc[2 * i + 1]);
-        out.x = pack4_lowbytes(cc[0], cc[1], cc[2], cc[3]);
-        out.y = pack4_lowbytes(cc[4], cc[5], cc[6], cc[7]);
-    } else if (fast) {
-        uint32_t h[4];
-#pragma unroll
-        for (int i = 0; i < 4; ++i) {
-            float q0, q1;
-            x2_split(x2_quot(x2(v[2 * i], v[2 * i + 1]), ns, rs), q0, q1);
-            h[i] = pack2_e4m3(copysignf(q0, v[2 * i]), copysignf(q1, v[2 * i + 1]));
-        }
-        out.x = h[0] | (h[1] << 16);
-        out.y = h[2] | (h[3] << 16);
-    } else if (KIND == 0) {
-        int cc[8];
-#pragma unroll
-        for (int i = 0; i < 8; ++i) cc[i] = RNE ? code_i8_rne(__fdiv_rn(v[i], sc)) : code_i8(__fdiv_rn(v[i], sc));
-        out.x = pack4_i8(cc[0], cc[1], cc[2], cc[3]);
-        out.y = pack4_i8(cc[4], cc[5], cc[6], cc[7]);
-    } else {
-        uint32_t h[4];
-#pragma unroll
-        for (int i = 0; i < 4; ++i) h[i] = pack2_e4m3(__fdiv_rn(v[2 * i], sc), __fdiv_rn(v[2 * i + 1], sc));
-        out.x = h[0] | (h[1] << 16);
-        out.y = h[2] | (h[3] << 16);
-    }
-    return out;
-}
-
 // Per-row variant: one CTA of 256 threads per row. NCH > 0: the row stays in registers, NCH chunks of 8
 // elements per thread (chunk c at elements [8c, 8c + 8), thread t holding chunks t, t + 256, ...: one HBM
 // pass, coalesced 16-byte loads); NCH == 0 (rows longer than 16384): two passes, the second from L2.

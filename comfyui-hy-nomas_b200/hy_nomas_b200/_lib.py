@@ -44,6 +44,8 @@ SIGNATURES = {
     "hn_dequantize_kv": [_V, _V, _I64, _I64, _V, _V],
     "hn_qk_norm_rope_kv": [_V, _I64, _V, _V, _V, _I64, _I64, _I64, _I64, _F32, _V, _V, _V, _V],
     "hn_quantize_fp8_block": [_V, _I32, _I64, _I64, _V, _V, _V],
+    "hn_rmsnorm_quant": [_V, _I64, _V, _I64, _I64, _F32, _I32, _V, _I64, _V, _I64, _I64, _V],
+    "hn_silu_mul_quant": [_V, _I64, _V, _I64, _I64, _I64, _I32, _V, _I64, _V, _I64, _I64, _V],
 }
 
 

@@ -11,7 +11,9 @@ libhynomas_b200.so and rounds where the reference rounds:
 
 Two fused variants go further than the reference: `gated_residual_adaln_quant` (the residual and the next
 LayerNorm/modulate/int8 quantization in one pass, hy_nomas/model.py:280-282) and `qk_norm_rope2` (q and k
-in one launch, reading the RoPE tables once). `HY_NOMAS_FUSED=0` disables `available()`, as in the
+in one launch, reading the RoPE tables once). For the PixelUMM decoder, `rmsnorm_quant` and `silu_mul_quant`
+are the RMSNorm and SiLU fusions the reference's notes name (README.md:266): each ends in the activation
+quantizer of the FP8 linears that read its output, so neither writes its bf16 result. `HY_NOMAS_FUSED=0` disables `available()`, as in the
 reference.
 """
 import os
@@ -182,3 +184,49 @@ def pixelumm_qk(x, weight_t, weight_hw, cos, sin, eps=1e-6):
                                  n, h, d, eps, _lib.ptr(y), _lib.stream_of(x))
     _lib.check(rc, "pixelumm_qk")
     return y
+
+
+_KINDS = {"int8": (0, torch.int8), "fp8": (1, torch.float8_e4m3fn)}
+
+
+def rmsnorm_quant(x, weight, eps=1e-6, kind="fp8"):
+    """The decoder's RMSNorm (hy_nomas/pixelumm.py:246-259: normalize in fp32, cast to bf16, times the bf16
+    weight) and the quantizer of the linears that read it (kernels.quantize_activations, as block_linear runs it
+    for the FP8 decoder linears, pixelumm.py:147-155) in one pass: x [..., D] bf16 -> (codes [rows, D], fp32
+    scales [rows, D / 128]), the normalized activations never written."""
+    _lib.require_cuda(x, weight)
+    _bf16(x)
+    d = x.shape[-1]
+    x2 = _lib.dense(x.reshape(-1, d))
+    rows = x2.shape[0]
+    code, dtype = _KINDS[kind]
+    w = _lib.dense(weight.to(torch.bfloat16))
+    q = torch.empty((rows, d), device=x.device, dtype=dtype)
+    s, srs, sgs = _lib.group_scales(rows, d // 128, x.device)
+    rc = _lib.lib.hn_rmsnorm_quant(_lib.ptr(x2), x2.stride(0), _lib.ptr(w), rows, d, eps, code, _lib.ptr(q),
+                                   q.stride(0), _lib.ptr(s), srs, sgs, _lib.stream_of(x2))
+    _lib.check(rc, "rmsnorm_quant")
+    return q, s
+
+
+def silu_mul_quant(gate, up, kind="fp8"):
+    """silu(gate) * up of the decoder MLP (hy_nomas/pixelumm.py:322-323, with torch's bf16 roundings) and down_proj's
+    activation quantizer in one pass: gate, up [rows, I] bf16 (rows may be strided, e.g. the two halves of one
+    stacked gate|up GEMM output) -> (codes [rows, I], fp32 scales [rows, I / 128])."""
+    _lib.require_cuda(gate, up)
+    _bf16(gate, up)
+    rows, i = gate.shape
+    if up.shape != gate.shape:
+        raise ValueError(f"silu_mul_quant: gate {tuple(gate.shape)} and up {tuple(up.shape)} differ")
+
+    def rows_ok(t):
+        return t.stride(1) == 1 and t.stride(0) % 8 == 0 and t.data_ptr() % 16 == 0
+    g = gate if rows_ok(gate) else _lib.dense(gate)
+    u = up if rows_ok(up) else _lib.dense(up)
+    code, dtype = _KINDS[kind]
+    q = torch.empty((rows, i), device=gate.device, dtype=dtype)
+    s, srs, sgs = _lib.group_scales(rows, i // 128, gate.device)
+    rc = _lib.lib.hn_silu_mul_quant(_lib.ptr(g), g.stride(0), _lib.ptr(u), u.stride(0), rows, i, code, _lib.ptr(q),
+                                    q.stride(0), _lib.ptr(s), srs, sgs, _lib.stream_of(g))
+    _lib.check(rc, "silu_mul_quant")
+    return q, s

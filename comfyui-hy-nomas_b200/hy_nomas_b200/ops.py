@@ -71,3 +71,25 @@ def fp8_block_linear(x, qdata, scale, bias=None):
     weights on the tensor cores, output in x's dtype."""
     from .kernels import block_linear
     return block_linear(x, qdata, scale, bias, kind="fp8")
+
+
+def stack_fp8_linears(*linears):
+    """FP8 block-scaled linears with the same K, stacked along N into one: (codes [sum N, K], block scales
+    [sum N / 128, K / 128]). The decoder MLP's gate_proj and up_proj read the same input, so one GEMM does both."""
+    return torch.cat([q for q, _ in linears]), torch.cat([s for _, s in linears])
+
+
+def decoder_mlp(x, norm_weight, gate_up, down, eps=1e-6):
+    """The MLP half of the PixelUMM decoder layer, x + mlp(post_attn_norm(x)) (hy_nomas/pixelumm.py:320-337), on the
+    fused kernels: RMSNorm + e4m3 quantization (one pass), the stacked gate|up FP8 GEMM (bf16 out), silu(gate) *
+    up + e4m3 quantization (one pass), down_proj's FP8 GEMM, the residual. x [..., hidden] bf16; gate_up =
+    stack_fp8_linears((gate codes, gate block scales), (up codes, up block scales)); down = (codes, block scales)."""
+    from . import fused
+    from .kernels import block_gemm
+    shape = x.shape
+    q, s = fused.rmsnorm_quant(x, norm_weight, eps, kind="fp8")
+    gu = block_gemm(q, s, gate_up[0], gate_up[1], kind="fp8")
+    inter = gu.shape[1] // 2
+    hq, hs = fused.silu_mul_quant(gu[:, :inter], gu[:, inter:], kind="fp8")
+    y = block_gemm(hq, hs, down[0], down[1], kind="fp8")
+    return x + y.view(shape)

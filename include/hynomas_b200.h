@@ -241,6 +241,29 @@ int hn_qk_norm_rope_kv(const void *x, int64_t row_stride, const void *weight, co
  */
 int hn_quantize_fp8_block(const void *w, int w_dtype, int64_t N, int64_t K, void *q, float *s, void *stream);
 
+/*
+ * PixelUMM decoder: RMSNorm + the activation quantizer of the FP8 (or int8) linears that read its output, in one
+ * pass. Replaces hy_nomas/pixelumm.py:246-259 (RMSNorm.forward, the decoder layer's input_norm and
+ * post_attn_norm) followed by the quantizer block_linear runs for the next linears (kernels.py:22-54 via
+ * pixelumm.py:147-155); the normalized activations are not written. A fusion of the reference's sequence, named
+ * in its notes (README.md:266 "RMSNorm/SiLU fusions").
+ * x [rows, D] bf16 (row pitch ldx), weight [D] bf16 -> y = rbf16(w * rbf16(x * 1/sqrt(mean(x^2) + eps))) quantized
+ * per row and 128 columns: codes q [rows, D] (int8 or e4m3 by `kind`, pitch ldq), scales s[r * s_rs + g * s_gs].
+ * D % 128 == 0, D <= 16384; x, weight, q 16-byte aligned with 16-byte row pitches.
+ */
+int hn_rmsnorm_quant(const void *x, int64_t ldx, const void *weight, int64_t rows, int64_t D, float eps, int kind,
+                     void *q, int64_t ldq, float *s, int64_t s_rs, int64_t s_gs, void *stream);
+
+/*
+ * PixelUMM decoder MLP gate: silu(gate) * up (torch's bf16 roundings: silu(g) = g / (1 + exp(-g)) in fp32 rounded
+ * to bf16, times up, rounded to bf16) quantized for down_proj in the same pass. Replaces hy_nomas/pixelumm.py:322-323
+ * (MLP.forward's F.silu(gate_proj(x)) * up_proj(x)) followed by down_proj's activation quantizer (kernels.py:22-54).
+ * g, u [rows, I] bf16 (pitches ldg, ldu; e.g. the two halves of one stacked gate|up GEMM output) -> codes q [rows, I]
+ * and scales s[r * s_rs + g * s_gs] per 128 columns. I % 128 == 0; g, u, q 16-byte aligned with 16-byte pitches.
+ */
+int hn_silu_mul_quant(const void *g, int64_t ldg, const void *u, int64_t ldu, int64_t rows, int64_t I, int kind,
+                      void *q, int64_t ldq, float *s, int64_t s_rs, int64_t s_gs, void *stream);
+
 #if defined(__GNUC__)
 #pragma GCC visibility pop
 #endif

@@ -448,6 +448,55 @@ void or_dequantize_kv(const int8_t *q, const float *s, int64_t rows, int64_t D, 
  * Helpers the tests use: bf16 rounding of fp32 arrays, and the Markstein-corrected quotient that the
  * quantizers may use in place of a division (checked here against IEEE division on the CPU).
  */
+/* ---------------------------------------------------------------------------------------------------
+ * PixelUMM decoder fusions (the RMSNorm and SiLU fusions the reference's notes name, README.md:266), each
+ * ending in the activation quantizer (kernels.py:22-42) of the linears that read its output: the FP8 decoder
+ * linears quantize their input per 1 x 128 through block_linear (pixelumm.py:147-155).
+ *
+ * or_rmsnorm_quant - pixelumm.py:246-259 (Qwen3 RMSNorm): ss = sum of x^2, a balanced pairwise tree in index
+ * order over the row zero-padded to 2048 * next_pow2(ceil(D / 2048)) (the kernel's layout: 8-element chunks,
+ * chunk c held by thread c % 256 of a 256-thread CTA); ms = ss / D; r = 1 / sqrt(ms + eps);
+ * y = rbf16(w * rbf16(x * r)) (normalize in fp32, cast to bf16, times the bf16 weight); then codes and scales
+ * per 128 (kind 0 int8, 1 e4m3).
+ */
+static int64_t chunk_pad(int64_t D) {
+    int64_t n = (D + 2047) / 2048, p = 1;
+    while (p < n) p <<= 1;
+    return 2048 * p;
+}
+
+void or_rmsnorm_quant(const float *x, const float *w, int64_t rows, int64_t D, float eps, int kind, uint8_t *q,
+                      float *s) {
+    float *sq = (float *)malloc(sizeof(float) * D), *y = (float *)malloc(sizeof(float) * D);
+    const int64_t P = chunk_pad(D);
+    for (int64_t r = 0; r < rows; ++r) {
+        const float *xr = x + r * D;
+        for (int64_t i = 0; i < D; ++i) sq[i] = xr[i] * xr[i];
+        float ms = pairwise(sq, D, P) / (float)D;
+        float rs = 1.0f / sqrtf(ms + eps);
+        for (int64_t i = 0; i < D; ++i) y[i] = rbf16(w[i] * rbf16(xr[i] * rs));
+        or_quant_act(y, 1, D, kind, GROUP, q + r * D, s + r * (D / GROUP));
+    }
+    free(sq);
+    free(y);
+}
+
+/* or_silu_mul_quant - pixelumm.py:322-323 (MLP.forward): h = silu(gate) * up with torch's bf16 roundings,
+ * silu(g) = g / (1 + exp(-g)) in fp32 rounded to bf16 (exp: this oracle's, the kernels' own), times u, rounded
+ * to bf16; then codes and scales per 128 for down_proj. g, u [rows, I] (bf16 values as fp32). */
+void or_silu_mul_quant(const float *g, const float *u, int64_t rows, int64_t I, int kind, uint8_t *q, float *s) {
+    float *h = (float *)malloc(sizeof(float) * I);
+    for (int64_t r = 0; r < rows; ++r) {
+        for (int64_t i = 0; i < I; ++i) {
+            float gv = g[r * I + i];
+            float sl = rbf16(gv / (1.0f + or_expf(-gv)));
+            h[i] = rbf16(sl * u[r * I + i]);
+        }
+        or_quant_act(h, 1, I, kind, GROUP, q + r * I, s + r * (I / GROUP));
+    }
+    free(h);
+}
+
 void or_round_bf16(const float *x, int64_t n, float *y) {
     for (int64_t i = 0; i < n; ++i) y[i] = rbf16(x[i]);
 }

@@ -18,6 +18,8 @@ built here with gcc -ffp-contract=off) behind numpy functions named after the re
   dequantize_g128        hy_nomas/ops.py:55-62
   quantize_fp8_block     hy_nomas/pixelumm.py:77-82
   quantize_kv            hy_nomas/world.py:83-90
+  rmsnorm_quant          hy_nomas/pixelumm.py:246-259 + kernels.py:22-42 (decoder norm, then the FP8 quantizer)
+  silu_mul_quant         hy_nomas/pixelumm.py:322-323 + kernels.py:22-42 (decoder MLP gate, then the quantizer)
 
 Parity of this oracle with the reference is pinned by tests/test_oracle_golden.py against vectors made
 by tests/golden/make_golden.py from the reference's own code.
@@ -58,6 +60,8 @@ def lib():
         p = ctypes.c_void_p
         sig = {
             "or_quant_act": [p, i64, i64, i32, i64, p, p],
+            "or_rmsnorm_quant": [p, p, i64, i64, f32, i32, p, p],
+            "or_silu_mul_quant": [p, p, i64, i64, i32, p, p],
             "or_quantize_fp8_block": [p, i64, i64, p, p],
             "or_block_gemm": [p, p, i32, p, p, i32, p, i64, i64, i64, i32, i32, i32, p, p, p],
             "or_adaln": [p, p, p, i64, i64, i64, f32, p],
@@ -275,6 +279,29 @@ def pixelumm_qk(x, weight_t, weight_hw, cos, sin, eps=1e-6):
     lib().or_pixelumm_qk(_ptr(x), _ptr(_f32(weight_t)), _ptr(_f32(weight_hw)), _ptr(_f32(cos)), _ptr(_f32(sin)),
                          n, h, d, eps, _ptr(y))
     return y
+
+
+def rmsnorm_quant(x, weight, eps=1e-6, kind="fp8"):
+    """The PixelUMM decoder's RMSNorm (hy_nomas/pixelumm.py:246-259) and the activation quantizer of the linears
+    that read it (kernels.py:22-42). x [rows, D] bf16 values as float32, weight [D] -> (codes uint8 [rows, D],
+    float32 scales [rows, D / 128])."""
+    x = _f32(x)
+    rows, d = x.shape
+    q = np.empty((rows, d), dtype=np.uint8)
+    s = np.empty((rows, d // GROUP), dtype=np.float32)
+    lib().or_rmsnorm_quant(_ptr(x), _ptr(_f32(weight)), rows, d, eps, 0 if kind == "int8" else 1, _ptr(q), _ptr(s))
+    return q, s
+
+
+def silu_mul_quant(g, u, kind="fp8"):
+    """silu(gate) * up of the decoder MLP (hy_nomas/pixelumm.py:322-323) and down_proj's activation quantizer.
+    g, u [rows, I] bf16 values as float32 -> (codes uint8 [rows, I], float32 scales [rows, I / 128])."""
+    g, u = _f32(g), _f32(u)
+    rows, i = g.shape
+    q = np.empty((rows, i), dtype=np.uint8)
+    s = np.empty((rows, i // GROUP), dtype=np.float32)
+    lib().or_silu_mul_quant(_ptr(g), _ptr(u), rows, i, 0 if kind == "int8" else 1, _ptr(q), _ptr(s))
+    return q, s
 
 
 def quantize_kv(x):

@@ -5,7 +5,7 @@ import numpy as np
 import pytest
 import torch
 
-from hn_testutil import bf16_from_bits, bits16, f32
+from hn_testutil import bf16_from_bits, bits16, f32, rel_l2, u8
 
 pytestmark = pytest.mark.gpu
 
@@ -170,3 +170,60 @@ def test_pixelumm_qk(hn, oracle, golden, cuda):
     ref = oracle.pixelumm_qk(f32(x), f32(wt), f32(whw), d["cos"], d["sin"])
     assert np.array_equal(bits16(y), oracle.bf16_bits(ref))
     assert (bits16(y) != d["y"]).mean() < 1e-3
+
+
+@pytest.mark.parametrize("kind", ["fp8", "int8"])
+@pytest.mark.parametrize("rows,d", [(300, 4096), (7, 640), (129, 2048), (33, 12288)])
+def test_rmsnorm_quant_bit_exact(hn, oracle, cuda, kind, rows, d):
+    """The decoder's RMSNorm + activation quantizer (pixelumm.py:246-259 then kernels.py:22-42) in one pass: codes
+    and scales equal the oracle's bit for bit (the oracle is pinned to the reference's RMSNorm by
+    test_decoder_fusions_pinned_to_reference)."""
+    gen = torch.Generator().manual_seed(rows + d)
+    x = (torch.randn(rows, d, generator=gen) * 2.0).bfloat16()
+    x[0] *= 50.0
+    x[1 % rows] = 0.0
+    w = (1.0 + 0.2 * torch.randn(d, generator=gen)).bfloat16()
+    q, s = hn.fused.rmsnorm_quant(x.to(cuda), w.to(cuda), 1e-6, kind)
+    torch.cuda.synchronize()
+    qo, so = oracle.rmsnorm_quant(f32(x), f32(w), 1e-6, kind)
+    assert np.array_equal(u8(q), qo) and np.array_equal(f32(s), so)
+
+
+@pytest.mark.parametrize("kind", ["fp8", "int8"])
+@pytest.mark.parametrize("rows,inter", [(300, 12288), (5, 384), (64, 128)])
+def test_silu_mul_quant_bit_exact(hn, oracle, cuda, kind, rows, inter):
+    """silu(gate) * up + quantizer (pixelumm.py:322-323 then kernels.py:22-42), reading the two halves of one
+    stacked gate|up output (strided rows): codes and scales equal the oracle's bit for bit."""
+    gen = torch.Generator().manual_seed(rows * 3 + inter)
+    gu = (torch.randn(rows, 2 * inter, generator=gen) * 3.0).bfloat16()
+    gu[0, :6] = torch.tensor([0.0, -0.0, 95.0, -95.0, 1e-3, -1e-3]).bfloat16()
+    dev = gu.to(cuda)
+    q, s = hn.fused.silu_mul_quant(dev[:, :inter], dev[:, inter:], kind)
+    torch.cuda.synchronize()
+    qo, so = oracle.silu_mul_quant(f32(gu[:, :inter]), f32(gu[:, inter:]), kind)
+    assert np.array_equal(u8(q), qo) and np.array_equal(f32(s), so)
+
+
+def test_decoder_mlp_against_reference_arithmetic(hn, cuda):
+    """The decoder layer's MLP half on the fused kernels (ops.decoder_mlp: RMSNorm + e4m3 quantization, one
+    stacked gate|up FP8 GEMM, silu * up + e4m3 quantization, down_proj's FP8 GEMM, residual) against the
+    reference's arithmetic in torch on the same FP8 weights (pixelumm.py:246-259, 320-337: RMSNorm, dequantized
+    weights, bf16 F.linear, F.silu): within the FP8 tolerance, rel-L2 <= 1e-2."""
+    import torch.nn.functional as F
+    from oracle import torch_ref
+    gen = torch.Generator().manual_seed(17)
+    m, hidden, inter = 256, 1024, 3072
+    x = torch.randn(1, m, hidden, generator=gen).bfloat16()
+    w_norm = (1.0 + 0.1 * torch.randn(hidden, generator=gen)).bfloat16()
+    wg, wu = torch.randn(inter, hidden, generator=gen) * 0.02, torch.randn(inter, hidden, generator=gen) * 0.02
+    wd = torch.randn(hidden, inter, generator=gen) * 0.02
+    q8 = [hn.ops.quantize_fp8_block(t.to(cuda)) for t in (wg, wu, wd)]
+    gate_up = hn.ops.stack_fp8_linears(q8[0], q8[1])
+    y = hn.ops.decoder_mlp(x.to(cuda), w_norm.to(cuda), gate_up, q8[2])
+    torch.cuda.synchronize()
+    xf = x.float()
+    n = (xf * torch.rsqrt(xf.pow(2).mean(-1, keepdim=True) + 1e-6)).to(torch.bfloat16)
+    n = w_norm * n
+    deq = [torch_ref.fp8_block_dequantize(q.cpu(), s.cpu()) for q, s in q8]
+    ref = x + F.linear(F.silu(F.linear(n, deq[0])) * F.linear(n, deq[1]), deq[2])
+    assert rel_l2(f32(y), f32(ref)) <= 1e-2

@@ -129,3 +129,20 @@ def test_dequantize_kv(oracle, golden):
     d = golden("quantize_kv")  # world.py:93-94, on the reference's own codes and scales
     y = oracle.dequantize_kv(d["q"], d["s"])
     assert np.array_equal(oracle.bf16_bits(y), d["y"])
+
+
+def test_decoder_fusions_pinned_to_reference(oracle, golden):
+    """The decoder fusions' oracle against the reference's own pixelumm.RMSNorm and MLP gate expression
+    (tests/golden/make_decoder_golden.py), each followed by the reference's activation quantizer: on these vectors
+    the codes and scales equal the quantizer's output for the reference's bf16 result, e4m3 and int8 alike
+    (torch's summation order and exp move no bf16 rounding here)."""
+    d = golden("decoder")
+    b2f = oracle.from_bf16_bits
+    x, w, y, g, u, h = (b2f(d[k]) for k in ("x", "w", "y", "g", "u", "h"))
+    for kind in ("fp8", "int8"):
+        q, s = oracle.rmsnorm_quant(x, w, float(d["eps"]), kind=kind)
+        q_ref, s_ref = oracle.quantize_activations(y, kind)
+        assert np.array_equal(q, q_ref) and np.array_equal(s, s_ref)
+        q, s = oracle.silu_mul_quant(g, u, kind=kind)
+        q_ref, s_ref = oracle.quantize_activations(h, kind)
+        assert np.array_equal(q, q_ref) and np.array_equal(s, s_ref)
