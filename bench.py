@@ -320,7 +320,9 @@ def workload_dit(args, world, rank, stream, pk, sampler):
               "model": "synthetic Hy-Nomas-style DiT (random init, seeded)", "global_batch": 1, "seq_len": L,
               "tokens_per_rank": hi - lo, "blocks": cfg.blocks, "hidden": d, "heads": cfg.heads, "mlp": d * cfg.mlp_ratio,
               "activation_scales": "per token x 128 channels", "weight_scales": "per output channel",
-              "parallelism": f"sp{world} (sequence-parallel, K/V all-gather over NCCL; weights replicated)",
+              "parallelism": f"sp{world} (sequence-parallel; weights replicated)",
+              "kv_exchange": {"ce": "copy-engine pushes over NVLink into CUDA-IPC-mapped peer buffers, flag-gated",
+                              "nccl": "NCCL all-gather", "none": "none (one rank)"}[sp.exchange],
               "l2": "12 GB of weights stream through L2 between reuses of a step's input",
               "step_breakdown_ms_rank0": {"gemm": round(gemm_ms, 2), "attention": round(attn_ms, 2),
                                           "other": round(max(step_ms - gemm_ms - attn_ms, 0.0), 2)},
@@ -334,6 +336,7 @@ def workload_dit(args, world, rank, stream, pk, sampler):
         config["segment2_with_int8_history"] = segment2_context(model, vec, world, stream)
     if world == 1 and not args.no_context:
         config["configs_1_to_3"] = path_context(stream, pk)
+    sp.close()
     return dict(metric="DiT denoise step tokens/s (40 blocks, 20240 tokens)", value=round(value, 1), unit="tokens/s",
                 ms_per_step=round(step_ms, 3), higher_is_better=True, scaling="strong", dtype="int8 (GEMMs), bf16",
                 config=config,

@@ -12,6 +12,9 @@
 #include <mutex>
 #include <string>
 
+#include <cuda.h>
+#include <cudaTypedefs.h>
+
 #include "../../include/hynomas_b200.h"
 #include "hn_common.cuh"
 #include "hn_kernels.h"
@@ -501,6 +504,109 @@ int hn_quantize_fp8_block(const void *w, int w_dtype, int64_t N, int64_t K, void
     if (N == 0 || K == 0) return HN_OK;
     CHECK_DEVICE(w);
     return launched(launch_quant_fp8_block(w, w_dtype, N, K, q, s, (cudaStream_t)stream), "hn_quantize_fp8_block launch");
+}
+
+} // extern "C"
+
+// ---------------------------------------------------------------------------------------------------
+// Sequence-parallel K/V exchange over NVLink by the copy engines (host-side only: CUDA IPC mappings, an
+// asynchronous peer copy, a 32-bit flag write the GPU's front end executes after the copy - no SM involved - and a
+// one-warp bounded wait for the peers' flags). No reference counterpart: the reference runs one GPU.
+
+namespace hn {
+
+typedef CUresult(CUDAAPI *PfnWrite32)(CUstream, CUdeviceptr, cuuint32_t, unsigned int);
+typedef CUresult(CUDAAPI *PfnAddrRange)(CUdeviceptr *, size_t *, CUdeviceptr);
+
+template <typename F> static F driver_fn(const char *name) {
+    void *ptr = nullptr;
+    cudaDriverEntryPointQueryResult q;
+    if (cudaGetDriverEntryPointByVersion(name, &ptr, 12000, cudaEnableDefault, &q) != cudaSuccess ||
+        q != cudaDriverEntryPointSuccess) {
+        cudaGetLastError();
+        return nullptr;
+    }
+    return reinterpret_cast<F>(ptr);
+}
+
+static int cu_fail(CUresult r, const char *what) {
+    return fail(HN_ERR_CUDA, "%s failed (CUresult %d)", what, (int)r);
+}
+
+} // namespace hn
+
+extern "C" {
+
+int hn_ipc_export(const void *ptr, void *handle_host, int64_t *offset_host) {
+    REQUIRE(ptr && handle_host && offset_host, HN_ERR_ARG, "hn_ipc_export: null pointer");
+    static PfnAddrRange range = driver_fn<PfnAddrRange>("cuMemGetAddressRange");
+    REQUIRE(range != nullptr, HN_ERR_CUDA, "hn_ipc_export: cuMemGetAddressRange unavailable");
+    CUdeviceptr base = 0;
+    size_t size = 0;
+    CUresult r = range(&base, &size, reinterpret_cast<CUdeviceptr>(ptr));
+    if (r != CUDA_SUCCESS) return cu_fail(r, "cuMemGetAddressRange");
+    cudaIpcMemHandle_t h;
+    cudaError_t e = cudaIpcGetMemHandle(&h, reinterpret_cast<void *>(base));
+    if (e != cudaSuccess) return cuda_fail(e, "cudaIpcGetMemHandle");
+    memcpy(handle_host, &h, sizeof(h));
+    *offset_host = (int64_t)(reinterpret_cast<CUdeviceptr>(ptr) - base);
+    t_last_error.clear();
+    return HN_OK;
+}
+
+int hn_ipc_import(const void *handle_host, void **base_host) {
+    REQUIRE(handle_host && base_host, HN_ERR_ARG, "hn_ipc_import: null pointer");
+    cudaIpcMemHandle_t h;
+    memcpy(&h, handle_host, sizeof(h));
+    void *base = nullptr;
+    cudaError_t e = cudaIpcOpenMemHandle(&base, h, cudaIpcMemLazyEnablePeerAccess);
+    if (e != cudaSuccess) return cuda_fail(e, "cudaIpcOpenMemHandle");
+    *base_host = base;
+    t_last_error.clear();
+    return HN_OK;
+}
+
+int hn_ipc_close(void *base) {
+    REQUIRE(base != nullptr, HN_ERR_ARG, "hn_ipc_close: null pointer");
+    cudaError_t e = cudaIpcCloseMemHandle(base);
+    if (e != cudaSuccess) return cuda_fail(e, "cudaIpcCloseMemHandle");
+    t_last_error.clear();
+    return HN_OK;
+}
+
+int hn_peer_push(void *dst, const void *src, int64_t bytes, void *flag, uint32_t value, void *stream) {
+    REQUIRE(dst && src && bytes >= 0, HN_ERR_ARG, "hn_peer_push: null pointer or negative size");
+    static PfnWrite32 write32 = driver_fn<PfnWrite32>("cuStreamWriteValue32");
+    REQUIRE(flag == nullptr || write32 != nullptr, HN_ERR_CUDA, "hn_peer_push: cuStreamWriteValue32 unavailable");
+    StreamDevice sd(stream);
+    if (sd.err != cudaSuccess) return cuda_fail(sd.err, "cudaStreamGetDevice");
+    cudaStream_t st = static_cast<cudaStream_t>(stream);
+    if (bytes > 0) {
+        cudaError_t e = cudaMemcpyAsync(dst, src, (size_t)bytes, cudaMemcpyDeviceToDevice, st);
+        if (e != cudaSuccess) return cuda_fail(e, "cudaMemcpyAsync (peer push)");
+    }
+    if (flag != nullptr) {
+        // default flags: a memory fence precedes the write, so the copy above is visible before the flag
+        CUresult r = write32(reinterpret_cast<CUstream>(st), reinterpret_cast<CUdeviceptr>(flag), value, 0);
+        if (r != CUDA_SUCCESS) return cu_fail(r, "cuStreamWriteValue32");
+    }
+    t_last_error.clear();
+    return HN_OK;
+}
+
+int hn_wait_flags(const int32_t *flags, int64_t groups, int64_t count, int64_t skip, uint32_t value,
+                  uint32_t timeout_us, void *stream) {
+    REQUIRE(flags != nullptr, HN_ERR_ARG, "hn_wait_flags: null pointer");
+    REQUIRE(groups >= 0 && count >= 0 && groups <= 1024 && count <= 1024 && groups * count <= 1024, HN_ERR_SHAPE,
+            "hn_wait_flags: need 0 <= groups * count <= 1024 (groups=%lld count=%lld)", (long long)groups,
+            (long long)count);
+    REQUIRE(timeout_us > 0 && timeout_us <= 600000000u, HN_ERR_ARG, "hn_wait_flags: timeout_us must be in (0, 6e8]");
+    REQUIRE(((uintptr_t)flags % 4) == 0, HN_ERR_ALIGN, "hn_wait_flags: flags must be 4-byte aligned");
+    if (groups * count == 0) return HN_OK;
+    CHECK_DEVICE(flags);
+    return launched(launch_wait_flags(reinterpret_cast<const uint32_t *>(flags), (int)groups, (int)count, (int)skip,
+                                      value, timeout_us, static_cast<cudaStream_t>(stream)),
+                    "hn_wait_flags launch");
 }
 
 } // extern "C"

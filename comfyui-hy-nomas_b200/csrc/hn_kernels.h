@@ -75,5 +75,8 @@ cudaError_t launch_wait_selftest(uint32_t timeout_us, cudaStream_t st);
 
 // read slot `slot` of the current device's error words into *value and clear it (synchronous)
 cudaError_t read_and_clear_device_error(int slot, int *value);
+// one warp waits (bounded) until flags[g * count + i] >= value for every g < groups, i < count, i != skip
+cudaError_t launch_wait_flags(const uint32_t *flags, int groups, int count, int skip, uint32_t value,
+                              uint32_t timeout_us, cudaStream_t st);
 
 } // namespace hn

@@ -46,6 +46,11 @@ SIGNATURES = {
     "hn_quantize_fp8_block": [_V, _I32, _I64, _I64, _V, _V, _V],
     "hn_rmsnorm_quant": [_V, _I64, _V, _I64, _I64, _F32, _I32, _V, _I64, _V, _I64, _I64, _V],
     "hn_silu_mul_quant": [_V, _I64, _V, _I64, _I64, _I64, _I32, _V, _I64, _V, _I64, _I64, _V],
+    "hn_ipc_export": [_V, _V, ctypes.POINTER(ctypes.c_int64)],
+    "hn_ipc_import": [_V, ctypes.POINTER(ctypes.c_void_p)],
+    "hn_ipc_close": [_V],
+    "hn_peer_push": [_V, _V, _I64, _V, _U32, _V],
+    "hn_wait_flags": [_V, _I64, _I64, _I64, _U32, _U32, _V],
 }
 
 
@@ -100,9 +105,10 @@ def last_error():
 calls = 0   # library calls made by this process (each launches at most one kernel); read by bench.py
 
 
-def check(rc, what):
+def check(rc, what, launches=1):
+    """Raise on a failed library call; `launches` = the kernels the call starts (0 for host-only entries)."""
     global calls
-    calls += 1
+    calls += launches
     if rc != HN_OK:
         raise RuntimeError(f"{what} failed with {STATUS.get(rc, rc)}: {last_error()}")
 

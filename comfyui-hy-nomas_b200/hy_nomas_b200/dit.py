@@ -205,6 +205,11 @@ def block_forward(cfg, w, x, vec, rope, sp, ops=CudaOps, trace=None, mods=None, 
         return _post(cfg, w, x, attn, qa, sa, qk, q_out, k_full, v_full, act, mods, gate1, shift2, scale2, gate2,
                      ops, trace, next_mods)
     lh = 0 if history is None else history[0].shape[0]
+    if sp.peer is not None:
+        attn, k_full, v_full, qk, q_out = _attention_pushed(cfg, w, qa, sa, rope, sp.peer, ops, b, l, lh, history,
+                                                            capture, x.dtype, trace is not None)
+        return _post(cfg, w, x, attn, qa, sa, qk, q_out, k_full, v_full, act, mods, gate1, shift2, scale2, gate2,
+                     ops, trace, next_mods)
     k_full, v_full, k_mine, v_mine = sp.kv_buffers(b, l, h, hd, x.dtype, x.device, prefix=lh)
     if history is not None:
         hk_q, hk_s, hv_q, hv_s = history
@@ -236,6 +241,38 @@ def block_forward(cfg, w, x, vec, rope, sp, ops=CudaOps, trace=None, mods=None, 
     attn = ops.attention(q_out, k_full, v_full).reshape(b * l, d)
     return _post(cfg, w, x, attn, qa, sa, qk, q_out, k_full, v_full, act, mods, gate1, shift2, scale2, gate2, ops,
                  trace, next_mods)
+
+
+def _attention_pushed(cfg, w, qa, sa, rope, peer, ops, b, l, lh, history, capture, dtype, keep_qk):
+    """Attention under the copy-engine exchange: K is projected and normalized first and pushed to the peers
+    while V is projected, V is pushed while Q is projected and normalized, and attention waits for the peers'
+    slices. Each of the q|k linear's halves is its own GEMM (the same output columns, so the same values).
+    `keep_qk`: also return the q|k projection [B*l, 2D] (for traces), else None."""
+    h, hd = cfg.heads, cfg.head_dim
+    d = h * hd
+    k_full, v_full, k_mine, v_mine = peer.begin(b, l, h, hd, dtype, prefix=lh)
+    if history is not None:
+        hk_q, hk_s, hv_q, hv_s = history
+        ops.dequantize_kv(hk_q, hk_s, out=k_full[0, :lh])
+        ops.dequantize_kv(hv_q, hv_s, out=v_full[0, :lh])
+    k_in = ops.gemm(qa, sa, _rows(w.qk, d, 2 * d)).view(b, l, h, hd)
+    if capture is not None:
+        kq, ks = ops.qk_norm_rope_kv(k_in, w.k_norm, rope, out=k_mine)
+    else:
+        ops.qk_norm_rope(k_in, w.k_norm, rope, out=k_mine)
+    peer.push(0)
+    ops.gemm(qa, sa, w.v, out=v_mine.view(b * l, d))
+    peer.push(1)
+    q_in = ops.gemm(qa, sa, _rows(w.qk, 0, d)).view(b, l, h, hd)
+    q_out = torch.empty((b, l, h, hd), dtype=dtype, device=qa.device)
+    ops.qk_norm_rope(q_in, w.q_norm, rope, out=q_out)
+    if capture is not None:
+        vq, vs = ops.quantize_kv(v_mine.reshape(b * l, h, hd))
+        capture.append((kq.reshape(b * l, h, hd), ks.reshape(b * l, h, 1), vq, vs))
+    peer.wait()
+    attn = ops.attention(q_out, k_full, v_full).reshape(b * l, d)
+    qk = torch.cat([q_in.reshape(b * l, d), k_in.reshape(b * l, d)], dim=1) if keep_qk else None
+    return attn, k_full, v_full, qk, q_out
 
 
 def _rows(w, lo, hi):

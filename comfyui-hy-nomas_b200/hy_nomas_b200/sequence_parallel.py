@@ -5,20 +5,34 @@ attend over the whole sequence.
 The reference runs one GPU (`sp_size: 1`, docs/upstream/single_gpu_low_mem_inference.yaml:22-23); this module
 is the B200 build's partition of the same block: every per-token op (LayerNorm, quantizers, the linears,
 QK-norm, the residuals) runs on the rank's own rows with no communication, and attention reads the gathered
-K/V. The gathers are issued asynchronously (NCCL on its own stream, or gloo on CPU for host-side tests), so
-K's gather overlaps the V projection.
+K/V. Two exchanges implement the gather:
+
+- the copy-engine exchange (GPUs, the default): every rank maps its peers' K/V buffers (CUDA IPC) and, as soon as
+  its own K (then V) slice exists, the copy engines push it into every peer's buffer over NVLink and write a
+  block counter into the peer's flag array. No SM is involved, so the pushes run under the V and Q projections
+  at full GEMM speed; a one-warp bounded wait for the peers' counters precedes attention. The buffers are double
+  buffered by block parity, and a rank's push into a peer's buffer of parity p is ordered after that peer's
+  attention of the previous parity-p block (the push follows this rank's wait for the peer's previous counters,
+  which the peer wrote after that attention), so no further handshake is needed.
+- an NCCL all-gather (or gloo on CPU for host-side tests), issued asynchronously on the library's stream:
+  used for head-chunked exchanges, when HN_SP_EXCHANGE=nccl, or when the IPC mappings cannot be made.
 
 Rank r owns tokens [r * L / P, (r + 1) * L / P); L must divide evenly (20240 does for P = 1, 2, 4, 8).
 The gather buffers are rank-major, so with batch 1 a rank's K/V rows are one contiguous slice that its own
 kernels write in place and that the all-gather uses as its input.
 """
+import ctypes
 import os
+import warnings
 
 import torch
 import torch.distributed as dist
 
 # K/V head chunks per block under sequence parallelism (HN_SP_HEAD_CHUNKS overrides)
 HEAD_CHUNKS = 1
+# limit of the wait for the peers' K/V (HN_SP_WAIT_TIMEOUT_S overrides); past it the stream's error word reads
+# HN_ERR_TIMEOUT and attention runs on what arrived
+WAIT_TIMEOUT_S = 120.0
 
 
 class SequenceParallel:
@@ -41,6 +55,26 @@ class SequenceParallel:
             raise ValueError(f"head_chunks must be >= 1, got {head_chunks}")
         self.head_chunks = head_chunks
         self._bufs = {}
+        self.peer = None
+        want = os.environ.get("HN_SP_EXCHANGE", "ce")
+        if want not in ("ce", "nccl"):
+            raise ValueError(f"HN_SP_EXCHANGE must be 'ce' or 'nccl', got {want!r}")
+        if (self.world > 1 and want == "ce" and head_chunks == 1 and torch.cuda.is_available()
+                and dist.get_backend(group) == "nccl"):
+            self.peer = PeerExchange.create(self)
+
+    @property
+    def exchange(self):
+        """'ce' (copy-engine pushes), 'nccl' (all-gather) or 'none' (one rank)."""
+        if self.world == 1:
+            return "none"
+        return "ce" if self.peer is not None else "nccl"
+
+    def close(self):
+        """Unmap the peers' buffers (collective: every rank calls it, after its last step)."""
+        if self.peer is not None:
+            self.peer.close()
+            self.peer = None
 
     def shard(self, length):
         """(start, stop) of this rank's tokens in a sequence of `length`."""
@@ -94,3 +128,151 @@ class SequenceParallel:
         for h in handles:
             if h is not None:
                 h.wait()
+
+
+def _ranks_agree(ok, group):
+    flags = [None] * dist.get_world_size(group)
+    dist.all_gather_object(flags, bool(ok), group=group)
+    return all(flags)
+
+
+class PeerExchange:
+    """The copy-engine K/V exchange of one `SequenceParallel` (its rank's GPU, the current device at creation).
+
+    Per buffer shape one allocation holds [parity 2][K, V][batch 1][prefix + local * world][heads][head_dim]; the
+    flags are int32 [K, V][world]: flags[kind][src] = the last block counter whose `kind` slice `src` pushed here.
+    Every rank runs the same blocks in the same order, so the counters (`epoch`, +1 per block) agree."""
+
+    def __init__(self, sp):
+        from . import _lib
+        self._lib = _lib
+        self.sp = sp
+        self.world, self.rank, self.group = sp.world, sp.rank, sp.group
+        self.device = torch.device("cuda", torch.cuda.current_device())
+        self.timeout_us = int(float(os.environ.get("HN_SP_WAIT_TIMEOUT_S", str(WAIT_TIMEOUT_S))) * 1e6)
+        self.epoch = 0
+        self._maps = {}                     # (peer, handle) -> mapped base address
+        self._bufs = {}
+        self.side = [torch.cuda.Stream(self.device), torch.cuda.Stream(self.device)]
+        self.flags = torch.zeros(2 * self.world, dtype=torch.int32, device=self.device)
+        # the zeros are written before this rank's contribution to the address exchange, which every peer
+        # receives before it can push
+        self.peer_flags = self._share(self.flags)
+
+    @classmethod
+    def create(cls, sp):
+        """A PeerExchange, or None (on every rank alike) when some rank cannot map its peers' memory."""
+        exch, err = None, None
+        try:
+            exch = cls(sp)
+        except (RuntimeError, OSError) as e:           # this rank failed; the others learn it below
+            err = e
+        if not _ranks_agree(err is None, sp.group):
+            if exch is not None:
+                exch.close()
+            warnings.warn(f"copy-engine K/V exchange unavailable ({err or 'a peer failed'}); using NCCL all-gather")
+            return None
+        return exch
+
+    def _share(self, t):
+        """Every rank's address of its `t` (collective), mapped into this process: a list indexed by rank."""
+        lib = self._lib
+        handle = (ctypes.c_uint8 * 64)()
+        off = ctypes.c_int64()
+        err = None
+        try:
+            lib.check(lib.lib.hn_ipc_export(ctypes.c_void_p(t.data_ptr()), handle, ctypes.byref(off)),
+                      "hn_ipc_export", launches=0)
+        except RuntimeError as e:
+            err = e
+        infos = [None] * self.world
+        dist.all_gather_object(infos, None if err else (bytes(handle), off.value), group=self.group)
+        if any(i is None for i in infos):
+            raise RuntimeError(f"a rank could not export its K/V buffers ({err})")
+        addrs = []
+        for r, (h, o) in enumerate(infos):
+            if r == self.rank:
+                addrs.append(t.data_ptr())
+                continue
+            if (r, h) not in self._maps:
+                base = ctypes.c_void_p()
+                buf = (ctypes.c_uint8 * 64).from_buffer_copy(h)
+                lib.check(lib.lib.hn_ipc_import(buf, ctypes.byref(base)), "hn_ipc_import", launches=0)
+                self._maps[(r, h)] = base.value
+            addrs.append(self._maps[(r, h)] + o)
+        return addrs
+
+    def _buffers(self, batch, local, heads, head_dim, dtype, prefix):
+        key = (batch, local, heads, head_dim, dtype, prefix)
+        ent = self._bufs.get(key)
+        if ent is None:
+            total = prefix + local * self.world
+            mem = torch.empty((2, 2, batch, total, heads, head_dim), dtype=dtype, device=self.device)
+            ok = True
+            try:
+                addrs = self._share(mem)
+            except RuntimeError as e:
+                ok, addrs = False, str(e)
+            if not _ranks_agree(ok, self.group):
+                raise RuntimeError(f"K/V buffer mapping failed: {addrs if not ok else 'on a peer'}")
+            row = heads * head_dim * mem.element_size()
+            ent = dict(mem=mem, addrs=addrs, total=total, prefix=prefix, local=local, row=row,
+                       done=[[None, None], [None, None]])
+            self._bufs[key] = ent
+        return ent
+
+    def begin(self, batch, local, heads, head_dim, dtype, prefix=0):
+        """Start a block: (k_full, v_full, k_mine, v_mine) of this block's parity. The current stream waits until
+        this rank's pushes of the previous block of that parity have read its slices."""
+        if batch != 1:
+            raise ValueError("sequence parallelism takes batch 1 (the denoise step's layout)")
+        self.epoch = (self.epoch + 1) & 0xFFFFFFFF
+        par = self.epoch & 1
+        ent = self._buffers(batch, local, heads, head_dim, dtype, prefix)
+        cur = torch.cuda.current_stream(self.device)
+        for ev in ent["done"][par]:
+            if ev is not None:
+                cur.wait_event(ev)
+        self._cur = (ent, par)
+        k_full, v_full = ent["mem"][par, 0], ent["mem"][par, 1]
+        lo = prefix + self.rank * local
+        return k_full, v_full, k_full[:, lo:lo + local], v_full[:, lo:lo + local]
+
+    def push(self, kind):
+        """Push this rank's slice of K (kind 0) or V (kind 1) - complete on the current stream - to every peer,
+        each followed by this block's counter in the peer's flags."""
+        lib = self._lib.lib
+        ent, par = self._cur
+        cur = torch.cuda.current_stream(self.device)
+        side = self.side[kind]
+        side.wait_stream(cur)
+        nbytes = ent["local"] * ent["row"]
+        region = ((par * 2 + kind) * ent["total"] + ent["prefix"] + self.rank * ent["local"]) * ent["row"]
+        src = ent["mem"].data_ptr() + region
+        st = ctypes.c_void_p(side.cuda_stream)
+        for step in range(1, self.world):
+            peer = (self.rank + step) % self.world     # staggered, so the ranks start on different peers
+            dst = ctypes.c_void_p(ent["addrs"][peer] + region)
+            flag = ctypes.c_void_p(self.peer_flags[peer] + 4 * (kind * self.world + self.rank))
+            self._lib.check(lib.hn_peer_push(dst, ctypes.c_void_p(src), nbytes, flag, self.epoch, st),
+                            "hn_peer_push", launches=0)
+        ev = torch.cuda.Event()
+        ev.record(side)
+        ent["done"][par][kind] = ev
+
+    def wait(self):
+        """The current stream waits (bounded) for every peer's K and V of this block."""
+        lib = self._lib
+        cur = torch.cuda.current_stream(self.device)
+        lib.check(lib.lib.hn_wait_flags(ctypes.c_void_p(self.flags.data_ptr()), 2, self.world, self.rank,
+                                        self.epoch, self.timeout_us, ctypes.c_void_p(cur.cuda_stream)),
+                  "hn_wait_flags")
+
+    def close(self):
+        """Unmap the peers' memory once every rank's pushes are complete (collective)."""
+        torch.cuda.synchronize(self.device)
+        dist.barrier(group=self.group)
+        for base in self._maps.values():
+            self._lib.lib.hn_ipc_close(ctypes.c_void_p(base))
+        self._maps.clear()
+        dist.barrier(group=self.group)

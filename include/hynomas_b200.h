@@ -264,6 +264,30 @@ int hn_rmsnorm_quant(const void *x, int64_t ldx, const void *weight, int64_t row
 int hn_silu_mul_quant(const void *g, int64_t ldg, const void *u, int64_t ldu, int64_t rows, int64_t I, int kind,
                       void *q, int64_t ldq, float *s, int64_t s_rs, int64_t s_gs, void *stream);
 
+/*
+ * Sequence-parallel K/V exchange over NVLink by the copy engines. No reference counterpart: the reference runs
+ * one GPU; these replace the NCCL all-gather of the build's own sequence-parallel DiT step, whose SM-based kernel
+ * cannot run beside the persistent GEMM. All host-side: no kernel of this library is involved.
+ *
+ * hn_ipc_export: a CUDA IPC handle (64 bytes at handle_host) for the device allocation that holds `ptr` (current
+ *   device), and ptr's byte offset in it.
+ * hn_ipc_import: map a peer process's exported allocation into the current device's context (peer access
+ *   enabled lazily); *base_host receives its base (add the exporter's offset). hn_ipc_close unmaps it.
+ * hn_peer_push: on `stream`, copy `bytes` from src (this device) to dst (a mapped peer address) by DMA, then write
+ *   the 32-bit `value` to `flag` (a mapped peer address, or NULL for none) after a memory fence, so the data is
+ *   visible before the flag.
+ * hn_wait_flags: on `stream`, one warp waits until every flags[g * count + i] (g < groups, i < count, i != skip;
+ *   groups * count <= 1024) has reached `value` (wrap-safe: (int32_t)(flag - value) >= 0), with system-scope
+ *   acquire loads, so that kernels after it on the stream see the data pushed before those flags. Bounded: after
+ *   `timeout_us` it records HN_ERR_TIMEOUT in the stream's error word (hn_device_error) and returns.
+ */
+int hn_ipc_export(const void *ptr, void *handle_host, int64_t *offset_host);
+int hn_ipc_import(const void *handle_host, void **base_host);
+int hn_ipc_close(void *base);
+int hn_peer_push(void *dst, const void *src, int64_t bytes, void *flag, uint32_t value, void *stream);
+int hn_wait_flags(const int32_t *flags, int64_t groups, int64_t count, int64_t skip, uint32_t value,
+                  uint32_t timeout_us, void *stream);
+
 #if defined(__GNUC__)
 #pragma GCC visibility pop
 #endif

@@ -59,24 +59,46 @@ def gloo_rank(rank, world, port, out_path, head_chunks=1, history_tokens=0):
         dist.destroy_process_group()
 
 
-def nccl_rank(rank, world, port, out_path, head_chunks=1):
+def nccl_rank(rank, world, port, out_path, head_chunks=1, exchange="ce", history_tokens=0):
+    """One rank of a sequence-parallel run on GPU `rank`: two steps (the second reuses the double-buffered K/V
+    exchange buffers) and, with `history_tokens`, a third step over an int8 K/V history. Rank 0 saves every
+    step's gathered output, the exchange used and the ranks' device error words."""
     import datetime
     import torch.distributed as dist
-    from hy_nomas_b200.sequence_parallel import SequenceParallel
     os.environ["MASTER_ADDR"] = "127.0.0.1"
     os.environ["MASTER_PORT"] = str(port)
     os.environ.setdefault("NCCL_NVLS_ENABLE", "0")
+    os.environ["HN_SP_EXCHANGE"] = exchange
     torch.cuda.set_device(rank)
     dist.init_process_group("nccl", rank=rank, world_size=world, device_id=torch.device("cuda", rank),
                             timeout=datetime.timedelta(seconds=60))
     try:
-        from hy_nomas_b200.dit import CudaOps
+        from hy_nomas_b200 import _lib
+        from hy_nomas_b200.dit import CudaOps, SyntheticDiT
+        from hy_nomas_b200.sequence_parallel import SequenceParallel
         cfg = small_config()
-        out = run_model(cfg, SequenceParallel(head_chunks=head_chunks), CudaOps, f"cuda:{rank}")
-        parts = [torch.empty_like(out) for _ in range(world)]
-        dist.all_gather(parts, out)
+        device = f"cuda:{rank}"
+        sp = SequenceParallel(head_chunks=head_chunks)
+        model = SyntheticDiT(cfg, device=device, seed=3, sp=sp, ops=CudaOps)
+        x, vec = inputs(cfg, device)
+        lo, hi = model.token_range
+        xs = x[:, lo:hi].contiguous()
+        outs = [model(xs, vec), model(xs, vec)]
+        if history_tokens:
+            outs.append(model(xs, vec, history=history(cfg, history_tokens, device)))
         torch.cuda.synchronize()
+        err = torch.tensor([_lib.device_error(torch.cuda.current_stream())[1]], device=device)
+        errs = [torch.empty_like(err) for _ in range(world)]
+        dist.all_gather(errs, err)
+        gathered = []
+        for out in outs:
+            parts = [torch.empty_like(out) for _ in range(world)]
+            dist.all_gather(parts, out)
+            gathered.append(torch.cat(parts, dim=1).cpu())
+        torch.cuda.synchronize()
+        kind = sp.exchange
+        sp.close()
         if rank == 0:
-            torch.save(torch.cat(parts, dim=1).cpu(), out_path)
+            torch.save({"outs": gathered, "exchange": kind, "errors": [int(e.item()) for e in errs]}, out_path)
     finally:
         dist.destroy_process_group()

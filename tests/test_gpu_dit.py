@@ -131,18 +131,12 @@ def free_port():
         return s.getsockname()[1]
 
 
-@pytest.mark.parametrize("head_chunks", [1, 2])
-def test_sequence_parallel_two_gpus(hn, cuda, tmp_path, head_chunks):
-    """2 ranks over NCCL (K/V all-gathered, whole or split by head) against the same model on one GPU."""
-    if torch.cuda.device_count() < 2:
-        pytest.skip("needs 2 GPUs")
-    from hy_nomas_b200.dit import CudaOps
-    from hy_nomas_b200.sequence_parallel import SequenceParallel
-    single = sp_worker.run_model(sp_worker.small_config(), SequenceParallel(), CudaOps, "cuda:0").cpu()
+def run_two_ranks(tmp_path, head_chunks=1, exchange="ce", history_tokens=0):
     ctx = mp.get_context("spawn")
     port = free_port()
-    out_path = os.path.join(tmp_path, "sp.pt")
-    procs = [ctx.Process(target=sp_worker.nccl_rank, args=(r, 2, port, out_path, head_chunks)) for r in range(2)]
+    out_path = os.path.join(tmp_path, f"sp_{exchange}_{head_chunks}_{history_tokens}.pt")
+    procs = [ctx.Process(target=sp_worker.nccl_rank, args=(r, 2, port, out_path, head_chunks, exchange,
+                                                           history_tokens)) for r in range(2)]
     for p in procs:
         p.start()
     for p in procs:
@@ -152,9 +146,39 @@ def test_sequence_parallel_two_gpus(hn, cuda, tmp_path, head_chunks):
         if p.is_alive():
             p.kill()
     assert codes == [0, 0], codes
-    got = torch.load(out_path)
-    assert got.shape == single.shape
-    assert rel_l2(got.float().numpy(), single.float().numpy()) < 1e-2
+    return torch.load(out_path)
+
+
+@pytest.mark.parametrize("head_chunks,exchange", [(1, "ce"), (1, "nccl"), (2, "nccl")])
+def test_sequence_parallel_two_gpus(hn, cuda, tmp_path, head_chunks, exchange):
+    """2 ranks (K/V pushed by the copy engines, or all-gathered over NCCL whole or split by head) against the
+    same model on one GPU, over two steps (the second reuses the double-buffered exchange buffers)."""
+    if torch.cuda.device_count() < 2:
+        pytest.skip("needs 2 GPUs")
+    from hy_nomas_b200.dit import CudaOps
+    from hy_nomas_b200.sequence_parallel import SequenceParallel
+    single = sp_worker.run_model(sp_worker.small_config(), SequenceParallel(), CudaOps, "cuda:0").cpu()
+    res = run_two_ranks(tmp_path, head_chunks, exchange)
+    assert res["exchange"] == exchange
+    assert res["errors"] == [0, 0]
+    first, second = res["outs"]
+    assert first.shape == single.shape
+    assert rel_l2(first.float().numpy(), single.float().numpy()) < 1e-2
+    assert torch.equal(first.view(torch.int16), second.view(torch.int16))
+
+
+def test_copy_engine_exchange_matches_nccl(hn, cuda, tmp_path):
+    """The copy-engine exchange moves the same bytes as the all-gather: outputs bit-identical to the NCCL run,
+    with and without a 30-token int8 K/V history (its own double-buffered exchange buffers)."""
+    if torch.cuda.device_count() < 2:
+        pytest.skip("needs 2 GPUs")
+    ce = run_two_ranks(tmp_path, 1, "ce", history_tokens=30)
+    nc = run_two_ranks(tmp_path, 1, "nccl", history_tokens=30)
+    assert ce["exchange"] == "ce" and nc["exchange"] == "nccl"
+    assert ce["errors"] == [0, 0] and nc["errors"] == [0, 0]
+    for a, b in zip(ce["outs"], nc["outs"]):
+        assert torch.equal(a.view(torch.int16), b.view(torch.int16))
+    assert not torch.equal(ce["outs"][0], ce["outs"][2])      # the history changed the output
 
 
 @pytest.fixture(scope="module")

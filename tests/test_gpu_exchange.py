@@ -1,0 +1,71 @@
+"""The copy-engine K/V exchange's device side on one GPU: a push (DMA copy + fenced flag write) into local
+memory, the bounded flag wait that gates attention, and the wait's time limit (a flag that nothing sets: the
+stream's error word reads HN_ERR_TIMEOUT and the context stays usable)."""
+import ctypes
+
+import pytest
+import torch
+
+pytestmark = pytest.mark.gpu
+
+
+def vp(x):
+    return ctypes.c_void_p(x)
+
+
+def test_push_then_wait_sees_data(hn, cuda):
+    L = hn.lib
+    st = torch.cuda.current_stream()
+    src = torch.randn(4096, 384, device=cuda).bfloat16()
+    dst = torch.zeros_like(src)
+    flags = torch.zeros(2 * 4, dtype=torch.int32, device=cuda)
+    # four "sources" x two kinds: rank 1's own flags (index 1 of each kind) are skipped
+    for kind in range(2):
+        for src_rank in (0, 2, 3):
+            L.check(L.lib.hn_peer_push(vp(dst.data_ptr()), vp(src.data_ptr()), src.numel() * 2,
+                                       vp(flags.data_ptr() + 4 * (kind * 4 + src_rank)), 7, vp(st.cuda_stream)),
+                    "hn_peer_push", launches=0)
+    L.check(L.lib.hn_wait_flags(vp(flags.data_ptr()), 2, 4, 1, 7, 2000000, vp(st.cuda_stream)), "hn_wait_flags")
+    out = dst.float().sum()
+    rc, code = L.device_error(st)
+    assert rc == 0 and code == 0
+    assert torch.equal(dst, src)
+    assert flags.tolist() == [7, 0, 7, 7, 7, 0, 7, 7]
+    assert torch.isfinite(out)
+
+
+def test_wait_compares_wrap_safe(hn, cuda):
+    """Counters compare by signed difference: 0x00000002 is 'after' 0xFFFFFFFE."""
+    L = hn.lib
+    st = torch.cuda.current_stream()
+    flags = torch.tensor([2, 2], dtype=torch.int32, device=cuda)
+    L.check(L.lib.hn_wait_flags(vp(flags.data_ptr()), 1, 2, -1, 0xFFFFFFFE, 2000000, vp(st.cuda_stream)),
+            "hn_wait_flags")
+    rc, code = L.device_error(st)
+    assert rc == 0 and code == 0
+
+
+def test_wait_runs_out_and_context_survives(hn, cuda):
+    L = hn.lib
+    st = torch.cuda.current_stream()
+    flags = torch.zeros(4, dtype=torch.int32, device=cuda)
+    flags[0] = 5                                                # one of the three waited flags arrived
+    L.check(L.lib.hn_wait_flags(vp(flags.data_ptr()), 1, 4, 3, 5, 20000, vp(st.cuda_stream)), "hn_wait_flags")
+    rc, code = L.device_error(st)
+    assert rc == 6 and code == 1                                # HN_ERR_TIMEOUT, HN_DEVERR_TIMEOUT
+    rc, code = L.device_error(st)
+    assert rc == 0 and code == 0
+    x = torch.randn(64, 256, device=cuda).bfloat16()
+    q, s = hn.kernels.quantize_activations(x)
+    torch.cuda.synchronize()
+    assert q.shape == (64, 256)
+
+
+def test_wait_rejects_bad_arguments(hn, cuda):
+    L = hn.lib
+    flags = torch.zeros(8, dtype=torch.int32, device=cuda)
+    st = vp(torch.cuda.current_stream().cuda_stream)
+    assert L.lib.hn_wait_flags(vp(flags.data_ptr()), 2, 1024, 0, 1, 1000, st) == 1        # HN_ERR_SHAPE
+    assert L.lib.hn_wait_flags(vp(flags.data_ptr() + 2), 1, 2, 0, 1, 1000, st) == 2       # HN_ERR_ALIGN
+    assert L.lib.hn_wait_flags(vp(flags.data_ptr()), 1, 2, 0, 1, 0, st) == 5              # HN_ERR_ARG
+    assert L.lib.hn_wait_flags(None, 1, 2, 0, 1, 1000, st) == 5
