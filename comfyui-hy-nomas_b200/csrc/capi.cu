@@ -12,6 +12,7 @@
 #include <mutex>
 #include <string>
 
+#include <cmath>
 #include <cuda.h>
 #include <cudaTypedefs.h>
 
@@ -504,6 +505,43 @@ int hn_quantize_fp8_block(const void *w, int w_dtype, int64_t N, int64_t K, void
     if (N == 0 || K == 0) return HN_OK;
     CHECK_DEVICE(w);
     return launched(launch_quant_fp8_block(w, w_dtype, N, K, q, s, (cudaStream_t)stream), "hn_quantize_fp8_block launch");
+}
+
+int hn_attention(const void *q, int64_t q_rs, int64_t q_hs, int64_t q_bs, const void *k, int64_t k_rs, int64_t k_hs,
+                 int64_t k_bs, const void *v, int64_t v_rs, int64_t v_hs, int64_t v_bs, int64_t B, int64_t Lq,
+                 int64_t Lk, int64_t H, int64_t D, float scale, void *out, int64_t o_rs, int64_t o_hs, int64_t o_bs,
+                 int8_t *q8, float *s8, void *stream) {
+    REQUIRE(q && k && v, HN_ERR_ARG, "hn_attention: null q/k/v");
+    REQUIRE(out != nullptr || q8 != nullptr, HN_ERR_ARG, "hn_attention: no output (out and q8 both null)");
+    REQUIRE((q8 == nullptr) == (s8 == nullptr), HN_ERR_ARG, "hn_attention: q8 and s8 go together");
+    REQUIRE(D == 128, HN_ERR_UNSUPPORTED, "hn_attention: head dim %lld (128 supported)", (long long)D);
+    REQUIRE(B >= 1 && H >= 1 && Lq >= 1 && Lk >= 1, HN_ERR_SHAPE, "hn_attention: empty shape B=%lld H=%lld Lq=%lld Lk=%lld",
+            (long long)B, (long long)H, (long long)Lq, (long long)Lk);
+    REQUIRE(B <= 65535 && H <= 65535 && Lq < (1LL << 31) && Lk < (1LL << 31) && B * Lq < (1LL << 31), HN_ERR_SHAPE,
+            "hn_attention: too large");
+    REQUIRE(std::isfinite(scale) && scale > 0.0f, HN_ERR_ARG, "hn_attention: scale must be positive and finite");
+    const int64_t st_in[9] = {q_rs, q_hs, q_bs, k_rs, k_hs, k_bs, v_rs, v_hs, v_bs};
+    for (int i = 0; i < 9; ++i)
+        REQUIRE(st_in[i] >= 0 && st_in[i] % 8 == 0 && st_in[i] < (1LL << 38), HN_ERR_ALIGN,
+                "hn_attention: input strides must be non-negative multiples of 8 elements");
+    REQUIRE(al16(q) && al16(k) && al16(v), HN_ERR_ALIGN, "hn_attention: q/k/v must be 16-byte aligned");
+    if (out != nullptr)
+        REQUIRE(al16(out) && o_rs >= 0 && o_hs >= 0 && o_bs >= 0 && o_rs % 8 == 0 && o_hs % 8 == 0 && o_bs % 8 == 0,
+                HN_ERR_ALIGN, "hn_attention: out must be 16-byte aligned with strides multiples of 8 elements");
+    if (q8 != nullptr)
+        REQUIRE(reinterpret_cast<uintptr_t>(q8) % 8 == 0 && reinterpret_cast<uintptr_t>(s8) % 4 == 0, HN_ERR_ALIGN,
+                "hn_attention: q8 must be 8-byte and s8 4-byte aligned");
+    CHECK_DEVICE(q);
+    AttnArgs a;
+    a.q = q; a.k = k; a.v = v;
+    a.q_rs = q_rs; a.q_hs = q_hs; a.q_bs = q_bs; a.k_rs = k_rs; a.k_hs = k_hs; a.k_bs = k_bs;
+    a.v_rs = v_rs; a.v_hs = v_hs; a.v_bs = v_bs;
+    a.B = B; a.Lq = Lq; a.Lk = Lk; a.H = H; a.scale = scale;
+    a.out = out; a.o_rs = o_rs; a.o_hs = o_hs; a.o_bs = o_bs; a.q8 = q8; a.s8 = s8;
+    const char *msg = nullptr;
+    cudaError_t e = launch_attention(a, (cudaStream_t)stream, &msg);
+    if (e != cudaSuccess && msg) return fail(HN_ERR_ALIGN, "hn_attention: %s", msg);
+    return launched(e, "hn_attention launch");
 }
 
 } // extern "C"

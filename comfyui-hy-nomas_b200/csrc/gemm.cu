@@ -48,6 +48,7 @@
 
 #include "hn_common.cuh"
 #include "hn_kernels.h"
+#include "hn_tc.cuh"
 
 namespace hn {
 
@@ -139,122 +140,8 @@ struct Params {
 };
 
 // ---------------------------------------------------------------------------------------------------
-// PTX wrappers
-
-__device__ __forceinline__ uint32_t smem_u32(const void *p) { return (uint32_t)__cvta_generic_to_shared(p); }
-
-__device__ __forceinline__ void mbar_init(uint32_t bar, uint32_t count) {
-    asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(bar), "r"(count) : "memory");
-}
-__device__ __forceinline__ void mbar_arrive(uint32_t bar) {
-    asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(bar) : "memory");
-}
-__device__ __forceinline__ void mbar_arrive_tx(uint32_t bar, uint32_t bytes) {
-    asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(bar), "r"(bytes) : "memory");
-}
-__device__ __forceinline__ bool mbar_try(uint32_t bar, uint32_t parity) {
-    uint32_t ok;
-    asm volatile("{\n\t.reg .pred p;\n\t"
-                 "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n\t"
-                 "selp.u32 %0, 1, 0, p;\n\t}"
-                 : "=r"(ok)
-                 : "r"(bar), "r"(parity)
-                 : "memory");
-    return ok != 0;
-}
-// bounded wait: false when the kernel is aborting (this wait timed out, or another role's did)
-__device__ __forceinline__ bool mbar_wait(uint32_t bar, uint32_t parity, volatile int *abort_flag, uint64_t limit_ns,
-                                          int *err) {
-    if (mbar_try(bar, parity)) return true;
-    const uint64_t t0 = globaltimer_ns();
-    while (true) {
-#pragma unroll 1
-        for (int i = 0; i < 32; ++i)
-            if (mbar_try(bar, parity)) return true;
-        if (*abort_flag) return false;
-        if (globaltimer_ns() - t0 > limit_ns) {
-            *abort_flag = 1;
-            atomicOr(err, HN_DEVERR_TIMEOUT);
-            return false;
-        }
-    }
-}
-
-// 3-D tile load: {128 bytes of one K group, rows, GPS groups} -> GPS stacked [rows][128 B] swizzled tiles
-// One lane polls the barrier and the result is broadcast to the warp: a try_wait costs ~100 cycles even
-// on a completed phase, and 32 lanes polling one barrier serialize. The shuffle also orders the other
-// lanes after the waiting lane's acquire.
-__device__ __forceinline__ bool warp_wait(int lane, uint32_t bar, uint32_t parity, volatile int *abort_flag,
-                                          uint64_t limit_ns, int *err) {
-    bool ok = true;
-    if (lane == 0) ok = mbar_wait(bar, parity, abort_flag, limit_ns, err);
-    return __shfl_sync(0xffffffffu, ok ? 1 : 0, 0) != 0;
-}
-
-// 1-D bulk copy global -> shared (16-byte aligned, size a multiple of 16), completing on an mbarrier
-__device__ __forceinline__ void bulk_load(uint32_t dst, const void *src, uint32_t bytes, uint32_t bar) {
-    asm volatile("cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];"
-                 ::"r"(dst), "l"(src), "r"(bytes), "r"(bar)
-                 : "memory");
-}
-
-// 4-byte asynchronous copy global -> shared; `valid` false writes zero and reads nothing (src-size 0)
-__device__ __forceinline__ void cp_async4(uint32_t dst, const float *src, bool valid) {
-    asm volatile("cp.async.ca.shared.global [%0], [%1], 4, %2;" ::"r"(dst), "l"(src), "r"(valid ? 4 : 0) : "memory");
-}
-
-// the mbarrier receives one arrival when this thread's earlier cp.async copies have landed (the pending count
-// is raised now and lowered then, so the barrier's expected count is unchanged)
-__device__ __forceinline__ void cp_async_arrive(uint32_t bar) {
-    asm volatile("cp.async.mbarrier.arrive.shared::cta.b64 [%0];" ::"r"(bar) : "memory");
-}
-
-__device__ __forceinline__ void tma_load_3d(const CUtensorMap *map, uint32_t dst, uint32_t bar, int row, int group) {
-    asm volatile("cp.async.bulk.tensor.3d.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1, {%3, %4, %5}], [%2];"
-                 ::"r"(dst), "l"((uint64_t)map), "r"(bar), "r"(0), "r"(row), "r"(group)
-                 : "memory");
-}
-
-__device__ __forceinline__ void tc_fence_before() { asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory"); }
-__device__ __forceinline__ void tc_fence_after() { asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory"); }
-
-// K-major operand tile, 128-byte rows, 128B swizzle: SBO = 1024 B between 8-row core groups,
-// LBO unused (16 B), descriptor version 1 (sm_100), layout type 2 (SWIZZLE_128B).
-__device__ __forceinline__ uint64_t sdesc(uint32_t saddr) {
-    return (uint64_t)((saddr >> 4) & 0x3FFF) | ((uint64_t)1 << 16) | ((uint64_t)(1024 >> 4) << 32) |
-           ((uint64_t)1 << 46) | ((uint64_t)2 << 61);
-}
-
-template <int KIND>
-__device__ __forceinline__ void mma_128xNx32(uint32_t d_tmem, uint64_t ad, uint64_t bd, uint32_t idesc, uint32_t acc) {
-    if (KIND == 0)
-        asm volatile("{\n\t.reg .pred p;\n\tsetp.ne.b32 p, %4, 0;\n\t"
-                     "tcgen05.mma.cta_group::1.kind::i8 [%0], %1, %2, %3, p;\n\t}"
-                     ::"r"(d_tmem), "l"(ad), "l"(bd), "r"(idesc), "r"(acc) : "memory");
-    else
-        asm volatile("{\n\t.reg .pred p;\n\tsetp.ne.b32 p, %4, 0;\n\t"
-                     "tcgen05.mma.cta_group::1.kind::f8f6f4 [%0], %1, %2, %3, p;\n\t}"
-                     ::"r"(d_tmem), "l"(ad), "l"(bd), "r"(idesc), "r"(acc) : "memory");
-}
-__device__ __forceinline__ void mma_commit(uint32_t bar) {
-    asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(bar) : "memory");
-}
-
-// 32 lanes x 32 consecutive 32-bit columns, completed (wait::ld) inside the same statement so no use of
-// the destination registers can be scheduled before the data has arrived.
-__device__ __forceinline__ void tmem_ld32(uint32_t taddr, uint32_t (&r)[32]) {
-    asm volatile(
-        "tcgen05.ld.sync.aligned.32x32b.x32.b32 "
-        "{%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15,"
-        "%16,%17,%18,%19,%20,%21,%22,%23,%24,%25,%26,%27,%28,%29,%30,%31}, [%32];\n\t"
-        "tcgen05.wait::ld.sync.aligned;"
-        : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]), "=r"(r[7]),
-          "=r"(r[8]), "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]), "=r"(r[14]), "=r"(r[15]),
-          "=r"(r[16]), "=r"(r[17]), "=r"(r[18]), "=r"(r[19]), "=r"(r[20]), "=r"(r[21]), "=r"(r[22]), "=r"(r[23]),
-          "=r"(r[24]), "=r"(r[25]), "=r"(r[26]), "=r"(r[27]), "=r"(r[28]), "=r"(r[29]), "=r"(r[30]), "=r"(r[31])
-        : "r"(taddr)
-        : "memory");
-}
+// PTX wrappers (hn_tc.cuh)
+using namespace tc;
 
 // ---- packed fp32x2 promotion steps (sm_100 f32x2 instructions, explicit .rn: never contracted) ----
 union F2 {

@@ -75,6 +75,18 @@ cudaError_t launch_wait_selftest(uint32_t timeout_us, cudaStream_t st);
 
 // read slot `slot` of the current device's error words into *value and clear it (synchronous)
 cudaError_t read_and_clear_device_error(int slot, int *value);
+// attention (attention.cu): q [B, Lq, H, 128], k / v [B, Lk, H, 128] bf16 with the head dim contiguous (strides
+// in elements); out [B, Lq, H, 128] bf16 (or null) and the int8 codes [B*Lq, H*128] + scales [B*Lq, H] (or null)
+struct AttnArgs {
+    const void *q, *k, *v;
+    int64_t q_rs, q_hs, q_bs, k_rs, k_hs, k_bs, v_rs, v_hs, v_bs;
+    int64_t B, Lq, Lk, H;
+    float scale;
+    void *out; int64_t o_rs, o_hs, o_bs;
+    int8_t *q8; float *s8;
+};
+cudaError_t launch_attention(const AttnArgs &a, cudaStream_t st, const char **msg);
+
 // one warp waits (bounded) until flags[g * count + i] >= value for every g < groups, i < count, i != skip
 cudaError_t launch_wait_flags(const uint32_t *flags, int groups, int count, int skip, uint32_t value,
                               uint32_t timeout_us, cudaStream_t st);

@@ -46,6 +46,8 @@ SIGNATURES = {
     "hn_quantize_fp8_block": [_V, _I32, _I64, _I64, _V, _V, _V],
     "hn_rmsnorm_quant": [_V, _I64, _V, _I64, _I64, _F32, _I32, _V, _I64, _V, _I64, _I64, _V],
     "hn_silu_mul_quant": [_V, _I64, _V, _I64, _I64, _I64, _I32, _V, _I64, _V, _I64, _I64, _V],
+    "hn_attention": [_V, _I64, _I64, _I64, _V, _I64, _I64, _I64, _V, _I64, _I64, _I64, _I64, _I64, _I64, _I64, _I64,
+                     _F32, _V, _I64, _I64, _I64, _V, _V, _V],
     "hn_ipc_export": [_V, _V, ctypes.POINTER(ctypes.c_int64)],
     "hn_ipc_import": [_V, ctypes.POINTER(ctypes.c_void_p)],
     "hn_ipc_close": [_V],

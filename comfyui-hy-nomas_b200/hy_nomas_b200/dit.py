@@ -33,9 +33,13 @@ from dataclasses import dataclass
 import torch
 import torch.nn.functional as F
 
+from . import attention as attention_mod
 from . import fused, kernels, world
 from .sequence_parallel import SequenceParallel
 
+# the step's attention (HN_ATTENTION overrides): "sdpa" - torch SDPA, as the reference's pytorch backend - or
+# "native" - the library's kernel, whose fused output quantizer feeds the projection linear directly
+ATTENTION = "sdpa"
 # SMs each GEMM leaves free under sequence parallelism (HN_SP_GEMM_SM_RESERVE overrides)
 SP_GEMM_SM_RESERVE = 0
 
@@ -158,6 +162,12 @@ class CudaOps:
         return world.dequantize_kv(q, s, out=out)
 
     @staticmethod
+    def attention_quant(q, k, v, keep_output=False):
+        """The library's attention with the projection linear's input quantizer fused into its epilogue:
+        (codes, scales) or, with keep_output, (bf16 output, (codes, scales))."""
+        return attention_mod.attention_quant(q, k, v, keep_output=keep_output)
+
+    @staticmethod
     def gated_residual(x, y, gate):
         return fused.gated_residual(x, y, gate)
 
@@ -238,9 +248,22 @@ def block_forward(cfg, w, x, vec, rope, sp, ops=CudaOps, trace=None, mods=None, 
         ops.qk_norm_rope2(q_in, k_in, w.q_norm, w.k_norm, rope, out=(q_out, k_mine))
         gather_k = None
     sp.wait(gather_k, gather_v)
-    attn = ops.attention(q_out, k_full, v_full).reshape(b * l, d)
+    attn = _attend(ops, q_out, k_full, v_full, trace is not None)
     return _post(cfg, w, x, attn, qa, sa, qk, q_out, k_full, v_full, act, mods, gate1, shift2, scale2, gate2, ops,
                  trace, next_mods)
+
+
+def _attend(ops, q, k, v, keep):
+    """Attention for the projection linear: (attn [B*l, D] bf16 or None, (codes, scales) or None). With the native
+    kernel the projection's input quantization comes out of attention's epilogue (and the bf16 output only when
+    `keep`, for traces); with SDPA the projection quantizes the bf16 output itself."""
+    b, l, h, hd = q.shape
+    if os.environ.get("HN_ATTENTION", ATTENTION) == "native" and hasattr(ops, "attention_quant"):
+        if keep:
+            out, codes = ops.attention_quant(q, k, v, keep_output=True)
+            return out.reshape(b * l, h * hd), codes
+        return None, ops.attention_quant(q, k, v)
+    return ops.attention(q, k, v).reshape(b * l, h * hd), None
 
 
 def _attention_pushed(cfg, w, qa, sa, rope, peer, ops, b, l, lh, history, capture, dtype, keep_qk):
@@ -270,7 +293,7 @@ def _attention_pushed(cfg, w, qa, sa, rope, peer, ops, b, l, lh, history, captur
         vq, vs = ops.quantize_kv(v_mine.reshape(b * l, h, hd))
         capture.append((kq.reshape(b * l, h, hd), ks.reshape(b * l, h, 1), vq, vs))
     peer.wait()
-    attn = ops.attention(q_out, k_full, v_full).reshape(b * l, d)
+    attn = _attend(ops, q_out, k_full, v_full, keep_qk)
     qk = torch.cat([q_in.reshape(b * l, d), k_in.reshape(b * l, d)], dim=1) if keep_qk else None
     return attn, k_full, v_full, qk, q_out
 
@@ -308,7 +331,7 @@ def _attention_chunked(cfg, w, qa, sa, rope, sp, ops, b, l, chunks, keep_kv=Fals
         attn[:, :, c * hc:(c + 1) * hc] = ops.attention(q_out[:, :, c * hc:(c + 1) * hc], kf, vf)
     k_full = torch.cat([kf for kf, _, _, _ in bufs], dim=2) if keep_kv else None
     v_full = torch.cat([vf for _, vf, _, _ in bufs], dim=2) if keep_kv else None
-    return attn.view(b * l, d), k_full, v_full, qk, q_out
+    return (attn.view(b * l, d), None), k_full, v_full, qk, q_out
 
 
 def _post(cfg, w, x, attn, qa, sa, qk, q_out, k_full, v_full, act, mods, gate1, shift2, scale2, gate2, ops, trace,
@@ -316,7 +339,8 @@ def _post(cfg, w, x, attn, qa, sa, qk, q_out, k_full, v_full, act, mods, gate1, 
     """The block after attention: projection, gated residual + LN + quant, MLP, gated residual (fused with the
     next block's LN + quant when `next_mods` is given: returns (out, (qa, sa)) then)."""
     b, l, d = x.shape
-    proj = ops.linear(attn, w.proj).view(b, l, d)
+    attn, attn_q = attn
+    proj = (ops.gemm(*attn_q, w.proj) if attn_q is not None else ops.linear(attn, w.proj)).view(b, l, d)
     x1, qa2, sa2 = ops.gated_residual_adaln_quant(x, proj, gate1, shift2, scale2)
     qh, sh = ops.gemm(qa2, sa2, w.fc1, epilogue="gelu_quant")
     y = ops.gemm(qh, sh, w.fc2).view(b, l, d)

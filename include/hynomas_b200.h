@@ -265,6 +265,23 @@ int hn_silu_mul_quant(const void *g, int64_t ldg, const void *u, int64_t ldu, in
                       void *q, int64_t ldq, float *s, int64_t s_rs, int64_t s_gs, void *stream);
 
 /*
+ * Attention: out = softmax(q k^T * scale) v per batch item and head, no mask, head dim 128, bf16 - the SDPA call of
+ * the DiT block. Replaces hy_nomas/model.py:145-151 (`attention`, ComfyUI's optimized_attention over
+ * q/k/v [B, L, H, D]). q [B, Lq, H, 128], k / v [B, Lk, H, 128], out [B, Lq, H, 128]; each with its own row /
+ * head / batch strides in elements (multiples of 8), the head dim contiguous, 16-byte aligned bases.
+ * Optionally fused: the output quantized per token x 128 channels (one head's row) exactly as hn_quant_act does
+ * for the [B*Lq, H*128] attention output (int8, round half away): q8 [B*Lq, H*128] int8 and s8 [B*Lq, H] fp32,
+ * row-major - the input of the projection linear. `out` may be NULL when only the codes are wanted; q8 and s8 are
+ * both NULL or both set. The softmax runs in base 2 with fp32 statistics, P is rounded to bf16 for the P V
+ * product, the accumulators are fp32 (differences to the reference's SDPA are those of two valid bf16 attention
+ * implementations, not bit-level).
+ */
+int hn_attention(const void *q, int64_t q_rs, int64_t q_hs, int64_t q_bs, const void *k, int64_t k_rs, int64_t k_hs,
+                 int64_t k_bs, const void *v, int64_t v_rs, int64_t v_hs, int64_t v_bs, int64_t B, int64_t Lq,
+                 int64_t Lk, int64_t H, int64_t D, float scale, void *out, int64_t o_rs, int64_t o_hs, int64_t o_bs,
+                 int8_t *q8, float *s8, void *stream);
+
+/*
  * Sequence-parallel K/V exchange over NVLink by the copy engines. No reference counterpart: the reference runs
  * one GPU; these replace the NCCL all-gather of the build's own sequence-parallel DiT step, whose SM-based kernel
  * cannot run beside the persistent GEMM. All host-side: no kernel of this library is involved.
