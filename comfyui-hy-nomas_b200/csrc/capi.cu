@@ -544,6 +544,41 @@ int hn_attention(const void *q, int64_t q_rs, int64_t q_hs, int64_t q_bs, const 
     return launched(e, "hn_attention launch");
 }
 
+int hn_attn_merge(const void *const *parts, const float *const *lses, int64_t n, int64_t o_bs, int64_t o_qs,
+                  int64_t o_hs, int64_t l_bs, int64_t l_hs, int64_t l_qs, int64_t B, int64_t Lq, int64_t H, int64_t D,
+                  void *out, int64_t out_bs, int64_t out_qs, int64_t out_hs, int8_t *q8, float *s8, void *stream) {
+    REQUIRE(parts && lses, HN_ERR_ARG, "hn_attn_merge: null piece arrays");
+    REQUIRE(n >= 1 && n <= 16, HN_ERR_SHAPE, "hn_attn_merge: %lld pieces (1 to 16)", (long long)n);
+    REQUIRE(out != nullptr || q8 != nullptr, HN_ERR_ARG, "hn_attn_merge: no output");
+    REQUIRE((q8 == nullptr) == (s8 == nullptr), HN_ERR_ARG, "hn_attn_merge: q8 and s8 go together");
+    REQUIRE(D == 128, HN_ERR_UNSUPPORTED, "hn_attn_merge: head dim %lld (128 supported)", (long long)D);
+    REQUIRE(B >= 1 && Lq >= 0 && H >= 1 && B * Lq * H < (1LL << 40) && B * Lq < (1LL << 31), HN_ERR_SHAPE,
+            "hn_attn_merge: bad shape");
+    for (int64_t i = 0; i < n; ++i) {
+        REQUIRE(parts[i] && lses[i], HN_ERR_ARG, "hn_attn_merge: null piece %lld", (long long)i);
+        REQUIRE(reinterpret_cast<uintptr_t>(parts[i]) % 8 == 0 && reinterpret_cast<uintptr_t>(lses[i]) % 4 == 0,
+                HN_ERR_ALIGN, "hn_attn_merge: piece %lld misaligned", (long long)i);
+    }
+    REQUIRE(o_bs % 4 == 0 && o_qs % 4 == 0 && o_hs % 4 == 0 && o_bs >= 0 && o_qs >= 0 && o_hs >= 0, HN_ERR_ALIGN,
+            "hn_attn_merge: piece strides must be non-negative multiples of 4 elements");
+    REQUIRE(l_bs >= 0 && l_hs >= 0 && l_qs >= 0, HN_ERR_ARG, "hn_attn_merge: negative log-sum-exp stride");
+    if (out != nullptr)
+        REQUIRE(reinterpret_cast<uintptr_t>(out) % 8 == 0 && out_bs % 4 == 0 && out_qs % 4 == 0 && out_hs % 4 == 0 &&
+                    out_bs >= 0 && out_qs >= 0 && out_hs >= 0,
+                HN_ERR_ALIGN, "hn_attn_merge: out must be 8-byte aligned with strides multiples of 4 elements");
+    if (q8 != nullptr)
+        REQUIRE(reinterpret_cast<uintptr_t>(q8) % 4 == 0 && reinterpret_cast<uintptr_t>(s8) % 4 == 0, HN_ERR_ALIGN,
+                "hn_attn_merge: q8 / s8 must be 4-byte aligned");
+    if (Lq == 0) return HN_OK;
+    CHECK_DEVICE(parts[0]);
+    MergeArgs a;
+    a.parts = parts; a.lses = lses; a.n = n;
+    a.o_bs = o_bs; a.o_qs = o_qs; a.o_hs = o_hs; a.l_bs = l_bs; a.l_hs = l_hs; a.l_qs = l_qs;
+    a.B = B; a.Lq = Lq; a.H = H;
+    a.out = out; a.out_bs = out_bs; a.out_qs = out_qs; a.out_hs = out_hs; a.q8 = q8; a.s8 = s8;
+    return launched(launch_attn_merge(a, (cudaStream_t)stream), "hn_attn_merge launch");
+}
+
 } // extern "C"
 
 // ---------------------------------------------------------------------------------------------------
@@ -632,18 +667,20 @@ int hn_peer_push(void *dst, const void *src, int64_t bytes, void *flag, uint32_t
     return HN_OK;
 }
 
-int hn_wait_flags(const int32_t *flags, int64_t groups, int64_t count, int64_t skip, uint32_t value,
-                  uint32_t timeout_us, void *stream) {
+int hn_wait_flags(const int32_t *flags, int64_t groups, int64_t count, int64_t group_stride, int64_t skip,
+                  uint32_t value, uint32_t timeout_us, void *stream) {
     REQUIRE(flags != nullptr, HN_ERR_ARG, "hn_wait_flags: null pointer");
     REQUIRE(groups >= 0 && count >= 0 && groups <= 1024 && count <= 1024 && groups * count <= 1024, HN_ERR_SHAPE,
             "hn_wait_flags: need 0 <= groups * count <= 1024 (groups=%lld count=%lld)", (long long)groups,
             (long long)count);
+    REQUIRE(group_stride >= 0 && group_stride <= (1LL << 20), HN_ERR_SHAPE, "hn_wait_flags: group_stride out of range");
     REQUIRE(timeout_us > 0 && timeout_us <= 600000000u, HN_ERR_ARG, "hn_wait_flags: timeout_us must be in (0, 6e8]");
     REQUIRE(((uintptr_t)flags % 4) == 0, HN_ERR_ALIGN, "hn_wait_flags: flags must be 4-byte aligned");
     if (groups * count == 0) return HN_OK;
     CHECK_DEVICE(flags);
-    return launched(launch_wait_flags(reinterpret_cast<const uint32_t *>(flags), (int)groups, (int)count, (int)skip,
-                                      value, timeout_us, static_cast<cudaStream_t>(stream)),
+    return launched(launch_wait_flags(reinterpret_cast<const uint32_t *>(flags), (int)groups, (int)count,
+                                      (int)group_stride, (int)(skip < 0 || skip >= count ? -1 : skip), value,
+                                      timeout_us, static_cast<cudaStream_t>(stream)),
                     "hn_wait_flags launch");
 }
 

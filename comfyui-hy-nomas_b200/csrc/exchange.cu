@@ -12,14 +12,15 @@
 
 namespace hn {
 
-__global__ void k_wait_flags(const uint32_t *flags, int groups, int count, int skip, uint32_t value,
+__global__ void k_wait_flags(const uint32_t *flags, int groups, int count, int group_stride, int skip, uint32_t value,
                              uint64_t limit_ns, int *err) {
     const uint64_t t0 = globaltimer_ns();
     const int total = groups * count;
     bool timed_out = false;
     for (int i = threadIdx.x; i < total && !timed_out; i += blockDim.x) {
-        if (i % count == skip) continue;
-        const uint32_t *f = flags + i;
+        const int g = i / count, c = i - g * count;
+        if (c == skip) continue;
+        const uint32_t *f = flags + (int64_t)g * group_stride + c;
         while (true) {
             uint32_t v;
             asm volatile("ld.acquire.sys.global.u32 %0, [%1];" : "=r"(v) : "l"(f) : "memory");
@@ -35,12 +36,13 @@ __global__ void k_wait_flags(const uint32_t *flags, int groups, int count, int s
     __syncwarp();
 }
 
-cudaError_t launch_wait_flags(const uint32_t *flags, int groups, int count, int skip, uint32_t value,
-                              uint32_t timeout_us, cudaStream_t st) {
+cudaError_t launch_wait_flags(const uint32_t *flags, int groups, int count, int group_stride, int skip,
+                              uint32_t value, uint32_t timeout_us, cudaStream_t st) {
     int *err = nullptr;
     cudaError_t e = device_error_word(err_slot(st), &err);
     if (e != cudaSuccess) return e;
-    k_wait_flags<<<1, 32, 0, st>>>(flags, groups, count, skip, value, (uint64_t)timeout_us * 1000ull, err);
+    k_wait_flags<<<1, 32, 0, st>>>(flags, groups, count, group_stride, skip, value, (uint64_t)timeout_us * 1000ull,
+                                   err);
     return cudaGetLastError();
 }
 

@@ -86,9 +86,18 @@ struct AttnArgs {
     int8_t *q8; float *s8;
 };
 cudaError_t launch_attention(const AttnArgs &a, cudaStream_t st, const char **msg);
+// merge of attention pieces by their log-sum-exp (attention.cu); n <= 16 pieces, head dim 128
+struct MergeArgs {
+    const void *const *parts; const float *const *lses; int64_t n;
+    int64_t o_bs, o_qs, o_hs, l_bs, l_hs, l_qs;
+    int64_t B, Lq, H;
+    void *out; int64_t out_bs, out_qs, out_hs;
+    int8_t *q8; float *s8;
+};
+cudaError_t launch_attn_merge(const MergeArgs &a, cudaStream_t st);
 
-// one warp waits (bounded) until flags[g * count + i] >= value for every g < groups, i < count, i != skip
-cudaError_t launch_wait_flags(const uint32_t *flags, int groups, int count, int skip, uint32_t value,
-                              uint32_t timeout_us, cudaStream_t st);
+// one warp waits (bounded) until flags[g * group_stride + i] >= value for every g < groups, i < count, i != skip
+cudaError_t launch_wait_flags(const uint32_t *flags, int groups, int count, int group_stride, int skip,
+                              uint32_t value, uint32_t timeout_us, cudaStream_t st);
 
 } // namespace hn

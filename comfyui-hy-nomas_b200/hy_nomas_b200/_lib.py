@@ -48,11 +48,13 @@ SIGNATURES = {
     "hn_silu_mul_quant": [_V, _I64, _V, _I64, _I64, _I64, _I32, _V, _I64, _V, _I64, _I64, _V],
     "hn_attention": [_V, _I64, _I64, _I64, _V, _I64, _I64, _I64, _V, _I64, _I64, _I64, _I64, _I64, _I64, _I64, _I64,
                      _F32, _V, _I64, _I64, _I64, _V, _V, _V],
+    "hn_attn_merge": [_V, _V, _I64, _I64, _I64, _I64, _I64, _I64, _I64, _I64, _I64, _I64, _I64, _V, _I64, _I64, _I64,
+                      _V, _V, _V],
     "hn_ipc_export": [_V, _V, ctypes.POINTER(ctypes.c_int64)],
     "hn_ipc_import": [_V, ctypes.POINTER(ctypes.c_void_p)],
     "hn_ipc_close": [_V],
     "hn_peer_push": [_V, _V, _I64, _V, _U32, _V],
-    "hn_wait_flags": [_V, _I64, _I64, _I64, _U32, _U32, _V],
+    "hn_wait_flags": [_V, _I64, _I64, _I64, _I64, _U32, _U32, _V],
 }
 
 

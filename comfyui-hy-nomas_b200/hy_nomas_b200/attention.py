@@ -5,7 +5,13 @@ item and head, no mask, head dim 128, q/k/v and out in the reference's [B, L, H,
 accepted and ignored: the B200 build has one backend). `attention_quant` is the fusion the block needs before
 its projection linear: the output quantized per token x 128 channels - one head's row of the [B*Lq, H*128]
 output - with the arithmetic of `kernels.quantize_activations` (int8, round half away), from the same launch.
+
+`attention_lse` + `merge` attend in key pieces (the sequence-parallel step attends to each rank's keys as they
+arrive): each piece is torch's cuDNN attention over a key range with its log-sum-exp, and the library's merge
+kernel combines them exactly as one softmax over all keys would (up to rounding), optionally quantizing the result
+for the projection linear in the same pass.
 """
+import ctypes
 import math
 
 import torch
@@ -84,3 +90,52 @@ def attention_quant(q, k, v, scale=None, keep_output=False):
     out = torch.empty(q.shape, dtype=torch.bfloat16, device=q.device) if keep_output else None
     _launch(q, k, v, scale, out, q8, s8)
     return (out, (q8, s8)) if keep_output else (q8, s8)
+
+
+def attention_lse(q, k, v, scale=None):
+    """Attention over these keys with its log-sum-exp: (o [B, Lq, H, 128] bf16, lse [B, H, Lq] fp32, natural log),
+    torch's cuDNN kernel (the reference's pytorch backend runs the same through SDPA)."""
+    r = torch.ops.aten._scaled_dot_product_cudnn_attention(q.transpose(1, 2), k.transpose(1, 2), v.transpose(1, 2),
+                                                            None, True, 0.0, False, False, scale=scale)
+    o, lse = r[0].transpose(1, 2), r[1]
+    if lse.dim() == 4:
+        lse = lse[..., 0]
+    return o, lse
+
+
+def merge(pieces, quantize=True, keep_output=False):
+    """Combine [(o_i, lse_i)] pieces of one attention (disjoint key ranges, same queries) into the attention over
+    all their keys. Returns the projection input (codes int8 [B*Lq, H*128], scales fp32 [B*Lq, H]) when
+    `quantize`, the bf16 output [B, Lq, H, 128] otherwise, and (out, (codes, scales)) with both."""
+    if not 1 <= len(pieces) <= 16:
+        raise ValueError(f"merge: {len(pieces)} pieces (1 to 16)")
+    parts = [o for o, _ in pieces]
+    lses = [l.float() for _, l in pieces]
+    b, lq, h, d = parts[0].shape
+    if d != HEAD_DIM:
+        raise ValueError(f"merge: head dim {d}")
+    st = parts[0].stride()
+    if any(o.stride() != st or o.shape != parts[0].shape or o.dtype != torch.bfloat16 for o in parts) \
+            or st[3] != 1 or any(x % 4 for x in st[:3]) or any(o.data_ptr() % 8 for o in parts):
+        parts = [o.contiguous() for o in parts]
+        st = parts[0].stride()
+    lst = lses[0].stride()
+    if any(l.stride() != lst or l.shape != (b, h, lq) for l in lses):
+        lses = [l.reshape(b, h, lq).contiguous() for l in lses]
+        lst = lses[0].stride()
+    _lib.require_cuda(*parts, *lses)
+    want_out = keep_output or not quantize
+    out = torch.empty((b, lq, h, d), dtype=torch.bfloat16, device=parts[0].device) if want_out else None
+    q8 = torch.empty((b * lq, h * d), dtype=torch.int8, device=parts[0].device) if quantize else None
+    s8 = torch.empty((b * lq, h), dtype=torch.float32, device=parts[0].device) if quantize else None
+    n = len(parts)
+    pp = (ctypes.c_void_p * n)(*[o.data_ptr() for o in parts])
+    lp = (ctypes.c_void_p * n)(*[l.data_ptr() for l in lses])
+    ost = out.stride() if out is not None else (0, 0, 0)
+    rc = _lib.lib.hn_attn_merge(pp, lp, n, st[0], st[1], st[2], lst[0], lst[1], lst[2], b, lq, h, d,
+                                _lib.ptr(out), ost[0], ost[1], ost[2], _lib.ptr(q8), _lib.ptr(s8),
+                                _lib.stream_of(parts[0]))
+    _lib.check(rc, "attn_merge")
+    if quantize and keep_output:
+        return out, (q8, s8)
+    return (q8, s8) if quantize else out

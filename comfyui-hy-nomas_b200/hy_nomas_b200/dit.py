@@ -40,6 +40,9 @@ from .sequence_parallel import SequenceParallel
 # the step's attention (HN_ATTENTION overrides): "sdpa" - torch SDPA, as the reference's pytorch backend - or
 # "native" - the library's kernel, whose fused output quantizer feeds the projection linear directly
 ATTENTION = "sdpa"
+# under the copy-engine exchange, attend in key pieces - the local keys first, then each peer's slice as it arrives
+# - merged by log-sum-exp (HN_SP_ATTENTION_PIECES=0 waits for every slice and attends once)
+SP_ATTENTION_PIECES = True
 # SMs each GEMM leaves free under sequence parallelism (HN_SP_GEMM_SM_RESERVE overrides)
 SP_GEMM_SM_RESERVE = 0
 
@@ -160,6 +163,15 @@ class CudaOps:
     @staticmethod
     def dequantize_kv(q, s, out):
         return world.dequantize_kv(q, s, out=out)
+
+    @staticmethod
+    def attention_lse(q, k, v):
+        return attention_mod.attention_lse(q, k, v)
+
+    @staticmethod
+    def attention_merge(pieces, keep_output=False):
+        """The projection input (codes, scales) from attention pieces, and the bf16 output first with keep_output."""
+        return attention_mod.merge(pieces, quantize=True, keep_output=keep_output)
 
     @staticmethod
     def attention_quant(q, k, v, keep_output=False):
@@ -292,10 +304,33 @@ def _attention_pushed(cfg, w, qa, sa, rope, peer, ops, b, l, lh, history, captur
     if capture is not None:
         vq, vs = ops.quantize_kv(v_mine.reshape(b * l, h, hd))
         capture.append((kq.reshape(b * l, h, hd), ks.reshape(b * l, h, 1), vq, vs))
-    peer.wait()
-    attn = _attend(ops, q_out, k_full, v_full, keep_qk)
+    pieces = os.environ.get("HN_SP_ATTENTION_PIECES", "1" if SP_ATTENTION_PIECES else "0") != "0"
+    if pieces and hasattr(ops, "attention_lse"):
+        attn = _attend_pieces(ops, q_out, k_full, v_full, lh, l, peer, keep_qk)
+    else:
+        peer.wait()
+        attn = _attend(ops, q_out, k_full, v_full, keep_qk)
     qk = torch.cat([q_in.reshape(b * l, d), k_in.reshape(b * l, d)], dim=1) if keep_qk else None
     return attn, k_full, v_full, qk, q_out
+
+
+def _attend_pieces(ops, q, k_full, v_full, lh, l, peer, keep):
+    """Attention over the history, this rank's slice and then each peer's slice in arrival order, every piece as
+    soon as its keys are here (a bounded wait per peer), merged by log-sum-exp into the projection linear's input;
+    returns what `_attend` returns."""
+    b, lq, h, hd = q.shape
+    mine = lh + peer.rank * l
+    ranges = ([(0, lh, None)] if lh else []) + [(mine, mine + l, None)]
+    ranges += [(lh + p * l, lh + (p + 1) * l, p) for p in peer.arrival_order()]
+    pieces = []
+    for lo, hi, p in ranges:
+        if p is not None:
+            peer.wait(p)
+        pieces.append(ops.attention_lse(q, k_full[:, lo:hi], v_full[:, lo:hi]))
+    if keep:
+        out, codes = ops.attention_merge(pieces, keep_output=True)
+        return out.reshape(b * lq, h * hd), codes
+    return None, ops.attention_merge(pieces)
 
 
 def _rows(w, lo, hi):

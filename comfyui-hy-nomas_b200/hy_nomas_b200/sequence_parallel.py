@@ -260,13 +260,20 @@ class PeerExchange:
         ev.record(side)
         ent["done"][par][kind] = ev
 
-    def wait(self):
-        """The current stream waits (bounded) for every peer's K and V of this block."""
+    def wait(self, peer=None):
+        """The current stream waits (bounded) for every peer's K and V of this block, or for `peer`'s only."""
         lib = self._lib
         cur = torch.cuda.current_stream(self.device)
-        lib.check(lib.lib.hn_wait_flags(ctypes.c_void_p(self.flags.data_ptr()), 2, self.world, self.rank,
-                                        self.epoch, self.timeout_us, ctypes.c_void_p(cur.cuda_stream)),
+        base = self.flags.data_ptr() + (0 if peer is None else 4 * peer)
+        count, skip = (self.world, self.rank) if peer is None else (1, -1)
+        lib.check(lib.lib.hn_wait_flags(ctypes.c_void_p(base), 2, count, self.world, skip, self.epoch,
+                                        self.timeout_us, ctypes.c_void_p(cur.cuda_stream)),
                   "hn_wait_flags")
+
+    def arrival_order(self):
+        """The peers in the order their slices reach this rank: every rank pushes to rank + 1 first, so this rank
+        hears from rank - 1 first, then rank - 2, ..."""
+        return [(self.rank - s) % self.world for s in range(1, self.world)]
 
     def close(self):
         """Unmap the peers' memory once every rank's pushes are complete (collective)."""

@@ -282,6 +282,19 @@ int hn_attention(const void *q, int64_t q_rs, int64_t q_hs, int64_t q_bs, const 
                  int8_t *q8, float *s8, void *stream);
 
 /*
+ * Merge of attention computed in key pieces: piece i (i < n <= 16) holds o_i [B, Lq, H, 128] bf16 (strides o_*, the
+ * same for every piece) = softmax(q k_i^T * scale) v_i over its keys and lse_i [B, H, Lq] fp32 (strides l_*) = the
+ * natural log of that softmax's sum of exp(logits). Writes out = sum_i exp(lse_i - L) o_i, L = log sum_i exp(lse_i),
+ * as bf16 [B, Lq, H, 128] (strides out_*) and/or its int8 codes per token x 128 channels (q8 [B*Lq, H*128], s8
+ * [B*Lq, H]; the hn_quant_act arithmetic, as in hn_attention). `parts` and `lses` are host arrays of device
+ * pointers. No reference counterpart: the reference attends in one call; this lets the sequence-parallel step
+ * attend to each rank's keys as they arrive. Piece strides multiples of 4 elements, 8-byte aligned pieces.
+ */
+int hn_attn_merge(const void *const *parts, const float *const *lses, int64_t n, int64_t o_bs, int64_t o_qs,
+                  int64_t o_hs, int64_t l_bs, int64_t l_hs, int64_t l_qs, int64_t B, int64_t Lq, int64_t H, int64_t D,
+                  void *out, int64_t out_bs, int64_t out_qs, int64_t out_hs, int8_t *q8, float *s8, void *stream);
+
+/*
  * Sequence-parallel K/V exchange over NVLink by the copy engines. No reference counterpart: the reference runs
  * one GPU; these replace the NCCL all-gather of the build's own sequence-parallel DiT step, whose SM-based kernel
  * cannot run beside the persistent GEMM. All host-side: no kernel of this library is involved.
@@ -293,8 +306,8 @@ int hn_attention(const void *q, int64_t q_rs, int64_t q_hs, int64_t q_bs, const 
  * hn_peer_push: on `stream`, copy `bytes` from src (this device) to dst (a mapped peer address) by DMA, then write
  *   the 32-bit `value` to `flag` (a mapped peer address, or NULL for none) after a memory fence, so the data is
  *   visible before the flag.
- * hn_wait_flags: on `stream`, one warp waits until every flags[g * count + i] (g < groups, i < count, i != skip;
- *   groups * count <= 1024) has reached `value` (wrap-safe: (int32_t)(flag - value) >= 0), with system-scope
+ * hn_wait_flags: on `stream`, one warp waits until every flags[g * group_stride + i] (g < groups, i < count,
+ *   i != skip; groups * count <= 1024) has reached `value` (wrap-safe: (int32_t)(flag - value) >= 0), with system-scope
  *   acquire loads, so that kernels after it on the stream see the data pushed before those flags. Bounded: after
  *   `timeout_us` it records HN_ERR_TIMEOUT in the stream's error word (hn_device_error) and returns.
  */
@@ -302,8 +315,8 @@ int hn_ipc_export(const void *ptr, void *handle_host, int64_t *offset_host);
 int hn_ipc_import(const void *handle_host, void **base_host);
 int hn_ipc_close(void *base);
 int hn_peer_push(void *dst, const void *src, int64_t bytes, void *flag, uint32_t value, void *stream);
-int hn_wait_flags(const int32_t *flags, int64_t groups, int64_t count, int64_t skip, uint32_t value,
-                  uint32_t timeout_us, void *stream);
+int hn_wait_flags(const int32_t *flags, int64_t groups, int64_t count, int64_t group_stride, int64_t skip,
+                  uint32_t value, uint32_t timeout_us, void *stream);
 
 #if defined(__GNUC__)
 #pragma GCC visibility pop

@@ -59,7 +59,7 @@ def gloo_rank(rank, world, port, out_path, head_chunks=1, history_tokens=0):
         dist.destroy_process_group()
 
 
-def nccl_rank(rank, world, port, out_path, head_chunks=1, exchange="ce", history_tokens=0):
+def nccl_rank(rank, world, port, out_path, head_chunks=1, exchange="ce", history_tokens=0, pieces=True):
     """One rank of a sequence-parallel run on GPU `rank`: two steps (the second reuses the double-buffered K/V
     exchange buffers) and, with `history_tokens`, a third step over an int8 K/V history. Rank 0 saves every
     step's gathered output, the exchange used and the ranks' device error words."""
@@ -69,6 +69,7 @@ def nccl_rank(rank, world, port, out_path, head_chunks=1, exchange="ce", history
     os.environ["MASTER_PORT"] = str(port)
     os.environ.setdefault("NCCL_NVLS_ENABLE", "0")
     os.environ["HN_SP_EXCHANGE"] = exchange
+    os.environ["HN_SP_ATTENTION_PIECES"] = "1" if pieces else "0"
     torch.cuda.set_device(rank)
     dist.init_process_group("nccl", rank=rank, world_size=world, device_id=torch.device("cuda", rank),
                             timeout=datetime.timedelta(seconds=60))

@@ -120,6 +120,36 @@ def test_dit_rank_shape(hn, cuda):
     assert err < TOL
 
 
+def test_log_sum_exp_is_natural_log(hn, cuda):
+    from hy_nomas_b200.attention import attention_lse
+    gen = torch.Generator(device=cuda).manual_seed(10)
+    q, k, v = rand((1, 64, 2, 128), gen, cuda), rand((1, 96, 2, 128), gen, cuda), rand((1, 96, 2, 128), gen, cuda)
+    o, lse = attention_lse(q, k, v)
+    logits = torch.einsum("bqhd,bkhd->bhqk", q.float(), k.float()) / math.sqrt(128)
+    want = torch.logsumexp(logits, dim=-1)
+    assert lse.shape == (1, 2, 64)
+    assert torch.allclose(lse.float(), want, atol=2e-2, rtol=0), (lse.float() - want).abs().max().item()
+
+
+def test_merge_of_pieces_equals_whole(hn, cuda):
+    """Attention in three key pieces merged by log-sum-exp: the whole attention within the bf16 tolerance; its
+    fused quantizer equals the activation quantizer on the merged output; one piece merges to itself exactly."""
+    from hy_nomas_b200.attention import attention_lse, merge
+    gen = torch.Generator(device=cuda).manual_seed(11)
+    b, lq, lk, h = 1, 300, 1000, 4
+    q, k, v = rand((b, lq, h, 128), gen, cuda), rand((b, lk, h, 128), gen, cuda), rand((b, lk, h, 128), gen, cuda)
+    cuts = [0, 100, 612, lk]
+    pieces = [attention_lse(q, k[:, a:c], v[:, a:c]) for a, c in zip(cuts[:-1], cuts[1:])]
+    out, (q8, s8) = merge(pieces, quantize=True, keep_output=True)
+    err = rel_l2(out.float().cpu().numpy(), ref_fp32(q, k, v).cpu().numpy())
+    print(f"merged pieces rel-L2 {err:.2e}")
+    assert err < TOL
+    rq, rs = hn.kernels.quantize_activations(out.reshape(b * lq, h * 128))
+    assert torch.equal(q8, rq) and torch.equal(s8.view(torch.int32), rs.view(torch.int32))
+    one = attention_lse(q, k, v)
+    assert torch.equal(merge([one], quantize=False).view(torch.int16), one[0].contiguous().view(torch.int16))
+
+
 def test_rejects_bad_arguments(hn, cuda):
     import ctypes
     from hy_nomas_b200.attention import attention

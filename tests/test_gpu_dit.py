@@ -131,12 +131,12 @@ def free_port():
         return s.getsockname()[1]
 
 
-def run_two_ranks(tmp_path, head_chunks=1, exchange="ce", history_tokens=0):
+def run_two_ranks(tmp_path, head_chunks=1, exchange="ce", history_tokens=0, pieces=True):
     ctx = mp.get_context("spawn")
     port = free_port()
-    out_path = os.path.join(tmp_path, f"sp_{exchange}_{head_chunks}_{history_tokens}.pt")
+    out_path = os.path.join(tmp_path, f"sp_{exchange}_{head_chunks}_{history_tokens}_{int(pieces)}.pt")
     procs = [ctx.Process(target=sp_worker.nccl_rank, args=(r, 2, port, out_path, head_chunks, exchange,
-                                                           history_tokens)) for r in range(2)]
+                                                           history_tokens, pieces)) for r in range(2)]
     for p in procs:
         p.start()
     for p in procs:
@@ -168,17 +168,21 @@ def test_sequence_parallel_two_gpus(hn, cuda, tmp_path, head_chunks, exchange):
 
 
 def test_copy_engine_exchange_matches_nccl(hn, cuda, tmp_path):
-    """The copy-engine exchange moves the same bytes as the all-gather: outputs bit-identical to the NCCL run,
-    with and without a 30-token int8 K/V history (its own double-buffered exchange buffers)."""
+    """The copy-engine exchange moves the same bytes as the all-gather: attending once after every slice arrived,
+    the outputs are bit-identical to the NCCL run, with and without a 30-token int8 K/V history (its own
+    double-buffered exchange buffers). Attending in pieces as the slices arrive (the default) agrees within the
+    bf16 attention tolerance."""
     if torch.cuda.device_count() < 2:
         pytest.skip("needs 2 GPUs")
-    ce = run_two_ranks(tmp_path, 1, "ce", history_tokens=30)
+    whole = run_two_ranks(tmp_path, 1, "ce", history_tokens=30, pieces=False)
     nc = run_two_ranks(tmp_path, 1, "nccl", history_tokens=30)
-    assert ce["exchange"] == "ce" and nc["exchange"] == "nccl"
-    assert ce["errors"] == [0, 0] and nc["errors"] == [0, 0]
-    for a, b in zip(ce["outs"], nc["outs"]):
+    piecewise = run_two_ranks(tmp_path, 1, "ce", history_tokens=30, pieces=True)
+    assert whole["exchange"] == "ce" and nc["exchange"] == "nccl" and piecewise["exchange"] == "ce"
+    assert whole["errors"] == [0, 0] and nc["errors"] == [0, 0] and piecewise["errors"] == [0, 0]
+    for a, b, c in zip(whole["outs"], nc["outs"], piecewise["outs"]):
         assert torch.equal(a.view(torch.int16), b.view(torch.int16))
-    assert not torch.equal(ce["outs"][0], ce["outs"][2])      # the history changed the output
+        assert rel_l2(c.float().numpy(), b.float().numpy()) < 1e-2
+    assert not torch.equal(whole["outs"][0], whole["outs"][2])      # the history changed the output
 
 
 @pytest.fixture(scope="module")

@@ -25,7 +25,10 @@ def test_push_then_wait_sees_data(hn, cuda):
             L.check(L.lib.hn_peer_push(vp(dst.data_ptr()), vp(src.data_ptr()), src.numel() * 2,
                                        vp(flags.data_ptr() + 4 * (kind * 4 + src_rank)), 7, vp(st.cuda_stream)),
                     "hn_peer_push", launches=0)
-    L.check(L.lib.hn_wait_flags(vp(flags.data_ptr()), 2, 4, 1, 7, 2000000, vp(st.cuda_stream)), "hn_wait_flags")
+    L.check(L.lib.hn_wait_flags(vp(flags.data_ptr()), 2, 4, 4, 1, 7, 2000000, vp(st.cuda_stream)), "hn_wait_flags")
+    # one source's two flags (kinds 0 and 1, `count` apart)
+    L.check(L.lib.hn_wait_flags(vp(flags.data_ptr() + 4 * 2), 2, 1, 4, -1, 7, 2000000, vp(st.cuda_stream)),
+            "hn_wait_flags")
     out = dst.float().sum()
     rc, code = L.device_error(st)
     assert rc == 0 and code == 0
@@ -39,7 +42,7 @@ def test_wait_compares_wrap_safe(hn, cuda):
     L = hn.lib
     st = torch.cuda.current_stream()
     flags = torch.tensor([2, 2], dtype=torch.int32, device=cuda)
-    L.check(L.lib.hn_wait_flags(vp(flags.data_ptr()), 1, 2, -1, 0xFFFFFFFE, 2000000, vp(st.cuda_stream)),
+    L.check(L.lib.hn_wait_flags(vp(flags.data_ptr()), 1, 2, 2, -1, 0xFFFFFFFE, 2000000, vp(st.cuda_stream)),
             "hn_wait_flags")
     rc, code = L.device_error(st)
     assert rc == 0 and code == 0
@@ -50,7 +53,7 @@ def test_wait_runs_out_and_context_survives(hn, cuda):
     st = torch.cuda.current_stream()
     flags = torch.zeros(4, dtype=torch.int32, device=cuda)
     flags[0] = 5                                                # one of the three waited flags arrived
-    L.check(L.lib.hn_wait_flags(vp(flags.data_ptr()), 1, 4, 3, 5, 20000, vp(st.cuda_stream)), "hn_wait_flags")
+    L.check(L.lib.hn_wait_flags(vp(flags.data_ptr()), 1, 4, 4, 3, 5, 20000, vp(st.cuda_stream)), "hn_wait_flags")
     rc, code = L.device_error(st)
     assert rc == 6 and code == 1                                # HN_ERR_TIMEOUT, HN_DEVERR_TIMEOUT
     rc, code = L.device_error(st)
@@ -65,7 +68,7 @@ def test_wait_rejects_bad_arguments(hn, cuda):
     L = hn.lib
     flags = torch.zeros(8, dtype=torch.int32, device=cuda)
     st = vp(torch.cuda.current_stream().cuda_stream)
-    assert L.lib.hn_wait_flags(vp(flags.data_ptr()), 2, 1024, 0, 1, 1000, st) == 1        # HN_ERR_SHAPE
-    assert L.lib.hn_wait_flags(vp(flags.data_ptr() + 2), 1, 2, 0, 1, 1000, st) == 2       # HN_ERR_ALIGN
-    assert L.lib.hn_wait_flags(vp(flags.data_ptr()), 1, 2, 0, 1, 0, st) == 5              # HN_ERR_ARG
-    assert L.lib.hn_wait_flags(None, 1, 2, 0, 1, 1000, st) == 5
+    assert L.lib.hn_wait_flags(vp(flags.data_ptr()), 2, 1024, 1024, 0, 1, 1000, st) == 1    # HN_ERR_SHAPE
+    assert L.lib.hn_wait_flags(vp(flags.data_ptr() + 2), 1, 2, 2, 0, 1, 1000, st) == 2       # HN_ERR_ALIGN
+    assert L.lib.hn_wait_flags(vp(flags.data_ptr()), 1, 2, 2, 0, 1, 0, st) == 5              # HN_ERR_ARG
+    assert L.lib.hn_wait_flags(None, 1, 2, 2, 0, 1, 1000, st) == 5
