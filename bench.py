@@ -1,6 +1,6 @@
 """Benchmark of the quantized DiT linear path on B200 - one JSON line on rank 0.
 
-    python bench.py [--gpus N] [--steps K] [--warmup W] [--workload dit|dit_gemms|gemm|fp8|elementwise]
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--workload dit|dit_gemms|attention|gemm|fp8|elementwise]
                     [--impl ours|reference]
 
 Workloads (synthetic, seeded; the reference publishes no dataset for this path):
@@ -1132,7 +1132,154 @@ def reference_elementwise(args):
 # --------------------------------------------------------------------------------------------------------
 
 
+# --------------------------------------------------------------------------------------------------------
+# attention (configs 4 and 5's attention, hy_nomas/model.py:145-151)
+
+ATTN_L, ATTN_H = 20240, 32
+
+
+def attn_inputs(lq, lk, gen, dev):
+    q = torch.randn(1, lq, ATTN_H, 128, generator=gen, device=dev).to(torch.bfloat16)
+    k = torch.randn(1, lk, ATTN_H, 128, generator=gen, device=dev).to(torch.bfloat16)
+    v = torch.randn(1, lk, ATTN_H, 128, generator=gen, device=dev).to(torch.bfloat16)
+    return q, k, v
+
+
+def workload_attention(args, world, rank, stream, pk, sampler):
+    """The block's attention at the DiT shape (20240 queries x 20240 keys x 32 heads x 128) on the library's
+    sm_100a kernel with the projection's input quantizer fused (attention.attention_quant, the path the block
+    takes with HN_ATTENTION=native); torch's cuDNN SDPA on the same inputs, the one-rank-of-eight shape and the
+    key-piece merge of the sequence-parallel step are reported beside it."""
+    import torch.nn.functional as F
+    from hy_nomas_b200 import attention as attn
+    dev = torch.device("cuda")
+    gen = torch.Generator(device=dev).manual_seed(77 + rank)
+    q, k, v = attn_inputs(ATTN_L, ATTN_L, gen, dev)
+    flops = 4.0 * ATTN_L * ATTN_L * ATTN_H * 128
+    timer = KernelTimer(stream)
+
+    def step(i):
+        timer.wrap(lambda: attn.attention_quant(q, k, v), flops)
+
+    ms = timed_steps(step, args.steps, args.warmup, world, stream, sampler)
+    timer.active = True
+    timed_steps(step, args.steps, 0, world, stream)
+    kernel_ms = timer.mean_ms()
+    launches = launch_count(lambda: step(0))
+
+    def bench_ms(fn, it=5):
+        for _ in range(2):
+            fn()
+        torch.cuda.synchronize()
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record(stream)
+        for _ in range(it):
+            fn()
+        e1.record(stream)
+        torch.cuda.synchronize()
+        return e0.elapsed_time(e1) / it
+
+    sdpa = lambda qq, kk, vv: F.scaled_dot_product_attention(qq.transpose(1, 2), kk.transpose(1, 2), vv.transpose(1, 2))
+    sdpa_ms = bench_ms(lambda: sdpa(q, k, v))
+    plain_ms = bench_ms(lambda: attn.attention(q, k, v))
+    lr = ATTN_L // 8
+    qr = q[:, :lr].contiguous()
+    rank_native = bench_ms(lambda: attn.attention_quant(qr, k, v))
+    rank_sdpa = bench_ms(lambda: sdpa(qr, k, v))
+    rank_pieces = bench_ms(lambda: attn.merge([attn.attention_lse(qr, k[:, i * lr:(i + 1) * lr], v[:, i * lr:(i + 1) * lr])
+                                               for i in range(8)]))
+    rflops = 4.0 * lr * ATTN_L * ATTN_H * 128
+    # e2e: q, k, v from pinned host memory through the public API, the quantized projection input read back
+    qh, kh, vh = q.cpu().pin_memory(), k.cpu().pin_memory(), v.cpu().pin_memory()
+    ch = torch.empty((ATTN_L, ATTN_H * 128), dtype=torch.int8).pin_memory()
+    sh = torch.empty((ATTN_L, ATTN_H), dtype=torch.float32).pin_memory()
+
+    def e2e_step(i):
+        c, sc = attn.attention_quant(qh.to(dev, non_blocking=True), kh.to(dev, non_blocking=True),
+                                     vh.to(dev, non_blocking=True))
+        ch.copy_(c, non_blocking=True)
+        sh.copy_(sc, non_blocking=True)
+
+    e2e_ms = timed_steps(e2e_step, args.steps, 1, world, stream)
+    total = sum_over_ranks(flops * args.steps, world)
+    achieved = flops / (kernel_ms * 1e-3) / 1e12
+    roof = {"kernel": "hn::attn::k_attention (fused int8 output quantizer)", "bound": "tensor",
+            "achieved": round(achieved, 1), "peak": pk["bf16_tflops"], "unit": "TFLOP/s",
+            "frac": round(achieved / pk["bf16_tflops"], 4),
+            "peak_note": f"{pk['source']} bf16 dense burst (the kernel is timed alone)", "traffic": None}
+    config = {"workload": f"attention_L{ATTN_L}_H{ATTN_H}_D128 (configs 4/5): softmax(q k^T / sqrt(128)) v + the "
+                          "projection's int8 input quantizer",
+              "q_k_v": f"bf16 [1, {ATTN_L}, {ATTN_H}, 128] each (166 MB; 498 MB together, above L2)",
+              "native_fused_quant_ms": round(kernel_ms, 3), "native_bf16_out_ms": round(plain_ms, 3),
+              "torch_cudnn_sdpa_ms": round(sdpa_ms, 3),
+              "torch_cudnn_sdpa_tflops": round(flops / (sdpa_ms * 1e-3) / 1e12, 1),
+              "one_rank_of_8": {"queries": lr, "native_quant_ms": round(rank_native, 3),
+                                "native_tflops": round(rflops / (rank_native * 1e-3) / 1e12, 1),
+                                "cudnn_sdpa_ms": round(rank_sdpa, 3),
+                                "cudnn_8_key_pieces_plus_merge_ms": round(rank_pieces, 3)},
+              "parallelism": f"replicas x{world}"}
+    return dict(metric="attention TFLOP/s (20240 x 20240 x 32 heads x 128)", value=round(total / (ms * 1e-3) / 1e12, 1),
+                unit="TFLOP/s", ms_per_step=round(ms / args.steps, 3), higher_is_better=True, scaling="weak",
+                dtype="bf16 (fp32 softmax and accumulators)", config=config,
+                e2e={"value": round(total / (e2e_ms * 1e-3) / 1e12, 1), "unit": "TFLOP/s",
+                     "h2d_bytes_per_step": 3 * q.numel() * 2 * world,
+                     "d2h_bytes_per_step": (ch.numel() + sh.numel() * 4) * world},
+                roofline=roof, gpu_launches=launches * args.steps,
+                cpu_baseline_fn=lambda: cpu_baseline_attention())
+
+
+def attention_cpu_sample(rows, gen):
+    q = torch.randn(1, rows, ATTN_H, 128, generator=gen).to(torch.bfloat16)
+    k = torch.randn(1, ATTN_L, ATTN_H, 128, generator=gen).to(torch.bfloat16)
+    v = torch.randn(1, ATTN_L, ATTN_H, 128, generator=gen).to(torch.bfloat16)
+    return q, k, v
+
+
+def attention_cpu(q, k, v):
+    """The reference's attention through torch SDPA (ComfyUI's pytorch backend, hy_nomas/model.py:145-151)."""
+    import torch.nn.functional as F
+    return F.scaled_dot_product_attention(q.transpose(1, 2), k.transpose(1, 2), v.transpose(1, 2)).transpose(1, 2)
+
+
+def cpu_baseline_attention(budget_s=10.0):
+    rows = 64
+    q, k, v = attention_cpu_sample(rows, torch.Generator().manual_seed(6))
+    attention_cpu(q, k, v)
+    t0 = time.perf_counter()
+    it = 0
+    while time.perf_counter() - t0 < budget_s:
+        attention_cpu(q, k, v)
+        it += 1
+    dt = (time.perf_counter() - t0) / it
+    cores, threads = cpu_threads()
+    return {"value": round(4.0 * rows * ATTN_L * ATTN_H * 128 / dt / 1e12, 4), "unit": "TFLOP/s", "cores": threads,
+            "kind": "reference",
+            "sample": f"{rows} of {ATTN_L} queries against all keys, {it} iterations in {budget_s:.0f}+ s (torch "
+                      f"{torch.__version__} SDPA on bf16, {threads} threads on {cores} cores)"}
+
+
+def reference_attention(args):
+    """The reference's attention on the host: torch SDPA (its pytorch backend) on 64 of the 20240 queries per
+    step against all keys."""
+    rows = 64
+    q, k, v = attention_cpu_sample(rows, torch.Generator().manual_seed(6))
+    for _ in range(args.warmup):
+        attention_cpu(q, k, v)
+    t0 = time.perf_counter()
+    for _ in range(args.steps):
+        attention_cpu(q, k, v)
+    dt = time.perf_counter() - t0
+    cores, threads = cpu_threads()
+    return dict(metric="attention TFLOP/s (20240 x 20240 x 32 heads x 128)",
+                value=round(4.0 * rows * ATTN_L * ATTN_H * 128 * args.steps / dt / 1e12, 4), unit="TFLOP/s",
+                ms_per_step=round(dt / args.steps * 1e3, 3), higher_is_better=True, scaling="weak",
+                dtype="bf16 (fp32 softmax and accumulators)", kind="reference", cores=threads,
+                config={"workload": f"attention_L{ATTN_L}_H{ATTN_H}_D128 (configs 4/5)"},
+                sample=f"{rows} of {ATTN_L} queries per step (torch SDPA on bf16, {threads} threads)")
+
+
 WORKLOADS = {"dit": (workload_dit, reference_dit), "dit_gemms": (workload_dit_gemms, reference_dit_gemms),
+             "attention": (workload_attention, reference_attention),
              "gemm": (workload_gemm, reference_gemm),
              "fp8": (workload_fp8, reference_fp8), "elementwise": (workload_elementwise, reference_elementwise)}
 
