@@ -11,7 +11,8 @@
 //               tensor-memory form of the MMA) and V MN-major straight from its TMA tile. S(j+1) is issued
 //               before P(j) V_j, so the tensor core computes the next logits while the softmax warps work.
 //   warps 4-7   softmax, one thread per query row (its TMEM lane): loads its 128 logits of S(j) at once,
-//               keeps a running maximum m (base-2 logits) and sum l, writes P = 2^(s * scale * log2 e - m) as
+//               takes their maximum with three-input max, keeps a running maximum m (base-2 logits) and sum l
+//               (the scaling and the sums in packed f32x2 arithmetic), writes P = 2^(s * scale * log2 e - m) as
 //               bf16 pairs into one of two 64-column TMEM buffers, and rescales its O row in TMEM only when the
 //               maximum grew by more than 2^8 (a stale maximum leaves every P <= 2^8: exact in fp32 and bf16
 //               range). After the last step: O / l -> bf16 rows (and the int8 codes + scale of each row).
@@ -59,6 +60,12 @@ struct Params {
     int8_t *q8; float *s8;                      // [B*Lq, H*128] codes and [B*Lq, H] scales, or null
     int *err;
 };
+
+__device__ __forceinline__ float fmax3(float a, float b, float c) {
+    float y;
+    asm("max.f32 %0, %1, %2, %3;" : "=f"(y) : "f"(a), "f"(b), "f"(c));
+    return y;
+}
 
 __device__ __forceinline__ float ex2(float x) {
     float y;
@@ -305,19 +312,20 @@ __global__ void __launch_bounds__(THREADS, 1)
                     if (kb + 96 + c >= p.Lk) r3[c] = __float_as_uint(-INFINITY);
                 }
             }
+            // row maximum: three-input max, two new logits per instruction in eight independent chains
             float mx[8];
 #pragma unroll
-            for (int i = 0; i < 8; ++i)
-                mx[i] = fmaxf(fmaxf(__uint_as_float(r0[i]), __uint_as_float(r1[i])),
-                              fmaxf(__uint_as_float(r2[i]), __uint_as_float(r3[i])));
+            for (int i = 0; i < 8; ++i) mx[i] = fmax3(__uint_as_float(r0[i]), __uint_as_float(r1[i]), __uint_as_float(r2[i]));
+#pragma unroll
+            for (int i = 0; i < 8; ++i) mx[i] = fmax3(mx[i], __uint_as_float(r3[i]), __uint_as_float(r0[8 + i]));
 #pragma unroll
             for (int c = 8; c < 32; c += 8)
 #pragma unroll
-                for (int i = 0; i < 8; ++i)
-                    mx[i] = fmaxf(mx[i], fmaxf(fmaxf(__uint_as_float(r0[c + i]), __uint_as_float(r1[c + i])),
-                                               fmaxf(__uint_as_float(r2[c + i]), __uint_as_float(r3[c + i]))));
-            const float tmax = fmaxf(fmaxf(fmaxf(mx[0], mx[1]), fmaxf(mx[2], mx[3])),
-                                     fmaxf(fmaxf(mx[4], mx[5]), fmaxf(mx[6], mx[7])));
+                for (int i = 0; i < 8; ++i) {
+                    mx[i] = fmax3(mx[i], __uint_as_float(r1[c + i]), __uint_as_float(r2[c + i]));
+                    mx[i] = fmax3(mx[i], __uint_as_float(r3[c + i]), c + 8 < 32 ? __uint_as_float(r0[c + 8 + i]) : mx[i]);
+                }
+            const float tmax = fmax3(fmax3(mx[0], mx[1], mx[2]), fmax3(mx[3], mx[4], mx[5]), fmaxf(mx[6], mx[7]));
             const float m_new = fmaxf(m_run, tmax * sl2);
             if (j == 0) {
                 m_run = m_new;
@@ -346,17 +354,17 @@ __global__ void __launch_bounds__(THREADS, 1)
                 ok = warp_wait(lane, bar_pv + 8 * bs, ((j - 2) >> 1) & 1, abort_flag, WAIT_NS, p.err);
                 if (!ok) break;
             }
-            const float nm = -m_run;
             const uint32_t pa = tl + (uint32_t)(P_COL + bs * (BKV / 2));
-            float ps0 = 0.0f, ps1 = 0.0f;
+            const uint64_t nm2 = x2_splat(-m_run), sl22 = x2_splat(sl2);
+            uint64_t ps2 = 0ull;                                    // packed partial sums (+0.0f, +0.0f)
             auto emit = [&](const uint32_t (&r)[32], uint32_t col) {
                 uint32_t pk[16];
 #pragma unroll
                 for (int c = 0; c < 32; c += 2) {
-                    const float e0 = ex2(fmaf(__uint_as_float(r[c]), sl2, nm));
-                    const float e1 = ex2(fmaf(__uint_as_float(r[c + 1]), sl2, nm));
-                    ps0 += e0;
-                    ps1 += e1;
+                    float a0, a1;
+                    x2_split(x2_fma(x2(__uint_as_float(r[c]), __uint_as_float(r[c + 1])), sl22, nm2), a0, a1);
+                    const float e0 = ex2(a0), e1 = ex2(a1);
+                    ps2 = x2_add(ps2, x2(e0, e1));
                     pk[c >> 1] = pack_bf16_rn(e0, e1);
                 }
                 tmem_st16(pa + col, pk);
@@ -365,7 +373,11 @@ __global__ void __launch_bounds__(THREADS, 1)
             emit(r1, 16);
             emit(r2, 32);
             emit(r3, 48);
-            l += ps0 + ps1;
+            {
+                float p0, p1;
+                x2_split(ps2, p0, p1);
+                l += p0 + p1;
+            }
             tmem_wait_st();
             tc_fence_before();
             __syncwarp();
