@@ -336,6 +336,7 @@ def workload_dit(args, world, rank, stream, pk, sampler):
         config["segment2_with_int8_history"] = segment2_context(model, vec, world, stream)
     if world == 1 and not args.no_context:
         config["configs_1_to_3"] = path_context(stream, pk)
+        config["attention_kernel"] = attention_context(stream, pk)
     sp.close()
     return dict(metric="DiT denoise step tokens/s (40 blocks, 20240 tokens)", value=round(value, 1), unit="tokens/s",
                 ms_per_step=round(step_ms, 3), higher_is_better=True, scaling="strong", dtype="int8 (GEMMs), bf16",
@@ -1226,6 +1227,36 @@ def workload_attention(args, world, rank, stream, pk, sampler):
                      "d2h_bytes_per_step": (ch.numel() + sh.numel() * 4) * world},
                 roofline=roof, gpu_launches=launches * args.steps,
                 cpu_baseline_fn=lambda: cpu_baseline_attention())
+
+
+def attention_context(stream, pk):
+    """The library's attention kernel (fused projection quantizer) against cuDNN SDPA at the step's shape, for
+    the default line (the step itself runs cuDNN)."""
+    import torch.nn.functional as F
+    from hy_nomas_b200 import attention as attn
+    gen = torch.Generator(device="cuda").manual_seed(78)
+    q, k, v = attn_inputs(ATTN_L, ATTN_L, gen, torch.device("cuda"))
+    flops = 4.0 * ATTN_L * ATTN_L * ATTN_H * 128
+
+    def ms(fn, it=5):
+        for _ in range(2):
+            fn()
+        torch.cuda.synchronize()
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record(stream)
+        for _ in range(it):
+            fn()
+        e1.record(stream)
+        torch.cuda.synchronize()
+        return e0.elapsed_time(e1) / it
+
+    nat = ms(lambda: attn.attention_quant(q, k, v))
+    ref = ms(lambda: F.scaled_dot_product_attention(q.transpose(1, 2), k.transpose(1, 2), v.transpose(1, 2)))
+    return {"shape": f"{ATTN_L} x {ATTN_L} x {ATTN_H} heads x 128", "kernel": "hn::attn::k_attention",
+            "native_fused_quant_ms": round(nat, 3), "native_tflops": round(flops / (nat * 1e-3) / 1e12, 1),
+            "native_frac_of_bf16_burst": round(flops / (nat * 1e-3) / 1e12 / pk["bf16_tflops"], 3),
+            "cudnn_sdpa_ms": round(ref, 3), "cudnn_sdpa_tflops": round(flops / (ref * 1e-3) / 1e12, 1),
+            "step_uses": "cudnn_sdpa (faster); HN_ATTENTION=native switches the block to the kernel"}
 
 
 def attention_cpu_sample(rows, gen):
