@@ -173,7 +173,7 @@ class PeerExchange:
             err = e
         if not _ranks_agree(err is None, sp.group):
             if exch is not None:
-                exch.close()
+                exch._unmap()                      # local only: the failing rank enters no further collective
             warnings.warn(f"copy-engine K/V exchange unavailable ({err or 'a peer failed'}); using NCCL all-gather")
             return None
         return exch
@@ -284,11 +284,15 @@ class PeerExchange:
         hears from rank - 1 first, then rank - 2, ..."""
         return [(self.rank - s) % self.world for s in range(1, self.world)]
 
+    def _unmap(self):
+        """Unmap the peers' memory this rank mapped (no collective; nothing may be pushed through it anymore)."""
+        for base in self._maps.values():
+            self._lib.lib.hn_ipc_close(ctypes.c_void_p(base))
+        self._maps.clear()
+
     def close(self):
         """Unmap the peers' memory once every rank's pushes are complete (collective)."""
         torch.cuda.synchronize(self.device)
         dist.barrier(group=self.group)
-        for base in self._maps.values():
-            self._lib.lib.hn_ipc_close(ctypes.c_void_p(base))
-        self._maps.clear()
+        self._unmap()
         dist.barrier(group=self.group)

@@ -103,3 +103,39 @@ def nccl_rank(rank, world, port, out_path, head_chunks=1, exchange="ce", history
             torch.save({"outs": gathered, "exchange": kind, "errors": [int(e.item()) for e in errs]}, out_path)
     finally:
         dist.destroy_process_group()
+
+
+def fallback_rank(rank, world, port, out_path, failing_rank):
+    """A copy-engine exchange whose set-up fails on `failing_rank` only (its mapping raises, as it would for
+    memory with no IPC handle): every rank must come out without it (NCCL all-gather instead), none may wait
+    for the others in a collective they never enter. Host logic only, on gloo."""
+    import torch.distributed as dist
+    from hy_nomas_b200 import sequence_parallel as S
+    os.environ["MASTER_ADDR"] = "127.0.0.1"
+    os.environ["MASTER_PORT"] = str(port)
+    dist.init_process_group("gloo", rank=rank, world_size=world)
+    try:
+        unmapped = []
+
+        class Failing(S.PeerExchange):
+            """The real class with set-up replaced: mapping fails on `failing_rank`; close() stays the real,
+            collective one, so a fallback that called it on the other ranks would hang this test."""
+            def __init__(self, sp):
+                if sp.rank == failing_rank:
+                    raise RuntimeError("hn_ipc_export failed (no legacy IPC handle)")
+
+            def _unmap(self):
+                unmapped.append(True)
+
+        sp = S.SequenceParallel(local=False)
+        import warnings
+        with warnings.catch_warnings(record=True) as caught:
+            warnings.simplefilter("always")
+            exch = Failing.create(sp)
+        ok = torch.tensor([1 if exch is None else 0, len(caught), len(unmapped)])
+        parts = [torch.zeros_like(ok) for _ in range(world)]
+        dist.all_gather(parts, ok)
+        if rank == 0:
+            torch.save(torch.stack(parts), out_path)
+    finally:
+        dist.destroy_process_group()

@@ -105,3 +105,27 @@ def test_capture_is_the_kv_quantizer_of_the_block_kv(hn, oracle):
     v_ref = OracleOps.quantize_kv(trace["v_full"].reshape(l, h, d))
     assert torch.equal(kq, k_ref[0]) and torch.equal(ks, k_ref[1])
     assert torch.equal(vq, v_ref[0]) and torch.equal(vs, v_ref[1])
+
+
+@pytest.mark.parametrize("failing_rank", [0, 1])
+def test_copy_engine_setup_failure_falls_back_on_every_rank(tmp_path, failing_rank):
+    """If one rank cannot map its peers' memory, the copy-engine exchange is abandoned on every rank (each gets
+    None and a warning) - no rank is left waiting in a collective the others skipped."""
+    ctx = mp.get_context("spawn")
+    port = free_port()
+    out_path = os.path.join(tmp_path, "fallback.pt")
+    procs = [ctx.Process(target=sp_worker.fallback_rank, args=(r, 2, port, out_path, failing_rank)) for r in range(2)]
+    for p in procs:
+        p.start()
+    for p in procs:
+        p.join(timeout=120)
+    codes = [p.exitcode for p in procs]
+    for p in procs:
+        if p.is_alive():
+            p.kill()
+    assert codes == [0, 0], codes
+    got = torch.load(out_path)
+    assert got[:, 0].tolist() == [1, 1]        # no exchange on either rank
+    assert got[:, 1].tolist() == [1, 1]        # each rank warned once
+    # the rank whose set-up succeeded released its mappings locally; the failing rank had none
+    assert got[:, 2].tolist() == [0 if r == failing_rank else 1 for r in range(2)]
