@@ -321,8 +321,14 @@ def workload_dit(args, world, rank, stream, pk, sampler):
               "tokens_per_rank": hi - lo, "blocks": cfg.blocks, "hidden": d, "heads": cfg.heads, "mlp": d * cfg.mlp_ratio,
               "activation_scales": "per token x 128 channels", "weight_scales": "per output channel",
               "parallelism": f"sp{world} (sequence-parallel; weights replicated)",
-              "kv_exchange": {"ce": "copy-engine pushes over NVLink into CUDA-IPC-mapped peer buffers, flag-gated",
-                              "nccl": "NCCL all-gather", "none": "none (one rank)"}[sp.exchange],
+              "sp_exchange": {"tokens-ce": "token split: K/V slices pushed by the copy engines over NVLink into "
+                                           "CUDA-IPC-mapped peer buffers, flag-gated",
+                              "tokens-nccl": "token split: NCCL all-gather of K/V",
+                              "heads-ce": "head split: every rank attends for heads/N heads over all tokens; Q/K/V "
+                                          "head groups and the output rows pushed by the copy engines (strided DMA) "
+                                          "into CUDA-IPC-mapped peer buffers, flag-gated",
+                              "heads-collective": "head split: Q/K/V and output exchanged by NCCL all-to-all",
+                              "none": "none (one rank)"}[sp.split_name(cfg.heads)],
               "l2": "12 GB of weights stream through L2 between reuses of a step's input",
               "step_breakdown_ms_rank0": {"gemm": round(gemm_ms, 2), "attention": round(attn_ms, 2),
                                           "other": round(max(step_ms - gemm_ms - attn_ms, 0.0), 2)},

@@ -667,6 +667,31 @@ int hn_peer_push(void *dst, const void *src, int64_t bytes, void *flag, uint32_t
     return HN_OK;
 }
 
+int hn_peer_push2d(void *dst, int64_t dpitch, const void *src, int64_t spitch, int64_t width, int64_t height,
+                   void *flag, uint32_t value, void *stream) {
+    REQUIRE(dst && src, HN_ERR_ARG, "hn_peer_push2d: null pointer");
+    REQUIRE(width >= 0 && height >= 0 && dpitch >= width && spitch >= width, HN_ERR_SHAPE,
+            "hn_peer_push2d: need 0 <= width <= pitches and height >= 0 (width=%lld dpitch=%lld spitch=%lld "
+            "height=%lld)", (long long)width, (long long)dpitch, (long long)spitch, (long long)height);
+    static PfnWrite32 write32 = driver_fn<PfnWrite32>("cuStreamWriteValue32");
+    REQUIRE(flag == nullptr || write32 != nullptr, HN_ERR_CUDA, "hn_peer_push2d: cuStreamWriteValue32 unavailable");
+    StreamDevice sd(stream);
+    if (sd.err != cudaSuccess) return cuda_fail(sd.err, "cudaStreamGetDevice");
+    cudaStream_t st = static_cast<cudaStream_t>(stream);
+    if (width > 0 && height > 0) {
+        cudaError_t e = cudaMemcpy2DAsync(dst, (size_t)dpitch, src, (size_t)spitch, (size_t)width, (size_t)height,
+                                          cudaMemcpyDeviceToDevice, st);
+        if (e != cudaSuccess) return cuda_fail(e, "cudaMemcpy2DAsync (peer push)");
+    }
+    if (flag != nullptr) {
+        // default flags: a memory fence precedes the write, so the rows above are visible before the flag
+        CUresult r = write32(reinterpret_cast<CUstream>(st), reinterpret_cast<CUdeviceptr>(flag), value, 0);
+        if (r != CUDA_SUCCESS) return cu_fail(r, "cuStreamWriteValue32");
+    }
+    t_last_error.clear();
+    return HN_OK;
+}
+
 int hn_wait_flags(const int32_t *flags, int64_t groups, int64_t count, int64_t group_stride, int64_t skip,
                   uint32_t value, uint32_t timeout_us, void *stream) {
     REQUIRE(flags != nullptr, HN_ERR_ARG, "hn_wait_flags: null pointer");

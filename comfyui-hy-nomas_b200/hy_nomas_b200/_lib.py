@@ -54,6 +54,7 @@ SIGNATURES = {
     "hn_ipc_import": [_V, ctypes.POINTER(ctypes.c_void_p)],
     "hn_ipc_close": [_V],
     "hn_peer_push": [_V, _V, _I64, _V, _U32, _V],
+    "hn_peer_push2d": [_V, _I64, _V, _I64, _I64, _I64, _V, _U32, _V],
     "hn_wait_flags": [_V, _I64, _I64, _I64, _I64, _U32, _U32, _V],
 }
 

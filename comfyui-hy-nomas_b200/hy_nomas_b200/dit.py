@@ -229,6 +229,11 @@ def block_forward(cfg, w, x, vec, rope, sp, ops=CudaOps, trace=None, mods=None, 
         return _post(cfg, w, x, attn, qa, sa, qk, q_out, k_full, v_full, act, mods, gate1, shift2, scale2, gate2,
                      ops, trace, next_mods)
     lh = 0 if history is None else history[0].shape[0]
+    if chunks == 1 and sp.head_split(h):
+        attn, k_full, v_full, qk, q_out = _attention_heads(cfg, w, qa, sa, rope, sp, ops, b, l, lh, history, capture,
+                                                           x.dtype, trace is not None)
+        return _post(cfg, w, x, attn, qa, sa, qk, q_out, k_full, v_full, act, mods, gate1, shift2, scale2, gate2,
+                     ops, trace, next_mods)
     if sp.peer is not None:
         attn, k_full, v_full, qk, q_out = _attention_pushed(cfg, w, qa, sa, rope, sp.peer, ops, b, l, lh, history,
                                                             capture, x.dtype, trace is not None)
@@ -314,6 +319,48 @@ def _attention_pushed(cfg, w, qa, sa, rope, peer, ops, b, l, lh, history, captur
         attn = _attend(ops, q_out, k_full, v_full, keep_qk)
     qk = torch.cat([q_in.reshape(b * l, d), k_in.reshape(b * l, d)], dim=1) if keep_qk else None
     return attn, k_full, v_full, qk, q_out
+
+
+def _attention_heads(cfg, w, qa, sa, rope, sp, ops, b, l, lh, history, capture, dtype, keep_qk):
+    """Head-parallel attention: this rank attends for its head group over all tokens. K is projected, normalized
+    and sent (every peer's head group to that peer) while V is projected, V is sent while Q is projected and
+    normalized, Q is sent; after the wait for the peers' rows, attention over [history + all tokens] for the
+    group, and its output goes back to the ranks owning the tokens, into the projection's input [l, heads * D].
+    The history, the same on every rank, is dequantized for this rank's heads only. `keep_qk`: also return the
+    q|k projection (for traces); the K/V returned are this head group's."""
+    h, hd = cfg.heads, cfg.head_dim
+    d = h * hd
+    ex = sp.head_exchange()
+    hpg = h // sp.world
+    mine = slice(sp.rank * hpg, (sp.rank + 1) * hpg)
+    bufs = ex.begin(l, h, hd, dtype, qa.device, prefix=lh)
+    q_all, k_all, v_all, o_mine = bufs
+    if history is not None:
+        hk_q, hk_s, hv_q, hv_s = history
+        ops.dequantize_kv(hk_q[:, mine], hk_s[:, mine], out=k_all[0, :lh])
+        ops.dequantize_kv(hv_q[:, mine], hv_s[:, mine], out=v_all[0, :lh])
+    k_in = ops.gemm(qa, sa, _rows(w.qk, d, 2 * d)).view(b, l, h, hd)
+    k_mine = torch.empty((b, l, h, hd), dtype=dtype, device=qa.device)
+    if capture is not None:
+        kq, ks = ops.qk_norm_rope_kv(k_in, w.k_norm, rope, out=k_mine)
+    else:
+        ops.qk_norm_rope(k_in, w.k_norm, rope, out=k_mine)
+    ex.send("k", k_mine, bufs)
+    v_mine = ops.gemm(qa, sa, w.v).view(b, l, h, hd)
+    ex.send("v", v_mine, bufs)
+    q_in = ops.gemm(qa, sa, _rows(w.qk, 0, d)).view(b, l, h, hd)
+    q_out = torch.empty((b, l, h, hd), dtype=dtype, device=qa.device)
+    ops.qk_norm_rope(q_in, w.q_norm, rope, out=q_out)
+    ex.send("q", q_out, bufs)
+    if capture is not None:
+        vq, vs = ops.quantize_kv(v_mine.reshape(b * l, h, hd))
+        capture.append((kq.reshape(b * l, h, hd), ks.reshape(b * l, h, 1), vq, vs))
+    ex.wait("kvq")
+    out = ops.attention(q_all, k_all, v_all).contiguous()              # [1, L, hpg, D]
+    ex.send_output(out, bufs)
+    ex.wait("o")
+    qk = torch.cat([q_in.reshape(b * l, d), k_in.reshape(b * l, d)], dim=1) if keep_qk else None
+    return (o_mine.reshape(b * l, d), None), k_all, v_all, qk, q_out
 
 
 def _attend_pieces(ops, q, k_full, v_full, lh, l, peer, keep):

@@ -306,6 +306,8 @@ int hn_attn_merge(const void *const *parts, const float *const *lses, int64_t n,
  * hn_peer_push: on `stream`, copy `bytes` from src (this device) to dst (a mapped peer address) by DMA, then write
  *   the 32-bit `value` to `flag` (a mapped peer address, or NULL for none) after a memory fence, so the data is
  *   visible before the flag.
+ * hn_peer_push2d: hn_peer_push for `height` rows of `width` bytes, row r read at src + r * spitch and written at
+ *   dst + r * dpitch (one strided DMA): the head-parallel exchange moves one head group of every token this way.
  * hn_wait_flags: on `stream`, one warp waits until every flags[g * group_stride + i] (g < groups, i < count,
  *   i != skip; groups * count <= 1024) has reached `value` (wrap-safe: (int32_t)(flag - value) >= 0), with system-scope
  *   acquire loads, so that kernels after it on the stream see the data pushed before those flags. Bounded: after
@@ -315,6 +317,8 @@ int hn_ipc_export(const void *ptr, void *handle_host, int64_t *offset_host);
 int hn_ipc_import(const void *handle_host, void **base_host);
 int hn_ipc_close(void *base);
 int hn_peer_push(void *dst, const void *src, int64_t bytes, void *flag, uint32_t value, void *stream);
+int hn_peer_push2d(void *dst, int64_t dpitch, const void *src, int64_t spitch, int64_t width, int64_t height,
+                   void *flag, uint32_t value, void *stream);
 int hn_wait_flags(const int32_t *flags, int64_t groups, int64_t count, int64_t group_stride, int64_t skip,
                   uint32_t value, uint32_t timeout_us, void *stream);
 

@@ -4,10 +4,10 @@ import os
 import torch
 
 
-def small_config():
+def small_config(heads=2):
     from hy_nomas_b200.dit import DiTConfig
-    # 2 heads x 128, hidden 256, 2 blocks, a 2 x 3 x 4 grid = 24 tokens (splits over 1, 2, 4 ranks)
-    return DiTConfig(hidden=256, heads=2, mlp_ratio=4, blocks=2, grid=(2, 3, 4))
+    # `heads` x 128 (hidden 256 by default), 2 blocks, a 2 x 3 x 4 grid = 24 tokens (splits over 1, 2, 4 ranks)
+    return DiTConfig(hidden=128 * heads, heads=heads, mlp_ratio=4, blocks=2, grid=(2, 3, 4))
 
 
 def inputs(cfg, device="cpu"):
@@ -41,7 +41,7 @@ def run_model(cfg, sp, ops, device, history_tokens=0):
     return model(x[:, lo:hi].contiguous(), vec, history=hist)
 
 
-def gloo_rank(rank, world, port, out_path, head_chunks=1, history_tokens=0):
+def gloo_rank(rank, world, port, out_path, head_chunks=1, history_tokens=0, split="tokens", heads=2):
     import torch.distributed as dist
     from dit_oracle_ops import OracleOps
     from hy_nomas_b200.sequence_parallel import SequenceParallel
@@ -49,8 +49,11 @@ def gloo_rank(rank, world, port, out_path, head_chunks=1, history_tokens=0):
     os.environ["MASTER_PORT"] = str(port)
     dist.init_process_group("gloo", rank=rank, world_size=world)
     try:
-        cfg = small_config()
-        out = run_model(cfg, SequenceParallel(head_chunks=head_chunks), OracleOps, "cpu", history_tokens)
+        cfg = small_config(heads)
+        sp = SequenceParallel(head_chunks=head_chunks, split=split)
+        if sp.split_name(cfg.heads) != ("heads-collective" if split == "heads" else "tokens-nccl"):
+            raise AssertionError(f"unexpected attention split {sp.split_name(cfg.heads)}")
+        out = run_model(cfg, sp, OracleOps, "cpu", history_tokens)
         parts = [torch.empty_like(out) for _ in range(world)]
         dist.all_gather(parts, out)
         if rank == 0:
@@ -59,7 +62,8 @@ def gloo_rank(rank, world, port, out_path, head_chunks=1, history_tokens=0):
         dist.destroy_process_group()
 
 
-def nccl_rank(rank, world, port, out_path, head_chunks=1, exchange="ce", history_tokens=0, pieces=True):
+def nccl_rank(rank, world, port, out_path, head_chunks=1, exchange="ce", history_tokens=0, pieces=True,
+              split="tokens", heads=2):
     """One rank of a sequence-parallel run on GPU `rank`: two steps (the second reuses the double-buffered K/V
     exchange buffers) and, with `history_tokens`, a third step over an int8 K/V history. Rank 0 saves every
     step's gathered output, the exchange used and the ranks' device error words."""
@@ -77,9 +81,9 @@ def nccl_rank(rank, world, port, out_path, head_chunks=1, exchange="ce", history
         from hy_nomas_b200 import _lib
         from hy_nomas_b200.dit import CudaOps, SyntheticDiT
         from hy_nomas_b200.sequence_parallel import SequenceParallel
-        cfg = small_config()
+        cfg = small_config(heads)
         device = f"cuda:{rank}"
-        sp = SequenceParallel(head_chunks=head_chunks)
+        sp = SequenceParallel(head_chunks=head_chunks, split=split)
         model = SyntheticDiT(cfg, device=device, seed=3, sp=sp, ops=CudaOps)
         x, vec = inputs(cfg, device)
         lo, hi = model.token_range
@@ -97,7 +101,7 @@ def nccl_rank(rank, world, port, out_path, head_chunks=1, exchange="ce", history
             dist.all_gather(parts, out)
             gathered.append(torch.cat(parts, dim=1).cpu())
         torch.cuda.synchronize()
-        kind = sp.exchange
+        kind = sp.split_name(cfg.heads) if split == "heads" else sp.exchange
         sp.close()
         if rank == 0:
             torch.save({"outs": gathered, "exchange": kind, "errors": [int(e.item()) for e in errs]}, out_path)

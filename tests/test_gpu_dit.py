@@ -131,12 +131,12 @@ def free_port():
         return s.getsockname()[1]
 
 
-def run_two_ranks(tmp_path, head_chunks=1, exchange="ce", history_tokens=0, pieces=True):
+def run_two_ranks(tmp_path, head_chunks=1, exchange="ce", history_tokens=0, pieces=True, split="tokens"):
     ctx = mp.get_context("spawn")
     port = free_port()
-    out_path = os.path.join(tmp_path, f"sp_{exchange}_{head_chunks}_{history_tokens}_{int(pieces)}.pt")
+    out_path = os.path.join(tmp_path, f"sp_{exchange}_{head_chunks}_{history_tokens}_{int(pieces)}_{split}.pt")
     procs = [ctx.Process(target=sp_worker.nccl_rank, args=(r, 2, port, out_path, head_chunks, exchange,
-                                                           history_tokens, pieces)) for r in range(2)]
+                                                           history_tokens, pieces, split)) for r in range(2)]
     for p in procs:
         p.start()
     for p in procs:
@@ -183,6 +183,31 @@ def test_copy_engine_exchange_matches_nccl(hn, cuda, tmp_path):
         assert torch.equal(a.view(torch.int16), b.view(torch.int16))
         assert rel_l2(c.float().numpy(), b.float().numpy()) < 1e-2
     assert not torch.equal(whole["outs"][0], whole["outs"][2])      # the history changed the output
+
+
+def test_head_split_two_gpus(hn, cuda, tmp_path):
+    """Head-parallel attention on 2 GPUs: each rank attends for one head over all tokens, Q/K/V and the output
+    exchanged by strided copy-engine pushes or by NCCL all-to-all; two steps, then one over a 30-token int8
+    history. Both exchanges move the same rows into the same buffers, so their outputs are bit-identical; against
+    the same model on one GPU (both heads in one attention call) within the bf16 attention tolerance."""
+    if torch.cuda.device_count() < 2:
+        pytest.skip("needs 2 GPUs")
+    from hy_nomas_b200.dit import CudaOps
+    from hy_nomas_b200.sequence_parallel import SequenceParallel
+    cfg = sp_worker.small_config()
+    single = sp_worker.run_model(cfg, SequenceParallel(), CudaOps, "cuda:0").cpu()
+    single_h = sp_worker.run_model(cfg, SequenceParallel(), CudaOps, "cuda:0", history_tokens=30).cpu()
+    ce = run_two_ranks(tmp_path, 1, "ce", history_tokens=30, pieces=False, split="heads")
+    nc = run_two_ranks(tmp_path, 1, "nccl", history_tokens=30, pieces=False, split="heads")
+    assert ce["exchange"] == "heads-ce" and nc["exchange"] == "heads-collective"
+    assert ce["errors"] == [0, 0] and nc["errors"] == [0, 0]
+    for a, b in zip(ce["outs"], nc["outs"]):
+        assert torch.equal(a.view(torch.int16), b.view(torch.int16))
+    first, second, hist = ce["outs"]
+    assert torch.equal(first.view(torch.int16), second.view(torch.int16))
+    assert rel_l2(first.float().numpy(), single.float().numpy()) < 1e-2
+    assert rel_l2(hist.float().numpy(), single_h.float().numpy()) < 1e-2
+    assert not torch.equal(first, hist)
 
 
 @pytest.fixture(scope="module")

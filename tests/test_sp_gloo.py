@@ -64,6 +64,78 @@ def test_gloo_matches_single_rank(single_rank, tmp_path, world, head_chunks):
     assert torch.equal(got.view(torch.int16), single_rank.view(torch.int16))
 
 
+def _run_gloo(tmp_path, world, **kw):
+    ctx = mp.get_context("spawn")
+    port = free_port()
+    out_path = os.path.join(tmp_path, "out.pt")
+    args = dict(head_chunks=1, history_tokens=0, split="tokens", heads=2)
+    args.update(kw)
+    procs = [ctx.Process(target=sp_worker.gloo_rank, args=(r, world, port, out_path, args["head_chunks"],
+                                                           args["history_tokens"], args["split"], args["heads"]))
+             for r in range(world)]
+    for p in procs:
+        p.start()
+    for p in procs:
+        p.join(timeout=240)
+    codes = [p.exitcode for p in procs]
+    for p in procs:
+        if p.is_alive():
+            p.kill()
+    assert codes == [0] * world, codes
+    return torch.load(out_path)
+
+
+@pytest.mark.parametrize("world,heads,history_tokens", [(2, 2, 0), (4, 4, 0), (2, 2, 12), (4, 4, 12)])
+def test_gloo_head_split_matches_single_rank(hn, oracle, tmp_path, world, heads, history_tokens):
+    """Head-parallel attention (every rank attends for heads / world heads over all tokens; Q, K, V and the output
+    exchanged by all-to-all), with and without an int8 history, equals the single-rank model bit for bit."""
+    from hy_nomas_b200.sequence_parallel import SequenceParallel
+    single = sp_worker.run_model(sp_worker.small_config(heads), SequenceParallel(), OracleOps, "cpu",
+                                 history_tokens=history_tokens)
+    got = _run_gloo(tmp_path, world, split="heads", heads=heads, history_tokens=history_tokens)
+    assert got.shape == single.shape
+    assert torch.equal(got.view(torch.int16), single.view(torch.int16))
+
+
+def test_head_split_selection():
+    """"auto" takes the head split from HEADS_MIN_WORLD ranks on; never when the heads do not divide over the
+    ranks, or with head chunks."""
+    from hy_nomas_b200 import sequence_parallel as S
+    sp = S.SequenceParallel(split="auto")
+    assert not sp.head_split(32)                  # one rank
+    for world in (2, 4, 8):
+        sp.world = world
+        assert sp.head_split(32) == (world >= S.HEADS_MIN_WORLD)
+    sp.world = 8
+    assert not sp.head_split(12)                  # 12 heads do not split over 8 ranks
+    sp.split = "tokens"
+    assert not sp.head_split(32)
+    sp.split, sp.world = "heads", 2
+    assert sp.head_split(32)
+    sp.head_chunks = 2
+    assert not sp.head_split(32)
+    with pytest.raises(ValueError):
+        S.SequenceParallel(split="rows")
+
+
+def test_head_layout_offsets():
+    """The head-parallel buffers: per set K, V (history + all tokens), Q (all tokens) and the output (own tokens,
+    all heads), each starting on a 256-byte boundary for bf16, in that order and without overlap."""
+    from hy_nomas_b200.sequence_parallel import _HeadLayout
+    lay = _HeadLayout(world=8, local=2530, heads=32, head_dim=128, prefix=15840)
+    assert lay.hpg == 4 and lay.tokens == 20240
+    ends = 0
+    for kind in ("k", "v", "q", "o"):
+        assert lay.offs[kind] == ends and (lay.offs[kind] * 2) % 256 == 0
+        ends += lay.sizes[kind]
+    assert ends == lay.numel
+    flat = torch.arange(lay.numel, dtype=torch.float32)
+    q, k, v, o = lay.views(flat)
+    assert q.shape == (1, 20240, 4, 128) and k.shape == v.shape == (1, 15840 + 20240, 4, 128)
+    assert o.shape == (1, 2530, 32, 128)
+    assert lay.row0("k", 3) == 15840 + 3 * 2530 and lay.row0("q", 3) == 3 * 2530
+
+
 def test_gloo_with_history_matches_single_rank(hn, oracle, tmp_path):
     """With a replicated int8 K/V history (every block's attention runs over the dequantized history followed by
     the gathered current tokens), 2 gloo ranks equal the single-rank model bit for bit."""
