@@ -97,6 +97,10 @@ def test_validation_errors_before_launch(hn):
     assert L.hn_qk_norm_rope(FAKE, 4096, FAKE, None, None, 1, 4, 32, 64, 1e-6, FAKE, None) == 7   # D != 128
     assert L.hn_gated_residual(FAKE, FAKE, FAKE, 1, 4, 12, FAKE, None) == 1                     # D % 8
     assert L.hn_selftest_wait_timeout(0, None) in (3, 4, 5)        # no device here, or bad timeout
+    # the strided push: null pointers and a row wider than a pitch are refused before anything is queued
+    assert L.hn_peer_push2d(None, 1024, FAKE, 4096, 1024, 10, None, 0, None) == 5
+    assert L.hn_peer_push2d(FAKE, 1024, FAKE, 512, 1024, 10, None, 0, None) == 1
+    assert b"hn_peer_push2d" in L.hn_last_error()
 
 
 def test_no_cpu_path(hn):

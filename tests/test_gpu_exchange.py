@@ -37,6 +37,33 @@ def test_push_then_wait_sees_data(hn, cuda):
     assert torch.isfinite(out)
 
 
+def test_strided_push_moves_one_head_group(hn, cuda):
+    """hn_peer_push2d as the head-parallel exchange uses it: head group 2 (4 heads of 128) of every token of a
+    [tokens, 16 heads, 128] tensor into a contiguous [tokens, 4, 128] buffer, and back into the head columns of a
+    [tokens, 16, 128] buffer; then the flag."""
+    L = hn.lib
+    st = torch.cuda.current_stream()
+    tok, heads, hpg, g = 1000, 16, 4, 2
+    src = torch.randn(tok, heads, 128, device=cuda).bfloat16()
+    grp = torch.zeros(tok, hpg, 128, dtype=torch.bfloat16, device=cuda)
+    back = torch.zeros_like(src)
+    flag = torch.zeros(1, dtype=torch.int32, device=cuda)
+    width, row = hpg * 128 * 2, heads * 128 * 2
+    L.check(L.lib.hn_peer_push2d(vp(grp.data_ptr()), width, vp(src.data_ptr() + g * width), row, width, tok, None, 0,
+                                 vp(st.cuda_stream)), "hn_peer_push2d", launches=0)
+    L.check(L.lib.hn_peer_push2d(vp(back.data_ptr() + g * width), row, vp(grp.data_ptr()), width, width, tok,
+                                 vp(flag.data_ptr()), 3, vp(st.cuda_stream)), "hn_peer_push2d", launches=0)
+    torch.cuda.synchronize()
+    assert torch.equal(grp, src[:, g * hpg:(g + 1) * hpg])
+    assert torch.equal(back[:, g * hpg:(g + 1) * hpg], src[:, g * hpg:(g + 1) * hpg])
+    assert int(back[:, :g * hpg].abs().sum()) == 0 and int(back[:, (g + 1) * hpg:].abs().sum()) == 0
+    assert flag.item() == 3
+    # a width beyond a pitch is refused before anything is queued
+    rc = L.lib.hn_peer_push2d(vp(grp.data_ptr()), width, vp(src.data_ptr()), width - 16, width, tok, None, 0,
+                              vp(st.cuda_stream))
+    assert rc == 1 and "hn_peer_push2d" in L.last_error()
+
+
 def test_wait_compares_wrap_safe(hn, cuda):
     """Counters compare by signed difference: 0x00000002 is 'after' 0xFFFFFFFE."""
     L = hn.lib
