@@ -50,6 +50,9 @@ PUSH_STREAMS = 1
 # HEADS_MIN_WORLD ranks on, where it moves less data (at 2 ranks both exchanges move the same bytes)
 SPLIT = "auto"
 HEADS_MIN_WORLD = 4
+# copy streams per kind of the head exchange, the peers spread over them (HN_SP_HEAD_PUSH_STREAMS overrides; capped
+# at world - 1): its per-peer copies are small (2.6 MB at 8 ranks) and latency-bound, so they go side by side
+HEAD_PUSH_STREAMS = 7
 
 
 class SequenceParallel:
@@ -417,8 +420,9 @@ class HeadExchange(_IpcExchange):
     tensors, kept from reuse until the copy streams have read them (`record_stream`)."""
 
     def __init__(self, sp):
+        nstreams = max(1, min(sp.world - 1, int(os.environ.get("HN_SP_HEAD_PUSH_STREAMS", str(HEAD_PUSH_STREAMS)))))
         self._setup(sp, len(HEAD_KINDS) * sp.world)
-        self.side = {k: torch.cuda.Stream(self.device) for k in HEAD_KINDS}
+        self.side = {k: [torch.cuda.Stream(self.device) for _ in range(nstreams)] for k in HEAD_KINDS}
 
     def _buffers(self, local, heads, head_dim, dtype, prefix):
         key = (local, heads, head_dim, dtype, prefix)
@@ -440,25 +444,27 @@ class HeadExchange(_IpcExchange):
         return lay.views(ent["mem"][par * lay.numel:(par + 1) * lay.numel])
 
     def _push_rows(self, kind, src, rows_of, dst_of, width, spitch, dpitch, height, own):
-        """On `kind`'s copy stream, after the current stream's work so far: for every peer (staggered from rank + 1)
-        a strided DMA of `height` rows (src + rows_of(peer) -> the peer's buffer at dst_of bytes) and its flag;
-        then `own()` on the current stream."""
+        """On `kind`'s copy streams, after the current stream's work so far: for every peer (staggered from rank + 1,
+        spread over the streams) a strided DMA of `height` rows (src + rows_of(peer) -> the peer's buffer at dst_of
+        bytes) followed by its flag; then `own()` on the current stream."""
         lib = self._lib
         ent, _ = self._cur
         cur = torch.cuda.current_stream(self.device)
-        side = self.side[kind]
+        sides = self.side[kind]
         ready = torch.cuda.Event()
         ready.record(cur)
-        side.wait_event(ready)
+        for side in sides:
+            side.wait_event(ready)
         k = HEAD_KINDS.index(kind)
-        st = ctypes.c_void_p(side.cuda_stream)
         for step in range(1, self.world):
             peer = (self.rank + step) % self.world
+            st = ctypes.c_void_p(sides[(step - 1) % len(sides)].cuda_stream)
             flag = ctypes.c_void_p(self.peer_flags[peer] + 4 * (k * self.world + self.rank))
             lib.check(lib.lib.hn_peer_push2d(ctypes.c_void_p(ent["addrs"][peer] + dst_of), dpitch,
                                              ctypes.c_void_p(src.data_ptr() + rows_of(peer)), spitch, width, height,
                                              flag, self.epoch, st), "hn_peer_push2d", launches=0)
-        src.record_stream(side)
+        for side in sides:
+            src.record_stream(side)
         own()
 
     def send(self, kind, src, bufs):
