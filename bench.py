@@ -285,6 +285,20 @@ def workload_dit(args, world, rank, stream, pk, sampler):
     def attn_wrap(q, k, v):
         return attn_t.wrap(lambda: orig_attn(q, k, v), 4.0 * q.shape[0] * q.shape[1] * k.shape[1] * q.shape[2] * q.shape[3])
 
+    # the exchange waits (flag waits of the copy-engine exchanges, NCCL handle waits): how long the stream sat
+    # waiting for the peers' data in the instrumented step
+    from hy_nomas_b200 import sequence_parallel as sp_mod
+    wait_t = KernelTimer(stream)
+    wait_t.active = world > 1
+    restore = []
+    for cls in (sp_mod.PeerExchange, sp_mod.HeadExchange, sp_mod.HeadCollective):
+        def timed_wait(self, *a, _orig=cls.wait, **kw):
+            return wait_t.wrap(lambda: _orig(self, *a, **kw))
+        restore.append((cls, "wait", cls.__dict__["wait"]))
+        cls.wait = timed_wait
+    orig_gather_wait = sp_mod.SequenceParallel.wait
+    restore.append((sp_mod.SequenceParallel, "wait", sp_mod.SequenceParallel.__dict__["wait"]))
+    sp_mod.SequenceParallel.wait = staticmethod(lambda *h: wait_t.wrap(lambda: orig_gather_wait(*h)))
     kernels.block_gemm, CudaOps.attention = gemm_wrap, staticmethod(attn_wrap)
     try:
         barrier(world)
@@ -292,7 +306,11 @@ def workload_dit(args, world, rank, stream, pk, sampler):
         torch.cuda.synchronize()
     finally:
         kernels.block_gemm, CudaOps.attention = orig_gemm, staticmethod(orig_attn)
+        for cls, name, orig in restore:
+            setattr(cls, name, orig)
     gemm_ms, attn_ms = gemm_t.total_ms(), attn_t.total_ms()
+    wait_ms = wait_t.total_ms()
+    wait_max = max_over_ranks(wait_ms, world)
     gemm_ops, attn_flops = gemm_t.work(), attn_t.work()
 
     # e2e through the public API: this rank's tokens and vec from pinned host memory, the output read back
@@ -331,7 +349,13 @@ def workload_dit(args, world, rank, stream, pk, sampler):
                               "none": "none (one rank)"}[sp.split_name(cfg.heads)],
               "l2": "12 GB of weights stream through L2 between reuses of a step's input",
               "step_breakdown_ms_rank0": {"gemm": round(gemm_ms, 2), "attention": round(attn_ms, 2),
-                                          "other": round(max(step_ms - gemm_ms - attn_ms, 0.0), 2)},
+                                          "other": round(max(step_ms - gemm_ms - attn_ms, 0.0), 2),
+                                          "of_other_exchange_wait": round(wait_ms, 2)},
+              "exchange_wait_ms_per_step": {"rank0": round(wait_ms, 2), "max_over_ranks": round(wait_max, 2),
+                                            "waits": len(wait_t.pairs),
+                                            "what": "CUDA events around each wait for the peers' data (flag wait "
+                                                    "or NCCL handle) in one instrumented step: exposed exchange "
+                                                    "plus the wait for slower ranks"},
               "attention_tflops": round(attn_flops / (attn_ms * 1e-3) / 1e12, 1) if attn_ms else None,
               "floor_ms_rank0": {"gemm_at_int8_peak": round(gemm_ops / (int8_peak * 1e12) * 1e3, 2),
                                  "attention_at_bf16_peak": round(attn_flops / (pk["bf16_tflops_sustained"] * 1e12) * 1e3, 2)},
