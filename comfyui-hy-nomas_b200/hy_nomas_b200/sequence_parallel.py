@@ -405,6 +405,20 @@ class _HeadLayout:
         """First row of `rank`'s tokens in a K, V or Q buffer."""
         return (self.prefix if kind in ("k", "v") else 0) + rank * self.local
 
+    def push_plan(self, kind, rank, peer, par, esz):
+        """The strided copy of `kind` from `rank` to `peer`'s set of parity `par`: (source byte offset, source
+        pitch, destination byte offset in the peer's allocation, destination pitch, row bytes, rows). The source
+        is rank's [local, heads, head_dim] tensor for K, V and Q (peer's head group of every own token), its
+        [L, hpg, head_dim] output for O (peer's token rows)."""
+        hd, hpg = self.head_dim, self.hpg
+        width = hpg * hd * esz
+        base = par * self.numel + self.offs[kind]
+        if kind == "o":
+            return (peer * self.local * width, width, (base + rank * hpg * hd) * esz, self.heads * hd * esz, width,
+                    self.local)
+        return (peer * width, self.heads * hd * esz, (base + self.row0(kind, rank) * hpg * hd) * esz, width, width,
+                self.local)
+
 
 class HeadExchange(_IpcExchange):
     """The copy-engine exchange of head-parallel attention.
@@ -443,12 +457,12 @@ class HeadExchange(_IpcExchange):
         self._cur = (ent, par)
         return lay.views(ent["mem"][par * lay.numel:(par + 1) * lay.numel])
 
-    def _push_rows(self, kind, src, rows_of, dst_of, width, spitch, dpitch, height, own):
+    def _push_rows(self, kind, src, own):
         """On `kind`'s copy streams, after the current stream's work so far: for every peer (staggered from rank + 1,
-        spread over the streams) a strided DMA of `height` rows (src + rows_of(peer) -> the peer's buffer at dst_of
-        bytes) followed by its flag; then `own()` on the current stream."""
+        spread over the streams) the strided DMA of `_HeadLayout.push_plan` followed by its flag; then `own()` on
+        the current stream."""
         lib = self._lib
-        ent, _ = self._cur
+        ent, par = self._cur
         cur = torch.cuda.current_stream(self.device)
         sides = self.side[kind]
         ready = torch.cuda.Event()
@@ -460,8 +474,9 @@ class HeadExchange(_IpcExchange):
             peer = (self.rank + step) % self.world
             st = ctypes.c_void_p(sides[(step - 1) % len(sides)].cuda_stream)
             flag = ctypes.c_void_p(self.peer_flags[peer] + 4 * (k * self.world + self.rank))
-            lib.check(lib.lib.hn_peer_push2d(ctypes.c_void_p(ent["addrs"][peer] + dst_of), dpitch,
-                                             ctypes.c_void_p(src.data_ptr() + rows_of(peer)), spitch, width, height,
+            soff, spitch, doff, dpitch, width, height = ent["lay"].push_plan(kind, self.rank, peer, par, ent["esz"])
+            lib.check(lib.lib.hn_peer_push2d(ctypes.c_void_p(ent["addrs"][peer] + doff), dpitch,
+                                             ctypes.c_void_p(src.data_ptr() + soff), spitch, width, height,
                                              flag, self.epoch, st), "hn_peer_push2d", launches=0)
         for side in sides:
             src.record_stream(side)
@@ -470,41 +485,36 @@ class HeadExchange(_IpcExchange):
     def send(self, kind, src, bufs):
         """Send this rank's K, V or Q ([1, local, heads, head_dim], contiguous, complete on the current stream):
         every peer's head group to that peer; `bufs` = this block's (q, k, v, o) from `begin`."""
-        ent, par = self._cur
+        ent = self._cur[0]
         lay, esz = ent["lay"], ent["esz"]
         hd, hpg = lay.head_dim, lay.hpg
         if (not src.is_contiguous() or tuple(src.shape) != (1, lay.local, lay.heads, hd)
                 or src.element_size() != esz or src.device != self.device):
             raise ValueError(f"send: need a contiguous [1, {lay.local}, {lay.heads}, {hd}] tensor on {self.device}")
-        width = hpg * hd * esz
         r0 = lay.row0(kind, self.rank)
-        dst_of = (par * lay.numel + lay.offs[kind] + r0 * hpg * hd) * esz
         mine = bufs["qkv".index(kind)]
 
         def own():
             mine[0, r0:r0 + lay.local].copy_(src[0, :, self.rank * hpg:(self.rank + 1) * hpg])
 
-        self._push_rows(kind, src, lambda p: p * width, dst_of, width, lay.heads * hd * esz, width, lay.local, own)
+        self._push_rows(kind, src, own)
 
     def send_output(self, out, bufs):
         """Return this rank's head group's attention output ([1, L, hpg, head_dim], contiguous) to the ranks that own
         its tokens, into their output buffers."""
-        ent, par = self._cur
+        ent = self._cur[0]
         lay, esz = ent["lay"], ent["esz"]
         hd, hpg = lay.head_dim, lay.hpg
         if (not out.is_contiguous() or tuple(out.shape) != (1, lay.tokens, hpg, hd) or out.element_size() != esz
                 or out.device != self.device):
             raise ValueError(f"send_output: need a contiguous [1, {lay.tokens}, {hpg}, {hd}] tensor on {self.device}")
-        width = hpg * hd * esz
-        dst_of = (par * lay.numel + lay.offs["o"] + self.rank * hpg * hd) * esz
         o_mine = bufs[3]
         lo = self.rank * lay.local
 
         def own():
             o_mine[0, :, self.rank * hpg:(self.rank + 1) * hpg].copy_(out[0, lo:lo + lay.local])
 
-        self._push_rows("o", out, lambda p: p * lay.local * width, dst_of, width, width, lay.heads * hd * esz,
-                        lay.local, own)
+        self._push_rows("o", out, own)
 
     def wait(self, kinds):
         """The current stream waits (bounded) until every peer's rows of `kinds` ("kvq" or "o") of this block are

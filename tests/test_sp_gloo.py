@@ -136,6 +136,37 @@ def test_head_layout_offsets():
     assert lay.row0("k", 3) == 15840 + 3 * 2530 and lay.row0("q", 3) == 3 * 2530
 
 
+@pytest.mark.parametrize("world,prefix", [(2, 0), (4, 7), (8, 0), (8, 15)])
+def test_head_push_plan_tiles_every_buffer(world, prefix):
+    """The head exchange's strided copies, checked byte by byte on the host before any of them runs on a GPU:
+    each reads inside its source tensor, writes inside the peer's set of its parity, and on every destination
+    rank the copies of all ranks (the rank's own one included, which it makes locally) cover each buffer's token
+    part exactly once, leaving the history prefix and the other parity untouched."""
+    import numpy as np
+    from hy_nomas_b200.sequence_parallel import HEAD_KINDS, _HeadLayout
+    local, heads, hd, esz = 3, 2 * world, 4, 2
+    lay = _HeadLayout(world, local, heads, hd, prefix)
+    src_bytes = {"k": local * heads * hd * esz, "o": lay.tokens * lay.hpg * hd * esz}
+    for par in (0, 1):
+        for dst in range(world):
+            cover = np.zeros(2 * lay.numel * esz, dtype=np.int32)
+            for kind in HEAD_KINDS:
+                for r in range(world):
+                    soff, spitch, doff, dpitch, width, height = lay.push_plan(kind, r, dst, par, esz)
+                    assert width <= spitch and width <= dpitch
+                    assert soff + (height - 1) * spitch + width <= src_bytes["o" if kind == "o" else "k"]
+                    for row in range(height):
+                        cover[doff + row * dpitch:doff + row * dpitch + width] += 1
+            sets = cover.reshape(2, lay.numel * esz)
+            assert (sets[1 - par] == 0).all()
+            mine = sets[par]
+            for kind in HEAD_KINDS:
+                lo, n = lay.offs[kind] * esz, lay.sizes[kind] * esz
+                skip = prefix * lay.hpg * hd * esz if kind in ("k", "v") else 0
+                assert (mine[lo:lo + skip] == 0).all()              # the history prefix is the rank's own
+                assert (mine[lo + skip:lo + n] == 1).all()
+
+
 def test_gloo_with_history_matches_single_rank(hn, oracle, tmp_path):
     """With a replicated int8 K/V history (every block's attention runs over the dequantized history followed by
     the gathered current tokens), 2 gloo ranks equal the single-rank model bit for bit."""
