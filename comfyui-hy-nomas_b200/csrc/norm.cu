@@ -84,13 +84,23 @@ __device__ __forceinline__ void store_words16(bf16 *p, const uint32_t *w) {
     reinterpret_cast<uint4 *>(p)[1] = make_uint4(w[4], w[5], w[6], w[7]);
 }
 
+// MODE 2 with up to 8 warps keeps the batch item's shift and gate in shared memory (each thread reads back only
+// its own 16 values), so that three CTAs fit an SM instead of two.
+template <int WP, int MODE> struct LnCfg {
+    static constexpr bool MOD_SMEM = MODE == 2 && WP <= 8;
+    static constexpr int MIN_CTAS = WP <= 8 ? 3 : 1;
+};
+
 template <int WP, int MODE>
-__global__ void __launch_bounds__(WP * 32, (WP <= 8) ? (MODE == 2 ? 2 : 3) : 1) k_ln_rows(const bf16 *__restrict__ x, const bf16 *__restrict__ yres,
+__global__ void __launch_bounds__(WP * 32, (LnCfg<WP, MODE>::MIN_CTAS)) k_ln_rows(const bf16 *__restrict__ x, const bf16 *__restrict__ yres,
                                                     const bf16 *__restrict__ gate, const bf16 *__restrict__ shift,
                                                     const bf16 *__restrict__ scale, int64_t rows, int64_t L, int D,
                                                     float eps, bf16 *__restrict__ out, int8_t *__restrict__ q,
                                                     float *__restrict__ s, int64_t s_rs, int64_t s_gs) {
+    constexpr bool MOD_SMEM = LnCfg<WP, MODE>::MOD_SMEM;
     __shared__ float red1[WP], red2[WP];
+    // [shift, gate][P0..3, Q0..3][thread] (MOD_SMEM)
+    __shared__ uint64_t mod_s[MOD_SMEM ? 2 : 1][8][MOD_SMEM ? WP * 32 : 1];
     const int t = threadIdx.x, lane = t & 31, warp = t >> 5;
     const bool active = t < (D >> 4);
     const float fd = (float)D;
@@ -134,6 +144,15 @@ __global__ void __launch_bounds__(WP * 32, (WP <= 8) ? (MODE == 2 ? 2 : 3) : 1) 
                 if (active) load_words16(gate + b * (int64_t)D + 16 * t, w);
                 G = row_from_words(w);
             }
+            if (MOD_SMEM) {
+#pragma unroll
+                for (int k = 0; k < 4; ++k) {
+                    mod_s[0][k][t] = SH.P[k];
+                    mod_s[0][4 + k][t] = SH.Q[k];
+                    mod_s[1][k][t] = G.P[k];
+                    mod_s[1][4 + k][t] = G.Q[k];
+                }
+            }
         }
         const int64_t off = row * (int64_t)D + 16 * t;
         // this row's words; start the next row's loads
@@ -151,7 +170,10 @@ __global__ void __launch_bounds__(WP * 32, (WP <= 8) ? (MODE == 2 ? 2 : 3) : 1) 
             const Row16 Y = row_from_words(cy);
             Row16 YG;
 #pragma unroll
-            for (int k = 0; k < 4; ++k) { YG.P[k] = x2_mul(Y.P[k], G.P[k]); YG.Q[k] = x2_mul(Y.Q[k], G.Q[k]); }
+            for (int k = 0; k < 4; ++k) {
+                YG.P[k] = x2_mul(Y.P[k], MOD_SMEM ? mod_s[1][k][t] : G.P[k]);
+                YG.Q[k] = x2_mul(Y.Q[k], MOD_SMEM ? mod_s[1][4 + k][t] : G.Q[k]);
+            }
             uint32_t w[8];
             words_from_row(YG, w);
             YG = row_from_words(w);
@@ -188,10 +210,10 @@ __global__ void __launch_bounds__(WP * 32, (WP <= 8) ? (MODE == 2 ? 2 : 3) : 1) 
         for (int k = 0; k < 4; ++k) {
             float a0, a1, h0, h1;
             x2_split(x2_mul(x2_mul(C.P[k], rstd), R.P[k]), a0, a1);
-            x2_split(SH.P[k], h0, h1);
+            x2_split(MOD_SMEM ? mod_s[0][k][t] : SH.P[k], h0, h1);
             Z.P[k] = x2(__fadd_rn(a0, h0), __fadd_rn(a1, h1));
             x2_split(x2_mul(x2_mul(C.Q[k], rstd), R.Q[k]), a0, a1);
-            x2_split(SH.Q[k], h0, h1);
+            x2_split(MOD_SMEM ? mod_s[0][4 + k][t] : SH.Q[k], h0, h1);
             Z.Q[k] = x2(__fadd_rn(a0, h0), __fadd_rn(a1, h1));
         }
         uint32_t zw[8];
