@@ -56,9 +56,11 @@ HEAD_PUSH_STREAMS = 7
 
 
 class SequenceParallel:
-    """`head_chunks` > 1 splits each block's K/V gathers and attention by heads, so that a chunk's attention runs
-    while the next chunk's K is still being gathered (every head's arithmetic is unchanged). `local=True` is a
-    partition of one rank even inside a process group: the whole sequence on this process, no exchange."""
+    """`split` ("auto", "tokens", "heads"; HN_SP_SPLIT): how attention's inputs move (see the module docstring).
+    `head_chunks` > 1 splits each block's K/V gathers and attention by heads, so that a chunk's attention runs
+    while the next chunk's K is still being gathered (every head's arithmetic is unchanged; token split only).
+    `local=True` is a partition of one rank even inside a process group: the whole sequence on this process, no
+    exchange."""
 
     def __init__(self, group=None, head_chunks=None, local=False, split=None):
         self.group = group
