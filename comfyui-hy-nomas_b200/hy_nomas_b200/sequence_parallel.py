@@ -55,7 +55,7 @@ HEADS_MIN_WORLD = 4
 HEAD_PUSH_STREAMS = 7
 # the head exchange's copy of a rank's own head group into its own buffers: a local DMA on a copy stream (1) or a
 # copy kernel on the compute stream (0) (HN_SP_HEAD_OWN_CE overrides)
-HEAD_OWN_CE = 0
+HEAD_OWN_CE = 1
 
 
 class SequenceParallel:
