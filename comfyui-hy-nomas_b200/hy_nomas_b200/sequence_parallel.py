@@ -53,9 +53,6 @@ HEADS_MIN_WORLD = 4
 # copy streams per kind of the head exchange, the peers spread over them (HN_SP_HEAD_PUSH_STREAMS overrides; capped
 # at world - 1): its per-peer copies are small (2.6 MB at 8 ranks) and latency-bound, so they go side by side
 HEAD_PUSH_STREAMS = 7
-# the head exchange's copy of a rank's own head group into its own buffers: a local DMA on a copy stream (1) or a
-# copy kernel on the compute stream (0) (HN_SP_HEAD_OWN_CE overrides)
-HEAD_OWN_CE = 1
 
 
 class SequenceParallel:
@@ -442,8 +439,6 @@ class HeadExchange(_IpcExchange):
         nstreams = max(1, min(sp.world - 1, int(os.environ.get("HN_SP_HEAD_PUSH_STREAMS", str(HEAD_PUSH_STREAMS)))))
         self._setup(sp, len(HEAD_KINDS) * sp.world)
         self.side = {k: [torch.cuda.Stream(self.device) for _ in range(nstreams)] for k in HEAD_KINDS}
-        self.own_ce = os.environ.get("HN_SP_HEAD_OWN_CE", str(HEAD_OWN_CE)) != "0"
-        self._own = {}                      # kind -> event after this block's own-group copy (own_ce)
 
     def _buffers(self, local, heads, head_dim, dtype, prefix):
         key = (local, heads, head_dim, dtype, prefix)
@@ -466,9 +461,8 @@ class HeadExchange(_IpcExchange):
 
     def _push_rows(self, kind, src, own):
         """On `kind`'s copy streams, after the current stream's work so far: for every peer (staggered from rank + 1,
-        spread over the streams) the strided DMA of `_HeadLayout.push_plan` followed by its flag; then the rank's
-        own head group, as a local DMA on the first copy stream that `wait` orders the current stream after
-        (`own_ce`), or as `own()` on the current stream."""
+        spread over the streams) the strided DMA of `_HeadLayout.push_plan` followed by its flag; then `own()` on
+        the current stream."""
         lib = self._lib
         ent, par = self._cur
         cur = torch.cuda.current_stream(self.device)
@@ -486,20 +480,9 @@ class HeadExchange(_IpcExchange):
             lib.check(lib.lib.hn_peer_push2d(ctypes.c_void_p(ent["addrs"][peer] + doff), dpitch,
                                              ctypes.c_void_p(src.data_ptr() + soff), spitch, width, height,
                                              flag, self.epoch, st), "hn_peer_push2d", launches=0)
-        if self.own_ce:
-            soff, spitch, doff, dpitch, width, height = ent["lay"].push_plan(kind, self.rank, self.rank, par,
-                                                                             ent["esz"])
-            lib.check(lib.lib.hn_peer_push2d(ctypes.c_void_p(ent["addrs"][self.rank] + doff), dpitch,
-                                             ctypes.c_void_p(src.data_ptr() + soff), spitch, width, height,
-                                             None, 0, ctypes.c_void_p(sides[0].cuda_stream)),
-                      "hn_peer_push2d", launches=0)
-            done = torch.cuda.Event()
-            done.record(sides[0])
-            self._own[kind] = done
         for side in sides:
             src.record_stream(side)
-        if not self.own_ce:
-            own()
+        own()
 
     def send(self, kind, src, bufs):
         """Send this rank's K, V or Q ([1, local, heads, head_dim], contiguous, complete on the current stream):
@@ -544,11 +527,6 @@ class HeadExchange(_IpcExchange):
             self._wait_flags(3 * self.world, 1, self.world, self.rank)
         else:
             raise ValueError(f"wait: kinds must be 'kvq' or 'o', got {kinds!r}")
-        cur = torch.cuda.current_stream(self.device)
-        for kind in kinds:
-            done = self._own.pop(kind, None)
-            if done is not None:
-                cur.wait_event(done)
 
 
 class HeadCollective:
